@@ -1,0 +1,220 @@
+"""ctypes wrapper of the CPU oracle (``oracle/libwavo_oracle.so``).
+
+TEST INFRASTRUCTURE ONLY: a restatement of the reference's CPU attention path (vladkens/wavo
+src/cpu/ops.rs, src/cpu/gemm.rs, src/cpu/mod.rs) used as the checker of the CUDA kernels and as the
+timed CPU baseline.  Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its
+``cpu_baseline`` leg and ``--impl reference`` arm) import this module; no product code does.
+Each function cites the reference function it restates (see wavo_oracle.cpp for file:line).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libwavo_oracle.so")
+_lib = None
+
+EPILOGUES = {"bias": 0, "silu": 1, "relu": 2, "residual": 3, "gelu": 4, "gelu_residual": 5, "tanh": 6}
+TY_F32, TY_F16, TY_Q8_0 = 0, 1, 8
+
+_f = ctypes.POINTER(ctypes.c_float)
+_sz = ctypes.c_size_t
+
+
+def build() -> None:
+    """Compile the oracle library in place (make)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.wo_random.argtypes = [_f, _sz, ctypes.c_uint32]
+        L.wo_to_half.argtypes = [ctypes.c_float]
+        L.wo_to_half.restype = ctypes.c_float
+        L.wo_to_half_n.argtypes = [_f, _f, _sz]
+        L.wo_f16_bits.argtypes = [ctypes.c_float]
+        L.wo_f16_bits.restype = ctypes.c_uint16
+        L.wo_f16_round_n.argtypes = [_f, _f, _sz]
+        for name in ("wo_exp", "wo_silu", "wo_gelu"):
+            getattr(L, name).argtypes = [ctypes.c_float]
+            getattr(L, name).restype = ctypes.c_float
+        L.wo_dot.argtypes = [_f, _f, _sz]
+        L.wo_dot.restype = ctypes.c_float
+        L.wo_attention.argtypes = [_f, _sz, _f, _sz, _f, _sz, _sz, _sz]
+        L.wo_relative_attention.argtypes = [_f, _f, _f, _f, _f, _sz, _sz, _sz]
+        L.wo_relative_attention.restype = ctypes.c_int
+        L.wo_attend.argtypes = [_f, _f, _sz, _sz, _f, _sz, _sz]
+        L.wo_pack_cache.argtypes = [_f, _sz, _sz, _sz, _f, _sz, _sz]
+        L.wo_rope.argtypes = [_f, _f, _sz, _sz, _sz, _sz, ctypes.c_int]
+        L.wo_rope_table.argtypes = [_sz, _sz, ctypes.c_double, _f]
+        L.wo_rel_positions.argtypes = [_sz, ctypes.c_int64, _sz, _f]
+        L.wo_pos_rows.argtypes = [_sz]
+        L.wo_pos_rows.restype = _sz
+        L.wo_linear_new.argtypes = [ctypes.c_int, _sz, _sz, ctypes.c_void_p, _f]
+        L.wo_linear_new.restype = ctypes.c_void_p
+        L.wo_linear_free.argtypes = [ctypes.c_void_p]
+        L.wo_gemm.argtypes = [_f, ctypes.c_void_p, _f, _sz, ctypes.c_int, ctypes.c_float]
+        L.wo_gemv.argtypes = [_f, ctypes.c_void_p, _f, ctypes.c_int, ctypes.c_float]
+        L.wo_set_threads.argtypes = [ctypes.c_int]
+        L.wo_threads.restype = ctypes.c_int
+        L.wo_set_vnni.argtypes = [ctypes.c_int]
+        L.wo_vnni.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"], (a.dtype, a.flags)
+    return a.ctypes.data_as(_f)
+
+
+def random(n: int, seed: int) -> np.ndarray:
+    """The reference tests' xorshift32 values in [-1, 1] (src/gpu/mod.rs:1717-1727)."""
+    out = np.empty(n, np.float32)
+    lib().wo_random(_p(out), n, seed)
+    return out
+
+
+def to_half(x: np.ndarray) -> np.ndarray:
+    """src/cpu/gemm.rs:210-221 `to_half`."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().wo_to_half_n(_p(x), _p(y), x.size)
+    return y
+
+
+def f16_round(x: np.ndarray) -> np.ndarray:
+    """`half::f16::from_f32(x).to_f32()` (IEEE round to nearest even)."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().wo_f16_round_n(_p(x), _p(y), x.size)
+    return y
+
+
+def exp(x: float) -> float:
+    """src/cpu/ops.rs:12-26 (Cephes expf)."""
+    return lib().wo_exp(x)
+
+
+def attention(qk, ld, v, ldv, t, heads, ch) -> np.ndarray:
+    """src/cpu/ops.rs:187-221 `attention` -> o [t][ch]."""
+    o = np.zeros(t * ch, np.float32)
+    lib().wo_attention(_p(qk), ld, _p(v), ldv, _p(o), t, heads, ch)
+    return o.reshape(t, ch)
+
+
+def relative_attention(qkv, pos, u, vb, t, heads, ch) -> np.ndarray:
+    """src/cpu/ops.rs:223-273 `relative_attention` over qkv [t][q|k|v] -> o [t][ch]."""
+    o = np.zeros(t * ch, np.float32)
+    if lib().wo_relative_attention(_p(qkv), _p(pos), _p(u), _p(vb), _p(o), t, heads, ch) != 0:
+        raise ValueError("relative_attention needs heads of a multiple of 16 dims")
+    return o.reshape(t, ch)
+
+
+def attend(q, kv, cols, n, heads, hd) -> np.ndarray:
+    """src/cpu/ops.rs:300-337 `attend` over a cache [K heads][cols][hd] + [V heads][cols][hd]."""
+    o = np.zeros(heads * hd, np.float32)
+    lib().wo_attend(_p(q), _p(kv), cols, n, _p(o), heads, hd)
+    return o
+
+
+def pack_cache(kv, rows, d, hd, cache, cols, col) -> None:
+    """src/cpu/transformer.rs:209-222 `Decoder::pack` (in place into cache)."""
+    lib().wo_pack_cache(_p(kv), rows, d, hd, _p(cache), cols, col)
+
+
+def rope(qkv, table, rows, heads, hd, rot, neox) -> None:
+    """src/cpu/ops.rs:339-355 `rope` (in place)."""
+    lib().wo_rope(_p(qkv), _p(table), rows, heads, hd, rot, int(neox))
+
+
+def rope_table(frames, hd, theta) -> np.ndarray:
+    """src/gigaam/mod.rs:88-96 `rope`: [frames][hd/2 cos | hd/2 sin]."""
+    out = np.empty(frames * hd, np.float32)
+    lib().wo_rope_table(frames, hd, float(theta), _p(out))
+    return out
+
+
+def rel_positions(d, first, rows) -> np.ndarray:
+    """src/conformer.rs:141-153 `rel_positions`."""
+    out = np.empty(rows * d, np.float32)
+    lib().wo_rel_positions(d, first, rows, _p(out))
+    return out.reshape(rows, d)
+
+
+def pos_rows(t: int) -> int:
+    """src/gpu/mod.rs:1060-1065."""
+    return 2 * t + 15
+
+
+class Linear:
+    """src/cpu/gemm.rs:36-75 `Linear` over GGUF bytes (F32 / F16 / Q8_0) and an optional bias."""
+
+    def __init__(self, ty: int, n: int, k: int, data: bytes, bias=None):
+        self.n, self.k, self.ty = n, k, ty
+        self._buf = ctypes.create_string_buffer(bytes(data), len(data))
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        self._h = lib().wo_linear_new(ty, n, k, ctypes.cast(self._buf, ctypes.c_void_p),
+                                      None if b is None else _p(b))
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.wo_linear_free(self._h)
+            self._h = None
+
+    def gemm(self, a: np.ndarray, m: int, c: np.ndarray | None = None, epilogue="bias", alpha=1.0):
+        """src/cpu/gemm.rs:125-177 `gemm`: c = epilogue(a·W^T + b); c updated in place."""
+        if c is None:
+            c = np.zeros(m * self.n, np.float32)
+        lib().wo_gemm(_p(a), self._h, _p(c), m, EPILOGUES[epilogue], alpha)
+        return c
+
+    def gemv(self, x: np.ndarray, c: np.ndarray | None = None, epilogue="bias", alpha=1.0):
+        """src/cpu/gemm.rs:179-208 `gemv`."""
+        if c is None:
+            c = np.zeros(self.n, np.float32)
+        lib().wo_gemv(_p(x), self._h, _p(c), EPILOGUES[epilogue], alpha)
+        return c
+
+
+def set_threads(n: int) -> None:
+    lib().wo_set_threads(n)
+
+
+def threads() -> int:
+    return lib().wo_threads()
+
+
+def set_vnni(mode: int) -> None:
+    """-1 detect (the reference's choice), 0 the f16 path, 1/2 the i16 VNNI path."""
+    lib().wo_set_vnni(mode)
+
+
+def vnni() -> int:
+    return lib().wo_vnni()
+
+
+def q8_0_bytes(values: np.ndarray, scale_mode: str = "absmax") -> bytes:
+    """GGUF Q8_0 blocks (f16 scale + 32 int8) of float rows, as the reference test builds them
+    (src/gpu/mod.rs:1888-1895: d = max|x| / 127 in f32, q = x / d rounded half away from zero,
+    saturated as Rust's `as i8`)."""
+    v = np.ascontiguousarray(values, np.float32).reshape(-1, 32)
+    out = bytearray()
+    for blk in v:
+        d = np.float32(np.abs(blk).max()) / np.float32(127.0)
+        if d != 0:
+            y = (blk / d).astype(np.float64)  # f32 quotient, as the reference divides
+            q = np.clip(np.sign(y) * np.floor(np.abs(y) + 0.5), -128, 127).astype(np.int8)
+        else:
+            q = np.zeros(32, np.int8)
+        out += np.float16(d).tobytes() + q.tobytes()
+    return bytes(out)

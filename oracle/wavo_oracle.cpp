@@ -1,0 +1,680 @@
+// CPU oracle for the wavo-b200 attention path.
+//
+// TEST INFRASTRUCTURE ONLY. This file restates, in C++, the reference's own CPU implementation of
+// the attention path (vladkens/wavo, Rust: src/cpu/ops.rs, src/cpu/gemm.rs, src/cpu/mod.rs) so that
+// the CUDA kernels can be checked against it and so that the reference CPU path can be timed on the
+// host cores. Only tests/, __graft_entry__.smoke() and bench.py (its cpu_baseline leg and its
+// `--impl reference` arm) may load it. No product code path calls into it.
+//
+// The reference is Rust and no Rust toolchain exists on this machine, so the reference itself cannot
+// be built; this restatement follows it function by function (file:line cited at each function).
+// Floating-point evaluation follows the reference exactly where the reference pins it: fused
+// multiply-adds only where the reference uses `_mm256_fmadd_ps` / `mul_add`, every other operation
+// separately rounded (the file is compiled with -ffp-contract=off).
+//
+// Parity pins: see tests/test_oracle.py. The oracle is checked against the naive references and the
+// inputs of the reference's own unit tests (src/gpu/mod.rs:1717-2330, src/cpu/gemm.rs:567-657).
+
+#include <immintrin.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#if !defined(__AVX2__) || !defined(__FMA__)
+#error "the oracle is built for x86-64-v3 (AVX2 + FMA): see oracle/Makefile"
+#endif
+
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// Threads: src/cpu/mod.rs:79-111 (`threads`, `par_each`). Each call spawns its threads, which take
+// the next item as they come free.
+// ---------------------------------------------------------------------------------------------
+
+int g_threads = 0;
+
+int threads() {
+  if (g_threads > 0) return g_threads;
+  unsigned n = std::thread::hardware_concurrency();
+  return n ? int(n) : 1;
+}
+
+void par_each(size_t items, const std::function<void(size_t)> &f) {
+  size_t spawn = std::min<size_t>(size_t(threads()), items);
+  if (spawn <= 1) {
+    for (size_t i = 0; i < items; ++i) f(i);
+    return;
+  }
+  std::atomic<size_t> next{0};
+  auto work = [&]() {
+    for (size_t i = next.fetch_add(1); i < items; i = next.fetch_add(1)) f(i);
+  };
+  std::vector<std::thread> pool;
+  for (size_t t = 1; t < spawn; ++t) pool.emplace_back(work);
+  work();
+  for (auto &t : pool) t.join();
+}
+
+// ---------------------------------------------------------------------------------------------
+// Scalars
+// ---------------------------------------------------------------------------------------------
+
+inline float from_bits(uint32_t b) {
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+inline uint32_t to_bits(float f) {
+  uint32_t b;
+  std::memcpy(&b, &f, 4);
+  return b;
+}
+
+// src/cpu/gemm.rs:210-221 `to_half`: x rounded to the nearest f16 value (ties to even), kept as an
+// f32; subnormal halves are multiples of 2^-24 and values past the f16 range keep their exponent.
+inline float to_half(float x) {
+  uint32_t b = to_bits(x);
+  float normal = from_bits((b + 0xfffu + ((b >> 13) & 1u)) & 0xffffe000u);
+  if (std::fabs(x) < from_bits(0x38800000u)) return std::nearbyint(x * 16777216.0f) / 16777216.0f;
+  return normal;
+}
+
+// IEEE binary16 from f32, round to nearest even, overflow to infinity, NaN kept quiet: the
+// conversion `half::f16::from_f32` (half 2.7.1) performs, as called at src/cpu/ops.rs:317 and
+// src/cpu/transformer.rs (Decoder::pack). Written from the IEEE 754 definition.
+inline uint16_t f16_bits(float x) {
+  uint32_t b = to_bits(x);
+  uint32_t sign = (b >> 16) & 0x8000u;
+  uint32_t exp = (b >> 23) & 0xffu;
+  uint32_t man = b & 0x7fffffu;
+  if (exp == 0xffu) return uint16_t(sign | 0x7c00u | (man ? 0x200u | (man >> 13) : 0u));
+  int e = int(exp) - 127 + 15;
+  if (e >= 0x1f) return uint16_t(sign | 0x7c00u);
+  if (e <= 0) {
+    if (e < -10) return uint16_t(sign);
+    uint32_t m = man | 0x800000u;
+    int shift = 14 - e;  // 24-bit significand down to the subnormal's 10 bits
+    uint32_t half = m >> shift;
+    uint32_t rem = m & ((1u << shift) - 1u);
+    uint32_t mid = 1u << (shift - 1);
+    if (rem > mid || (rem == mid && (half & 1u))) half += 1;
+    return uint16_t(sign | half);
+  }
+  uint32_t half = (uint32_t(e) << 10) | (man >> 13);
+  uint32_t rem = man & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (half & 1u))) half += 1;  // may carry into the exponent
+  return uint16_t(sign | half);
+}
+
+inline float f16_to_f32(uint16_t h) {
+  uint32_t sign = uint32_t(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  if (exp == 0) {
+    if (!man) return from_bits(sign);
+    float v = float(man) * from_bits(0x33800000u);  // man * 2^-24, exact
+    return sign ? -v : v;
+  }
+  if (exp == 0x1f) return from_bits(sign | 0x7f800000u | (man << 13));
+  return from_bits(sign | ((exp - 15 + 127) << 23) | (man << 13));
+}
+
+inline float f16_round(float x) { return f16_to_f32(f16_bits(x)); }
+
+// src/cpu/ops.rs:12-26 `exp`: Cephes' expf without branches. Every operation rounds separately.
+inline float cephes_exp(float x) {
+  const float MAGIC = 12582912.0f;
+  x = std::min(std::max(x, -87.0f), 88.0f);
+  float t = x * 1.44269504088896340736f + MAGIC;
+  float n = t - MAGIC;
+  float r = x - n * 0.6933594f + n * 2.1219444e-4f;
+  float p = 1.9875691e-4f * r + 1.3981999e-3f;
+  p = ((((p * r + 8.333452e-3f) * r + 4.1665796e-2f) * r + 0.16666665f) * r + 0.5f) * r * r;
+  uint32_t bits = (uint32_t(int32_t(to_bits(t)) - 0x4B400000 + 127)) << 23;
+  return (p + r + 1.0f) * from_bits(bits);
+}
+
+// src/cpu/ops.rs:28-40
+inline float silu(float x) { return x / (1.0f + cephes_exp(-x)); }
+inline float signum(float x) { return std::signbit(x) ? -1.0f : 1.0f; }
+inline float gelu(float x) {
+  float z = std::fabs(0.70710678118654752440f * x);
+  float t = 1.0f / (1.0f + 0.3275911f * z);
+  float p = (((1.0614054f * t - 1.453152f) * t + 1.4214138f) * t - 0.28449674f) * t + 0.2548296f;
+  return 0.5f * x * (1.0f + signum(x) * (1.0f - p * t * cephes_exp(-z * z)));
+}
+
+// src/cpu/ops.rs:55-63 `sum`: 8 lanes, then the lanes in order.
+inline float sum8(const float *v, size_t n) {
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (size_t i = 0; i < n; ++i) acc[i % 8] += v[i];
+  float s = 0.0f;
+  for (int i = 0; i < 8; ++i) s += acc[i];
+  return s;
+}
+
+// src/cpu/mod.rs:356-380 (x86 `sum` and `dot`): two 8-float FMA accumulators over chunks of 16,
+// the pairwise reduction of `sum`, then the tail in order.
+inline float hsum16(__m256 a, __m256 b) {
+  __m256 s = _mm256_add_ps(a, b);
+  __m128 q = _mm_add_ps(_mm256_castps256_ps128(s), _mm256_extractf128_ps(s, 1));
+  q = _mm_add_ps(q, _mm_movehl_ps(q, q));
+  return _mm_cvtss_f32(q) + _mm_cvtss_f32(_mm_shuffle_ps(q, q, 1));
+}
+
+float dot(const float *a, const float *b, size_t len) {
+  size_t n = len / 16 * 16;
+  __m256 acc0 = _mm256_setzero_ps(), acc1 = _mm256_setzero_ps();
+  for (size_t i = 0; i < n; i += 16) {
+    acc0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), acc0);
+    acc1 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 8), _mm256_loadu_ps(b + i + 8), acc1);
+  }
+  float tail = 0.0f;
+  for (size_t i = n; i < len; ++i) tail += a[i] * b[i];
+  return hsum16(acc0, acc1) + tail;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Panels and tiles: src/cpu/gemm.rs:23-28, 271-302, 354-377, 502-529
+// ---------------------------------------------------------------------------------------------
+
+constexpr size_t NR = 16;  // panel width
+constexpr size_t MR = 6;   // rows of `a` per tile
+
+inline size_t ceil_to(size_t x, size_t m) { return (x + m - 1) / m * m; }
+
+// src/cpu/gemm.rs:271-285 `panels`: the panels [k][NR] of b (a matrix [n][k] with row stride ld, or
+// with `transposed` [k][n]); zeros past n and past `rows` rows up to k.
+std::vector<float> panels(const float *b, size_t ld, size_t n, size_t k, size_t rows,
+                          bool transposed) {
+  std::vector<float> out((n + NR - 1) / NR * k * NR, 0.0f);
+  for (size_t p = 0; p * NR < n; ++p) {
+    float *o = out.data() + p * k * NR;
+    for (size_t j = 0; j < std::min(NR, n - NR * p); ++j) {
+      size_t col = NR * p + j;
+      for (size_t kk = 0; kk < rows; ++kk)
+        o[kk * NR + j] = transposed ? b[kk * ld + col] : b[col * ld + kk];
+    }
+  }
+  return out;
+}
+
+// src/cpu/gemm.rs:502-529 (x86 `tile`): MR rows of a times a panel [k][NR]; per output one FMA
+// chain over k in order.
+inline void tile(const float *const a[MR], const float *b, size_t k, float out[MR][NR]) {
+  __m256 acc[MR][2];
+  for (size_t r = 0; r < MR; ++r) acc[r][0] = acc[r][1] = _mm256_setzero_ps();
+  for (size_t kk = 0; kk < k; ++kk) {
+    __m256 b0 = _mm256_loadu_ps(b + kk * NR), b1 = _mm256_loadu_ps(b + kk * NR + 8);
+    for (size_t r = 0; r < MR; ++r) {
+      __m256 v = _mm256_broadcast_ss(a[r] + kk);
+      acc[r][0] = _mm256_fmadd_ps(v, b0, acc[r][0]);
+      acc[r][1] = _mm256_fmadd_ps(v, b1, acc[r][1]);
+    }
+  }
+  for (size_t r = 0; r < MR; ++r) {
+    _mm256_storeu_ps(out[r], acc[r][0]);
+    _mm256_storeu_ps(out[r] + 8, acc[r][1]);
+  }
+}
+
+// src/cpu/gemm.rs:287-302 `product`: c = a·b for m rows of a (stride lda, k long), b as panels;
+// all the panels' columns of c (stride ldc). The store adds a zero bias (`finish` with ZEROS).
+void product(const float *a, size_t lda, size_t m, const float *b, size_t b_len, size_t k,
+             float *c, size_t ldc) {
+  size_t np = b_len / (k * NR);
+  float acc[MR][NR];
+  for (size_t i = 0; i < m; i += MR) {
+    const float *rows[MR];
+    for (size_t r = 0; r < MR; ++r) rows[r] = a + std::min(i + r, m - 1) * lda;
+    for (size_t p = 0; p < np; ++p) {
+      tile(rows, b + p * k * NR, k, acc);
+      for (size_t r = 0; r < MR && i + r < m; ++r)
+        for (size_t j = 0; j < NR; ++j) c[(i + r) * ldc + NR * p + j] = acc[r][j] + 0.0f;
+    }
+  }
+}
+
+// src/cpu/ops.rs:275-287 `softmax`: scores × scale over the first t of each of m rows (rows of
+// ceil16(t)); the rest of each row zeroed.
+void softmax(float *scores, size_t m, size_t t, float scale) {
+  size_t tp = ceil_to(t, NR);
+  for (size_t r = 0; r < m; ++r) {
+    float *row = scores + r * tp;
+    float mx = -INFINITY;
+    for (size_t j = 0; j < t; ++j) mx = std::fmax(mx, row[j]);
+    mx = mx * scale;
+    for (size_t j = 0; j < t; ++j) row[j] = cephes_exp(row[j] * scale - mx);
+    float inv = 1.0f / sum8(row, t);
+    for (size_t j = 0; j < t; ++j) row[j] *= inv;
+    for (size_t j = t; j < tp; ++j) row[j] = 0.0f;
+  }
+}
+
+constexpr size_t QUERIES = 48;  // src/cpu/ops.rs:184-185
+
+}  // namespace
+
+// =============================================================================================
+// C ABI (ctypes)
+// =============================================================================================
+
+extern "C" {
+
+void wo_set_threads(int n) { g_threads = n; }
+int wo_threads(void) { return threads(); }
+
+// src/gpu/mod.rs:1717-1727 (the reference tests' `random`): xorshift32, values in [-1, 1].
+void wo_random(float *out, size_t n, uint32_t seed) {
+  uint32_t x = (seed * 2654435761u) | 1u;
+  const float max = float(UINT32_MAX);
+  for (size_t i = 0; i < n; ++i) {
+    x ^= x << 13;
+    x ^= x >> 17;
+    x ^= x << 5;
+    out[i] = float(x) / max * 2.0f - 1.0f;
+  }
+}
+
+float wo_to_half(float x) { return to_half(x); }
+void wo_to_half_n(const float *x, float *y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = to_half(x[i]);
+}
+uint16_t wo_f16_bits(float x) { return f16_bits(x); }
+float wo_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+void wo_f16_round_n(const float *x, float *y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = f16_round(x[i]);
+}
+float wo_exp(float x) { return cephes_exp(x); }
+float wo_silu(float x) { return silu(x); }
+float wo_gelu(float x) { return gelu(x); }
+float wo_dot(const float *a, const float *b, size_t n) { return dot(a, b, n); }
+
+// src/cpu/ops.rs:187-221 `attention`: row i's q at qk[i·ld..], its k at qk[i·ld + ch..], its v at
+// v[i·ldv..], into o [t][ch]; one head per job, 48 queries per step.
+void wo_attention(const float *qk, size_t ld, const float *v, size_t ldv, float *o, size_t t,
+                  size_t heads, size_t ch) {
+  size_t hd = ch / heads, tp = ceil_to(t, NR), hp = ceil_to(hd, NR);
+  float scale = 1.0f / std::sqrt(float(hd));
+  std::vector<std::vector<float>> outs(heads);
+  par_each(heads, [&](size_t h) {
+    std::vector<float> s(QUERIES * tp);
+    std::vector<float> keys = panels(qk + ch + h * hd, ld, t, hd, hd, false);
+    std::vector<float> values = panels(v + h * hd, ldv, hd, tp, t, true);
+    std::vector<float> &out = outs[h];
+    out.assign(t * hp, 0.0f);
+    for (size_t i = 0; i < t; i += QUERIES) {
+      size_t m = std::min(QUERIES, t - i);
+      product(qk + i * ld + h * hd, ld, m, keys.data(), keys.size(), hd, s.data(), tp);
+      softmax(s.data(), m, t, scale);
+      product(s.data(), tp, m, values.data(), values.size(), tp, out.data() + i * hp, hp);
+    }
+  });
+  // src/cpu/ops.rs:289-298 `gather`
+  for (size_t h = 0; h < heads; ++h)
+    for (size_t r = 0; r < t; ++r) std::memcpy(o + r * ch + h * hd, outs[h].data() + r * hp, hd * 4);
+}
+
+// src/gpu/mod.rs:1060-1065 `pos_rows`
+size_t wo_pos_rows(size_t t) { return 2 * t + 15; }
+
+// src/cpu/ops.rs:223-273 `relative_attention`: qkv [t][q | k | v], pos the projected positions
+// [pos_rows(t)][ch] (row r is position t + 15 - r), u and v [heads][hd]; score (i, j) is
+// ((q + u)_i·k_j + (q + v)_i·pos[j - i + t + 15]) / sqrt(hd). Heads of a multiple of 16 dims, as
+// the reference asserts (its `product` needs the value panels to fit the output rows); returns -1
+// otherwise.
+int wo_relative_attention(const float *qkv, const float *pos, const float *u, const float *vb,
+                          float *o, size_t t, size_t heads, size_t ch) {
+  size_t hd = ch / heads, tp = ceil_to(t, NR);
+  if (hd % NR != 0) return -1;
+  size_t pw = ceil_to(t + QUERIES + 2 * NR, NR);
+  float scale = 1.0f / std::sqrt(float(hd));
+  std::vector<std::vector<float>> outs(heads);
+  par_each(heads, [&](size_t h) {
+    std::vector<float> s(QUERIES * tp), sp(QUERIES * pw);
+    std::vector<float> keys = panels(qkv + ch + h * hd, 3 * ch, t, hd, hd, false);
+    std::vector<float> values = panels(qkv + 2 * ch + h * hd, 3 * ch, hd, tp, t, true);
+    std::vector<float> positions = panels(pos + h * hd, ch, 2 * t + 15, hd, hd, false);
+    std::vector<float> qu(t * hd), qv(t * hd);
+    for (size_t r = 0; r < t; ++r)
+      for (size_t c = 0; c < hd; ++c) {
+        float q = qkv[r * 3 * ch + h * hd + c];
+        qu[r * hd + c] = q + u[h * hd + c];
+        qv[r * hd + c] = q + vb[h * hd + c];
+      }
+    std::vector<float> &out = outs[h];
+    out.assign(t * hd, 0.0f);
+    for (size_t i = 0; i < t; i += QUERIES) {
+      size_t m = std::min(QUERIES, t - i);
+      product(qu.data() + i * hd, hd, m, keys.data(), keys.size(), hd, s.data(), tp);
+      size_t p0 = (t + 16 - i - m) / NR, p1 = (2 * t + 15 - i + NR - 1) / NR;
+      product(qv.data() + i * hd, hd, m, positions.data() + p0 * NR * hd, (p1 - p0) * NR * hd, hd,
+              sp.data(), pw);
+      for (size_t a = 0; a < m; ++a) {
+        // Query i + a, key j: position row j - i - a + t + 15, from p0·NR on.
+        const float *row = sp.data() + a * pw + (t + 15 - i - a - p0 * NR);
+        float *srow = s.data() + a * tp;
+        for (size_t j = 0; j < t; ++j) srow[j] += row[j];
+      }
+      softmax(s.data(), m, t, scale);
+      product(s.data(), tp, m, values.data(), values.size(), tp, out.data() + i * hd, hd);
+    }
+  });
+  for (size_t h = 0; h < heads; ++h)
+    for (size_t r = 0; r < t; ++r) std::memcpy(o + r * ch + h * hd, outs[h].data() + r * hd, hd * 4);
+  return 0;
+}
+
+// src/cpu/ops.rs:300-337 `attend`: one query per head, q [heads][hd] rounded to f16, over the first
+// n positions of a cache kv (K, then V, each [heads][cols][hd]), into o [heads][hd].
+void wo_attend(const float *q, const float *kv, size_t cols, size_t n, float *o, size_t heads,
+               size_t hd) {
+  float scale = 1.0f / std::sqrt(float(hd));
+  const float *k = kv, *v = kv + heads * cols * hd;
+  size_t jobs = std::min(std::max<size_t>((heads * n * hd) >> 16, 1), heads);
+  size_t per = (heads + jobs - 1) / jobs;
+  size_t njobs = (heads + per - 1) / per;
+  par_each(njobs, [&](size_t jb) {
+    std::vector<float> qh(hd), s(n);
+    for (size_t h = jb * per; h < std::min(heads, (jb + 1) * per); ++h) {
+      for (size_t c = 0; c < hd; ++c) qh[c] = f16_round(q[h * hd + c]);
+      const float *kh = k + h * cols * hd, *vh = v + h * cols * hd;
+      for (size_t j = 0; j < n; ++j) s[j] = dot(qh.data(), kh + j * hd, hd) * scale;
+      float mx = -INFINITY;
+      for (size_t j = 0; j < n; ++j) mx = std::fmax(mx, s[j]);
+      for (size_t j = 0; j < n; ++j) s[j] = cephes_exp(s[j] - mx);
+      float inv = 1.0f / sum8(s.data(), n);
+      float *oh = o + h * hd;
+      for (size_t c = 0; c < hd; ++c) oh[c] = 0.0f;
+      for (size_t j = 0; j < n; ++j)
+        for (size_t c = 0; c < hd; ++c) oh[c] += s[j] * vh[j * hd + c];
+      for (size_t c = 0; c < hd; ++c) oh[c] *= inv;
+    }
+  });
+}
+
+// src/cpu/transformer.rs:209-222 `Decoder::pack`: rows [k | v] of kv (2·d floats each) into the
+// cache (K heads then V heads, each [cols][hd]) at positions col.., rounded to f16.
+void wo_pack_cache(const float *kv, size_t rows, size_t d, size_t hd, float *cache, size_t cols,
+                   size_t col) {
+  for (size_t j = 0; j < rows; ++j)
+    for (size_t h = 0; h < 2 * d / hd; ++h) {
+      size_t at = (h * cols + col + j) * hd;
+      for (size_t c = 0; c < hd; ++c) cache[at + c] = f16_round(kv[j * 2 * d + h * hd + c]);
+    }
+}
+
+// src/cpu/ops.rs:339-355 `rope`: in place over rows [q | k | v] of heads × hd, row j at table row
+// j (rot/2 cosines then rot/2 sines); pairs (2i, 2i+1), or with neox (i, i + rot/2), of q's and k's
+// heads rotate.
+void wo_rope(float *qkv, const float *table, size_t rows, size_t heads, size_t hd, size_t rot,
+             int neox) {
+  size_t half = rot / 2, pair = neox ? half : 1, step = neox ? 1 : 2;
+  for (size_t r = 0; r < rows; ++r) {
+    float *row = qkv + r * 3 * heads * hd;
+    const float *cs = table + r * rot, *sn = cs + half;
+    for (size_t hh = 0; hh < 2 * heads; ++hh) {
+      float *head = row + hh * hd;
+      for (size_t i = 0; i < half; ++i) {
+        float a = head[step * i], b = head[step * i + pair];
+        head[step * i] = a * cs[i] - b * sn[i];
+        head[step * i + pair] = a * sn[i] + b * cs[i];
+      }
+    }
+  }
+}
+
+// src/gigaam/mod.rs:88-96 `rope`: per position hd/2 cosines then hd/2 sines, angles in f64.
+void wo_rope_table(size_t frames, size_t hd, double theta, float *out) {
+  for (size_t t = 0; t < frames; ++t)
+    for (size_t i = 0; i < hd / 2; ++i) {
+      double a = double(t) * std::pow(theta, -2.0 * double(i) / double(hd));
+      out[t * hd + i] = float(std::cos(a));
+      out[t * hd + hd / 2 + i] = float(std::sin(a));
+    }
+}
+
+// src/conformer.rs:141-153 `rel_positions`: the sinusoidal table of positions first, first - 1, …
+// for rows rows of d: [2k] = sin(pos·d_k), [2k + 1] = cos(pos·d_k), in f32.
+void wo_rel_positions(size_t d, int64_t first, size_t rows, float *out) {
+  std::vector<float> div(d / 2);
+  float c = -std::log(10000.0f) / float(d);
+  for (size_t k = 0; k < d / 2; ++k) div[k] = std::exp(float(2 * k) * c);
+  for (size_t r = 0; r < rows; ++r) {
+    float p = float(first - int64_t(r));
+    for (size_t k = 0; k < d / 2; ++k) {
+      out[r * d + 2 * k] = std::sin(p * div[k]);
+      out[r * d + 2 * k + 1] = std::cos(p * div[k]);
+    }
+  }
+}
+
+}  // extern "C"
+
+// =============================================================================================
+// Linear layers and the projection GEMM: src/cpu/gemm.rs:30-177, src/cpu/mod.rs:237-261
+// =============================================================================================
+
+namespace {
+
+enum Ty { TY_F32 = 0, TY_F16 = 1, TY_Q8_0 = 8 };  // GGUF type ids, src/gguf.rs:14-38
+
+enum Epi { E_BIAS = 0, E_SILU, E_RELU, E_RESIDUAL, E_GELU, E_GELU_RESIDUAL, E_TANH };
+
+struct Linear {
+  size_t n, k;
+  int ty;
+  std::vector<float> f32;      // F32
+  std::vector<uint16_t> f16;   // F16 bits
+  std::vector<int8_t> q;       // Q8_0 values [n][k]
+  std::vector<float> d;        // Q8_0 scales [n][k/32]
+  std::vector<float> bias;     // n values
+};
+
+// src/cpu/gemm.rs:339-352 `finish`
+inline void finish(float *c, const float *acc, const float *bias, size_t len, int epi,
+                   float alpha) {
+  for (size_t i = 0; i < len; ++i) {
+    float v = acc[i] + bias[i];
+    switch (epi) {
+      case E_BIAS: c[i] = v; break;
+      case E_SILU: c[i] = silu(v); break;
+      case E_RELU: c[i] = std::fmax(v, 0.0f); break;
+      case E_RESIDUAL: c[i] += alpha * v; break;
+      case E_GELU: c[i] = gelu(v); break;
+      case E_GELU_RESIDUAL: c[i] += gelu(v); break;
+      default: c[i] = std::tanh(std::min(std::max(v, -10.0f), 10.0f)); break;
+    }
+  }
+}
+
+// src/cpu/gemm.rs:87-122 `Linear::pack`: panel p as f32 [k][NR], W rounded to f16 (F16 exact).
+void pack_panel(const Linear &l, size_t p, float *out) {
+  size_t k = l.k;
+  for (size_t j = 0; j < NR; ++j) {
+    size_t row = NR * p + j;
+    for (size_t kk = 0; kk < k; ++kk) {
+      float w = 0.0f;
+      if (row < l.n) {
+        if (l.ty == TY_Q8_0) w = to_half(float(l.q[row * k + kk]) * l.d[row * k / 32 + kk / 32]);
+        else if (l.ty == TY_F16) w = f16_to_f32(l.f16[row * k + kk]);
+        else w = to_half(l.f32[row * k + kk]);
+      }
+      out[kk * NR + j] = w;
+    }
+  }
+}
+
+// CPUID: AVX-VNNI (leaf 7.1 EAX bit 4) or AVX512-VNNI with AVX512VL (leaf 7.0 ECX bit 11, EBX bit 31).
+// src/cpu/mod.rs:339-354 `vnni`.
+int detect_vnni() {
+  unsigned a, b, c, d;
+  __asm__ volatile("cpuid" : "=a"(a), "=b"(b), "=c"(c), "=d"(d) : "a"(7), "c"(1));
+  if (a & (1u << 4)) return 1;
+  __asm__ volatile("cpuid" : "=a"(a), "=b"(b), "=c"(c), "=d"(d) : "a"(7), "c"(0));
+  if ((c & (1u << 11)) && (b & (1u << 31))) return 2;
+  return 0;
+}
+int g_vnni = -1;  // -1: detect; 0: off (the f16 path); 1/2: on
+
+// src/cpu/gemm.rs:385-407 `x86::quantize`: rows per 32 values as i16 q and a scale d,
+// q = round(x / d) (x · 32767 / max, rounded to nearest even, saturated), d = max|x| / 32767.
+void quantize(const float *x, int16_t *q, float *d, size_t blocks) {
+  for (size_t blk = 0; blk < blocks; ++blk) {
+    const float *v = x + 32 * blk;
+    float mx = 0.0f;
+    for (int i = 0; i < 32; ++i) mx = std::fmax(mx, std::fabs(v[i]));
+    d[blk] = mx / 32767.0f;
+    float id = mx > 0.0f ? 32767.0f / mx : 0.0f;
+    for (int i = 0; i < 32; ++i) {
+      float s = v[i] * id;
+      long r = std::lrintf(s);  // round to nearest even, as cvtps_epi32
+      if (!(s == s) || s >= 2147483648.0f || s < -2147483648.0f) r = INT32_MIN;
+      q[32 * blk + i] = int16_t(std::min<long>(std::max<long>(r, -32768), 32767));
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void wo_set_vnni(int mode) { g_vnni = mode; }
+int wo_vnni(void) {
+  if (g_vnni < 0) g_vnni = detect_vnni();
+  return g_vnni;
+}
+
+// src/cpu/gemm.rs:45-75 `Linear::new`: weights [n][k] in a GGUF type (0 F32, 1 F16, 8 Q8_0: blocks
+// of an f16 scale and 32 int8), and n biases (NULL for zeros).
+void *wo_linear_new(int ty, size_t n, size_t k, const uint8_t *bytes, const float *bias) {
+  Linear *l = new Linear();
+  l->n = n;
+  l->k = k;
+  l->ty = ty;
+  if (ty == TY_F32) {
+    l->f32.resize(n * k);
+    std::memcpy(l->f32.data(), bytes, n * k * 4);
+  } else if (ty == TY_F16) {
+    l->f16.resize(n * k);
+    std::memcpy(l->f16.data(), bytes, n * k * 2);
+  } else {
+    l->q.resize(n * k);
+    l->d.resize(n * k / 32);
+    for (size_t blk = 0; blk < n * k / 32; ++blk) {
+      const uint8_t *b = bytes + 34 * blk;
+      l->d[blk] = f16_to_f32(uint16_t(b[0] | (b[1] << 8)));
+      std::memcpy(l->q.data() + 32 * blk, b + 2, 32);
+    }
+  }
+  l->bias.assign(n, 0.0f);
+  if (bias) std::memcpy(l->bias.data(), bias, n * 4);
+  return l;
+}
+
+void wo_linear_free(void *l) { delete static_cast<Linear *>(l); }
+
+// src/cpu/gemm.rs:125-177 `gemm`: c = epilogue(a·W^T + b) for m rows of a [m][k] into c [m][n].
+// Q8_0 weights on a CPU with VNNI take the i16 path (a quantized per 32 values, exact i32 sums);
+// otherwise a and W are rounded to f16 and the f32 tile runs.
+void wo_gemm(const float *a, const void *lp, float *c, size_t m, int epi, float alpha) {
+  const Linear &l = *static_cast<const Linear *>(lp);
+  size_t k = l.k, n = l.n, panels_n = (n + NR - 1) / NR;
+  if (l.ty == TY_Q8_0 && wo_vnni() > 0) {
+    std::vector<int16_t> aq(m * k);
+    std::vector<float> ad(m * k / 32);
+    par_each((m + 63) / 64, [&](size_t g) {
+      size_t r0 = g * 64, r1 = std::min(m, r0 + 64);
+      quantize(a + r0 * k, aq.data() + r0 * k, ad.data() + r0 * k / 32, (r1 - r0) * k / 32);
+    });
+    size_t blocks = k / 32;
+    // One job per (row group, panel group); exact integer sums make the order of products free.
+    par_each(panels_n, [&](size_t p) {
+      float acc[NR];
+      for (size_t r = 0; r < m; ++r) {
+        const int16_t *ar = aq.data() + r * k;
+        const float *adr = ad.data() + r * blocks;
+        size_t cols = std::min(NR, n - NR * p);
+        for (size_t j = 0; j < cols; ++j) {
+          size_t row = NR * p + j;
+          const int8_t *wq = l.q.data() + row * k;
+          const float *wd = l.d.data() + row * blocks;
+          float s_acc = 0.0f;
+          for (size_t blk = 0; blk < blocks; ++blk) {
+            __m256i s = _mm256_setzero_si256();
+            for (int h = 0; h < 2; ++h) {
+              __m256i av = _mm256_loadu_si256((const __m256i *)(ar + 32 * blk + 16 * h));
+              __m256i wv = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(wq + 32 * blk + 16 * h)));
+              s = _mm256_add_epi32(s, _mm256_madd_epi16(av, wv));
+            }
+            __m128i s4 = _mm_add_epi32(_mm256_castsi256_si128(s), _mm256_extracti128_si256(s, 1));
+            s4 = _mm_add_epi32(s4, _mm_shuffle_epi32(s4, 0x4e));
+            s4 = _mm_add_epi32(s4, _mm_shuffle_epi32(s4, 0xb1));
+            int32_t sum = _mm_cvtsi128_si32(s4);
+            s_acc = std::fma(float(sum), adr[blk] * wd[blk], s_acc);
+          }
+          acc[j] = s_acc;
+        }
+        finish(c + r * n + NR * p, acc, l.bias.data() + NR * p, cols, epi, alpha);
+      }
+    });
+    return;
+  }
+  std::vector<float> ah(m * k);
+  for (size_t i = 0; i < m * k; ++i) ah[i] = to_half(a[i]);
+  // Groups of panels that fit 384 KiB, then row splits (src/cpu/gemm.rs:223-269).
+  size_t bytes = 4 * k * NR;
+  size_t per_group = std::min(std::max<size_t>((384u << 10) / bytes, 1), panels_n);
+  size_t groups = (panels_n + per_group - 1) / per_group;
+  size_t splits = std::max<size_t>(
+      std::min((size_t(4 * threads()) + groups - 1) / groups, (m + 8 * MR - 1) / (8 * MR)), 1);
+  size_t rows = ceil_to((m + splits - 1) / splits, MR);
+  par_each(groups * splits, [&](size_t job) {
+    size_t g = job / splits, s = job % splits;
+    size_t p0 = g * per_group, p1 = std::min(panels_n, (g + 1) * per_group);
+    std::vector<float> buf((p1 - p0) * k * NR);
+    for (size_t p = p0; p < p1; ++p) pack_panel(l, p, buf.data() + (p - p0) * k * NR);
+    size_t r0 = s * rows, r1 = std::min(m, (s + 1) * rows);
+    float acc[MR][NR];
+    for (size_t row = r0; row < r1; row += MR) {
+      const float *ar[MR];
+      for (size_t r = 0; r < MR; ++r) ar[r] = ah.data() + std::min(row + r, r1 - 1) * k;
+      for (size_t p = p0; p < p1; ++p) {
+        tile(ar, buf.data() + (p - p0) * k * NR, k, acc);
+        size_t cols = std::min(NR, n - NR * p);
+        for (size_t r = 0; r < MR && row + r < r1; ++r)
+          finish(c + (row + r) * n + NR * p, acc[r], l.bias.data() + NR * p, cols, epi, alpha);
+      }
+    }
+  });
+}
+
+// src/cpu/gemm.rs:179-208 `gemv`: one row x [k] through the layer in f32 (W not rounded to f16).
+void wo_gemv(const float *x, const void *lp, float *c, int epi, float alpha) {
+  const Linear &l = *static_cast<const Linear *>(lp);
+  size_t k = l.k, n = l.n;
+  std::vector<float> acc(n), wide(k);
+  for (size_t r = 0; r < n; ++r) {
+    if (l.ty == TY_F32) {
+      acc[r] = dot(l.f32.data() + r * k, x, k);
+    } else if (l.ty == TY_F16) {
+      for (size_t i = 0; i < k; ++i) wide[i] = f16_to_f32(l.f16[r * k + i]);
+      acc[r] = dot(wide.data(), x, k);
+    } else {
+      // Q8::rows (src/cpu/mod.rs:412-436): (q · d) rounded to f32 (exact), FMA with x per lane.
+      for (size_t i = 0; i < k; ++i) wide[i] = float(l.q[r * k + i]) * l.d[(r * k + i) / 32];
+      acc[r] = dot(wide.data(), x, k);
+    }
+  }
+  finish(c, acc.data(), l.bias.data(), n, epi, alpha);
+}
+
+}  // extern "C"
