@@ -1,0 +1,209 @@
+/*
+ * wavo_cuda.h — C ABI of the wavo-b200 attention path (libwavo_cuda.so / libwavo_cuda.a, sm_100a).
+ *
+ * This is the drop-in boundary for the multi-head attention path of vladkens/wavo: the encoders'
+ * self-attention (Parakeet relative positions, GigaAM rotary, Whisper) with their QKV / output /
+ * linear_pos projections, and the Whisper decoder's attention over F16 KV caches. Each entry point
+ * replaces one method of the reference's GPU backend op interface (`gpu::Gpu` / `gpu::Pass`,
+ * src/gpu/mod.rs), cited beside it; the argument meanings and buffer layouts are the reference's.
+ *
+ * Conventions
+ *  - Pointers named as buffers are device pointers (cudaMalloc or wavo_malloc), except where a
+ *    comment says "host".
+ *  - Calls enqueue work on the context's stream and return at once; argument errors return at
+ *    once; device faults and kernel wait timeouts surface at wavo_sync (as the reference's surface
+ *    at `Gpu::run` / `Gpu::finish`, src/gpu/mod.rs:969-1003).
+ *  - No exception crosses this boundary. A context serialises its calls with an internal mutex
+ *    (the reference's `Gpu::busy`, src/gpu/mod.rs:233-235); wavo_linear_create may be called from
+ *    many threads at once.
+ *  - Element types: WAVO_F32 is the reference's buffer type; WAVO_F16 is the B200 fast path (the
+ *    GEMM writes f16 operands the attention kernel loads with TMA, and the attention writes f16
+ *    rows the output projection loads directly).
+ */
+#ifndef WAVO_CUDA_H
+#define WAVO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum wavo_status {
+  WAVO_OK = 0,
+  WAVO_EINVAL = 1,       /* bad argument: shape, layout, type (reference: Error::Model via bail!) */
+  WAVO_ENOMEM = 2,       /* device allocation failed */
+  WAVO_ECUDA = 3,        /* CUDA runtime error (reference: Error::Gpu) */
+  WAVO_ETIMEDOUT = 4,    /* wavo_sync ran past its limit (reference: Error::Poll) */
+  WAVO_EUNSUPPORTED = 5, /* no sm_100 device, or a shape outside the kernels' range */
+  WAVO_EDEVICE = 6       /* a kernel's bounded wait gave up (the device error word was set) */
+} wavo_status;
+
+typedef enum wavo_dtype { WAVO_F32 = 0, WAVO_F16 = 1 } wavo_dtype;
+
+/* GGUF tensor types the reference reads (src/gguf.rs:14-38). */
+typedef enum wavo_ggml_type { WAVO_GGML_F32 = 0, WAVO_GGML_F16 = 1, WAVO_GGML_Q8_0 = 8 } wavo_ggml_type;
+
+/* The reference's `Epilogue` (src/gpu/mod.rs:431-456), in its kernel order. */
+typedef enum wavo_epilogue {
+  WAVO_EPI_BIAS = 0,
+  WAVO_EPI_SILU = 1,
+  WAVO_EPI_RELU = 2,
+  WAVO_EPI_RESIDUAL = 3, /* c += alpha * (a·W^T + b) */
+  WAVO_EPI_GELU = 4,
+  WAVO_EPI_GELU_RESIDUAL = 5,
+  WAVO_EPI_TANH = 6
+} wavo_epilogue;
+
+typedef struct wavo_ctx wavo_ctx;
+typedef struct wavo_linear wavo_linear;
+typedef struct wavo_graph wavo_graph;
+
+/* ---- device and context: replaces Gpu::new (src/gpu/mod.rs:461-578) -------------------- */
+
+/* Number of CUDA devices visible to this process. */
+int wavo_device_count(void);
+
+/* A context on `device`: checks the device is sm_100 (B200 class), creates a stream and the
+ * device error word. Replaces Gpu::new (src/gpu/mod.rs:461-578). */
+wavo_status wavo_create(int device, wavo_ctx **out);
+void wavo_destroy(wavo_ctx *ctx);
+
+/* The last error message of the context (or of the last failed wavo_create when ctx is NULL). */
+const char *wavo_last_error(const wavo_ctx *ctx);
+
+/* Runs the context's work on `stream` (a cudaStream_t; NULL restores the context's own). */
+wavo_status wavo_set_stream(wavo_ctx *ctx, void *stream);
+void *wavo_get_stream(const wavo_ctx *ctx);
+int wavo_sm_count(const wavo_ctx *ctx);
+
+/* ---- buffers: replaces Gpu::buffer / upload / write / readback (src/gpu/mod.rs:741-756) -- */
+
+wavo_status wavo_malloc(wavo_ctx *ctx, size_t bytes, void **out);
+wavo_status wavo_free(wavo_ctx *ctx, void *ptr);
+/* Host -> device and device -> host copies on the context's stream (host: pinned for overlap). */
+wavo_status wavo_upload(wavo_ctx *ctx, void *dst, const void *host_src, size_t bytes);
+wavo_status wavo_download(wavo_ctx *ctx, void *host_dst, const void *src, size_t bytes);
+wavo_status wavo_memset(wavo_ctx *ctx, void *dst, int value, size_t bytes);
+/* Grows the context's scratch so that the calls that follow allocate nothing (needed before a
+ * graph capture). */
+wavo_status wavo_reserve(wavo_ctx *ctx, size_t workspace_bytes);
+/* Waits for the context's stream, at most timeout_ms (0: no limit). Device faults, the kernels'
+ * wait timeouts (WAVO_EDEVICE) and the limit (WAVO_ETIMEDOUT) surface here. Replaces the
+ * completion check of Gpu::run / Gpu::finish (src/gpu/mod.rs:969-1003). */
+wavo_status wavo_sync(wavo_ctx *ctx, uint32_t timeout_ms);
+
+/* ---- linear layers: replaces Gpu::linear (src/gpu/mod.rs:758-834) ------------------------ */
+
+/* Weights [rows][k] as GGUF tensor bytes of `ggml_type` (host), stacked along the rows, and a host
+ * bias: NULL/0 for zeros, `rows` values, or rows + dual values — the extra `dual` values write the
+ * first `dual` outputs a second time after the others with those biases (one q with the two
+ * position biases u and v, src/conformer.rs:174-200). k % 32 == 0. Output columns: the rows when
+ * a multiple of 32, else the rows padded to 64 (those outputs are epilogue(0)), plus `dual`.
+ * Thread-safe. */
+wavo_status wavo_linear_create(wavo_ctx *ctx, int ggml_type, uint32_t rows, uint32_t k,
+                               const void *data, const float *bias, size_t bias_len,
+                               wavo_linear **out);
+void wavo_linear_destroy(wavo_linear *l);
+/* Linear::width (src/gpu/mod.rs:408-413): output columns including the dual ones. */
+uint32_t wavo_linear_width(const wavo_linear *l);
+uint32_t wavo_linear_k(const wavo_linear *l);
+
+/* ---- projections: replaces Pass::gemm (src/gpu/mod.rs:1394-1425) and Pass::gemv (1461-1467) */
+
+/* c = epilogue(a·W^T + b) for m rows of a ([m][lda], a_dtype) into c ([m][ldc], c_dtype); lda = 0
+ * means k, ldc = 0 means wavo_linear_width. a and W are rounded to f16 (the reference GPU GEMM's
+ * rounding); sums in f32. */
+wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, const wavo_linear *l,
+                      void *c, int c_dtype, uint32_t ldc, uint32_t m, int epilogue, float alpha);
+
+/* Pass::gemv: c[offset..] = epilogue(a·W^T + b) for one f32 row, W not rounded (f32 sums). */
+wavo_status wavo_gemv(wavo_ctx *ctx, const float *a, const wavo_linear *l, float *c, int epilogue,
+                      float alpha, uint32_t offset);
+/* The same for `rows` rows at once (the decoder of a batch of segments): a [rows][lda],
+ * c [rows][ldc]. rows <= 32. */
+wavo_status wavo_gemv_rows(wavo_ctx *ctx, const float *a, uint32_t lda, const wavo_linear *l,
+                           float *c, uint32_t ldc, uint32_t rows, int epilogue, float alpha);
+
+/* ---- encoder attention: replaces Pass::attention (src/gpu/mod.rs:1556-1605) --------------- */
+
+/* Pass::attention over one segment of t rows, in the reference's three layouts:
+ *   v != NULL, pos == NULL : qk [t][q | k] and v [t][heads·hd]  (rotary: GigaAM)
+ *   v == NULL, pos == NULL : qk [t][q | k | v]                   (Whisper)
+ *   v == NULL, pos != NULL : qk [t][q+u | k | v | q+v] and pos [pos_rows(t)][heads·hd], row r the
+ *                            projected relative position t + 15 - r (Parakeet): score (i, j) =
+ *                            ((q+u)_i·k_j + (q+v)_i·pos[j - i + t + 15]) / sqrt(hd).
+ * o [t][heads·hd]. `dtype` is the element type of qk, v, pos and o. hd <= 128. */
+wavo_status wavo_attention(wavo_ctx *ctx, const void *qk, const void *v, const void *pos, void *o,
+                           uint32_t t, uint32_t heads, uint32_t hd, int dtype);
+
+/* The same over `nseg` independent segments in one launch (the reference runs one at a time,
+ * src/lib.rs:844-900): the operands hold `rows` rows, segment z is rows seg_start[z] ..
+ * + seg_len[z] of every operand (seg_start, seg_len: device int32 arrays); max_len >= every
+ * seg_len. A key-padding mask is the same call with the padded rows left out of seg_len. With
+ * positions, pos holds pos_rows(pos_t) rows, row r the relative position pos_t + 15 - r,
+ * pos_t >= every seg_len, and serves all segments. o has o_dtype; its rows outside the segments
+ * are left as they are. */
+wavo_status wavo_attention_varlen(wavo_ctx *ctx, const void *qk, const void *v, const void *pos,
+                                  void *o, uint32_t rows, const int32_t *seg_start,
+                                  const int32_t *seg_len, uint32_t nseg, uint32_t max_len,
+                                  uint32_t pos_t, uint32_t heads, uint32_t hd, int dtype,
+                                  int o_dtype);
+
+/* pos_rows (src/gpu/mod.rs:1060-1065): 2t + 15. */
+uint32_t wavo_pos_rows(uint32_t t);
+
+/* Pass::rope (src/gpu/mod.rs:1630-1649): in place over rows [q | k | v] of heads x hd at positions
+ * pos..: in q's and k's heads the pairs (2i, 2i+1) for 2i < rot rotate, or with neox (i, i+rot/2);
+ * the table holds per position rot/2 cosines, then as many sines. `stride` = 0 means 3·heads·hd. */
+wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, uint32_t stride,
+                      uint32_t rows, uint32_t pos, uint32_t heads, uint32_t hd, uint32_t rot,
+                      int neox);
+
+/* ---- decoder attention: replaces Pass::pack (src/gpu/mod.rs:1507-1522), Pass::attend
+ * (1485-1505) and attend_len (1053-1059) -------------------------------------------------- */
+
+/* Pass::pack: rows rows of x (f32) from float src on, stride floats apart, each K then V of d
+ * floats, into the F16 cache (32-bit words) of cols positions at positions col..: K transposed
+ * (pair i of position j at word i·cols + j), then V by position (word d/2·cols + j·d/2 + i). */
+wavo_status wavo_pack(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride, void *cache,
+                      uint32_t rows, uint32_t d, uint32_t cols, uint32_t col);
+
+/* attend_len: floats of wavo_attend's `part` scratch for up to n keys (per segment). */
+size_t wavo_attend_len(uint32_t n, uint32_t heads, uint32_t hd);
+
+/* Pass::attend: one query per head, q [heads·hd] (rounded to f16), over keys 0..n of a cache of
+ * cols positions (see wavo_pack), into o [heads·hd], through part (wavo_attend_len floats). */
+wavo_status wavo_attend(wavo_ctx *ctx, const float *q, const void *kv, float *part, float *o,
+                        uint32_t n, uint32_t cols, uint32_t heads, uint32_t hd);
+
+/* The same for `batch` segments in one launch: segment b's query at q + b·q_stride floats, its
+ * cache at kv + b·kv_stride 32-bit words, its output at o + b·o_stride floats; part holds
+ * batch·wavo_attend_len(n, heads, hd) floats. */
+wavo_status wavo_attend_batch(wavo_ctx *ctx, const float *q, uint64_t q_stride, const void *kv,
+                              uint64_t kv_stride, float *part, float *o, uint64_t o_stride,
+                              uint32_t n, uint32_t cols, uint32_t heads, uint32_t hd,
+                              uint32_t batch);
+
+/* ---- graphs: record a sequence of calls once, replay it with one launch ----------------- */
+
+/* Starts capturing the context's stream (the context's own stream must be current; reserve the
+ * scratch first). Every call until wavo_capture_end is recorded, not run. */
+wavo_status wavo_capture_begin(wavo_ctx *ctx);
+wavo_status wavo_capture_end(wavo_ctx *ctx, wavo_graph **out);
+wavo_status wavo_graph_launch(wavo_ctx *ctx, const wavo_graph *g);
+void wavo_graph_destroy(wavo_graph *g);
+
+/* ---- sharding: the segment partition of the multi-GPU runner ---------------------------- */
+
+/* Longest-processing-time-first assignment of n independent items of the given costs to `parts`
+ * devices: assign[i] = device of item i. No reference counterpart (the reference transcribes the
+ * pieces of src/split.rs one after another, src/lib.rs:844-900). */
+wavo_status wavo_partition_lpt(const uint64_t *cost, uint32_t n, uint32_t parts, uint32_t *assign);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WAVO_CUDA_H */

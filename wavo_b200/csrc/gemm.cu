@@ -1,0 +1,344 @@
+// Projection GEMM for sm_100a: c = epilogue(a · W^T + bias), the reference's `Pass::gemm`
+// (src/gpu/mod.rs:1394-1425, gemm.wgsl:167-242) re-designed for the 5th-generation tensor cores.
+//
+// a [m][k] f16 and W [n][k] f16 are streamed by TMA into 128-byte-swizzled shared-memory stages;
+// one thread issues tcgen05.mma (M=128, N=128, K=16, f32 accumulators in TMEM); four epilogue warps
+// read the accumulators back with tcgen05.ld (one row per thread), add the bias, apply the epilogue
+// and store the row. The kernel is persistent (one CTA per SM walks the output tiles) and keeps two
+// accumulators in TMEM, so the epilogue of one tile overlaps the MMAs of the next.
+//
+// Numerics match the reference GPU GEMM: a and W rounded to f16 (round to nearest even), products
+// exact, sums in f32. Dual outputs (a bias longer than the rows) write the first `dual` outputs a
+// second time at columns cols.. with their own bias and no epilogue, as src/gpu/mod.rs:758-834.
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace wv {
+namespace {
+
+constexpr int BM = kGemmBM, BN = kGemmBN, BK = kGemmBK, STAGES = kGemmStages;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = idesc_f16(BM, BN, 0);
+
+struct __align__(8) GemmBarriers {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+__device__ __forceinline__ float gelu_f(float x) {
+  // Abramowitz–Stegun 7.1.26 erf, as the reference's gelu (src/cpu/ops.rs:33-40).
+  float z = fabsf(0.70710678118654752f * x);
+  float t = 1.0f / (1.0f + 0.3275911f * z);
+  float p = (((1.0614054f * t - 1.453152f) * t + 1.4214138f) * t - 0.28449674f) * t + 0.2548296f;
+  float s = signbit(x) ? -1.0f : 1.0f;
+  return 0.5f * x * (1.0f + s * (1.0f - p * t * expf(-z * z)));
+}
+
+__device__ __forceinline__ float apply_epi(int e, float v, float c, float alpha) {
+  switch (e) {
+    case kBias: return v;
+    case kSilu: return v / (1.0f + expf(-v));
+    case kRelu: return fmaxf(v, 0.0f);
+    case kResidual: return c + alpha * v;
+    case kGelu: return gelu_f(v);
+    case kGeluResidual: return c + gelu_f(v);
+    default: return tanhf(fminf(fmaxf(v, -10.0f), 10.0f));
+  }
+}
+
+// Stores 32 consecutive outputs of one row (columns col0.. of `c`), reading c first for the
+// residual epilogues. `lim` is the number of valid columns (<= 32).
+__device__ __forceinline__ void store_row32(const GemmArgs &g, long long row, int col0, int lim,
+                                            const float (&v)[32], int e, const float *bias_at) {
+  const bool resid = (e == kResidual || e == kGeluResidual);
+  if (g.c_f16) {
+    __half *c = reinterpret_cast<__half *>(g.c) + row * g.ldc + col0;
+    const bool vec = lim == 32 && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 old = make_uint4(0, 0, 0, 0);
+        if (resid) old = *reinterpret_cast<const uint4 *>(c + 8 * q);
+        const __half *oh = reinterpret_cast<const __half *>(&old);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          int j = 8 * q + 2 * i;
+          float a = apply_epi(e, v[j] + bias_at[j], __half2float(oh[2 * i]), g.alpha);
+          float b = apply_epi(e, v[j + 1] + bias_at[j + 1], __half2float(oh[2 * i + 1]), g.alpha);
+          w[i] = pack_half2(a, b);
+        }
+        *reinterpret_cast<uint4 *>(c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < lim) {
+          float old = resid ? __half2float(c[j]) : 0.0f;
+          c[j] = __float2half_rn(apply_epi(e, v[j] + bias_at[j], old, g.alpha));
+        }
+      }
+    }
+  } else {
+    float *c = reinterpret_cast<float *>(g.c) + row * g.ldc + col0;
+    const bool vec = lim == 32 && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 old = make_float4(0, 0, 0, 0);
+        if (resid) old = *reinterpret_cast<const float4 *>(c + 4 * q);
+        float4 o;
+        o.x = apply_epi(e, v[4 * q + 0] + bias_at[4 * q + 0], old.x, g.alpha);
+        o.y = apply_epi(e, v[4 * q + 1] + bias_at[4 * q + 1], old.y, g.alpha);
+        o.z = apply_epi(e, v[4 * q + 2] + bias_at[4 * q + 2], old.z, g.alpha);
+        o.w = apply_epi(e, v[4 * q + 3] + bias_at[4 * q + 3], old.w, g.alpha);
+        *reinterpret_cast<float4 *>(c + 4 * q) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < lim) {
+          float old = resid ? c[j] : 0.0f;
+          c[j] = apply_epi(e, v[j] + bias_at[j], old, g.alpha);
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_w,
+                const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  GemmBarriers *bar = reinterpret_cast<GemmBarriers *>(smem + STAGES * STAGE_BYTES);
+  const uint32_t warp = warp_id(), lane = lane_id();
+
+  const int num_m = (g.m + BM - 1) / BM;
+  const int num_n = (g.cols + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (g.k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar->full[s], 1);
+      mbar_init(&bar->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar->acc_full[b], 1);
+      mbar_init(&bar->acc_empty[b], 4);
+    }
+    mbar_init(&bar->drain, 1);
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  const Abort ab{&bar->abort, g.err};
+
+  if (warp == 0) {
+    // ---- TMA producer --------------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;  // stages armed at least once
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bar->empty[stage], phase ^ 1u, ab, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&bar->full[stage], STAGE_BYTES);
+          tma_load_2d(sa, &tma_a, &bar->full[stage], kb * BK, m0);
+          tma_load_2d(sa + A_BYTES, &tma_w, &bar->full[stage], kb * BK, n0);
+          armed |= 1u << stage;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load this thread issued land before the CTA can exit: the last arm of each
+        // stage is the one before `stage` in ring order.
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(armed & (1u << s))) continue;
+          uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+          long long t0 = clock64();
+          while (!mbar_try_wait(&bar->full[s], par) && clock64() - t0 < kWaitCycles) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----------------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&bar->acc_empty[acc], acc_phase ^ 1u, ab, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bar->full[stage], phase, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            umma_f16(d, sdesc_sw128(sa + ks * 32, 16, 1024), sdesc_sw128(sb + ks * 32, 16, 1024),
+                     IDESC, (kb | ks) != 0);
+          }
+          issued = true;
+          umma_commit(&bar->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&bar->acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued) {
+        umma_commit(&bar->drain);
+        long long t0 = clock64();
+        while (!mbar_try_wait(&bar->drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {
+    // ---- epilogue: warps 2..5, one accumulator row per thread -----------------------------
+    const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
+    const int row_in_tile = int(quarter * 32 + lane);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+      if (!mbar_wait(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+      tc_fence_after();
+      const long long row = m0 + row_in_tile;
+      const bool row_ok = row < g.m;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        const int col0 = n0 + chunk * 32;
+        if (col0 >= g.cols) break;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((quarter * 32u) << 16) + uint32_t(acc * BN + chunk * 32), r);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const int lim = min(32, g.cols - col0);
+        if (row_ok) {
+          store_row32(g, row, col0, lim, v, g.epilogue, g.bias + col0);
+          if (col0 < g.dual) {
+            const int lim2 = min(lim, g.dual - col0);
+            store_row32(g, row, g.cols + col0, lim2, v, kBias, g.bias + g.cols + col0);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// f32 rows to f16 rows, zero padded to ld_out columns.
+__global__ void cast_rows_kernel(const float *__restrict__ in, long long ld_in,
+                                 __half *__restrict__ out, long long ld_out, int rows, int cols) {
+  for (long long row = blockIdx.y; row < rows; row += gridDim.y) {
+    const float *src = in + row * ld_in;
+    __half *dst = out + row * ld_out;
+    for (long long c = 2 * (blockIdx.x * (long long)blockDim.x + threadIdx.x); c < ld_out;
+         c += 2LL * gridDim.x * blockDim.x) {
+      float a = c < cols ? src[c] : 0.0f;
+      float b = c + 1 < cols ? src[c + 1] : 0.0f;
+      if (c + 1 < ld_out) {
+        *reinterpret_cast<__half2 *>(dst + c) = __floats2half2_rn(a, b);
+      } else {
+        dst[c] = __float2half_rn(a);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+size_t gemm_smem_bytes() { return 1024 + STAGES * STAGE_BYTES + sizeof(GemmBarriers); }
+
+cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int num_sms,
+                        cudaStream_t s) {
+  const size_t smem = gemm_smem_bytes();
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int tiles = ((g.m + BM - 1) / BM) * ((g.cols + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  if (grid <= 0) return cudaSuccess;
+  gemm_kernel<<<grid, kGemmThreads, smem, s>>>(a, w, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cast_rows(const float *in, long long ld_in, __half *out, long long ld_out,
+                             int rows, int cols, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  int threads = 256;
+  long long pairs = (ld_out + 1) / 2;
+  int bx = int((pairs + threads - 1) / threads);
+  if (bx > 64) bx = 64;
+  dim3 grid(bx, rows < 65535 ? rows : 65535);
+  cast_rows_kernel<<<grid, threads, 0, s>>>(in, ld_in, out, ld_out, rows, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace wv

@@ -1,0 +1,98 @@
+// Launch interfaces of the library's kernels (host side). The C ABI in wavo_cuda.cu validates the
+// arguments and builds the tensor maps; these functions only configure and launch.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wv {
+
+// Epilogue modes, the reference's `Epilogue` (src/gpu/mod.rs:431-456) in its kernel order.
+enum Epi : int { kBias = 0, kSilu, kRelu, kResidual, kGelu, kGeluResidual, kTanh };
+
+// ---- projection GEMM (gemm.cu) ----------------------------------------------------------
+
+struct GemmArgs {
+  int m;              // rows of a and c
+  int cols;           // main output columns
+  int dual;           // leading outputs written a second time at cols.. with bias[cols + j]
+  int k;              // inner dimension
+  const float *bias;  // at least max(cols, cols + dual) floats
+  void *c;
+  long long ldc;      // elements
+  int c_f16;          // 1: c is f16, 0: f32
+  int epilogue;
+  float alpha;
+  int *err;           // device error word
+};
+
+constexpr int kGemmBM = 128, kGemmBN = 128, kGemmBK = 64, kGemmStages = 6;
+constexpr int kGemmThreads = 192;
+size_t gemm_smem_bytes();
+cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g,
+                        int num_sms, cudaStream_t s);
+
+// f32 rows -> f16 rows (round to nearest even), into a padded row stride; columns past `cols`
+// up to `ld_out` are zeroed.
+cudaError_t launch_cast_rows(const float *in, long long ld_in, __half *out, long long ld_out,
+                             int rows, int cols, cudaStream_t s);
+
+// ---- encoder attention (attention.cu) ----------------------------------------------------
+
+struct AttnArgs {
+  // Segments: segment z covers rows seg_start[z] .. seg_start[z] + seg_len[z] of every operand.
+  // With seg_len == nullptr there is one segment of single_t rows from row 0.
+  const int *seg_start;
+  const int *seg_len;
+  int single_t;
+  int heads;
+  int hd;           // real head size
+  int head_stride;  // elements between heads inside a section of the f16 operand rows
+  int q_off, k_off, v_off, qv_off;  // section offsets (elements) inside the operand rows
+  int pos_off;      // head offset base inside the position rows
+  int pos_t;        // the position table's t: row r is relative position pos_t + 15 - r
+  float scale_log2; // log2(e) / sqrt(hd)
+  void *o;          // output rows
+  long long ldo;
+  int o_f16;
+  int *err;
+};
+
+constexpr int kAttnThreads = 192;
+constexpr int kAttnBlockQ = 128;  // queries per CTA (the TMA box height of map_q)
+size_t attn_smem_bytes(int hd_pad, bool rel);
+int attn_block_keys(bool rel);   // keys per block (the TMA box height of map_kv)
+int attn_pos_window_rows();      // position rows per block (the TMA box height of map_pos)
+// hd_pad: 64 or 128 (the padded head size of the operand tiles). All maps are 2D f16 tensor maps
+// with 64-column (128-byte) boxes and 128-byte swizzle.
+cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
+                             const CUtensorMap &map_pos, const AttnArgs &a, int hd_pad, bool rel,
+                             int max_len, int nseg, cudaStream_t s);
+
+// Repacks attention operands into f16 rows with heads padded to `hd_pad` (zeros past hd):
+// out[row][sec * heads * hd_pad + h * hd_pad + c] = in[row][in_off[sec] + h * hd + c], for
+// `sections` sections. `in_f16` selects the input type.
+cudaError_t launch_pack_heads(const void *in, int in_f16, long long ld_in, const int *in_off,
+                              int sections, __half *out, long long ld_out, int rows, int heads,
+                              int hd, int hd_pad, cudaStream_t s);
+
+// ---- decoder (decode.cu) -----------------------------------------------------------------
+
+cudaError_t launch_pack_cache(const float *x, long long src, long long stride, uint32_t *cache,
+                              int rows, int d, int cols, int col, cudaStream_t s);
+cudaError_t launch_attend(const float *q, long long q_stride, const uint32_t *kv,
+                          long long kv_stride, float *part, float *o, long long o_stride, int n,
+                          int cols, int heads, int hd, int batch, cudaStream_t s);
+size_t attend_part_floats(int n, int heads, int hd, int batch);
+cudaError_t launch_rope(const float *table, void *qkv, int x_f16, long long stride, int rows,
+                        int pos, int heads, int hd, int rot, int neox, int sections,
+                        cudaStream_t s);
+// Rows (<= 32) of f32 a through W of type wtype (0 f32 [n][k], 1 f16 [n][k], 8 int8 [n][k] with
+// f32 scales [n][k/32]) in f32: the reference's gemv (W not rounded to f16).
+cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
+                        const float *scales, const float *bias, float *c, long long ldc, int rows,
+                        int n, int k, int epilogue, float alpha, cudaStream_t s);
+
+}  // namespace wv

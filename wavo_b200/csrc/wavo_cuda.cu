@@ -1,0 +1,769 @@
+// C ABI of the wavo-b200 attention path (include/wavo_cuda.h): contexts, buffers, linear layers,
+// argument checks, tensor maps and kernel dispatch. Each entry point cites the reference method it
+// replaces in the header.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/wavo_cuda.h"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+struct wavo_ctx {
+  int device = 0;
+  int sms = 0;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  int *dev_err = nullptr;    // the kernels' error word
+  void *ws = nullptr;        // scratch for casts and repacks
+  size_t ws_bytes = 0;
+  bool capturing = false;
+  std::mutex mu;
+  std::string err;
+};
+
+struct wavo_linear {
+  int device = 0;
+  int ty = 0;
+  uint32_t rows = 0, n = 0, cols = 0, k = 0, dual = 0;
+  __half *w16 = nullptr;     // [n][k] f16, the GEMM's operand (W rounded to f16)
+  float *w32 = nullptr;      // [n][k] f32 (F32 weights), the gemv operand
+  int8_t *q8 = nullptr;      // [n][k] int8 (Q8_0 weights), the gemv operand
+  float *d8 = nullptr;       // [n][k/32] scales (Q8_0)
+  float *bias = nullptr;     // max(n, cols + dual) floats
+  CUtensorMap map_w;
+};
+
+struct wavo_graph {
+  cudaGraphExec_t exec = nullptr;
+  cudaGraph_t graph = nullptr;
+};
+
+namespace {
+
+std::mutex g_create_mu;
+std::string g_create_err;
+
+wavo_status fail(wavo_ctx *c, wavo_status s, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) {
+    c->err = buf;
+  } else {
+    std::lock_guard<std::mutex> g(g_create_mu);
+    g_create_err = buf;
+  }
+  return s;
+}
+
+wavo_status cuda_fail(wavo_ctx *c, cudaError_t e, const char *what) {
+  return fail(c, e == cudaErrorMemoryAllocation ? WAVO_ENOMEM : WAVO_ECUDA, "%s: %s", what,
+              cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                  \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, what); \
+  } while (0)
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+// A 2D f16 tensor map over rows x cols (row stride ld elements), 64-column x box_rows boxes,
+// 128-byte swizzle, zero fill outside.
+bool make_map(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
+              uint32_t box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15u) || cols == 0 || rows == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Scratch of at least `bytes` (grows outside of a capture only).
+wavo_status workspace(wavo_ctx *ctx, size_t bytes, void **out) {
+  if (bytes > ctx->ws_bytes) {
+    if (ctx->capturing)
+      return fail(ctx, WAVO_EINVAL, "scratch of %zu bytes needed during a capture: call "
+                  "wavo_reserve first", bytes);
+    if (ctx->ws) {
+      CK(cudaStreamSynchronize(ctx->stream), "scratch sync");
+      CK(cudaFree(ctx->ws), "scratch free");
+      ctx->ws = nullptr;
+      ctx->ws_bytes = 0;
+    }
+    size_t sz = std::max(bytes, size_t(1) << 20);
+    CK(cudaMalloc(&ctx->ws, sz), "scratch");
+    ctx->ws_bytes = sz;
+  }
+  *out = ctx->ws;
+  return WAVO_OK;
+}
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// IEEE binary16 from f32, round to nearest even (the reference GPU GEMM's rounding of W).
+uint16_t f16_bits(float x) {
+  __half h = __float2half_rn(x);
+  uint16_t b;
+  std::memcpy(&b, &h, 2);
+  return b;
+}
+
+float f16_value(uint16_t b) {
+  __half h;
+  std::memcpy(&h, &b, 2);
+  return __half2float(h);
+}
+
+}  // namespace
+
+extern "C" {
+
+int wavo_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+const char *wavo_last_error(const wavo_ctx *ctx) {
+  if (ctx) return ctx->err.c_str();
+  std::lock_guard<std::mutex> g(g_create_mu);
+  return g_create_err.c_str();
+}
+
+wavo_status wavo_create(int device, wavo_ctx **out) {
+  if (!out) return fail(nullptr, WAVO_EINVAL, "out is NULL");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0)
+    return fail(nullptr, WAVO_EUNSUPPORTED, "no CUDA device: %s", cudaGetErrorString(e));
+  if (device < 0 || device >= n)
+    return fail(nullptr, WAVO_EINVAL, "device %d of %d", device, n);
+  cudaDeviceProp prop;
+  if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+    return fail(nullptr, WAVO_ECUDA, "device properties: %s", cudaGetErrorString(e));
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(nullptr, WAVO_EUNSUPPORTED,
+                "device %d (%s) is sm_%d%d: this library is built for sm_100a (B200)", device,
+                prop.name, prop.major, prop.minor);
+  if (!encoder()) return fail(nullptr, WAVO_EUNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  wavo_ctx *ctx = new (std::nothrow) wavo_ctx();
+  if (!ctx) return fail(nullptr, WAVO_ENOMEM, "context");
+  ctx->device = device;
+  ctx->sms = prop.multiProcessorCount;
+  if ((e = cudaSetDevice(device)) != cudaSuccess ||
+      (e = cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaMalloc(&ctx->dev_err, sizeof(int))) != cudaSuccess ||
+      (e = cudaMemset(ctx->dev_err, 0, sizeof(int))) != cudaSuccess) {
+    fail(nullptr, WAVO_ECUDA, "context setup: %s", cudaGetErrorString(e));
+    if (ctx->own) cudaStreamDestroy(ctx->own);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    delete ctx;
+    return WAVO_ECUDA;
+  }
+  ctx->stream = ctx->own;
+  *out = ctx;
+  return WAVO_OK;
+}
+
+void wavo_destroy(wavo_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->dev_err) cudaFree(ctx->dev_err);
+  if (ctx->own) cudaStreamDestroy(ctx->own);
+  delete ctx;
+}
+
+wavo_status wavo_set_stream(wavo_ctx *ctx, void *stream) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own;
+  return WAVO_OK;
+}
+
+void *wavo_get_stream(const wavo_ctx *ctx) { return ctx ? ctx->stream : nullptr; }
+int wavo_sm_count(const wavo_ctx *ctx) { return ctx ? ctx->sms : 0; }
+
+wavo_status wavo_malloc(wavo_ctx *ctx, size_t bytes, void **out) {
+  if (!ctx || !out) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  *out = nullptr;
+  CK(cudaMalloc(out, bytes ? bytes : 1), "wavo_malloc");
+  return WAVO_OK;
+}
+
+wavo_status wavo_free(wavo_ctx *ctx, void *p) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  if (p) CK(cudaFree(p), "wavo_free");
+  return WAVO_OK;
+}
+
+wavo_status wavo_upload(wavo_ctx *ctx, void *dst, const void *src, size_t bytes) {
+  if (!ctx || (!dst && bytes) || (!src && bytes)) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream), "wavo_upload");
+  return WAVO_OK;
+}
+
+wavo_status wavo_download(wavo_ctx *ctx, void *dst, const void *src, size_t bytes) {
+  if (!ctx || (!dst && bytes) || (!src && bytes)) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "wavo_download");
+  return WAVO_OK;
+}
+
+wavo_status wavo_memset(wavo_ctx *ctx, void *dst, int value, size_t bytes) {
+  if (!ctx || (!dst && bytes)) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  CK(cudaMemsetAsync(dst, value, bytes, ctx->stream), "wavo_memset");
+  return WAVO_OK;
+}
+
+wavo_status wavo_reserve(wavo_ctx *ctx, size_t bytes) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  void *p;
+  return workspace(ctx, bytes, &p);
+}
+
+wavo_status wavo_sync(wavo_ctx *ctx, uint32_t timeout_ms) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t e = cudaStreamQuery(ctx->stream);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "device");
+    if (timeout_ms) {
+      auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                    std::chrono::steady_clock::now() - t0)
+                    .count();
+      if (ms > timeout_ms)
+        return fail(ctx, WAVO_ETIMEDOUT, "the stream did not finish within %u ms", timeout_ms);
+    }
+    std::this_thread::yield();
+  }
+  int code = 0;
+  CK(cudaMemcpy(&code, ctx->dev_err, sizeof code, cudaMemcpyDeviceToHost), "error word");
+  if (code) {
+    CK(cudaMemset(ctx->dev_err, 0, sizeof(int)), "error word reset");
+    static const char *what[] = {"", "TMA producer", "MMA issuer", "softmax/epilogue", "drain"};
+    return fail(ctx, WAVO_EDEVICE, "a kernel's bounded wait gave up (%s, code %d)",
+                code > 0 && code < 5 ? what[code] : "?", code);
+  }
+  return WAVO_OK;
+}
+
+// ---- linear layers ---------------------------------------------------------------------
+
+wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k, const void *data,
+                               const float *bias, size_t bias_len, wavo_linear **out) {
+  if (!ctx || !out || !data) return WAVO_EINVAL;
+  *out = nullptr;
+  // Argument checks as Gpu::upload_linear (src/gpu/mod.rs:775-827).
+  if (ty != WAVO_GGML_F32 && ty != WAVO_GGML_F16 && ty != WAVO_GGML_Q8_0)
+    return fail(ctx, WAVO_EINVAL, "linear layer: GGUF type %d is not F32, F16 or Q8_0", ty);
+  if (rows == 0 || k == 0 || k % 32 != 0)
+    return fail(ctx, WAVO_EINVAL, "linear layer %u->%u: needs k %% 32 == 0", k, rows);
+  const uint32_t dual = bias_len > rows ? uint32_t(bias_len - rows) : 0;
+  if ((bias_len != 0 && bias_len < rows) || dual > rows)
+    return fail(ctx, WAVO_EINVAL, "linear layer %u->%u: bias has %zu values", k, rows, bias_len);
+  const uint32_t n = (rows + 63) / 64 * 64;
+  const uint32_t cols = rows % 32 == 0 ? rows : n;
+  // W rounded to f16 for the GEMM, zero rows past `rows`.
+  std::vector<uint16_t> w16(size_t(n) * k, 0);
+  std::vector<float> w32;
+  std::vector<int8_t> q8;
+  std::vector<float> d8;
+  const size_t nk = size_t(rows) * k;
+  if (ty == WAVO_GGML_F32) {
+    const float *f = static_cast<const float *>(data);
+    w32.assign(f, f + nk);
+    w32.resize(size_t(n) * k, 0.0f);
+    for (size_t i = 0; i < nk; ++i) w16[i] = f16_bits(f[i]);
+  } else if (ty == WAVO_GGML_F16) {
+    std::memcpy(w16.data(), data, nk * 2);
+  } else {
+    const uint8_t *b = static_cast<const uint8_t *>(data);
+    q8.assign(size_t(n) * k, 0);
+    d8.assign(size_t(n) * k / 32, 0.0f);
+    for (size_t blk = 0; blk < nk / 32; ++blk) {
+      const uint8_t *p = b + 34 * blk;
+      const float d = f16_value(uint16_t(p[0] | (p[1] << 8)));
+      d8[blk] = d;
+      for (int i = 0; i < 32; ++i) {
+        const int8_t q = int8_t(p[2 + i]);
+        q8[32 * blk + i] = q;
+        w16[32 * blk + i] = f16_bits(float(q) * d);  // q·d exact in f32, then to f16
+      }
+    }
+  }
+  std::vector<float> bpad(std::max<size_t>(n, size_t(cols) + dual), 0.0f);
+  if (bias && bias_len) {
+    std::memcpy(bpad.data(), bias, size_t(rows) * 4);
+    if (dual) std::memcpy(bpad.data() + cols, bias + rows, size_t(dual) * 4);
+  }
+  wavo_linear *l = new (std::nothrow) wavo_linear();
+  if (!l) return fail(ctx, WAVO_ENOMEM, "linear");
+  l->device = ctx->device;
+  l->ty = ty;
+  l->rows = rows;
+  l->n = n;
+  l->cols = cols;
+  l->k = k;
+  l->dual = dual;
+  cudaError_t e = cudaSetDevice(ctx->device);
+  auto up = [&](void **dst, const void *src, size_t bytes) {
+    if (e != cudaSuccess) return;
+    if ((e = cudaMalloc(dst, bytes)) != cudaSuccess) return;
+    e = cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice);
+  };
+  up(reinterpret_cast<void **>(&l->w16), w16.data(), w16.size() * 2);
+  up(reinterpret_cast<void **>(&l->bias), bpad.data(), bpad.size() * 4);
+  if (!w32.empty()) up(reinterpret_cast<void **>(&l->w32), w32.data(), w32.size() * 4);
+  if (!q8.empty()) {
+    up(reinterpret_cast<void **>(&l->q8), q8.data(), q8.size());
+    up(reinterpret_cast<void **>(&l->d8), d8.data(), d8.size() * 4);
+  }
+  if (e != cudaSuccess) {
+    wavo_linear_destroy(l);
+    std::lock_guard<std::mutex> g(ctx->mu);
+    return cuda_fail(ctx, e, "linear upload");
+  }
+  if (!make_map(&l->map_w, l->w16, k, n, k, wv::kGemmBN)) {
+    wavo_linear_destroy(l);
+    return fail(ctx, WAVO_ECUDA, "linear: tensor map");
+  }
+  *out = l;
+  return WAVO_OK;
+}
+
+void wavo_linear_destroy(wavo_linear *l) {
+  if (!l) return;
+  cudaSetDevice(l->device);
+  cudaFree(l->w16);
+  cudaFree(l->w32);
+  cudaFree(l->q8);
+  cudaFree(l->d8);
+  cudaFree(l->bias);
+  delete l;
+}
+
+uint32_t wavo_linear_width(const wavo_linear *l) { return l ? l->cols + l->dual : 0; }
+uint32_t wavo_linear_k(const wavo_linear *l) { return l ? l->k : 0; }
+
+// ---- projections -----------------------------------------------------------------------
+
+wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, const wavo_linear *l,
+                      void *c, int c_dtype, uint32_t ldc, uint32_t m, int epilogue, float alpha) {
+  if (!ctx || !l) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (m == 0) return WAVO_OK;
+  if (!a || !c) return fail(ctx, WAVO_EINVAL, "gemm: NULL buffer");
+  if (l->device != ctx->device) return fail(ctx, WAVO_EINVAL, "gemm: layer of another device");
+  if (epilogue < 0 || epilogue > WAVO_EPI_TANH) return fail(ctx, WAVO_EINVAL, "gemm: epilogue");
+  if ((a_dtype != WAVO_F32 && a_dtype != WAVO_F16) || (c_dtype != WAVO_F32 && c_dtype != WAVO_F16))
+    return fail(ctx, WAVO_EINVAL, "gemm: dtype");
+  if (lda == 0) lda = l->k;
+  if (ldc == 0) ldc = l->cols + l->dual;
+  if (lda < l->k || ldc < l->cols + l->dual)
+    return fail(ctx, WAVO_EINVAL, "gemm: lda %u < k %u or ldc %u < width %u", lda, l->k, ldc,
+                l->cols + l->dual);
+  cudaSetDevice(ctx->device);
+  const __half *a16 = static_cast<const __half *>(a);
+  uint32_t lda16 = lda;
+  if (a_dtype == WAVO_F32 || (lda % 8) || (reinterpret_cast<uintptr_t>(a) & 15u)) {
+    // The reference rounds a to f16 in the GEMM (src/cpu/gemm.rs:163): one cast pass.
+    void *ws;
+    wavo_status s = workspace(ctx, size_t(m) * l->k * 2, &ws);
+    if (s) return s;
+    if (a_dtype == WAVO_F32) {
+      CK(wv::launch_cast_rows(static_cast<const float *>(a), lda, static_cast<__half *>(ws), l->k,
+                              int(m), int(l->k), ctx->stream),
+         "gemm cast");
+    } else {
+      CK(cudaMemcpy2DAsync(ws, size_t(l->k) * 2, a, size_t(lda) * 2, size_t(l->k) * 2, m,
+                           cudaMemcpyDeviceToDevice, ctx->stream),
+         "gemm repack");
+    }
+    a16 = static_cast<const __half *>(ws);
+    lda16 = l->k;
+  }
+  CUtensorMap map_a;
+  if (!make_map(&map_a, a16, l->k, m, lda16, wv::kGemmBM))
+    return fail(ctx, WAVO_ECUDA, "gemm: tensor map of a");
+  wv::GemmArgs ga;
+  ga.m = int(m);
+  ga.cols = int(l->cols);
+  ga.dual = int(l->dual);
+  ga.k = int(l->k);
+  ga.bias = l->bias;
+  ga.c = c;
+  ga.ldc = ldc;
+  ga.c_f16 = c_dtype == WAVO_F16;
+  ga.epilogue = epilogue;
+  ga.alpha = alpha;
+  ga.err = ctx->dev_err;
+  CK(wv::launch_gemm(map_a, l->map_w, ga, ctx->sms, ctx->stream), "gemm launch");
+  return WAVO_OK;
+}
+
+wavo_status wavo_gemv_rows(wavo_ctx *ctx, const float *a, uint32_t lda, const wavo_linear *l,
+                           float *c, uint32_t ldc, uint32_t rows, int epilogue, float alpha) {
+  if (!ctx || !l) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (rows == 0) return WAVO_OK;
+  if (!a || !c) return fail(ctx, WAVO_EINVAL, "gemv: NULL buffer");
+  if (rows > 32) return fail(ctx, WAVO_EINVAL, "gemv: %u rows (at most 32)", rows);
+  if (epilogue < 0 || epilogue > WAVO_EPI_TANH) return fail(ctx, WAVO_EINVAL, "gemv: epilogue");
+  if (lda == 0) lda = l->k;
+  if (ldc == 0) ldc = l->cols;
+  if (lda < l->k || (lda % 4) || (reinterpret_cast<uintptr_t>(a) & 15u))
+    return fail(ctx, WAVO_EINVAL, "gemv: a rows need k floats, 16-byte aligned");
+  if (rows > 1 && ldc < l->cols) return fail(ctx, WAVO_EINVAL, "gemv: ldc");
+  cudaSetDevice(ctx->device);
+  const void *w = l->ty == WAVO_GGML_F32 ? static_cast<const void *>(l->w32)
+                  : l->ty == WAVO_GGML_Q8_0 ? static_cast<const void *>(l->q8)
+                                            : static_cast<const void *>(l->w16);
+  const int wt = l->ty == WAVO_GGML_F32 ? 0 : l->ty == WAVO_GGML_Q8_0 ? 8 : 1;
+  // Pass::gemv writes l.cols outputs (src/gpu/mod.rs:1461-1467).
+  CK(wv::launch_gemv(a, lda, wt, w, l->d8, l->bias, c, ldc, int(rows), int(l->cols), int(l->k),
+                     epilogue, alpha, ctx->stream),
+     "gemv launch");
+  return WAVO_OK;
+}
+
+wavo_status wavo_gemv(wavo_ctx *ctx, const float *a, const wavo_linear *l, float *c, int epilogue,
+                      float alpha, uint32_t offset) {
+  if (!c) return WAVO_EINVAL;
+  return wavo_gemv_rows(ctx, a, 0, l, c + offset, 0, 1, epilogue, alpha);
+}
+
+// ---- encoder attention -------------------------------------------------------------------
+
+uint32_t wavo_pos_rows(uint32_t t) { return 2 * t + 15; }
+
+namespace {
+
+// The layout of one attention call's operands.
+struct AttnLayout {
+  int sections;          // operand sections in qk: 2 ([q|k]), 3 ([q|k|v]) or 4 ([q+u|k|v|q+v])
+  bool sep_v;            // v is its own buffer
+  bool rel;
+};
+
+wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const void *pos, void *o,
+                           const int32_t *seg_start, const int32_t *seg_len, uint32_t nseg,
+                           uint32_t max_len, uint32_t pos_t, uint32_t single_t, uint32_t heads,
+                           uint32_t hd, int dtype, int o_dtype) {
+  if (!qk || !o) return fail(ctx, WAVO_EINVAL, "attention: NULL buffer");
+  if (dtype != WAVO_F32 && dtype != WAVO_F16) return fail(ctx, WAVO_EINVAL, "attention: dtype");
+  if (o_dtype != WAVO_F32 && o_dtype != WAVO_F16) return fail(ctx, WAVO_EINVAL, "attention: o dtype");
+  if (heads == 0 || hd == 0 || hd > 128 || hd % 2)
+    return fail(ctx, WAVO_EINVAL, "attention: heads %u of %u dims (hd even, <= 128)", heads, hd);
+  if (max_len == 0 || nseg == 0) return WAVO_OK;
+  const bool rel = pos != nullptr;
+  if (rel && v) return fail(ctx, WAVO_EINVAL, "attention: relative positions take no separate v");
+  if (rel && pos_t < max_len)
+    return fail(ctx, WAVO_EINVAL, "attention: position table for t=%u < segment length %u", pos_t,
+                max_len);
+  const AttnLayout L{rel ? 4 : (v ? 2 : 3), v != nullptr, rel};
+  const uint32_t ch = heads * hd;
+  const uint32_t ld = L.sections * ch;  // elements per qk row
+  // Rows of every operand (the tensor maps' extent): the segment, or the caller's total.
+  const uint64_t rows = single_t;
+  // f16 operands in the reference layout go to the kernel as they are when every TMA box starts
+  // on a 16-byte boundary; anything else is repacked into padded f16 heads first.
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(qk) & 15u) == 0 && ld % 8 == 0;
+  const bool direct = dtype == WAVO_F16 && !v && aligned16 && hd % 16 == 0 &&
+                      (rel ? (hd == 128 && (reinterpret_cast<uintptr_t>(pos) & 15u) == 0)
+                           : (hd <= 64 || hd == 128));
+  const int hd_pad = rel ? 128 : (hd <= 64 ? 64 : 128);
+  cudaSetDevice(ctx->device);
+
+  wv::AttnArgs a{};
+  a.seg_start = seg_start;
+  a.seg_len = seg_len;
+  a.single_t = int(single_t);
+  a.heads = int(heads);
+  a.hd = int(hd);
+  a.pos_t = int(pos_t);
+  a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(hd)));
+  a.o = o;
+  a.ldo = ch;
+  a.o_f16 = o_dtype == WAVO_F16;
+  a.err = ctx->dev_err;
+
+  CUtensorMap mq, mkv, mpos;
+  const int bk = wv::attn_block_keys(rel);
+  if (direct) {
+    a.head_stride = int(hd);
+    a.q_off = 0;
+    a.k_off = int(ch);
+    a.v_off = int(2 * ch);
+    a.qv_off = int(3 * ch);
+    a.pos_off = 0;
+    if (!make_map(&mq, qk, ld, rows, ld, wv::kAttnBlockQ) ||
+        !make_map(&mkv, qk, ld, rows, ld, uint32_t(bk)))
+      return fail(ctx, WAVO_ECUDA, "attention: tensor map");
+    mpos = mq;
+    if (rel && !make_map(&mpos, pos, ch, wavo_pos_rows(pos_t), ch,
+                         uint32_t(wv::attn_pos_window_rows())))
+      return fail(ctx, WAVO_ECUDA, "attention: tensor map of pos");
+  } else {
+    // Repack into f16 rows [sections][heads][hd_pad] (zeros past hd) in the scratch.
+    const int sec = L.sections + (L.sep_v ? 1 : 0);
+    const uint64_t ldp = uint64_t(sec) * heads * hd_pad;
+    const uint64_t prow = rel ? wavo_pos_rows(pos_t) : 0;
+    const size_t bytes = align_up(rows * ldp * 2, 256) + prow * heads * hd_pad * 2;
+    void *ws;
+    wavo_status st = workspace(ctx, bytes, &ws);
+    if (st) return st;
+    __half *pk = static_cast<__half *>(ws);
+    __half *pp = reinterpret_cast<__half *>(static_cast<uint8_t *>(ws) + align_up(rows * ldp * 2, 256));
+    const int in_f16 = dtype == WAVO_F16;
+    if (L.sep_v) {
+      const int off2[2] = {0, int(ch)};
+      CK(wv::launch_pack_heads(qk, in_f16, 2 * ch, off2, 2, pk, ldp, int(rows), int(heads), int(hd),
+                               hd_pad, ctx->stream),
+         "attention repack");
+      const int off1[1] = {0};
+      CK(wv::launch_pack_heads(v, in_f16, ch, off1, 1, pk + 2 * heads * hd_pad, ldp, int(rows),
+                               int(heads), int(hd), hd_pad, ctx->stream),
+         "attention repack v");
+    } else {
+      const int offs[4] = {0, int(ch), int(2 * ch), int(3 * ch)};
+      CK(wv::launch_pack_heads(qk, in_f16, ld, offs, L.sections, pk, ldp, int(rows), int(heads),
+                               int(hd), hd_pad, ctx->stream),
+         "attention repack");
+    }
+    a.head_stride = hd_pad;
+    a.q_off = 0;
+    a.k_off = int(heads * hd_pad);
+    a.v_off = int(2 * heads * hd_pad);
+    a.qv_off = int(3 * heads * hd_pad);
+    if (!make_map(&mq, pk, ldp, rows, ldp, wv::kAttnBlockQ) ||
+        !make_map(&mkv, pk, ldp, rows, ldp, uint32_t(bk)))
+      return fail(ctx, WAVO_ECUDA, "attention: tensor map");
+    mpos = mq;
+    if (rel) {
+      const int off1[1] = {0};
+      CK(wv::launch_pack_heads(pos, in_f16, ch, off1, 1, pp, uint64_t(heads) * hd_pad, int(prow),
+                               int(heads), int(hd), hd_pad, ctx->stream),
+         "attention repack pos");
+      a.pos_off = 0;
+      if (!make_map(&mpos, pp, uint64_t(heads) * hd_pad, prow, uint64_t(heads) * hd_pad,
+                    uint32_t(wv::attn_pos_window_rows())))
+        return fail(ctx, WAVO_ECUDA, "attention: tensor map of pos");
+    }
+  }
+  CK(wv::launch_attention(mq, mkv, mpos, a, hd_pad, rel, int(max_len), int(nseg), ctx->stream),
+     "attention launch");
+  return WAVO_OK;
+}
+
+}  // namespace
+
+wavo_status wavo_attention(wavo_ctx *ctx, const void *qk, const void *v, const void *pos, void *o,
+                           uint32_t t, uint32_t heads, uint32_t hd, int dtype) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  return attention_impl(ctx, qk, v, pos, o, nullptr, nullptr, 1, t, t, t, heads, hd, dtype, dtype);
+}
+
+wavo_status wavo_attention_varlen(wavo_ctx *ctx, const void *qk, const void *v, const void *pos,
+                                  void *o, uint32_t rows, const int32_t *seg_start,
+                                  const int32_t *seg_len, uint32_t nseg, uint32_t max_len,
+                                  uint32_t pos_t, uint32_t heads, uint32_t hd, int dtype,
+                                  int o_dtype) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (!seg_start || !seg_len) return fail(ctx, WAVO_EINVAL, "attention: NULL segment arrays");
+  if (max_len > rows) return fail(ctx, WAVO_EINVAL, "attention: max_len %u > rows %u", max_len, rows);
+  if (nseg > 65535) return fail(ctx, WAVO_EINVAL, "attention: %u segments (at most 65535)", nseg);
+  return attention_impl(ctx, qk, v, pos, o, seg_start, seg_len, nseg, max_len, pos ? pos_t : 0,
+                        rows, heads, hd, dtype, o_dtype);
+}
+
+// ---- rope --------------------------------------------------------------------------------
+
+wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, uint32_t stride,
+                      uint32_t rows, uint32_t pos, uint32_t heads, uint32_t hd, uint32_t rot,
+                      int neox) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (rows == 0) return WAVO_OK;
+  if (!table || !qkv) return fail(ctx, WAVO_EINVAL, "rope: NULL buffer");
+  if (rot > hd || rot % 2 || (dtype != WAVO_F32 && dtype != WAVO_F16))
+    return fail(ctx, WAVO_EINVAL, "rope: rot %u of hd %u", rot, hd);
+  if (stride == 0) stride = 3 * heads * hd;
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_rope(table, qkv, dtype == WAVO_F16, stride, int(rows), int(pos), int(heads),
+                     int(hd), int(rot), neox ? 1 : 0, 2, ctx->stream),
+     "rope launch");
+  return WAVO_OK;
+}
+
+// ---- decoder -----------------------------------------------------------------------------
+
+wavo_status wavo_pack(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride, void *cache,
+                      uint32_t rows, uint32_t d, uint32_t cols, uint32_t col) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (rows == 0) return WAVO_OK;
+  if (!x || !cache) return fail(ctx, WAVO_EINVAL, "pack: NULL buffer");
+  if (d % 2 || col + rows > cols || (src % 2) || (stride % 2))
+    return fail(ctx, WAVO_EINVAL, "pack: rows %u at %u of %u positions, d %u", rows, col, cols, d);
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_pack_cache(x, src, stride, static_cast<uint32_t *>(cache), int(rows), int(d),
+                           int(cols), int(col), ctx->stream),
+     "pack launch");
+  return WAVO_OK;
+}
+
+size_t wavo_attend_len(uint32_t n, uint32_t heads, uint32_t hd) {
+  return wv::attend_part_floats(int(n), int(heads), int(hd), 1);
+}
+
+wavo_status wavo_attend_batch(wavo_ctx *ctx, const float *q, uint64_t q_stride, const void *kv,
+                              uint64_t kv_stride, float *part, float *o, uint64_t o_stride,
+                              uint32_t n, uint32_t cols, uint32_t heads, uint32_t hd,
+                              uint32_t batch) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (n == 0 || batch == 0) return WAVO_OK;
+  if (!q || !kv || !o) return fail(ctx, WAVO_EINVAL, "attend: NULL buffer");
+  if (n > cols || hd > 128 || hd % 2 || heads == 0)
+    return fail(ctx, WAVO_EINVAL, "attend: n %u of %u positions, heads %u of %u", n, cols, heads, hd);
+  if (wv::attend_part_floats(int(n), int(heads), int(hd), 1) > size_t(heads) * (hd + 2) && !part)
+    return fail(ctx, WAVO_EINVAL, "attend: part is NULL");
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_attend(q, q_stride, static_cast<const uint32_t *>(kv), kv_stride, part, o, o_stride,
+                       int(n), int(cols), int(heads), int(hd), int(batch), ctx->stream),
+     "attend launch");
+  return WAVO_OK;
+}
+
+wavo_status wavo_attend(wavo_ctx *ctx, const float *q, const void *kv, float *part, float *o,
+                        uint32_t n, uint32_t cols, uint32_t heads, uint32_t hd) {
+  return wavo_attend_batch(ctx, q, 0, kv, 0, part, o, 0, n, cols, heads, hd, 1);
+}
+
+// ---- graphs ------------------------------------------------------------------------------
+
+wavo_status wavo_capture_begin(wavo_ctx *ctx) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (ctx->capturing) return fail(ctx, WAVO_EINVAL, "already capturing");
+  cudaSetDevice(ctx->device);
+  CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "capture begin");
+  ctx->capturing = true;
+  return WAVO_OK;
+}
+
+wavo_status wavo_capture_end(wavo_ctx *ctx, wavo_graph **out) {
+  if (!ctx || !out) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (!ctx->capturing) return fail(ctx, WAVO_EINVAL, "not capturing");
+  ctx->capturing = false;
+  cudaSetDevice(ctx->device);
+  wavo_graph *gr = new (std::nothrow) wavo_graph();
+  if (!gr) return fail(ctx, WAVO_ENOMEM, "graph");
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &gr->graph);
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&gr->exec, gr->graph, 0);
+  if (e != cudaSuccess) {
+    wavo_graph_destroy(gr);
+    return cuda_fail(ctx, e, "capture end");
+  }
+  *out = gr;
+  return WAVO_OK;
+}
+
+wavo_status wavo_graph_launch(wavo_ctx *ctx, const wavo_graph *gr) {
+  if (!ctx || !gr) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  CK(cudaGraphLaunch(gr->exec, ctx->stream), "graph launch");
+  return WAVO_OK;
+}
+
+void wavo_graph_destroy(wavo_graph *gr) {
+  if (!gr) return;
+  if (gr->exec) cudaGraphExecDestroy(gr->exec);
+  if (gr->graph) cudaGraphDestroy(gr->graph);
+  delete gr;
+}
+
+// ---- sharding ----------------------------------------------------------------------------
+
+wavo_status wavo_partition_lpt(const uint64_t *cost, uint32_t n, uint32_t parts, uint32_t *assign) {
+  if ((!cost || !assign) && n) return WAVO_EINVAL;
+  if (parts == 0) return WAVO_EINVAL;
+  std::vector<uint32_t> order(n);
+  for (uint32_t i = 0; i < n; ++i) order[i] = i;
+  // Longest first; ties by index so the partition is deterministic.
+  std::stable_sort(order.begin(), order.end(),
+                   [&](uint32_t a, uint32_t b) { return cost[a] > cost[b]; });
+  std::vector<uint64_t> load(parts, 0);
+  for (uint32_t i : order) {
+    uint32_t best = 0;
+    for (uint32_t p = 1; p < parts; ++p)
+      if (load[p] < load[best]) best = p;
+    assign[i] = best;
+    load[best] += cost[i];
+  }
+  return WAVO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,241 @@
+"""Host-side mirror of the reference's GPU backend op interface for the attention path
+(vladkens/wavo src/gpu/mod.rs: `Gpu`, `Linear`, `Pass`), over the C ABI of libwavo_cuda.
+
+Device memory comes from torch (CUDA tensors); the context runs on torch's current stream, so the
+calls order with the torch work around them. Method names, argument meanings and layouts follow the
+reference; errors raise `WavoError` at the call (argument errors) or at `Gpu.sync` (device errors),
+as the reference returns `Error::Model` at load and `Error::Gpu`/`Poll` at completion.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import WavoError, check  # noqa: F401  (re-exported)
+
+EPILOGUES = L.EPILOGUES
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    assert t.is_cuda, "buffers are CUDA tensors"
+    return t.data_ptr()
+
+
+def _dtype(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return L.F32
+    if t.dtype == torch.float16:
+        return L.F16
+    raise TypeError(f"unsupported buffer dtype {t.dtype} (float32 or float16)")
+
+
+def pos_rows(t: int) -> int:
+    """src/gpu/mod.rs:1060-1065."""
+    return 2 * t + 15
+
+
+def attend_len(n: int, heads: int, hd: int) -> int:
+    """src/gpu/mod.rs:1053-1059 (this build's split size)."""
+    return int(L.lib().wavo_attend_len(n, heads, hd))
+
+
+def device_count() -> int:
+    return int(L.lib().wavo_device_count())
+
+
+class Linear:
+    """`Gpu::linear` (src/gpu/mod.rs:758-834): W [rows][k] in a GGUF type, stacked tensors along
+    the rows, a bias of 0, rows or rows + dual values."""
+
+    def __init__(self, gpu: "Gpu", ggml_type: int, rows: int, k: int, data: bytes | np.ndarray,
+                 bias=None):
+        raw = bytes(data) if not isinstance(data, np.ndarray) else data.tobytes()
+        self._buf = ctypes.create_string_buffer(raw, len(raw))
+        b = None
+        if bias is not None and len(bias):
+            b = np.ascontiguousarray(bias, np.float32)
+        self._bias = b
+        h = ctypes.c_void_p()
+        check(L.lib().wavo_linear_create(gpu.ctx, ggml_type, rows, k, ctypes.addressof(self._buf),
+                                         None if b is None else b.ctypes.data,
+                                         0 if b is None else b.size, ctypes.byref(h)), gpu.ctx)
+        self.h = h
+        self.rows, self.k, self.ty = rows, k, ggml_type
+        self.n = (rows + 63) // 64 * 64
+        self.cols = rows if rows % 32 == 0 else self.n
+        self.dual = int(L.lib().wavo_linear_width(h)) - self.cols
+        del self._buf
+
+    def width(self) -> int:
+        """`Linear::width`: output columns including the dual ones."""
+        return self.cols + self.dual
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h is not None and h.value:
+            L.lib().wavo_linear_destroy(h)
+            self.h = None
+
+
+class Gpu:
+    """`Gpu::new` (src/gpu/mod.rs:461-578): a context on one B200, on torch's current stream."""
+
+    def __init__(self, device: int = 0):
+        self.device = device
+        self.torch_device = torch.device("cuda", device)
+        ctx = ctypes.c_void_p()
+        check(L.lib().wavo_create(device, ctypes.byref(ctx)), None)
+        self.ctx = ctx
+        with torch.cuda.device(device):
+            self.use_stream(torch.cuda.current_stream(device))
+
+    def use_stream(self, stream: torch.cuda.Stream) -> None:
+        check(L.lib().wavo_set_stream(self.ctx, stream.cuda_stream), self.ctx)
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None) is not None and self.ctx.value:
+            L.lib().wavo_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def sm_count(self) -> int:
+        return int(L.lib().wavo_sm_count(self.ctx))
+
+    def linear(self, ggml_type: int, rows: int, k: int, data, bias=None) -> Linear:
+        return Linear(self, ggml_type, rows, k, data, bias)
+
+    def buffer(self, n: int, dtype=torch.float32) -> torch.Tensor:
+        """`Gpu::buffer`: zeroed device memory."""
+        return torch.zeros(n, dtype=dtype, device=self.torch_device)
+
+    def upload(self, data, dtype=torch.float32) -> torch.Tensor:
+        """`Gpu::upload`."""
+        return torch.as_tensor(np.ascontiguousarray(data)).to(self.torch_device, dtype)
+
+    def reserve(self, nbytes: int) -> None:
+        check(L.lib().wavo_reserve(self.ctx, nbytes), self.ctx)
+
+    def sync(self, timeout_ms: int = 60000) -> None:
+        """Completion check (src/gpu/mod.rs:969-1003): device errors raise here."""
+        check(L.lib().wavo_sync(self.ctx, timeout_ms), self.ctx)
+
+    def pass_(self) -> "Pass":
+        return Pass(self)
+
+    # -- graphs ------------------------------------------------------------------------------
+    def capture(self, record) -> "Graph":
+        """Records `record(Pass)` into a CUDA graph on a side stream and returns it."""
+        s = torch.cuda.Stream(self.torch_device)
+        s.wait_stream(torch.cuda.current_stream(self.torch_device))
+        self.use_stream(s)
+        try:
+            with torch.cuda.stream(s):
+                check(L.lib().wavo_capture_begin(self.ctx), self.ctx)
+                try:
+                    record(Pass(self))
+                finally:
+                    g = ctypes.c_void_p()
+                    status = L.lib().wavo_capture_end(self.ctx, ctypes.byref(g))
+                check(status, self.ctx)
+        finally:
+            torch.cuda.current_stream(self.torch_device).wait_stream(s)
+            self.use_stream(torch.cuda.current_stream(self.torch_device))
+        return Graph(self, g)
+
+
+class Graph:
+    def __init__(self, gpu: Gpu, h: ctypes.c_void_p):
+        self.gpu, self.h = gpu, h
+
+    def launch(self) -> None:
+        check(L.lib().wavo_graph_launch(self.gpu.ctx, self.h), self.gpu.ctx)
+
+    def __del__(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            L.lib().wavo_graph_destroy(self.h)
+            self.h = None
+
+
+class Pass:
+    """`Pass` (src/gpu/mod.rs:1293-1680): the attention path's ops, enqueued on the context."""
+
+    def __init__(self, gpu: Gpu):
+        self.gpu = gpu
+        self.ctx = gpu.ctx
+
+    def gemm(self, a: torch.Tensor, l: Linear, c: torch.Tensor, m: int, epilogue="bias",
+             alpha: float = 1.0, lda: int = 0, ldc: int = 0) -> None:
+        """`Pass::gemm` (src/gpu/mod.rs:1394-1425): c = epilogue(a·W^T + b) for m rows."""
+        check(L.lib().wavo_gemm(self.ctx, _ptr(a), _dtype(a), lda, l.h, _ptr(c), _dtype(c), ldc, m,
+                                EPILOGUES[epilogue], alpha), self.ctx)
+
+    def gemv(self, a: torch.Tensor, l: Linear, c: torch.Tensor, epilogue="bias", offset: int = 0,
+             alpha: float = 1.0) -> None:
+        """`Pass::gemv` (src/gpu/mod.rs:1461-1467)."""
+        check(L.lib().wavo_gemv(self.ctx, _ptr(a), l.h, _ptr(c), EPILOGUES[epilogue], alpha,
+                                offset), self.ctx)
+
+    def gemv_rows(self, a: torch.Tensor, l: Linear, c: torch.Tensor, rows: int, epilogue="bias",
+                  alpha: float = 1.0, lda: int = 0, ldc: int = 0) -> None:
+        check(L.lib().wavo_gemv_rows(self.ctx, _ptr(a), lda, l.h, _ptr(c), ldc, rows,
+                                     EPILOGUES[epilogue], alpha), self.ctx)
+
+    def attention(self, qk: torch.Tensor, v: torch.Tensor | None, pos: torch.Tensor | None,
+                  o: torch.Tensor, t: int, heads: int, hd: int) -> None:
+        """`Pass::attention` (src/gpu/mod.rs:1556-1605); the scores scratch `s` is not needed."""
+        check(L.lib().wavo_attention(self.ctx, _ptr(qk), _ptr(v), _ptr(pos), _ptr(o), t, heads,
+                                     hd, _dtype(qk)), self.ctx)
+
+    def attention_varlen(self, qk, v, pos, o, rows: int, seg_start: torch.Tensor,
+                         seg_len: torch.Tensor, max_len: int, heads: int, hd: int,
+                         pos_t: int = 0) -> None:
+        """Attention over independent segments in one launch (int32 device arrays)."""
+        assert seg_start.dtype == torch.int32 and seg_len.dtype == torch.int32
+        check(L.lib().wavo_attention_varlen(self.ctx, _ptr(qk), _ptr(v), _ptr(pos), _ptr(o), rows,
+                                            _ptr(seg_start), _ptr(seg_len), seg_len.numel(),
+                                            max_len, pos_t, heads, hd, _dtype(qk), _dtype(o)),
+              self.ctx)
+
+    def rope(self, table: torch.Tensor, qkv: torch.Tensor, rows: int, pos: int,
+             shape: tuple[int, int, int], neox: bool, stride: int = 0) -> None:
+        """`Pass::rope` (src/gpu/mod.rs:1630-1649): shape = [heads, hd, rot]."""
+        heads, hd, rot = shape
+        check(L.lib().wavo_rope(self.ctx, _ptr(table), _ptr(qkv), _dtype(qkv), stride, rows, pos,
+                                heads, hd, rot, int(neox)), self.ctx)
+
+    def pack(self, x: torch.Tensor, src_stride: tuple[int, int], cache: torch.Tensor, rows: int,
+             d: int, cols_col: tuple[int, int]) -> None:
+        """`Pass::pack` (src/gpu/mod.rs:1507-1522)."""
+        src, stride = src_stride
+        cols, col = cols_col
+        check(L.lib().wavo_pack(self.ctx, _ptr(x), src, stride, _ptr(cache), rows, d, cols, col),
+              self.ctx)
+
+    def attend(self, q: torch.Tensor, kv: torch.Tensor, part: torch.Tensor, o: torch.Tensor,
+               n: int, cols: int, heads: int, hd: int) -> None:
+        """`Pass::attend` (src/gpu/mod.rs:1485-1505)."""
+        check(L.lib().wavo_attend(self.ctx, _ptr(q), _ptr(kv), _ptr(part), _ptr(o), n, cols, heads,
+                                  hd), self.ctx)
+
+    def attend_batch(self, q, q_stride: int, kv, kv_stride: int, part, o, o_stride: int, n: int,
+                     cols: int, heads: int, hd: int, batch: int) -> None:
+        check(L.lib().wavo_attend_batch(self.ctx, _ptr(q), q_stride, _ptr(kv), kv_stride,
+                                        _ptr(part), _ptr(o), o_stride, n, cols, heads, hd, batch),
+              self.ctx)
+
+
+def partition_lpt(costs, parts: int) -> list[int]:
+    """Longest-processing-time-first assignment of independent items to `parts` devices."""
+    c = np.ascontiguousarray(costs, np.uint64)
+    out = np.zeros(len(c), np.uint32)
+    check(L.lib().wavo_partition_lpt(c.ctypes.data, len(c), parts, out.ctypes.data))
+    return out.tolist()
