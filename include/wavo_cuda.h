@@ -73,9 +73,11 @@ void wavo_destroy(wavo_ctx *ctx);
 /* The last error message of the context (or of the last failed wavo_create when ctx is NULL). */
 const char *wavo_last_error(const wavo_ctx *ctx);
 
-/* Runs the context's work on `stream` (a cudaStream_t; NULL restores the context's own). */
+/* Runs the context's work on `stream` (a cudaStream_t; NULL is the CUDA default stream). A new
+ * context runs on a stream of its own, which wavo_own_stream returns. */
 wavo_status wavo_set_stream(wavo_ctx *ctx, void *stream);
 void *wavo_get_stream(const wavo_ctx *ctx);
+void *wavo_own_stream(const wavo_ctx *ctx);
 int wavo_sm_count(const wavo_ctx *ctx);
 
 /* ---- buffers: replaces Gpu::buffer / upload / write / readback (src/gpu/mod.rs:741-756) -- */

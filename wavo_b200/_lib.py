@@ -30,6 +30,7 @@ SIGNATURES = {
     "wavo_last_error": ([_vp], ctypes.c_char_p),
     "wavo_set_stream": ([_vp, _vp], _st),
     "wavo_get_stream": ([_vp], _vp),
+    "wavo_own_stream": ([_vp], _vp),
     "wavo_sm_count": ([_vp], _i32),
     "wavo_malloc": ([_vp, _sz, ctypes.POINTER(_vp)], _st),
     "wavo_free": ([_vp, _vp], _st),

@@ -23,7 +23,8 @@ __global__ void pack_cache_kernel(const float *__restrict__ x, long long src, lo
   for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
        t += (long long)gridDim.x * blockDim.x) {
     const int j = int(t % rows), i = int(t / rows);
-    const float2 v = *reinterpret_cast<const float2 *>(x + src + j * stride + 2LL * i);
+    const float *p = x + src + j * stride + 2LL * i;  // any float offset: two scalar loads
+    const float2 v = make_float2(p[0], p[1]);
     const long long at = i < half ? (long long)i * cols + col + j
                                   : (long long)half * cols + (long long)(col + j) * half + (i - half);
     cache[at] = pack_half2(v.x, v.y);

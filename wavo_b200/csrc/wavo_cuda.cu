@@ -220,11 +220,13 @@ void wavo_destroy(wavo_ctx *ctx) {
 wavo_status wavo_set_stream(wavo_ctx *ctx, void *stream) {
   if (!ctx) return WAVO_EINVAL;
   std::lock_guard<std::mutex> g(ctx->mu);
-  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own;
+  if (ctx->capturing) return fail(ctx, WAVO_EINVAL, "set_stream during a capture");
+  ctx->stream = static_cast<cudaStream_t>(stream);  // NULL: the CUDA default stream
   return WAVO_OK;
 }
 
 void *wavo_get_stream(const wavo_ctx *ctx) { return ctx ? ctx->stream : nullptr; }
+void *wavo_own_stream(const wavo_ctx *ctx) { return ctx ? ctx->own : nullptr; }
 int wavo_sm_count(const wavo_ctx *ctx) { return ctx ? ctx->sms : 0; }
 
 wavo_status wavo_malloc(wavo_ctx *ctx, size_t bytes, void **out) {
@@ -663,7 +665,7 @@ wavo_status wavo_pack(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stri
   std::lock_guard<std::mutex> g(ctx->mu);
   if (rows == 0) return WAVO_OK;
   if (!x || !cache) return fail(ctx, WAVO_EINVAL, "pack: NULL buffer");
-  if (d % 2 || col + rows > cols || (src % 2) || (stride % 2))
+  if (d % 2 || col + rows > cols)
     return fail(ctx, WAVO_EINVAL, "pack: rows %u at %u of %u positions, d %u", rows, col, cols, d);
   cudaSetDevice(ctx->device);
   CK(wv::launch_pack_cache(x, src, stride, static_cast<uint32_t *>(cache), int(rows), int(d),
