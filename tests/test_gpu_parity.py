@@ -1,0 +1,193 @@
+"""Parity of the CUDA path with the CPU oracle (the reference's src/cpu attention path restated) at
+the BASELINE.json configurations' shapes, within the BASELINE tolerance: max-abs error 2e-3 and
+relative-L2 error 1e-3.
+
+Level (i): identical attention inputs (the f16 values the kernel reads) into the oracle's f32
+attention. Level (ii): a whole attention layer — projection, attention, output projection with its
+residual — against the oracle's f16-rounded GEMM and f32 attention (src/cpu/gemm.rs, ops.rs).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_L2 = 2e-3, 1e-3
+
+
+def check(got, want, max_abs=MAX_ABS, rel_l2=REL_L2):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    err = np.abs(got - want)
+    rel = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+    assert err.max() <= max_abs and rel <= rel_l2, f"max-abs {err.max():.3g}, rel-L2 {rel:.3g}"
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    from wavo_b200.gpu import Gpu
+    g = Gpu(0)
+    yield g
+    g.sync()
+    g.close()
+
+
+def f16(x):
+    return np.ascontiguousarray(np.asarray(x, np.float32).astype(np.float16).astype(np.float32))
+
+
+def qkv_like(rng, t, ch, sections, std=0.7):
+    """Activations shaped like projection outputs of N(0,1) rows through N(0, 0.02) weights."""
+    return (rng.standard_normal((t, sections * ch)) * std).astype(np.float32)
+
+
+@pytest.mark.parametrize("t,heads,hd", [(1500, 20, 64), (750, 16, 48), (300, 4, 128), (129, 2, 64)])
+def test_plain_attention_level_i(gpu, t, heads, hd):
+    # C2 (Whisper turbo encoder), C3 (GigaAM heads of 48), and tile edges; f16 operands straight
+    # from a [t][q | k | v] f16 buffer (the fast path).
+    rng = np.random.default_rng(t + hd)
+    ch = heads * hd
+    x = f16(qkv_like(rng, t, ch, 3))
+    want = O.attention(x.ravel(), 3 * ch, np.ascontiguousarray(x.ravel()[2 * ch:]), 3 * ch, t,
+                       heads, ch)
+    xb = torch.from_numpy(x).cuda().half()
+    o = torch.zeros(t, ch, dtype=torch.float16, device="cuda")
+    gpu.pass_().attention(xb, None, None, o, t, heads, hd)
+    gpu.sync()
+    check(o.float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("t", [138, 300, 64, 1])
+def test_relative_attention_level_i(gpu, t):
+    # C1 / C5 shapes: 8 heads of 128, positions pos_rows(t); inputs rounded to f16 for the oracle.
+    heads, hd = 8, 128
+    ch = heads * hd
+    rng = np.random.default_rng(t)
+    qkv = f16(qkv_like(rng, t, ch, 3))
+    u = f16(rng.standard_normal(ch) * 0.02)
+    vb = f16(rng.standard_normal(ch) * 0.02)
+    pos = f16(rng.standard_normal((O.pos_rows(t), ch)) * 0.5)
+    # The oracle forms q+u and q+v in f32; the kernel reads them as f16, so round them first.
+    q = qkv[:, :ch]
+    quv = np.concatenate([f16(q + u), qkv[:, ch:], f16(q + vb)], axis=1)
+    want = naive_rel(quv, pos, t, heads, hd)
+    for dtype in (torch.float32, torch.float16):
+        xb = torch.from_numpy(quv).cuda().to(dtype)
+        pb = torch.from_numpy(pos).cuda().to(dtype)
+        o = torch.zeros(t, ch, dtype=dtype, device="cuda")
+        gpu.pass_().attention(xb, None, pb, o, t, heads, hd)
+        gpu.sync()
+        check(o.float().cpu().numpy(), want)
+
+
+def naive_rel(quv, pos, t, heads, hd):
+    d = heads * hd
+    i = np.arange(t)[:, None]
+    j = np.arange(t)[None, :]
+    out = np.zeros((t, d))
+    for h in range(heads):
+        sl = slice(h * hd, (h + 1) * hd)
+        qu, k, v, qv = (quv[:, s * d:(s + 1) * d][:, sl].astype(np.float64) for s in range(4))
+        bd = np.take_along_axis(qv @ pos[:, sl].astype(np.float64).T, j + t + 15 - i, axis=1)
+        s = (qu @ k.T + bd) / np.sqrt(hd)
+        e = np.exp(s - s.max(axis=1, keepdims=True))
+        out[:, sl] = (e / e.sum(axis=1, keepdims=True)) @ v
+    return out
+
+
+def test_relative_attention_matches_the_cpu_oracle(gpu):
+    # The oracle's own relative_attention (src/cpu/ops.rs:223-273) on qkv [q | k | v], u and v:
+    # the GPU gets [q+u | k | v | q+v] as the reference's dual-bias projection writes it.
+    t, heads, hd = 138, 8, 128
+    ch = heads * hd
+    rng = np.random.default_rng(7)
+    qkv = qkv_like(rng, t, ch, 3)
+    u = (rng.standard_normal(ch) * 0.02).astype(np.float32)
+    vb = (rng.standard_normal(ch) * 0.02).astype(np.float32)
+    pos = (rng.standard_normal((O.pos_rows(t), ch)) * 0.5).astype(np.float32)
+    want = O.relative_attention(qkv.ravel(), pos.ravel(), u, vb, t, heads, ch)
+    q = qkv[:, :ch]
+    quv = np.ascontiguousarray(np.concatenate([q + u, qkv[:, ch:], q + vb], axis=1))
+    o = torch.zeros(t, ch, device="cuda")
+    gpu.pass_().attention(torch.from_numpy(quv).cuda(), None, torch.from_numpy(pos).cuda(), o, t,
+                          heads, hd)
+    gpu.sync()
+    check(o.cpu().numpy(), want)
+
+
+def test_varlen_segments(gpu):
+    # Independent segments in one launch equal each segment alone (plain and relative).
+    rng = np.random.default_rng(3)
+    lens = [200, 37, 129, 300, 1, 256]
+    starts = np.cumsum([0] + lens[:-1]).astype(np.int32)
+    rows = int(sum(lens))
+    for rel in (False, True):
+        heads, hd = (8, 128) if rel else (4, 64)
+        ch = heads * hd
+        secs = 4 if rel else 3
+        x = f16(qkv_like(rng, rows, ch, secs))
+        pos_t = max(lens)
+        pos = f16(rng.standard_normal((O.pos_rows(pos_t), ch)) * 0.5) if rel else None
+        xb = torch.from_numpy(x).cuda().half()
+        pb = torch.from_numpy(pos).cuda().half() if rel else None
+        o = torch.full((rows, ch), 7.0, dtype=torch.float16, device="cuda")
+        gpu.pass_().attention_varlen(xb, None, pb, o, rows, torch.from_numpy(starts).cuda(),
+                                     torch.tensor(lens, dtype=torch.int32, device="cuda"),
+                                     max(lens), heads, hd, pos_t)
+        gpu.sync()
+        got = o.float().cpu().numpy()
+        for s, n in zip(starts, lens):
+            seg = x[s:s + n]
+            if rel:
+                # The shared table: row r is position pos_t + 15 - r; this segment's rows r' =
+                # r - (pos_t - n) give its own pos_rows(n) table.
+                p = pos[pos_t - n: pos_t - n + O.pos_rows(n)]
+                want = naive_rel(seg, p, n, heads, hd)
+            else:
+                want = O.attention(np.ascontiguousarray(seg.ravel()), 3 * ch,
+                                   np.ascontiguousarray(seg.ravel()[2 * ch:]), 3 * ch, n, heads, ch)
+            check(got[s:s + n], want)
+
+
+@pytest.mark.parametrize("ty", [O.TY_F16, O.TY_Q8_0])
+def test_layer_level_ii(gpu, ty):
+    # A Whisper-shaped layer (C2 weights f16) and a Parakeet-shaped one (C5 weights Q8_0): the
+    # oracle's GEMM rounds a and W to f16 (its f16 path, as the reference GPU GEMM).
+    from wavo_b200 import GGML_F16, GGML_Q8_0
+    O.set_vnni(0)
+    try:
+        rng = np.random.default_rng(11)
+        t, heads, hd = (1500, 20, 64) if ty == O.TY_F16 else (300, 8, 128)
+        d = heads * hd
+        y = rng.standard_normal((t, d)).astype(np.float32)
+        wq = (rng.standard_normal((3 * d, d)) * 0.02).astype(np.float32)
+        wo = (rng.standard_normal((d, d)) * 0.02).astype(np.float32)
+        bq = np.concatenate([rng.standard_normal(d) * 0.02, np.zeros(d),
+                             rng.standard_normal(d) * 0.02]).astype(np.float32)
+        bo = (rng.standard_normal(d) * 0.02).astype(np.float32)
+        if ty == O.TY_F16:
+            dq, do_, gty = wq.astype(np.float16).tobytes(), wo.astype(np.float16).tobytes(), GGML_F16
+        else:
+            dq, do_, gty = O.q8_0_bytes(wq), O.q8_0_bytes(wo), GGML_Q8_0
+        lq, lo = gpu.linear(gty, 3 * d, d, dq, bq), gpu.linear(gty, d, d, do_, bo)
+        yb = torch.from_numpy(y).cuda()
+        qkv = torch.zeros(t, 3 * d, dtype=torch.float16, device="cuda")
+        o = torch.zeros(t, d, dtype=torch.float16, device="cuda")
+        x = torch.ones(t, d, device="cuda")
+        p = gpu.pass_()
+        p.gemm(yb, lq, qkv, t, "bias")
+        p.attention(qkv, None, None, o, t, heads, hd)
+        p.gemm(o, lo, x, t, "residual", 1.0)
+        gpu.sync()
+        ref_qkv = O.Linear(ty, 3 * d, d, dq, bq).gemm(y.ravel(), t)
+        r16 = f16(ref_qkv)
+        ref_o = O.attention(r16, 3 * d, np.ascontiguousarray(r16[2 * d:]), 3 * d, t, heads, d)
+        want = np.ones(t * d, np.float32)
+        O.Linear(ty, d, d, do_, bo).gemm(np.ascontiguousarray(ref_o.ravel()), t, want, "residual",
+                                         1.0)
+        check(x.cpu().numpy(), want)
+    finally:
+        O.set_vnni(-1)

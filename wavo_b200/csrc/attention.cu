@@ -461,22 +461,17 @@ cudaError_t launch_one(const CUtensorMap &q, const CUtensorMap &kv, const CUtens
 
 }  // namespace
 
-size_t attn_smem_bytes(int hd_pad, bool rel) {
-  if (rel) return 1024 + Cfg<128, true>::OFF_BAR + sizeof(AttnBarriers);
-  return hd_pad == 64 ? 1024 + Cfg<64, false>::OFF_BAR + sizeof(AttnBarriers)
-                      : 1024 + Cfg<128, false>::OFF_BAR + sizeof(AttnBarriers);
-}
-
 cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
                              const CUtensorMap &map_pos, const AttnArgs &a, int hd_pad, bool rel,
                              int max_len, int nseg, cudaStream_t s) {
   if (max_len <= 0 || nseg <= 0) return cudaSuccess;
   if (rel) return launch_one<128, true>(map_q, map_kv, map_pos, a, max_len, nseg, s);
-  if (hd_pad == 64) return launch_one<64, false>(map_q, map_kv, map_pos, a, max_len, nseg, s);
-  return launch_one<128, false>(map_q, map_kv, map_pos, a, max_len, nseg, s);
+  return launch_fa_attention(map_q, map_kv, a, hd_pad, max_len, nseg, s);
 }
 
-int attn_block_keys(bool rel) { return rel ? Cfg<128, true>::BN : Cfg<64, false>::BN; }
+int attn_block_keys(bool rel, int hd_pad) {
+  return rel ? Cfg<128, true>::BN : fa_block_keys(hd_pad);
+}
 int attn_pos_window_rows() { return Cfg<128, true>::PW_ROWS; }
 
 cudaError_t launch_pack_heads(const void *in, int in_f16, long long ld_in, const int *in_off,

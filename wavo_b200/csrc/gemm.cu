@@ -2,10 +2,11 @@
 // (src/gpu/mod.rs:1394-1425, gemm.wgsl:167-242) re-designed for the 5th-generation tensor cores.
 //
 // a [m][k] f16 and W [n][k] f16 are streamed by TMA into 128-byte-swizzled shared-memory stages;
-// one thread issues tcgen05.mma (M=128, N=128, K=16, f32 accumulators in TMEM); four epilogue warps
+// one thread issues tcgen05.mma (M=128, N=BN, K=16, f32 accumulators in TMEM); four epilogue warps
 // read the accumulators back with tcgen05.ld (one row per thread), add the bias, apply the epilogue
-// and store the row. The kernel is persistent (one CTA per SM walks the output tiles) and keeps two
-// accumulators in TMEM, so the epilogue of one tile overlaps the MMAs of the next.
+// (a compile-time mode) and store the row. The kernel is persistent (one CTA per SM walks the output
+// tiles) and keeps two accumulators in TMEM, so the epilogue of one tile overlaps the MMAs of the
+// next. The tile width BN (128 or 256) is chosen per shape to even out the last wave of tiles.
 //
 // Numerics match the reference GPU GEMM: a and W rounded to f16 (round to nearest even), products
 // exact, sums in f32. Dual outputs (a bias longer than the rows) write the first `dual` outputs a
@@ -16,16 +17,21 @@
 namespace wv {
 namespace {
 
-constexpr int BM = kGemmBM, BN = kGemmBN, BK = kGemmBK, STAGES = kGemmStages;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
-constexpr uint32_t IDESC = idesc_f16(BM, BN, 0);
+constexpr int BM = kGemmBM, BK = kGemmBK;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr uint32_t IDESC = idesc_f16(BM, BN, 0);
+};
 
 struct __align__(8) GemmBarriers {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[6];
+  uint64_t empty[6];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
@@ -42,27 +48,26 @@ __device__ __forceinline__ float gelu_f(float x) {
   return 0.5f * x * (1.0f + s * (1.0f - p * t * expf(-z * z)));
 }
 
-__device__ __forceinline__ float apply_epi(int e, float v, float c, float alpha) {
-  switch (e) {
-    case kBias: return v;
-    case kSilu: return v / (1.0f + expf(-v));
-    case kRelu: return fmaxf(v, 0.0f);
-    case kResidual: return c + alpha * v;
-    case kGelu: return gelu_f(v);
-    case kGeluResidual: return c + gelu_f(v);
-    default: return tanhf(fminf(fmaxf(v, -10.0f), 10.0f));
-  }
+template <int E>
+__device__ __forceinline__ float epi(float v, float c, float alpha) {
+  if (E == kBias) return v;
+  if (E == kSilu) return v / (1.0f + expf(-v));
+  if (E == kRelu) return fmaxf(v, 0.0f);
+  if (E == kResidual) return c + alpha * v;
+  if (E == kGelu) return gelu_f(v);
+  if (E == kGeluResidual) return c + gelu_f(v);
+  return tanhf(fminf(fmaxf(v, -10.0f), 10.0f));
 }
 
 // Stores 32 consecutive outputs of one row (columns col0.. of `c`), reading c first for the
-// residual epilogues. `lim` is the number of valid columns (<= 32).
+// residual epilogues. `lim` is the number of valid columns (<= 32); b holds the 32 biases.
+template <int E>
 __device__ __forceinline__ void store_row32(const GemmArgs &g, long long row, int col0, int lim,
-                                            const float (&v)[32], int e, const float *bias_at) {
-  const bool resid = (e == kResidual || e == kGeluResidual);
+                                            const float (&v)[32], const float (&b)[32]) {
+  constexpr bool resid = (E == kResidual || E == kGeluResidual);
   if (g.c_f16) {
     __half *c = reinterpret_cast<__half *>(g.c) + row * g.ldc + col0;
-    const bool vec = lim == 32 && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
-    if (vec) {
+    if (lim == 32 && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 old = make_uint4(0, 0, 0, 0);
@@ -71,56 +76,72 @@ __device__ __forceinline__ void store_row32(const GemmArgs &g, long long row, in
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          int j = 8 * q + 2 * i;
-          float a = apply_epi(e, v[j] + bias_at[j], __half2float(oh[2 * i]), g.alpha);
-          float b = apply_epi(e, v[j + 1] + bias_at[j + 1], __half2float(oh[2 * i + 1]), g.alpha);
-          w[i] = pack_half2(a, b);
+          const int j = 8 * q + 2 * i;
+          w[i] = pack_half2(epi<E>(v[j] + b[j], __half2float(oh[2 * i]), g.alpha),
+                            epi<E>(v[j + 1] + b[j + 1], __half2float(oh[2 * i + 1]), g.alpha));
         }
         *reinterpret_cast<uint4 *>(c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      for (int j = 0; j < 32; ++j)
         if (j < lim) {
-          float old = resid ? __half2float(c[j]) : 0.0f;
-          c[j] = __float2half_rn(apply_epi(e, v[j] + bias_at[j], old, g.alpha));
+          const float old = resid ? __half2float(c[j]) : 0.0f;
+          c[j] = __float2half_rn(epi<E>(v[j] + b[j], old, g.alpha));
         }
-      }
     }
   } else {
     float *c = reinterpret_cast<float *>(g.c) + row * g.ldc + col0;
-    const bool vec = lim == 32 && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
-    if (vec) {
+    if (lim == 32 && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float4 old = make_float4(0, 0, 0, 0);
         if (resid) old = *reinterpret_cast<const float4 *>(c + 4 * q);
         float4 o;
-        o.x = apply_epi(e, v[4 * q + 0] + bias_at[4 * q + 0], old.x, g.alpha);
-        o.y = apply_epi(e, v[4 * q + 1] + bias_at[4 * q + 1], old.y, g.alpha);
-        o.z = apply_epi(e, v[4 * q + 2] + bias_at[4 * q + 2], old.z, g.alpha);
-        o.w = apply_epi(e, v[4 * q + 3] + bias_at[4 * q + 3], old.w, g.alpha);
+        o.x = epi<E>(v[4 * q + 0] + b[4 * q + 0], old.x, g.alpha);
+        o.y = epi<E>(v[4 * q + 1] + b[4 * q + 1], old.y, g.alpha);
+        o.z = epi<E>(v[4 * q + 2] + b[4 * q + 2], old.z, g.alpha);
+        o.w = epi<E>(v[4 * q + 3] + b[4 * q + 3], old.w, g.alpha);
         *reinterpret_cast<float4 *>(c + 4 * q) = o;
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      for (int j = 0; j < 32; ++j)
         if (j < lim) {
-          float old = resid ? c[j] : 0.0f;
-          c[j] = apply_epi(e, v[j] + bias_at[j], old, g.alpha);
+          const float old = resid ? c[j] : 0.0f;
+          c[j] = epi<E>(v[j] + b[j], old, g.alpha);
         }
-      }
     }
   }
 }
 
+// 32 biases from `bias` (16-byte aligned when `vec`), zeros past `lim`.
+__device__ __forceinline__ void load_bias32(const float *bias, int lim, float (&b)[32]) {
+  if (lim == 32 && ((reinterpret_cast<uintptr_t>(bias) & 15u) == 0)) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = __ldg(reinterpret_cast<const float4 *>(bias) + q);
+      b[4 * q] = t.x;
+      b[4 * q + 1] = t.y;
+      b[4 * q + 2] = t.z;
+      b[4 * q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) b[j] = j < lim ? __ldg(bias + j) : 0.0f;
+  }
+}
+
+template <int BN, int E>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_w,
                 const GemmArgs g) {
+  using C = GemmCfg<BN>;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  GemmBarriers *bar = reinterpret_cast<GemmBarriers *>(smem + STAGES * STAGE_BYTES);
+  GemmBarriers *bar = reinterpret_cast<GemmBarriers *>(smem + STAGES * C::STAGE_BYTES);
   const uint32_t warp = warp_id(), lane = lane_id();
 
   const int num_m = (g.m + BM - 1) / BM;
@@ -146,7 +167,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tma_w);
   }
   if (warp == 1) {
-    tmem_alloc(&bar->tmem_base, TMEM_COLS);
+    tmem_alloc(&bar->tmem_base, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -169,10 +190,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
-          uint8_t *sa = smem + stage * STAGE_BYTES;
-          mbar_arrive_expect_tx(&bar->full[stage], STAGE_BYTES);
+          uint8_t *sa = smem + stage * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&bar->full[stage], C::STAGE_BYTES);
           tma_load_2d(sa, &tma_a, &bar->full[stage], kb * BK, m0);
-          tma_load_2d(sa + A_BYTES, &tma_w, &bar->full[stage], kb * BK, n0);
+          tma_load_2d(sa + C::A_BYTES, &tma_w, &bar->full[stage], kb * BK, n0);
           armed |= 1u << stage;
           if (++stage == STAGES) {
             stage = 0;
@@ -185,8 +206,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // stage is the one before `stage` in ring order.
         for (int s = 0; s < STAGES; ++s) {
           if (!(armed & (1u << s))) continue;
-          uint32_t par = (s < stage) ? phase : (phase ^ 1u);
-          long long t0 = clock64();
+          const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+          const long long t0 = clock64();
           while (!mbar_try_wait(&bar->full[s], par) && clock64() - t0 < kWaitCycles) {
           }
         }
@@ -214,12 +235,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t sb = sa + A_BYTES;
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
             umma_f16(d, sdesc_sw128(sa + ks * 32, 16, 1024), sdesc_sw128(sb + ks * 32, 16, 1024),
-                     IDESC, (kb | ks) != 0);
+                     C::IDESC, (kb | ks) != 0);
           }
           issued = true;
           umma_commit(&bar->empty[stage]);
@@ -237,7 +258,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok && issued) {
         umma_commit(&bar->drain);
-        long long t0 = clock64();
+        const long long t0 = clock64();
         while (!mbar_try_wait(&bar->drain, 0) && clock64() - t0 < kWaitCycles) {
         }
       }
@@ -260,17 +281,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (col0 >= g.cols) break;
         uint32_t r[32];
         tmem_ld32(tmem + ((quarter * 32u) << 16) + uint32_t(acc * BN + chunk * 32), r);
+        const int lim = min(32, g.cols - col0);
+        float b[32];
+        load_bias32(g.bias + col0, lim, b);
         tmem_wait_ld();
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const int lim = min(32, g.cols - col0);
-        if (row_ok) {
-          store_row32(g, row, col0, lim, v, g.epilogue, g.bias + col0);
-          if (col0 < g.dual) {
-            const int lim2 = min(lim, g.dual - col0);
-            store_row32(g, row, g.cols + col0, lim2, v, kBias, g.bias + g.cols + col0);
-          }
+        if (row_ok) store_row32<E>(g, row, col0, lim, v, b);
+        if (col0 < g.dual) {
+          const int lim2 = min(lim, g.dual - col0);
+          load_bias32(g.bias + g.cols + col0, lim2, b);
+          if (row_ok) store_row32<kBias>(g, row, g.cols + col0, lim2, v, b);
         }
       }
       tc_fence_before();
@@ -286,7 +308,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 // f32 rows to f16 rows, zero padded to ld_out columns.
@@ -308,25 +330,63 @@ __global__ void cast_rows_kernel(const float *__restrict__ in, long long ld_in,
   }
 }
 
+template <int BN, int E>
+cudaError_t launch_bn_e(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int grid,
+                        cudaStream_t s) {
+  using C = GemmCfg<BN>;
+  const size_t smem = 1024 + C::STAGES * C::STAGE_BYTES + sizeof(GemmBarriers);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, E>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  gemm_kernel<BN, E><<<grid, kGemmThreads, smem, s>>>(a, w, g);
+  return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int grid,
+                      cudaStream_t s) {
+  switch (g.epilogue) {
+    case kBias: return launch_bn_e<BN, kBias>(a, w, g, grid, s);
+    case kSilu: return launch_bn_e<BN, kSilu>(a, w, g, grid, s);
+    case kRelu: return launch_bn_e<BN, kRelu>(a, w, g, grid, s);
+    case kResidual: return launch_bn_e<BN, kResidual>(a, w, g, grid, s);
+    case kGelu: return launch_bn_e<BN, kGelu>(a, w, g, grid, s);
+    case kGeluResidual: return launch_bn_e<BN, kGeluResidual>(a, w, g, grid, s);
+    default: return launch_bn_e<BN, kTanh>(a, w, g, grid, s);
+  }
+}
+
 }  // namespace
 
-size_t gemm_smem_bytes() { return 1024 + STAGES * STAGE_BYTES + sizeof(GemmBarriers); }
+int gemm_pick_bn(int m, int cols, int num_sms) {
+  // Waves of tiles times the tile width: the cost of the last, partial wave included. The wider
+  // tile moves a quarter fewer bytes per flop, so it wins ties.
+  const int mt = (m + BM - 1) / BM;
+  auto cost = [&](int bn) {
+    const long long tiles = (long long)mt * ((cols + bn - 1) / bn);
+    const long long waves = (tiles + num_sms - 1) / num_sms;
+    return waves * bn;
+  };
+  return cost(256) <= cost(128) ? 256 : 128;
+}
 
-cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int num_sms,
-                        cudaStream_t s) {
-  const size_t smem = gemm_smem_bytes();
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  const int tiles = ((g.m + BM - 1) / BM) * ((g.cols + BN - 1) / BN);
+size_t gemm_smem_bytes(int bn) {
+  return bn == 256 ? 1024 + GemmCfg<256>::STAGES * GemmCfg<256>::STAGE_BYTES + sizeof(GemmBarriers)
+                   : 1024 + GemmCfg<128>::STAGES * GemmCfg<128>::STAGE_BYTES + sizeof(GemmBarriers);
+}
+
+cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int bn,
+                        int num_sms, cudaStream_t s) {
+  const int tiles = ((g.m + BM - 1) / BM) * ((g.cols + bn - 1) / bn);
   const int grid = tiles < num_sms ? tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
-  gemm_kernel<<<grid, kGemmThreads, smem, s>>>(a, w, g);
-  return cudaGetLastError();
+  return bn == 256 ? launch_bn<256>(a, w, g, grid, s) : launch_bn<128>(a, w, g, grid, s);
 }
 
 cudaError_t launch_cast_rows(const float *in, long long ld_in, __half *out, long long ld_out,

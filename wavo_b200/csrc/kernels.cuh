@@ -28,10 +28,12 @@ struct GemmArgs {
   int *err;           // device error word
 };
 
-constexpr int kGemmBM = 128, kGemmBN = 128, kGemmBK = 64, kGemmStages = 6;
+constexpr int kGemmBM = 128, kGemmBK = 64;
 constexpr int kGemmThreads = 192;
-size_t gemm_smem_bytes();
-cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g,
+// Tile width (128 or 256) for an m x cols output on num_sms SMs; the W tensor map's box height.
+int gemm_pick_bn(int m, int cols, int num_sms);
+size_t gemm_smem_bytes(int bn);
+cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int bn,
                         int num_sms, cudaStream_t s);
 
 // f32 rows -> f16 rows (round to nearest even), into a padded row stride; columns past `cols`
@@ -61,10 +63,14 @@ struct AttnArgs {
 };
 
 constexpr int kAttnThreads = 192;
-constexpr int kAttnBlockQ = 128;  // queries per CTA (the TMA box height of map_q)
-size_t attn_smem_bytes(int hd_pad, bool rel);
-int attn_block_keys(bool rel);   // keys per block (the TMA box height of map_kv)
+constexpr int kAttnBlockQ = 128;  // queries per tile (the TMA box height of map_q)
+int attn_block_keys(bool rel, int hd_pad);  // keys per block (the TMA box height of map_kv)
 int attn_pos_window_rows();      // position rows per block (the TMA box height of map_pos)
+// The plain-layout kernel (attention_fa.cu): two query tiles per CTA.
+int fa_block_keys(int hd_pad);
+cudaError_t launch_fa_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
+                                const AttnArgs &a, int hd_pad, int max_len, int nseg,
+                                cudaStream_t s);
 // hd_pad: 64 or 128 (the padded head size of the operand tiles). All maps are 2D f16 tensor maps
 // with 64-column (128-byte) boxes and 128-byte swizzle.
 cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
