@@ -4,15 +4,17 @@
 //
 // A CTA takes two 128-query tiles of one head of one segment, so that the tensor core works on one
 // tile while the other tile's softmax runs:
-//   warp 0     TMA: both Q tiles once, then K and V blocks through two-slot rings;
-//   warp 1     one thread issues the UMMAs: S_t = Q_t·K^T into TMEM, then O_t += P_t·V;
+//   warp 0     TMA: both Q tiles once, then K and V blocks through three-slot rings;
+//   warp 1     one thread issues the UMMAs: S_t = Q_t·K^T into TMEM, then O_t += P_t·V with P_t
+//              read from TMEM;
 //   warps 2-5  softmax of tile 0, warps 6-9 softmax of tile 1: one query row per thread, read from
-//              TMEM with tcgen05.ld; online softmax in registers with a lagging maximum (the TMEM
-//              accumulator is rescaled only when a row maximum grows by more than 2^8); a quarter
-//              of the exponentials on the FMA pipe (a degree-4 polynomial for 2^f on [-1/2, 1/2]
-//              fitted for this kernel, with the exponent added in the integer bits), the rest on
-//              the MUFU; probabilities as f16 into a 128-byte-swizzled shared tile (the A operand
-//              of P·V); at the end the accumulator row is normalised and stored.
+//              TMEM with tcgen05.ld in two passes (row maximum, then probabilities); a lagging
+//              maximum (the TMEM accumulator is rescaled only when a row maximum grows by more than
+//              2^8); a quarter of the exponentials on the FMA pipe (a degree-4 polynomial for 2^f
+//              on [-1/2, 1/2] fitted for this kernel, with the exponent added in the integer bits),
+//              the rest on the MUFU; probabilities written back to TMEM as f16 pairs with
+//              tcgen05.st (the UMMAs already use shared memory at its full read rate, so P stays
+//              out of it); at the end the accumulator row is normalised and stored.
 #include "kernels.cuh"
 #include "ptx.cuh"
 
@@ -22,6 +24,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int NT = 2;  // query tiles per CTA
 constexpr int THREADS = 64 + NT * 128;
+constexpr int KVS = 3;  // K and V ring slots
 
 template <int HD, int BN>
 struct Fa {
@@ -30,24 +33,27 @@ struct Fa {
   static constexpr int ATOM_KV = BN * 128;
   static constexpr int Q_BYTES = BM * HD * 2;
   static constexpr int KV_BYTES = BN * HD * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + NT * P_BYTES;
-  static constexpr int T_S = 0;        // tile t: S at t·BN
-  static constexpr int T_O = NT * BN;  // tile t: O at T_O + t·HD
+  static constexpr int OFF_V = OFF_K + KVS * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + KVS * KV_BYTES;
+  // TMEM columns of tile t, from t·256: the scores S (BN f32 columns), the probabilities P (BN
+  // f16, two per column: the A operand of P·V, read by the tensor core from TMEM, so that neither
+  // the softmax's writes nor the UMMA's reads of P touch shared memory), the accumulator O.
+  static constexpr int T_TILE = 256;
+  static constexpr int T_S = 0;
+  static constexpr int T_P = BN;
+  static constexpr int T_O = (BN + BN / 2 + 31) / 32 * 32;
   static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
   static constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
-  static_assert(NT * (BN + HD) <= TMEM_COLS, "TMEM");
+  static_assert(T_O + HD <= T_TILE && NT * T_TILE <= TMEM_COLS, "TMEM");
 };
 
 struct __align__(8) FaBarriers {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
+  uint64_t k_full[KVS], k_empty[KVS];
+  uint64_t v_full[KVS], v_empty[KVS];
   uint64_t s_full[NT], s_free[NT];
   uint64_t p_full[NT], pv_done[NT];
   uint64_t o_full;
@@ -99,7 +105,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KVS; ++i) {
       mbar_init(&bar->k_full[i], 1);
       mbar_init(&bar->k_empty[i], 1);
       mbar_init(&bar->v_full[i], 1);
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- TMA producer ------------------------------------------------------------------------
     if (lane == 0) {
       bool ok = true;
-      uint32_t k_last[2] = {0, 0}, v_last[2] = {0, 0};  // bit 1: armed; bit 0: parity
+      uint32_t k_last[KVS] = {}, v_last[KVS] = {};  // bit 1: armed; bit 0: parity
       mbar_arrive_expect_tx(&bar->q_full, NT * C::Q_BYTES);
       for (int t = 0; t < NT; ++t)
 #pragma unroll
@@ -143,22 +149,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_2d(smem + C::OFF_Q + t * C::Q_BYTES + b * C::ATOM_Q, &map_q, &bar->q_full,
                       a.q_off + hoff + 64 * b, row0 + m0 + t * BM);
       for (int j = 0; j < nb; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1u;
+        const int s = j % KVS;
+        const uint32_t par = ((j / KVS) & 1) ^ 1u;
         if (!mbar_wait(&bar->k_empty[s], par, ab, kErrTimeoutProducer)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar->k_full[s], C::KV_BYTES);
 #pragma unroll
         for (int b = 0; b < C::NBOX; ++b)
           tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + b * C::ATOM_KV, &map_kv, &bar->k_full[s],
                       a.k_off + hoff + 64 * b, row0 + j * BN);
-        k_last[s] = 2u | ((j >> 1) & 1u);
+        k_last[s] = 2u | ((j / KVS) & 1u);
         if (!mbar_wait(&bar->v_empty[s], par, ab, kErrTimeoutProducer)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar->v_full[s], C::KV_BYTES);
 #pragma unroll
         for (int b = 0; b < C::NBOX; ++b)
           tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + b * C::ATOM_KV, &map_kv, &bar->v_full[s],
                       a.v_off + hoff + 64 * b, row0 + j * BN);
-        v_last[s] = 2u | ((j >> 1) & 1u);
+        v_last[s] = 2u | ((j / KVS) & 1u);
       }
       if (!ok) {
         const long long t0 = clock64();
@@ -168,7 +174,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         };
         drain(&bar->q_full, 2u);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < KVS; ++s) {
           drain(&bar->k_full[s], k_last[s]);
           drain(&bar->v_full[s], v_last[s]);
         }
@@ -181,13 +187,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool issued = false;
       const int hsteps = (a.hd + 15) / 16;
       const uint32_t sq = smem_u32(smem + C::OFF_Q), sk = smem_u32(smem + C::OFF_K);
-      const uint32_t sv = smem_u32(smem + C::OFF_V), sp = smem_u32(smem + C::OFF_P);
+      const uint32_t sv = smem_u32(smem + C::OFF_V);
       tc_fence_after();
+      // Per block j, tile by tile: S_t(j) as soon as tile t's softmax released S_t(j-1), then
+      // P_t(j-1)·V(j-1). Tiles advance independently, so one tile's softmax overlaps the other
+      // tile's UMMAs.
       for (int j = 0; j <= nb && ok; ++j) {
-        if (j < nb) {
-          const int s = j & 1;
-          if (!mbar_wait(&bar->k_full[s], (j >> 1) & 1, ab, kErrTimeoutMma)) { ok = false; break; }
-          for (int t = 0; t < nt && ok; ++t) {
+        const int sk_slot = j % KVS, sv_slot = (j + KVS - 1) % KVS;
+        if (j < nb && !mbar_wait(&bar->k_full[sk_slot], (j / KVS) & 1, ab, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        if (j >= 1 &&
+            !mbar_wait(&bar->v_full[sv_slot], ((j - 1) / KVS) & 1, ab, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        for (int t = 0; t < nt && ok; ++t) {
+          if (j < nb) {
             if (j >= 1 && !mbar_wait(&bar->s_free[t], (j - 1) & 1, ab, kErrTimeoutMma)) {
               ok = false;
               break;
@@ -197,34 +214,30 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint64_t ad =
                   sdesc_sw128(sq + t * C::Q_BYTES + (kk >> 2) * C::ATOM_Q + (kk & 3) * 32, 16, 1024);
               const uint64_t bd = sdesc_sw128(
-                  sk + s * C::KV_BYTES + (kk >> 2) * C::ATOM_KV + (kk & 3) * 32, 16, 1024);
-              umma_f16(tmem + C::T_S + t * BN, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+                  sk + sk_slot * C::KV_BYTES + (kk >> 2) * C::ATOM_KV + (kk & 3) * 32, 16, 1024);
+              umma_f16(tmem + t * C::T_TILE + C::T_S, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
             }
             issued = true;
             umma_commit(&bar->s_full[t]);
           }
-          if (!ok) break;
-          umma_commit(&bar->k_empty[s]);
-        }
-        if (j >= 1) {
-          const int i = j - 1, s = i & 1;
-          if (!mbar_wait(&bar->v_full[s], (i >> 1) & 1, ab, kErrTimeoutMma)) { ok = false; break; }
-          for (int t = 0; t < nt && ok; ++t) {
+          if (j >= 1) {
+            const int i = j - 1;
             if (!mbar_wait(&bar->p_full[t], i & 1, ab, kErrTimeoutMma)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t ad = sdesc_sw128(
-                  sp + t * C::P_BYTES + (kk >> 2) * C::ATOM_Q + (kk & 3) * 32, 16, 1024);
+              // A = P from TMEM: keys 16kk.. are columns 8kk.. of the P region.
               const uint64_t bd =
-                  sdesc_sw128(sv + s * C::KV_BYTES + kk * 16 * 128, C::ATOM_KV, 1024);
-              umma_f16(tmem + C::T_O + t * HD, ad, bd, C::IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
+                  sdesc_sw128(sv + sv_slot * C::KV_BYTES + kk * 16 * 128, C::ATOM_KV, 1024);
+              umma_f16_ts(tmem + t * C::T_TILE + C::T_O, tmem + t * C::T_TILE + C::T_P + kk * 8,
+                          bd, C::IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
             }
             umma_commit(&bar->pv_done[t]);
           }
-          if (!ok) break;
-          umma_commit(&bar->v_empty[s]);
         }
+        if (!ok) break;
+        if (j < nb) umma_commit(&bar->k_empty[sk_slot]);
+        if (j >= 1) umma_commit(&bar->v_empty[sv_slot]);
       }
       if (ok) {
         umma_commit(&bar->o_full);
@@ -241,11 +254,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t quarter = warp & 3u;
     const int ii = int(quarter * 32 + lane);
     const uint32_t tl = tmem + ((quarter * 32u) << 16);
-    const uint32_t ts = tl + C::T_S + t * BN, to = tl + C::T_O + t * HD;
+    const uint32_t ts = tl + t * C::T_TILE + C::T_S, tp = tl + t * C::T_TILE + C::T_P;
+    const uint32_t to = tl + t * C::T_TILE + C::T_O;
     const float c = a.scale_log2;
     float m_use = -INFINITY, l = 0.0f;
     bool ok = t < nt;
-    uint8_t *prow = smem + C::OFF_P + t * C::P_BYTES;
     for (int j = 0; j < nb && ok; ++j) {
       if (!mbar_wait(&bar->s_full[t], j & 1, ab, kErrTimeoutConsumer)) { ok = false; break; }
       tc_fence_after();
@@ -311,6 +324,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int x = 0; x < 32; ++x)
               if (q * 32 + x >= kvalid) cur[x] = __float_as_uint(-INFINITY);
           }
+          uint32_t pk[16];  // 32 probabilities as 16 f16 pairs: 16 columns of the P region
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             float p[8];
@@ -320,21 +334,21 @@ __global__ void __launch_bounds__(THREADS, 1)
               p[x] = ((x & 3) == 3) ? exp2_poly(e) : ex2(e);
             }
             l += ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
-            const uint4 v = make_uint4(pack_half2(p[0], p[1]), pack_half2(p[2], p[3]),
-                                       pack_half2(p[4], p[5]), pack_half2(p[6], p[7]));
-            const int chunk = 4 * q + g;  // 16-byte chunk of the row: 8 keys
-            *reinterpret_cast<uint4 *>(prow + (chunk >> 3) * C::ATOM_Q +
-                                       sw128_offset(ii, chunk & 7)) = v;
+#pragma unroll
+            for (int x = 0; x < 4; ++x) pk[4 * g + x] = pack_half2(p[2 * x], p[2 * x + 1]);
           }
+          tmem_st16(tp + q * 16, pk);
         }
       }
-      // The S columns are read: the next S of this tile may overwrite them.
+      // The S columns are read and P is in TMEM: the next S of this tile may overwrite S, and the
+      // P·V UMMA may read P.
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->s_free[t]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->p_full[t]);
+      if (lane == 0) {
+        mbar_arrive(&bar->s_free[t]);
+        mbar_arrive(&bar->p_full[t]);
+      }
     }
     if (ok && mbar_wait(&bar->o_full, 0, ab, kErrTimeoutConsumer)) {
       tc_fence_after();

@@ -6,7 +6,7 @@
 // read the accumulators back with tcgen05.ld (one row per thread), add the bias, apply the epilogue
 // (a compile-time mode) and store the row. The kernel is persistent (one CTA per SM walks the output
 // tiles) and keeps two accumulators in TMEM, so the epilogue of one tile overlaps the MMAs of the
-// next. The tile width BN (128 or 256) is chosen per shape to even out the last wave of tiles.
+// next. The tile width BN (128, 160 or 256) is chosen per shape to even out the last wave of tiles.
 //
 // Numerics match the reference GPU GEMM: a and W rounded to f16 (round to nearest even), products
 // exact, sums in f32. Dual outputs (a bias longer than the rows) write the first `dual` outputs a
@@ -21,11 +21,13 @@ constexpr int BM = kGemmBM, BK = kGemmBK;
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 160 ? 5 : 6);
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;
+  // Two accumulators of BN columns; tcgen05.alloc takes a power of two.
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+  static_assert(BN % 32 == 0 && STAGE_BYTES % 1024 == 0, "tile shape");
   static constexpr uint32_t IDESC = idesc_f16(BM, BN, 0);
 };
 
@@ -373,10 +375,15 @@ int gemm_pick_bn(int m, int cols, int num_sms) {
     const long long waves = (tiles + num_sms - 1) / num_sms;
     return waves * bn;
   };
-  return cost(256) <= cost(128) ? 256 : 128;
+  // Relative throughput of a full wave by tile width (measured: wider tiles move fewer bytes per
+  // flop through TMA and shared memory).
+  const double c128 = cost(128) / 0.75, c160 = cost(160) / 0.85, c256 = double(cost(256));
+  if (c256 <= c160 && c256 <= c128) return 256;
+  return c160 <= c128 ? 160 : 128;
 }
 
 size_t gemm_smem_bytes(int bn) {
+  if (bn == 160) return 1024 + GemmCfg<160>::STAGES * GemmCfg<160>::STAGE_BYTES + sizeof(GemmBarriers);
   return bn == 256 ? 1024 + GemmCfg<256>::STAGES * GemmCfg<256>::STAGE_BYTES + sizeof(GemmBarriers)
                    : 1024 + GemmCfg<128>::STAGES * GemmCfg<128>::STAGE_BYTES + sizeof(GemmBarriers);
 }
@@ -386,6 +393,7 @@ cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmAr
   const int tiles = ((g.m + BM - 1) / BM) * ((g.cols + bn - 1) / bn);
   const int grid = tiles < num_sms ? tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
+  if (bn == 160) return launch_bn<160>(a, w, g, grid, s);
   return bn == 256 ? launch_bn<256>(a, w, g, grid, s) : launch_bn<128>(a, w, g, grid, s);
 }
 

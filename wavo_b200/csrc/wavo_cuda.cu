@@ -43,7 +43,7 @@ struct wavo_linear {
   int8_t *q8 = nullptr;      // [n][k] int8 (Q8_0 weights), the gemv operand
   float *d8 = nullptr;       // [n][k/32] scales (Q8_0)
   float *bias = nullptr;     // max(n, cols + dual) floats
-  CUtensorMap map_w128, map_w256;  // W tiles of 128 and 256 rows
+  CUtensorMap map_w128, map_w160, map_w256;  // W tiles of 128, 160 and 256 rows
 };
 
 struct wavo_graph {
@@ -383,7 +383,8 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
     std::lock_guard<std::mutex> g(ctx->mu);
     return cuda_fail(ctx, e, "linear upload");
   }
-  if (!make_map(&l->map_w128, l->w16, k, n, k, 128) || !make_map(&l->map_w256, l->w16, k, n, k, 256)) {
+  if (!make_map(&l->map_w128, l->w16, k, n, k, 128) || !make_map(&l->map_w160, l->w16, k, n, k, 160) ||
+      !make_map(&l->map_w256, l->w16, k, n, k, 256)) {
     wavo_linear_destroy(l);
     return fail(ctx, WAVO_ECUDA, "linear: tensor map");
   }
@@ -458,7 +459,8 @@ wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, c
   ga.alpha = alpha;
   ga.err = ctx->dev_err;
   const int bn = wv::gemm_pick_bn(int(m), int(l->cols), ctx->sms);
-  CK(wv::launch_gemm(map_a, bn == 256 ? l->map_w256 : l->map_w128, ga, bn, ctx->sms, ctx->stream),
+  const CUtensorMap &mw = bn == 256 ? l->map_w256 : bn == 160 ? l->map_w160 : l->map_w128;
+  CK(wv::launch_gemm(map_a, mw, ga, bn, ctx->sms, ctx->stream),
      "gemm launch");
   return WAVO_OK;
 }
