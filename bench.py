@@ -2,18 +2,20 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl wavo|reference]
 
-Workload (default, BASELINE.json configs[1] "C2"): Whisper large-v3-turbo-shaped encoder
-self-attention, all 32 layers, batch 1, T=1500 frames (one 30 s window), d_model 1280, 20 heads x 64,
-non-causal, no mask; f16 weights ~N(0, 0.02) with biases on Q/V/out and none on K; the input of
-every layer a pre-LayerNorm activation ~N(0, 1) (synthetic, seeded). A step is one window through
-the 32 layers' attention path: QKV projection (f16 out) -> flash attention -> output projection
-(residual into the f32 stream). The weights (419 MB per step) exceed the 126 MB L2, so no flush is
-needed between steps.
+Workloads (synthetic seeded inputs of their shapes and distributions):
+  c1  Parakeet/FastConformer rel-pos MHSA layer, f32 weights, T=138, d 1024, 8 x 128
+  c2  Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500, d 1280, 20 x 64 (default)
+  c3  GigaAM-v3-shaped RoPE attention, 16 layers, d 768, 16 x 48, 16 segments of U[400,750]
+  c4  Whisper-turbo decoder attention, 4 layers, batch 32, 224 greedy steps, cross K/V 32x1500
+  c5  Parakeet-0.6B long form: 24 rel-pos layers over 400 segments of U[120,300] frames, Q8_0
 
-Multi-GPU (torchrun, one rank per GPU): the windows are independent, so each rank runs its own
-window (replicas, weak scaling, no collective); value = windows x 30 s / max-over-ranks time.
-`--impl reference` times the reference's CPU path (the oracle restatement, all host threads) on a
-bounded sample of the same workload and prints the same metric.
+A step is one pass of the config's unit of work (c2: one 30 s window through 32 layers; c4: one
+whole 224-token decode of the batch; c3/c5: the whole batch of segments), captured once as a CUDA
+graph and replayed. Every layer's input is a pre-LayerNorm activation ~N(0,1) and its output is
+added into an f32 residual stream (the LayerNorm and FFN around the attention are out of scope).
+The default is c2; the multi-segment configs shard their segments over the ranks by
+longest-processing-time-first (strong scaling, no collective), c1/c2 run one unit per rank
+(replicas, weak scaling).
 """
 
 from __future__ import annotations
@@ -62,10 +64,11 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            time.sleep(0.3)
         except OSError:
             self.proc = None
         return self
@@ -104,100 +107,525 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def normal_f16(rng, shape, std):
+    return (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float16)
+
+
+def q8_0_weights(rng, rows, k):
+    """GGUF Q8_0 bytes: blocks of 32 int8 ~U[-127,127] with an f16 scale ~|N(0,0.02)|/127."""
+    nb = rows * k // 32
+    q = rng.integers(-127, 128, size=(nb, 32), dtype=np.int8)
+    d = (np.abs(rng.standard_normal(nb, dtype=np.float32)) * 0.02 / 127).astype(np.float16)
+    out = np.empty((nb, 34), np.uint8)
+    out[:, :2] = d.view(np.uint8).reshape(nb, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.tobytes()
+
+
+def bf16_weights(rng, rows, k, std):
+    w = (rng.standard_normal((rows, k), dtype=np.float32) * std)
+    return (w.view(np.uint32) >> 16).astype(np.uint16).tobytes()  # truncated to bf16
+
+
+def segment_lengths(seed, n, lo, hi):
+    return np.random.default_rng(seed).integers(lo, hi + 1, size=n).tolist()
+
+
+def my_segments(lengths, rank, world, cost):
+    """This rank's segments (LPT over the ranks, deterministic), in their original order."""
+    if world == 1:
+        return list(range(len(lengths)))
+    from wavo_b200.gpu import partition_lpt
+    assign = partition_lpt([cost(t) for t in lengths], world)
+    return [i for i, a in enumerate(assign) if a == rank]
+
+
 # ---------------------------------------------------------------------------------------------
-# C2: Whisper-turbo encoder attention
+# Workloads
 # ---------------------------------------------------------------------------------------------
 
-class WhisperEncoderAttention:
-    T, D, H, HD, LAYERS = 1500, 1280, 20, 64, 32
-    AUDIO_S = 30.0
+class Workload:
+    scaling = "weak"
+    dtype = "f16 operands, f32 accumulate"
+    bound = "tensor"
 
-    def __init__(self, gpu, seed: int, layers: int | None = None):
+    def audio_s(self) -> float:  # audio seconds this rank processes per step
+        raise NotImplementedError
+
+    def total_audio_s(self, world) -> float:  # whole job per step
+        return self.audio_s() * world
+
+
+class C2(Workload):
+    """Whisper large-v3-turbo encoder self-attention, 32 layers, batch 1, T=1500."""
+    T, D, H, LAYERS = 1500, 1280, 20, 32
+
+    def __init__(self, gpu, rank, world, seed=2000):
         import torch
         from wavo_b200 import GGML_F16
+        from wavo_b200.blocks import EncoderAttention
         self.gpu = gpu
-        self.layers = layers or self.LAYERS
         T, D = self.T, self.D
-        rng = np.random.default_rng(seed)
-        self.lin_qkv, self.lin_out = [], []
-        for _ in range(self.layers):
-            wqkv = (rng.standard_normal((3 * D, D), dtype=np.float32) * 0.02).astype(np.float16)
-            bq = (rng.standard_normal(D, dtype=np.float32) * 0.02)
-            bv = (rng.standard_normal(D, dtype=np.float32) * 0.02)
-            bqkv = np.concatenate([bq, np.zeros(D, np.float32), bv])  # no bias on k
-            wo = (rng.standard_normal((D, D), dtype=np.float32) * 0.02).astype(np.float16)
-            bo = rng.standard_normal(D, dtype=np.float32) * 0.02
-            self.lin_qkv.append(gpu.linear(GGML_F16, 3 * D, D, wqkv.tobytes(), bqkv))
-            self.lin_out.append(gpu.linear(GGML_F16, D, D, wo.tobytes(), bo))
+        rng = np.random.default_rng(seed + rank)
+        self.layers = []
+        for _ in range(self.LAYERS):
+            bqkv = np.concatenate([rng.standard_normal(D, dtype=np.float32) * 0.02,
+                                   np.zeros(D, np.float32),  # no bias on k
+                                   rng.standard_normal(D, dtype=np.float32) * 0.02])
+            self.layers.append(EncoderAttention(
+                gpu, GGML_F16, D, self.H, normal_f16(rng, (3 * D, D), 0.02).tobytes(),
+                normal_f16(rng, (D, D), 0.02).tobytes(), bqkv,
+                rng.standard_normal(D, dtype=np.float32) * 0.02))
         dev = gpu.torch_device
         self.y_host = torch.from_numpy(rng.standard_normal((T, D), dtype=np.float32)).pin_memory()
         self.x_host = torch.empty((T, D), dtype=torch.float32).pin_memory()
         self.y = self.y_host.to(dev)
         self.y16 = torch.empty((T, D), dtype=torch.float16, device=dev)
-        self.qkv = torch.empty((T, 3 * D), dtype=torch.float16, device=dev)
-        self.o = torch.empty((T, D), dtype=torch.float16, device=dev)
         self.x = torch.zeros((T, D), dtype=torch.float32, device=dev)
-        self.gpu.reserve(64 << 20)
+        self.s = self.layers[0].scratch(T)
 
-    # One window through the attention path of every layer.
     def record(self, p, timer=None):
-        T, D, H, HD = self.T, self.D, self.H, self.HD
         tick = timer or (lambda name, fn: fn())
         tick("cast", lambda: self.y16.copy_(self.y))
-        for l in range(self.layers):
-            tick("gemm_qkv", lambda: p.gemm(self.y16, self.lin_qkv[l], self.qkv, T, "bias"))
-            tick("attention", lambda: p.attention(self.qkv, None, None, self.o, T, H, HD))
-            tick("gemm_out", lambda: p.gemm(self.o, self.lin_out[l], self.x, T, "residual", 1.0))
+        for lay in self.layers:
+            tick("gemm_qkv", lambda: p.gemm(self.y16, lay.qkv, self.s["qkv"], self.T, "bias"))
+            tick("attention", lambda: p.attention(self.s["qkv"], None, None, self.s["o"], self.T,
+                                                  self.H, self.D // self.H))
+            tick("gemm_out", lambda: p.gemm(self.s["o"], lay.out, self.x, self.T, "residual", 1.0))
 
-    def launches_per_step(self) -> int:
-        return 1 + 3 * self.layers
+    def inputs(self):
+        return [(self.y, self.y_host)]
 
-    def flops(self) -> dict:
+    def outputs(self):
+        return [(self.x_host, self.x)]
+
+    def launches(self):
+        return 1 + 3 * self.LAYERS
+
+    def work(self):
         T, D = self.T, self.D
         return {"gemm_qkv": 2.0 * T * D * 3 * D, "gemm_out": 2.0 * T * D * D,
                 "attention": 4.0 * T * T * D, "cast": 0.0}
 
-    def h2d_bytes(self) -> int:
-        return self.T * self.D * 4
+    def audio_s(self):
+        return 30.0
 
-    def d2h_bytes(self) -> int:
-        return self.T * self.D * 4
-
-    def config(self) -> dict:
+    def config(self):
         return {"workload": "C2: Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500",
                 "global_batch": 1, "seq_len": self.T, "d_model": self.D, "heads": self.H,
-                "head_dim": self.HD, "layers": self.layers, "weights": "f16 ~N(0,0.02)",
+                "head_dim": self.D // self.H, "layers": self.LAYERS, "weights": "f16 ~N(0,0.02)",
                 "l2": "no flush: the step's weights (419 MB) exceed the 126 MB L2",
                 "parallelism": "replicas (independent windows), no collective"}
 
+    @staticmethod
+    def cpu_sample(layers=1, seed=1):
+        from oracle import oracle as O
+        T, D, H = 1500, 1280, 20
+        rng = np.random.default_rng(seed)
+        y = rng.standard_normal(T * D, dtype=np.float32)
+        x = np.zeros(T * D, np.float32)
+        lins = [(O.Linear(O.TY_F16, 3 * D, D, normal_f16(rng, (3 * D, D), 0.02).tobytes(),
+                          np.zeros(3 * D, np.float32)),
+                 O.Linear(O.TY_F16, D, D, normal_f16(rng, (D, D), 0.02).tobytes(),
+                          np.zeros(D, np.float32))) for _ in range(layers)]
+        t0 = time.perf_counter()
+        for lq, lo in lins:
+            qkv = lq.gemm(y, T)
+            o = O.attention(qkv, 3 * D, np.ascontiguousarray(qkv[2 * D:]), 3 * D, T, H, D)
+            lo.gemm(np.ascontiguousarray(o.ravel()), T, x, "residual", 1.0)
+        return time.perf_counter() - t0, 30.0 * layers / 32, f"{layers} of 32 layers of a C2 window"
 
-def cpu_reference_c2(layers: int, seed: int = 1):
-    """The reference CPU path (oracle restatement) on `layers` layers of the C2 window: returns
-    seconds. Inputs are the same distributions as the GPU arm."""
+
+class RelPosWorkload(Workload):
+    """Parakeet rel-pos MHSA layers over segments (C1: one layer, one segment of 138, f32
+    weights; C5: 24 layers, 400 segments of U[120,300], Q8_0 weights, sharded)."""
+    D, H = 1024, 8
+    FRAME_S = 0.08
+
+    def __init__(self, gpu, rank, world, lengths, layers, ty_name, seed):
+        import torch
+        from wavo_b200 import GGML_F32, GGML_Q8_0
+        from wavo_b200.blocks import RelPosAttention, Segments, rel_positions
+        self.gpu, self.layers_n, self.world = gpu, layers, world
+        D = self.D
+        self.all_lengths = lengths
+        cost = lambda t: 24 * (6 * t * t * D + 10 * t * D * D)  # noqa: E731
+        mine = my_segments(lengths, rank, world, cost)
+        self.lengths = [lengths[i] for i in mine]
+        rng = np.random.default_rng(seed)  # the same weights on every rank
+        ty = GGML_Q8_0 if ty_name == "q8_0" else GGML_F32
+        self.blocks = []
+        for _ in range(layers):
+            if ty == GGML_Q8_0:
+                wqkv, wpos, wout = (q8_0_weights(rng, 3 * D, D), q8_0_weights(rng, D, D),
+                                    q8_0_weights(rng, D, D))
+            else:
+                wqkv = (rng.standard_normal((3 * D, D), dtype=np.float32) * 0.02).tobytes()
+                wpos = (rng.standard_normal((D, D), dtype=np.float32) * 0.02).tobytes()
+                wout = (rng.standard_normal((D, D), dtype=np.float32) * 0.02).tobytes()
+            u = rng.standard_normal(D, dtype=np.float32) * 0.02
+            v = rng.standard_normal(D, dtype=np.float32) * 0.02
+            self.blocks.append(RelPosAttention(gpu, ty, D, self.H, wqkv, wpos, wout, u, v))
+        dev = gpu.torch_device
+        self.segs = Segments(self.lengths, dev)
+        rows = self.segs.rows
+        self.t_pos = max(lengths)
+        self.table = gpu.upload(rel_positions(D, self.t_pos + 15, 2 * self.t_pos + 15))
+        drng = np.random.default_rng(seed + 1 + rank)
+        self.y_host = torch.from_numpy(drng.standard_normal((rows, D), dtype=np.float32)).pin_memory()
+        self.x_host = torch.empty((rows, D), dtype=torch.float32).pin_memory()
+        self.y = self.y_host.to(dev)
+        self.y16 = torch.empty((rows, D), dtype=torch.float16, device=dev)
+        self.x = torch.zeros((rows, D), dtype=torch.float32, device=dev)
+        self.s = self.blocks[0].scratch(rows, self.t_pos)
+
+    def record(self, p, timer=None):
+        tick = timer or (lambda name, fn: fn())
+        rows, D = self.segs.rows, self.D
+        tick("cast", lambda: self.y16.copy_(self.y))
+        from wavo_b200.gpu import pos_rows
+        for b in self.blocks:
+            tick("gemm_qkv", lambda: p.gemm(self.y16, b.qkv, self.s["qkv"], rows, "bias"))
+            tick("gemm_pos", lambda: p.gemm(self.table, b.pos, self.s["p"], pos_rows(self.t_pos),
+                                            "bias"))
+            tick("attention", lambda: p.attention_varlen(
+                self.s["qkv"], None, self.s["p"], self.s["o"], rows, self.segs.start_t,
+                self.segs.len_t, self.segs.max_len, self.H, D // self.H, self.t_pos))
+            tick("gemm_out", lambda: p.gemm(self.s["o"], b.out, self.x, rows, "residual", 1.0))
+
+    def inputs(self):
+        return [(self.y, self.y_host)]
+
+    def outputs(self):
+        return [(self.x_host, self.x)]
+
+    def launches(self):
+        return 1 + 4 * self.layers_n
+
+    def work(self):
+        D = self.D
+        rows = self.segs.rows
+        att = sum(6.0 * t * t * D for t in self.lengths)  # AC + BD + PV (the reference's count)
+        return {"gemm_qkv": 2.0 * rows * D * 4 * D, "gemm_out": 2.0 * rows * D * D,
+                "gemm_pos": 2.0 * (2 * self.t_pos + 15) * D * D, "attention": att, "cast": 0.0}
+
+    def audio_s(self):
+        return sum(self.lengths) * self.FRAME_S
+
+    def total_audio_s(self, world):
+        return sum(self.all_lengths) * self.FRAME_S
+
+
+class C1(RelPosWorkload):
+    scaling = "weak"
+
+    def __init__(self, gpu, rank, world, seed=1000):
+        super().__init__(gpu, rank, 1, [138], 1, "f32", seed)
+
+    def total_audio_s(self, world):
+        return self.audio_s() * world
+
+    def config(self):
+        return {"workload": "C1: Parakeet rel-pos MHSA layer, f32 weights, batch 1, T=138",
+                "global_batch": 1, "seq_len": 138, "d_model": 1024, "heads": 8, "head_dim": 128,
+                "layers": 1, "weights": "f32 ~N(0,0.02) (rounded to f16 in the GEMM, as the "
+                "reference GPU GEMM)", "l2": "small working set: L2-resident (latency-bound)",
+                "parallelism": "replicas, no collective"}
+
+    @staticmethod
+    def cpu_sample(layers=1, seed=1):
+        return RelPosWorkload.cpu(seed, [138], layers, "f32", 1)
+
+
+def _relpos_cpu(seed, lengths, layers, ty_name, reps):
     from oracle import oracle as O
-    T, D, H = 1500, 1280, 20
+    D, H = 1024, 8
     rng = np.random.default_rng(seed)
-    y = rng.standard_normal(T * D, dtype=np.float32)
-    x = np.zeros(T * D, np.float32)
     lins = []
     for _ in range(layers):
-        wqkv = (rng.standard_normal((3 * D, D), dtype=np.float32) * 0.02).astype(np.float16)
-        bqkv = np.concatenate([rng.standard_normal(D, dtype=np.float32) * 0.02,
-                               np.zeros(D, np.float32),
-                               rng.standard_normal(D, dtype=np.float32) * 0.02])
-        wo = (rng.standard_normal((D, D), dtype=np.float32) * 0.02).astype(np.float16)
-        bo = rng.standard_normal(D, dtype=np.float32) * 0.02
-        lins.append((O.Linear(O.TY_F16, 3 * D, D, wqkv.tobytes(), bqkv),
-                     O.Linear(O.TY_F16, D, D, wo.tobytes(), bo)))
+        if ty_name == "q8_0":
+            ws = [(O.TY_Q8_0, q8_0_weights(rng, r, D)) for r in (3 * D, D, D)]
+        else:
+            ws = [(O.TY_F32, (rng.standard_normal((r, D), dtype=np.float32) * 0.02).tobytes())
+                  for r in (3 * D, D, D)]
+        lins.append([O.Linear(ty, r, D, data) for (ty, data), r in zip(ws, (3 * D, D, D))] +
+                    [rng.standard_normal(D, dtype=np.float32) * 0.02,
+                     rng.standard_normal(D, dtype=np.float32) * 0.02])
+    ys = [np.random.default_rng(seed + 7 + i).standard_normal(t * D, dtype=np.float32)
+          for i, t in enumerate(lengths)]
     t0 = time.perf_counter()
-    for lq, lo in lins:
-        qkv = lq.gemm(y, T)
-        o = O.attention(qkv, 3 * D, np.ascontiguousarray(qkv[2 * D:]), 3 * D, T, H, D)
-        lo.gemm(np.ascontiguousarray(o.ravel()), T, x, "residual", 1.0)
+    for _ in range(reps):
+        for y, t in zip(ys, lengths):
+            x = np.zeros(t * D, np.float32)
+            tab = O.rel_positions(D, t + 15, O.pos_rows(t))
+            for lq, lp, lo, u, v in lins:
+                qkv = lq.gemm(y, t)
+                pos = lp.gemm(np.ascontiguousarray(tab.ravel()), O.pos_rows(t))
+                o = O.relative_attention(qkv, pos, u, v, t, H, D)
+                lo.gemm(np.ascontiguousarray(o.ravel()), t, x, "residual", 1.0)
     return time.perf_counter() - t0
 
 
-WORKLOADS = {"c2": WhisperEncoderAttention}
+RelPosWorkload.cpu = staticmethod(
+    lambda seed, lengths, layers, ty, reps: (
+        _relpos_cpu(seed, lengths, layers, ty, reps),
+        reps * sum(lengths) * 0.08 * layers / (24 if ty == "q8_0" else 1),
+        f"{reps} x {len(lengths)} segment(s) {lengths[:4]}... through {layers} layer(s)"))
+
+
+class C5(RelPosWorkload):
+    scaling = "strong"
+
+    def __init__(self, gpu, rank, world, seed=5000):
+        super().__init__(gpu, rank, world, segment_lengths(seed, 400, 120, 300), 24, "q8_0", seed)
+
+    def config(self):
+        return {"workload": "C5: Parakeet-0.6B long form, 24 rel-pos layers, 400 segments of "
+                "U[120,300] frames, Q8_0 weights", "global_batch": 400, "seq_len": "120-300",
+                "total_frames": int(sum(self.all_lengths)), "d_model": 1024, "heads": 8,
+                "head_dim": 128, "layers": 24, "weights": "GGUF Q8_0 (dequantized to f16 at load)",
+                "l2": "inputs larger than L2", "parallelism": f"segments sharded LPT over "
+                f"{self.world} GPU(s), no collective"}
+
+    @staticmethod
+    def cpu_sample(layers=1, seed=5000):
+        lens = segment_lengths(seed, 400, 120, 300)[:2]
+        return RelPosWorkload.cpu(seed, lens, layers, "q8_0", 1)
+
+
+class C3(Workload):
+    """GigaAM-v3-shaped attention with RoPE: 16 layers, d 768, 16 x 48, 16 segments."""
+    D, H, LAYERS = 768, 16, 16
+    FRAME_S = 0.04
+    scaling = "strong"
+
+    def __init__(self, gpu, rank, world, seed=3000):
+        import torch
+        from wavo_b200 import GGML_BF16
+        from wavo_b200.blocks import RotaryAttention, Segments
+        self.gpu, self.world = gpu, world
+        D = self.D
+        self.all_lengths = segment_lengths(seed, 16, 400, 750)
+        cost = lambda t: 16 * (4 * t * t * D + 8 * t * D * D)  # noqa: E731
+        self.lengths = [self.all_lengths[i] for i in my_segments(self.all_lengths, rank, world,
+                                                                 cost)]
+        rng = np.random.default_rng(seed)
+        self.blocks = [RotaryAttention(gpu, GGML_BF16, D, self.H, bf16_weights(rng, 3 * D, D, 0.02),
+                                       bf16_weights(rng, D, D, 0.02), theta=10000.0,
+                                       max_frames=750) for _ in range(self.LAYERS)]
+        dev = gpu.torch_device
+        self.segs = Segments(self.lengths, dev)
+        rows = self.segs.rows
+        drng = np.random.default_rng(seed + 1 + rank)
+        self.y_host = torch.from_numpy(drng.standard_normal((rows, D), dtype=np.float32)).pin_memory()
+        self.x_host = torch.empty((rows, D), dtype=torch.float32).pin_memory()
+        self.y = self.y_host.to(dev)
+        self.y16 = torch.empty((rows, D), dtype=torch.float16, device=dev)
+        self.x = torch.zeros((rows, D), dtype=torch.float32, device=dev)
+        self.s = self.blocks[0].scratch(rows)
+
+    def record(self, p, timer=None):
+        tick = timer or (lambda name, fn: fn())
+        rows, D, H = self.segs.rows, self.D, self.H
+        tick("cast", lambda: self.y16.copy_(self.y))
+        for b in self.blocks:
+            tick("gemm_qkv", lambda: p.gemm(self.y16, b.qkv, self.s["qkv"], rows, "bias"))
+            tick("rope", lambda: p.rope_rows(b.table, self.s["qkv"], rows, self.segs.positions,
+                                             (H, D // H, D // H), True))
+            tick("attention", lambda: p.attention_varlen(
+                self.s["qkv"], None, None, self.s["o"], rows, self.segs.start_t, self.segs.len_t,
+                self.segs.max_len, H, D // H))
+            tick("gemm_out", lambda: p.gemm(self.s["o"], b.out, self.x, rows, "residual", 1.0))
+
+    def inputs(self):
+        return [(self.y, self.y_host)]
+
+    def outputs(self):
+        return [(self.x_host, self.x)]
+
+    def launches(self):
+        return 1 + 4 * self.LAYERS
+
+    def work(self):
+        D, rows = self.D, self.segs.rows
+        return {"gemm_qkv": 2.0 * rows * D * 3 * D, "gemm_out": 2.0 * rows * D * D,
+                "attention": sum(4.0 * t * t * D for t in self.lengths), "rope": 0.0, "cast": 0.0}
+
+    def audio_s(self):
+        return sum(self.lengths) * self.FRAME_S
+
+    def total_audio_s(self, world):
+        return sum(self.all_lengths) * self.FRAME_S
+
+    def config(self):
+        return {"workload": "C3: GigaAM-v3-shaped RoPE attention, 16 layers, 16 segments of "
+                "U[400,750] frames (key-padding mask as per-segment lengths)", "global_batch": 16,
+                "seq_len": "400-750", "total_frames": int(sum(self.all_lengths)), "d_model": 768,
+                "heads": 16, "head_dim": 48, "layers": 16, "rope": "base 10000 on Q/K, NEOX",
+                "weights": "bf16 ~N(0,0.02) (converted to f16 at load)",
+                "parallelism": f"segments sharded LPT over {self.world} GPU(s), no collective"}
+
+    @staticmethod
+    def cpu_sample(layers=1, seed=3000):
+        from oracle import oracle as O
+        D, H = 768, 16
+        t = segment_lengths(seed, 16, 400, 750)[0]
+        rng = np.random.default_rng(seed)
+        lq = O.Linear(O.TY_F32, 3 * D, D, (rng.standard_normal((3 * D, D), dtype=np.float32) *
+                                          0.02).tobytes())
+        lo = O.Linear(O.TY_F32, D, D, (rng.standard_normal((D, D), dtype=np.float32) * 0.02)
+                      .tobytes())
+        y = rng.standard_normal(t * D, dtype=np.float32)
+        tab = O.rope_table(t, D // H, 10000.0)
+        x = np.zeros(t * D, np.float32)
+        t0 = time.perf_counter()
+        for _ in range(layers):
+            qkv = lq.gemm(y, t)
+            O.rope(qkv, tab, t, H, D // H, D // H, True)
+            o = O.attention(qkv, 3 * D, np.ascontiguousarray(qkv[2 * D:]), 3 * D, t, H, D)
+            lo.gemm(np.ascontiguousarray(o.ravel()), t, x, "residual", 1.0)
+        return (time.perf_counter() - t0, t * 0.04 * layers / 16,
+                f"1 segment of {t} frames through {layers} of 16 layers")
+
+
+class C4(Workload):
+    """Whisper-turbo decoder attention: 4 layers, batch 32, 224 greedy steps over F16 caches."""
+    D, H, LAYERS, FRAMES, CONTEXT, STEPS, BATCH = 1280, 20, 4, 1500, 448, 224, 32
+    scaling = "strong"
+    bound = "hbm"
+
+    def __init__(self, gpu, rank, world, seed=4000):
+        import torch
+        from wavo_b200 import GGML_F16
+        from wavo_b200.blocks import DecoderAttention
+        self.gpu, self.world = gpu, world
+        D = self.D
+        per = [len(range(r, self.BATCH, world)) for r in range(world)]
+        self.batch = per[rank]
+        rng = np.random.default_rng(seed)
+        self.layers = []
+        for _ in range(self.LAYERS):
+            w = {"qkv": normal_f16(rng, (3 * D, D), 0.02).tobytes(),
+                 "self_out": normal_f16(rng, (D, D), 0.02).tobytes(),
+                 "cross_q": normal_f16(rng, (D, D), 0.02).tobytes(),
+                 "cross_kv": normal_f16(rng, (2 * D, D), 0.02).tobytes(),
+                 "cross_out": normal_f16(rng, (D, D), 0.02).tobytes()}
+            b = {"qkv": np.concatenate([rng.standard_normal(D, dtype=np.float32) * 0.02,
+                                        np.zeros(D, np.float32),
+                                        rng.standard_normal(D, dtype=np.float32) * 0.02]),
+                 "cross_kv": np.concatenate([np.zeros(D, np.float32),
+                                             rng.standard_normal(D, dtype=np.float32) * 0.02])}
+            self.layers.append(DecoderAttention(gpu, GGML_F16, D, self.H, self.CONTEXT,
+                                                self.FRAMES, self.batch, w, b))
+        dev = gpu.torch_device
+        drng = np.random.default_rng(seed + 1 + rank)
+        # The one-time cross K/V of the batch: encoder outputs ~N(0,1), projected and packed.
+        enc = torch.from_numpy(drng.standard_normal((self.batch, self.FRAMES, D),
+                                                    dtype=np.float32)).to(dev)
+        p = gpu.pass_()
+        t0 = time.perf_counter()
+        for lay in self.layers:
+            lay.record_cross(p, enc)
+        gpu.sync()
+        self.cross_setup_s = time.perf_counter() - t0
+        del enc
+        self.y_host = torch.from_numpy(drng.standard_normal((2, self.batch, D),
+                                                            dtype=np.float32)).pin_memory()
+        self.x_host = torch.empty((self.batch, D), dtype=torch.float32).pin_memory()
+        self.y = self.y_host.to(dev)
+        self.x = torch.zeros((self.batch, D), dtype=torch.float32, device=dev)
+
+    def record(self, p, timer=None):
+        tick = timer or (lambda name, fn: fn())
+        for pos in range(self.STEPS):
+            for lay in self.layers:
+                if timer is None:
+                    lay.record_step(p, self.y[0], self.y[1], self.x, pos)
+                else:
+                    self._timed_step(p, lay, pos, tick)
+
+    def _timed_step(self, p, lay, pos, tick):
+        d, B = self.D, self.batch
+        tick("gemv_qkv", lambda: p.gemv_rows(self.y[0], lay.qkv, lay.qkv_buf, B, "bias",
+                                             ldc=3 * d))
+        tick("pack", lambda: p.pack_batch(lay.qkv_buf, (d, 0), 3 * d, lay.own, d * lay.context, 1,
+                                          d, (lay.context, pos), B))
+        tick("attend_self", lambda: p.attend_batch(lay.qkv_buf, 3 * d, lay.own, d * lay.context,
+                                                   lay.part, lay.att, d, pos + 1, lay.context,
+                                                   lay.heads, lay.hd, B))
+        tick("gemv_self_out", lambda: p.gemv_rows(lay.att, lay.self_out, self.x, B, "residual",
+                                                  1.0, ldc=d))
+        tick("gemv_cross_q", lambda: p.gemv_rows(self.y[1], lay.cross_q, lay.q_buf, B, "bias",
+                                                 ldc=d))
+        tick("attend_cross", lambda: p.attend_batch(lay.q_buf, d, lay.cross, d * lay.frames,
+                                                    lay.part, lay.att, d, lay.frames, lay.frames,
+                                                    lay.heads, lay.hd, B))
+        tick("gemv_cross_out", lambda: p.gemv_rows(lay.att, lay.cross_out, self.x, B, "residual",
+                                                   1.0, ldc=d))
+
+    def inputs(self):
+        return [(self.y, self.y_host)]
+
+    def outputs(self):
+        return [(self.x_host, self.x)]
+
+    def launches(self):
+        # per layer and step: 5 projections, pack, 2 attends (the cross one with its combine)
+        return self.STEPS * self.LAYERS * (5 + 1 + 1 + 2)
+
+    def work(self):
+        d, B, T = self.D, self.batch, self.FRAMES
+        # HBM bytes per launch: the cross cache of the batch (K and V, f16).
+        return {"attend_cross": 2.0 * B * T * d * 2, "attend_self": 0.0, "gemv_qkv": 0.0,
+                "pack": 0.0, "gemv_self_out": 0.0, "gemv_cross_q": 0.0, "gemv_cross_out": 0.0}
+
+    def audio_s(self):
+        return self.batch * 30.0
+
+    def total_audio_s(self, world):
+        return self.BATCH * 30.0
+
+    def config(self):
+        return {"workload": "C4: Whisper-turbo decoder attention, 4 layers, batch 32, 224 greedy "
+                "steps, self + cross attention over F16 caches", "global_batch": self.BATCH,
+                "seq_len": f"{self.CONTEXT} context, {self.FRAMES} frames", "d_model": self.D,
+                "heads": self.H, "head_dim": self.D // self.H, "layers": self.LAYERS,
+                "steps": self.STEPS, "weights": "f16 ~N(0,0.02)",
+                "cross_kv_setup_s": round(self.cross_setup_s, 4),
+                "l2": "cross K/V caches (983 MB per step) exceed L2",
+                "parallelism": f"segments split over {self.world} GPU(s), no collective"}
+
+    @staticmethod
+    def cpu_sample(layers=1, seed=4000):
+        from oracle import oracle as O
+        d, H, T = 1280, 20, 1500
+        rng = np.random.default_rng(seed)
+        kv = rng.standard_normal(T * 2 * d, dtype=np.float32)
+        cache = np.zeros(T * 2 * d, np.float32)
+        O.pack_cache(kv, T, d, d // H, cache, T, 0)
+        q = rng.standard_normal(d, dtype=np.float32)
+        lq = O.Linear(O.TY_F16, d, d, normal_f16(rng, (d, d), 0.02).tobytes())
+        steps = 32
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            qq = lq.gemv(q)
+            O.attend(qq, cache, T, T, H, d // H)
+        dt = time.perf_counter() - t0
+        # one cross attend + one projection per (segment, layer, step); scale to the unit
+        return dt, 30.0 * steps / (224 * 4), f"{steps} cross-attention steps of one segment"
+
+
+WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5}
+WORKLOAD_NAMES = {
+    "c1": "C1: Parakeet rel-pos MHSA layer, f32 weights, batch 1, T=138",
+    "c2": "C2: Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500",
+    "c3": "C3: GigaAM-v3-shaped RoPE attention, 16 layers, 16 segments of U[400,750] frames "
+          "(key-padding mask as per-segment lengths)",
+    "c4": "C4: Whisper-turbo decoder attention, 4 layers, batch 32, 224 greedy steps, self + "
+          "cross attention over F16 caches",
+    "c5": "C5: Parakeet-0.6B long form, 24 rel-pos layers, 400 segments of U[120,300] frames, "
+          "Q8_0 weights",
+}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -208,23 +636,24 @@ def run_reference(args):
         return
     from oracle import oracle as O
     O.set_threads(os.cpu_count() or 1)
-    layers = 1  # one layer of the window per step: a bounded sample of the 32-layer window
+    O.set_vnni(-1)
+    W = WORKLOADS[args.config]
     for _ in range(args.warmup):
-        cpu_reference_c2(layers)
-    times = [cpu_reference_c2(layers) for _ in range(args.steps)]
+        W.cpu_sample()
+    times, audio, sample = [], 0.0, ""
+    for _ in range(args.steps):
+        dt, audio, sample = W.cpu_sample()
+        times.append(dt)
     t = float(np.mean(times))
-    value = 30.0 * layers / 32 / t
-    cores = O.threads()
+    value = audio / t
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "C2: Whisper large-v3-turbo encoder self-attention, 32 "
-                       "layers, T=1500", "global_batch": 1, "seq_len": 1500, "d_model": 1280,
-                       "heads": 20, "head_dim": 64, "layers": 32},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{layers} of 32 layers of one C2 window per step "
-                                       "(CPU oracle restating src/cpu/ops.rs + src/cpu/gemm.rs)"},
+            "config": {"workload": WORKLOAD_NAMES[args.config]},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
+                             "sample": sample + " per step (CPU oracle restating the "
+                             "reference's src/cpu attention path)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -233,15 +662,18 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="wavo", choices=["wavo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-layers", type=int, default=2)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.steps is None:
+        args.steps = {"c1": 2000, "c2": 200, "c3": 100, "c4": 10, "c5": 30}[args.config]
     if args.impl == "reference":
+        if args.steps > 20:
+            args.steps = 5
         return run_reference(args)
 
     import torch
@@ -253,22 +685,19 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     from wavo_b200.gpu import Gpu
 
     gpu = Gpu(local)
-    wl = WORKLOADS[args.config](gpu, seed=1000 * 2 + rank)
+    gpu.reserve(256 << 20)
+    wl = WORKLOADS[args.config](gpu, rank, world)
     stream = torch.cuda.current_stream(local)
 
-    # Graph of one step (the whole window); capture needs the scratch reserved (done).
-    def record(p):
-        wl.record(p)
-
-    for _ in range(2):  # eager warm-up also configures the kernels before capture
+    for _ in range(2):  # eager warm-up (also configures the kernels before the capture)
         wl.record(gpu.pass_())
     gpu.sync()
-    graph = gpu.capture(record)
+    graph = gpu.capture(wl.record)
 
     def barrier():
         if world > 1:
@@ -291,46 +720,49 @@ def main():
     ms = e0.elapsed_time(e1) / args.steps
     barrier()
 
-    # ---- end to end through the public API: H2D input, step, D2H result ----
-    for _ in range(args.warmup):
-        wl.y.copy_(wl.y_host, non_blocking=True)
+    # ---- end to end: H2D of the step's inputs (pinned), the step, D2H of its result ----
+    def e2e_step():
+        for dev_t, host_t in wl.inputs():
+            dev_t.copy_(host_t, non_blocking=True)
         graph.launch()
-        wl.x_host.copy_(wl.x, non_blocking=True)
+        for host_t, dev_t in wl.outputs():
+            host_t.copy_(dev_t, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
     torch.cuda.synchronize()
     barrier()
-    torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(args.steps):
-        wl.y.copy_(wl.y_host, non_blocking=True)
-        graph.launch()
-        wl.x_host.copy_(wl.x, non_blocking=True)
+        e2e_step()
     f1.record(stream)
     torch.cuda.synchronize()
     gpu.sync()
     ms_e2e = f0.elapsed_time(f1) / args.steps
+    h2d = sum(t.numel() * t.element_size() for _, t in wl.inputs())
+    d2h = sum(t.numel() * t.element_size() for t, _ in wl.outputs())
 
     # ---- per-kernel durations (eager, CUDA events on the launch stream) for the roofline ----
-    times: dict[str, list[float]] = {}
+    events: dict[str, list] = {}
 
     def timer(name, fn):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         fn()
         b.record(stream)
-        times.setdefault(name, []).append((a, b))
+        events.setdefault(name, []).append((a, b))
 
     for _ in range(2):
-        times.clear()
+        events.clear()
         wl.record(gpu.pass_(), timer)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
     gpu.sync()
-    per = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in times.items()}
-    flops = wl.flops()
-    totals = {k: per[k] * len(times[k]) for k in per}
-    top = max(totals, key=totals.get)
+    per = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in events.items()}
+    totals = {k: per[k] * len(events[k]) for k in per}
+    work = wl.work()
+    top = max((k for k in totals if work.get(k, 0) > 0), key=totals.get)
 
-    # max over ranks
     vals = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
@@ -338,30 +770,34 @@ def main():
 
     if rank == 0:
         peaks = load_peaks()
-        achieved = flops[top] / (per[top] * 1e-3) / 1e12
-        peak = peaks["tensor_sustained"]
+        if wl.bound == "hbm":
+            achieved = work[top] / (per[top] * 1e-3) / 1e9
+            peak, unit, src = peaks["hbm"], "GB/s", "HBM copy"
+        else:
+            achieved = work[top] / (per[top] * 1e-3) / 1e12
+            peak, unit, src = peaks["tensor_sustained"], "TFLOP/s", "bf16 sustained"
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             from oracle import oracle as O
             O.set_threads(os.cpu_count() or 1)
-            cpu_reference_c2(1)  # warm
-            t = cpu_reference_c2(args.cpu_layers)
-            cpu = {"value": 30.0 * args.cpu_layers / 32 / t, "unit": UNIT, "cores": O.threads(),
-                   "kind": "port",
-                   "sample": f"{args.cpu_layers} of 32 layers of one C2 window (CPU oracle "
-                             "restating src/cpu/ops.rs attention + src/cpu/gemm.rs f16 GEMM)"}
-        value = world * wl.AUDIO_S / (ms * 1e-3)
+            O.set_vnni(-1)
+            type(wl).cpu_sample()  # warm
+            dt, audio, sample = type(wl).cpu_sample()
+            cpu = {"value": audio / dt, "unit": UNIT, "cores": O.threads(), "kind": "port",
+                   "sample": sample + " (CPU oracle restating the reference's src/cpu path)"}
+        total_audio = wl.total_audio_s(world)
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+            "metric": METRIC, "value": total_audio / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
+            "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE.json shapes/distributions)",
             "config": wl.config(),
-            "e2e": {"value": world * wl.AUDIO_S / (ms_e2e * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": wl.h2d_bytes(), "d2h_bytes_per_step": wl.d2h_bytes()},
-            "gpu_launches": wl.launches_per_step() * args.steps,
-            "roofline": {"bound": "tensor", "kernel": top, "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
-                         "peak_source": f"{peaks['source']} bf16 sustained"},
+            "e2e": {"value": total_audio / (ms_e2e * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": wl.launches() * args.steps,
+            "roofline": {"bound": wl.bound, "kernel": top, "achieved": achieved, "peak": peak,
+                         "unit": unit, "frac": achieved / peak, "traffic": None,
+                         "peak_source": f"{peaks['source']} {src}"},
             "kernels_ms": per,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

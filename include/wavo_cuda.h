@@ -42,8 +42,14 @@ typedef enum wavo_status {
 
 typedef enum wavo_dtype { WAVO_F32 = 0, WAVO_F16 = 1 } wavo_dtype;
 
-/* GGUF tensor types the reference reads (src/gguf.rs:14-38). */
-typedef enum wavo_ggml_type { WAVO_GGML_F32 = 0, WAVO_GGML_F16 = 1, WAVO_GGML_Q8_0 = 8 } wavo_ggml_type;
+/* GGUF tensor types: the three the reference reads (src/gguf.rs:14-38), and BF16 (GGUF id 30),
+ * which the reference does not read; BF16 weights are converted to the GEMM's f16 at load. */
+typedef enum wavo_ggml_type {
+  WAVO_GGML_F32 = 0,
+  WAVO_GGML_F16 = 1,
+  WAVO_GGML_Q8_0 = 8,
+  WAVO_GGML_BF16 = 30
+} wavo_ggml_type;
 
 /* The reference's `Epilogue` (src/gpu/mod.rs:431-456), in its kernel order. */
 typedef enum wavo_epilogue {
@@ -163,6 +169,13 @@ wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, u
                       uint32_t rows, uint32_t pos, uint32_t heads, uint32_t hd, uint32_t rot,
                       int neox);
 
+/* wavo_rope with the table row of each row given (device int32 `positions`, e.g. the position of
+ * each row inside its own segment when segments are packed one after another); NULL means
+ * pos + row, as wavo_rope. */
+wavo_status wavo_rope_rows(wavo_ctx *ctx, const float *table, void *qkv, int dtype,
+                           uint32_t stride, uint32_t rows, uint32_t pos, const int32_t *positions,
+                           uint32_t heads, uint32_t hd, uint32_t rot, int neox);
+
 /* ---- decoder attention: replaces Pass::pack (src/gpu/mod.rs:1507-1522), Pass::attend
  * (1485-1505) and attend_len (1053-1059) -------------------------------------------------- */
 
@@ -171,6 +184,12 @@ wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, u
  * (pair i of position j at word i·cols + j), then V by position (word d/2·cols + j·d/2 + i). */
 wavo_status wavo_pack(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride, void *cache,
                       uint32_t rows, uint32_t d, uint32_t cols, uint32_t col);
+
+/* wavo_pack for `batch` segments in one launch: segment b reads x + b·x_batch floats and writes
+ * the cache at cache + b·cache_batch 32-bit words (the decoder of a batch of segments). */
+wavo_status wavo_pack_batch(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride,
+                            uint64_t x_batch, void *cache, uint64_t cache_batch, uint32_t rows,
+                            uint32_t d, uint32_t cols, uint32_t col, uint32_t batch);
 
 /* attend_len: floats of wavo_attend's `part` scratch for up to n keys (per segment). */
 size_t wavo_attend_len(uint32_t n, uint32_t heads, uint32_t hd);

@@ -7,6 +7,6 @@ GPU backend op interface (src/gpu/mod.rs `Gpu` / `Pass`).
 segments over the GPUs of one node.
 """
 
-from ._lib import EPILOGUES, GGML_F16, GGML_F32, GGML_Q8_0, WavoError  # noqa: F401
+from ._lib import EPILOGUES, GGML_BF16, GGML_F16, GGML_F32, GGML_Q8_0, WavoError  # noqa: F401
 
-__all__ = ["EPILOGUES", "GGML_F16", "GGML_F32", "GGML_Q8_0", "WavoError"]
+__all__ = ["EPILOGUES", "GGML_BF16", "GGML_F16", "GGML_F32", "GGML_Q8_0", "WavoError"]

@@ -15,7 +15,7 @@ OK, EINVAL, ENOMEM, ECUDA, ETIMEDOUT, EUNSUPPORTED, EDEVICE = range(7)
 STATUS = {0: "OK", 1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEDOUT", 5: "EUNSUPPORTED",
           6: "EDEVICE"}
 F32, F16 = 0, 1
-GGML_F32, GGML_F16, GGML_Q8_0 = 0, 1, 8
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
 EPILOGUES = {"bias": 0, "silu": 1, "relu": 2, "residual": 3, "gelu": 4, "gelu_residual": 5,
              "tanh": 6}
 
@@ -51,7 +51,10 @@ SIGNATURES = {
                                _u32, _i32, _i32], _st),
     "wavo_pos_rows": ([_u32], _u32),
     "wavo_rope": ([_vp, _vp, _vp, _i32, _u32, _u32, _u32, _u32, _u32, _u32, _i32], _st),
+    "wavo_rope_rows": ([_vp, _vp, _vp, _i32, _u32, _u32, _u32, _vp, _u32, _u32, _u32, _i32], _st),
     "wavo_pack": ([_vp, _vp, _u32, _u32, _vp, _u32, _u32, _u32, _u32], _st),
+    "wavo_pack_batch": ([_vp, _vp, _u32, _u32, _u64, _vp, _u64, _u32, _u32, _u32, _u32, _u32],
+                        _st),
     "wavo_attend_len": ([_u32, _u32, _u32], _sz),
     "wavo_attend": ([_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32], _st),
     "wavo_attend_batch": ([_vp, _vp, _u64, _vp, _u64, _vp, _vp, _u64, _u32, _u32, _u32, _u32,

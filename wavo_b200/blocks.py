@@ -1,0 +1,208 @@
+"""The attention part of the reference's model blocks, over the `Pass` interface: what
+src/conformer.rs (`Block::record`, 238-252) and src/transformer.rs (`Encoder::record` 122-131,
+`Decoder::record_cross` 243-248, `Decoder::record_step` 254-290) record for attention, with the
+layer inputs and the residual stream as the caller's buffers.
+
+Every block runs over independent segments packed one after another (rows `seg_start[z] ..
++ seg_len[z]`); one segment of `rows` rows is the reference's case. Projections write f16
+operands that the attention kernel loads directly; the attention writes f16 rows the output
+projection reads; the output projection adds into the caller's f32 residual stream
+(`Epilogue::Residual(1.0)`, as the reference).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from ._lib import GGML_BF16, GGML_F16, GGML_F32, GGML_Q8_0  # noqa: F401
+from .gpu import Gpu, Linear, Pass, pos_rows
+
+
+def rel_positions(d: int, first: int, rows: int) -> np.ndarray:
+    """src/conformer.rs:141-153: the sinusoidal table of relative positions first, first - 1, …
+    for `rows` rows of d, in f32: [2k] = sin(pos·d_k), [2k + 1] = cos(pos·d_k)."""
+    c = np.float32(-math.log(10000.0)) / np.float32(d)
+    div = np.exp(np.arange(0, d, 2, dtype=np.float32) * c).astype(np.float32)
+    pos = (first - np.arange(rows)).astype(np.float32)[:, None]
+    ang = (pos * div[None, :]).astype(np.float32)
+    out = np.empty((rows, d), np.float32)
+    out[:, 0::2] = np.sin(ang)
+    out[:, 1::2] = np.cos(ang)
+    return out
+
+
+def rope_table(frames: int, hd: int, theta: float) -> np.ndarray:
+    """src/gigaam/mod.rs:88-96: per position hd/2 cosines then hd/2 sines, angles in f64."""
+    t = np.arange(frames, dtype=np.float64)[:, None]
+    inv = theta ** (-2.0 * np.arange(hd // 2, dtype=np.float64) / hd)
+    ang = t * inv[None, :]
+    return np.concatenate([np.cos(ang), np.sin(ang)], axis=1).astype(np.float32)
+
+
+class Segments:
+    """Independent segments packed one after another: device int32 starts and lengths."""
+
+    def __init__(self, lengths, device):
+        self.lengths = [int(n) for n in lengths]
+        starts = np.concatenate([[0], np.cumsum(self.lengths)[:-1]]).astype(np.int32)
+        self.starts = [int(s) for s in starts]
+        self.rows = int(sum(self.lengths))
+        self.max_len = max(self.lengths) if self.lengths else 0
+        self.start_t = torch.tensor(starts, dtype=torch.int32, device=device)
+        self.len_t = torch.tensor(self.lengths, dtype=torch.int32, device=device)
+        # Each row's position inside its segment (the RoPE table row).
+        pos = np.concatenate([np.arange(n, dtype=np.int32) for n in self.lengths]) \
+            if self.lengths else np.zeros(0, np.int32)
+        self.positions = torch.tensor(pos, dtype=torch.int32, device=device)
+
+
+class RelPosAttention:
+    """Parakeet's relative-position MHSA (src/conformer.rs:174-200, 238-252): one projection
+    [q | k | v] whose bias [u | 0 | 0 | v] writes q a second time (the dual outputs), so that it
+    produces [q+u | k | v | q+v]; linear_pos over the sinusoidal table; the attention with the
+    Transformer-XL terms; the output projection added into the residual stream.
+
+    The projected positions depend only on the position and the layer, so one table of
+    pos_rows(t_pos) rows serves every segment of length <= t_pos (the reference projects a table
+    of pos_rows(t) rows per segment, src/cpu/conformer.rs:181)."""
+
+    def __init__(self, gpu: Gpu, ty: int, d: int, heads: int, wqkv: bytes, wpos: bytes,
+                 wout: bytes, u: np.ndarray, v: np.ndarray, bias_qkv=None, bias_out=None):
+        self.gpu, self.d, self.heads, self.hd = gpu, d, heads, d // heads
+        bq = np.zeros(3 * d, np.float32) if bias_qkv is None else np.asarray(bias_qkv, np.float32)
+        bias = np.concatenate([bq[:d] + np.asarray(u, np.float32).ravel(), bq[d:3 * d],
+                               bq[:d] + np.asarray(v, np.float32).ravel()])
+        self.qkv = gpu.linear(ty, 3 * d, d, wqkv, bias)
+        self.pos = gpu.linear(ty, d, d, wpos, None)
+        self.out = gpu.linear(ty, d, d, wout, bias_out)
+
+    def scratch(self, rows: int, t_pos: int):
+        dev = self.gpu.torch_device
+        return {"qkv": torch.empty(rows, 4 * self.d, dtype=torch.float16, device=dev),
+                "p": torch.empty(pos_rows(t_pos), self.d, dtype=torch.float16, device=dev),
+                "o": torch.empty(rows, self.d, dtype=torch.float16, device=dev)}
+
+    def record(self, p: Pass, y: torch.Tensor, x: torch.Tensor, segs: Segments,
+               table: torch.Tensor, t_pos: int, s: dict) -> None:
+        """y: the layer input rows (LayerNorm output); x: the f32 residual stream; table: the
+        sinusoids of positions t_pos + 15 down to -t_pos (pos_rows(t_pos) rows)."""
+        rows = segs.rows
+        p.gemm(y, self.qkv, s["qkv"], rows, "bias")
+        p.gemm(table, self.pos, s["p"], pos_rows(t_pos), "bias")
+        p.attention_varlen(s["qkv"], None, s["p"], s["o"], rows, segs.start_t, segs.len_t,
+                           segs.max_len, self.heads, self.hd, t_pos)
+        p.gemm(s["o"], self.out, x, rows, "residual", 1.0)
+
+
+class RotaryAttention:
+    """Attention with rotary positions on q and k (BASELINE C3: GigaAM-shaped, RoPE on Q/K with
+    NEOX pairs; the reference's ops::rope placement, src/cpu/transformer.rs:104-106) over
+    [q | k | v] from one projection."""
+
+    def __init__(self, gpu: Gpu, ty: int, d: int, heads: int, wqkv: bytes, wout: bytes,
+                 bias_qkv=None, bias_out=None, theta: float = 10000.0, max_frames: int = 4096,
+                 neox: bool = True):
+        self.gpu, self.d, self.heads, self.hd = gpu, d, heads, d // heads
+        self.neox = neox
+        self.qkv = gpu.linear(ty, 3 * d, d, wqkv, bias_qkv)
+        self.out = gpu.linear(ty, d, d, wout, bias_out)
+        self.table = gpu.upload(rope_table(max_frames, self.hd, theta))
+
+    def scratch(self, rows: int):
+        dev = self.gpu.torch_device
+        return {"qkv": torch.empty(rows, 3 * self.d, dtype=torch.float16, device=dev),
+                "o": torch.empty(rows, self.d, dtype=torch.float16, device=dev)}
+
+    def record(self, p: Pass, y: torch.Tensor, x: torch.Tensor, segs: Segments, s: dict) -> None:
+        rows = segs.rows
+        p.gemm(y, self.qkv, s["qkv"], rows, "bias")
+        p.rope_rows(self.table, s["qkv"], rows, segs.positions, (self.heads, self.hd, self.hd),
+                    self.neox)
+        p.attention_varlen(s["qkv"], None, None, s["o"], rows, segs.start_t, segs.len_t,
+                           segs.max_len, self.heads, self.hd)
+        p.gemm(s["o"], self.out, x, rows, "residual", 1.0)
+
+
+class EncoderAttention:
+    """Whisper's encoder self-attention (src/transformer.rs:122-131): [q | k | v] with biases on
+    q and v (none on k, src/transformer.rs:56), attention, output projection."""
+
+    def __init__(self, gpu: Gpu, ty: int, d: int, heads: int, wqkv: bytes, wout: bytes,
+                 bias_qkv=None, bias_out=None):
+        self.gpu, self.d, self.heads, self.hd = gpu, d, heads, d // heads
+        self.qkv = gpu.linear(ty, 3 * d, d, wqkv, bias_qkv)
+        self.out = gpu.linear(ty, d, d, wout, bias_out)
+
+    def scratch(self, rows: int):
+        dev = self.gpu.torch_device
+        return {"qkv": torch.empty(rows, 3 * self.d, dtype=torch.float16, device=dev),
+                "o": torch.empty(rows, self.d, dtype=torch.float16, device=dev)}
+
+    def record(self, p: Pass, y: torch.Tensor, x: torch.Tensor, rows: int, s: dict,
+               segs: Segments | None = None) -> None:
+        p.gemm(y, self.qkv, s["qkv"], rows, "bias")
+        if segs is None:
+            p.attention(s["qkv"], None, None, s["o"], rows, self.heads, self.hd)
+        else:
+            p.attention_varlen(s["qkv"], None, None, s["o"], rows, segs.start_t, segs.len_t,
+                               segs.max_len, self.heads, self.hd)
+        p.gemm(s["o"], self.out, x, rows, "residual", 1.0)
+
+
+class DecoderAttention:
+    """Whisper's decoder attention for a batch of segments (src/transformer.rs:243-290): the
+    cross-attention K/V of every segment packed once into F16 caches (`record_cross`), then per
+    token: q|k|v of the token, k and v packed into the self cache at the token's position, the
+    self attention over positions 0..pos, its output projection into the residual stream; the
+    cross query, the cross attention over the encoder frames, its output projection.
+
+    Caches are the reference's layout (src/gpu/mod.rs:1507-1522), one per segment, `cols`
+    positions each; the batch of segments runs in one launch per op."""
+
+    def __init__(self, gpu: Gpu, ty: int, d: int, heads: int, context: int, frames: int,
+                 batch: int, w: dict, b: dict):
+        self.gpu, self.d, self.heads, self.hd = gpu, d, heads, d // heads
+        self.context, self.frames, self.batch = context, frames, batch
+        self.qkv = gpu.linear(ty, 3 * d, d, w["qkv"], b.get("qkv"))
+        self.self_out = gpu.linear(ty, d, d, w["self_out"], b.get("self_out"))
+        self.cross_q = gpu.linear(ty, d, d, w["cross_q"], b.get("cross_q"))
+        self.cross_kv = gpu.linear(ty, 2 * d, d, w["cross_kv"], b.get("cross_kv"))
+        self.cross_out = gpu.linear(ty, d, d, w["cross_out"], b.get("cross_out"))
+        dev = gpu.torch_device
+        # F16 caches as 32-bit words: own [batch][d][context/…], cross [batch][d · frames].
+        self.own = torch.zeros(batch, d * context, dtype=torch.int32, device=dev)
+        self.cross = torch.zeros(batch, d * frames, dtype=torch.int32, device=dev)
+        self.qkv_buf = torch.empty(batch, 3 * d, dtype=torch.float32, device=dev)
+        self.q_buf = torch.empty(batch, d, dtype=torch.float32, device=dev)
+        self.att = torch.empty(batch, d, dtype=torch.float32, device=dev)
+        from .gpu import attend_len
+        self.part = torch.empty(batch * attend_len(max(frames, context), heads, self.hd),
+                                dtype=torch.float32, device=dev)
+
+    def record_cross(self, p: Pass, enc: torch.Tensor, chunk: int = 8) -> None:
+        """enc: [batch][frames][d] encoder outputs (f32); chunk segments per projection."""
+        d, t = self.d, self.frames
+        kv = torch.empty(chunk * t, 2 * d, dtype=torch.float32, device=self.gpu.torch_device)
+        for b0 in range(0, self.batch, chunk):
+            nb = min(chunk, self.batch - b0)
+            p.gemm(enc[b0:b0 + nb].reshape(nb * t, d), self.cross_kv, kv, nb * t, "bias")
+            p.pack_batch(kv, (0, 2 * d), t * 2 * d, self.cross[b0], d * t, t, d, (t, 0), nb)
+
+    def record_step(self, p: Pass, y_self: torch.Tensor, y_cross: torch.Tensor, x: torch.Tensor,
+                    pos: int) -> None:
+        """One token per segment at position `pos`: y_self / y_cross are the LayerNorm outputs
+        feeding the self and cross projections ([batch][d]); x the residual stream."""
+        d, B = self.d, self.batch
+        p.gemv_rows(y_self, self.qkv, self.qkv_buf, B, "bias", ldc=3 * d)
+        p.pack_batch(self.qkv_buf, (d, 0), 3 * d, self.own, d * self.context, 1, d,
+                     (self.context, pos), B)
+        p.attend_batch(self.qkv_buf, 3 * d, self.own, d * self.context, self.part, self.att, d,
+                       pos + 1, self.context, self.heads, self.hd, B)
+        p.gemv_rows(self.att, self.self_out, x, B, "residual", 1.0, ldc=d)
+        p.gemv_rows(y_cross, self.cross_q, self.q_buf, B, "bias", ldc=d)
+        p.attend_batch(self.q_buf, d, self.cross, d * self.frames, self.part, self.att, d,
+                       self.frames, self.frames, self.heads, self.hd, B)
+        p.gemv_rows(self.att, self.cross_out, x, B, "residual", 1.0, ldc=d)

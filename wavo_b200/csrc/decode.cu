@@ -17,17 +17,20 @@ namespace {
 // col.. (decode.wgsl:152-173). One thread per (row, pair); rows run fastest so the transposed K
 // words of consecutive positions are written together.
 __global__ void pack_cache_kernel(const float *__restrict__ x, long long src, long long stride,
-                                  uint32_t *__restrict__ cache, int rows, int d, int cols, int col) {
+                                  uint32_t *__restrict__ cache, int rows, int d, int cols, int col,
+                                  long long x_batch, long long cache_batch) {
   const long long total = (long long)rows * d;  // d pairs per row (K: d/2, V: d/2)
   const int half = d / 2;
+  const float *xb = x + blockIdx.y * x_batch;
+  uint32_t *cb = cache + blockIdx.y * cache_batch;
   for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
        t += (long long)gridDim.x * blockDim.x) {
     const int j = int(t % rows), i = int(t / rows);
-    const float *p = x + src + j * stride + 2LL * i;  // any float offset: two scalar loads
+    const float *p = xb + src + j * stride + 2LL * i;  // any float offset: two scalar loads
     const float2 v = make_float2(p[0], p[1]);
     const long long at = i < half ? (long long)i * cols + col + j
                                   : (long long)half * cols + (long long)(col + j) * half + (i - half);
-    cache[at] = pack_half2(v.x, v.y);
+    cb[at] = pack_half2(v.x, v.y);
   }
 }
 
@@ -213,7 +216,8 @@ __global__ void combine_kernel(const float *__restrict__ part, float *__restrict
 // cosines then rot/2 sines) (ops.wgsl:191-215, src/cpu/ops.rs:339-355).
 template <typename T>
 __global__ void rope_kernel(const float *__restrict__ table, T *__restrict__ x, long long stride,
-                            int rows, int pos, int heads, int hd, int rot, int neox, int sections) {
+                            int rows, int pos, const int *__restrict__ positions, int heads, int hd,
+                            int rot, int neox, int sections) {
   const int half = rot / 2;
   const long long per_row = (long long)sections * heads * half;
   const long long total = per_row * rows;
@@ -222,7 +226,8 @@ __global__ void rope_kernel(const float *__restrict__ table, T *__restrict__ x, 
     const int r = int(t / per_row);
     const int rem = int(t % per_row);
     const int hh = rem / half, i = rem % half;
-    const float c = table[(long long)(pos + r) * rot + i], s = table[(long long)(pos + r) * rot + half + i];
+    const long long at = positions ? positions[r] : pos + r;  // the row's table row
+    const float c = table[at * rot + i], s = table[at * rot + half + i];
     T *head = x + r * stride + (long long)hh * hd;
     const int i0 = neox ? i : 2 * i, i1 = neox ? i + half : 2 * i + 1;
     const float a = float(head[i0]), b = float(head[i1]);
@@ -324,12 +329,14 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t launch_pack_cache(const float *x, long long src, long long stride, uint32_t *cache,
-                              int rows, int d, int cols, int col, cudaStream_t s) {
+                              int rows, int d, int cols, int col, long long x_batch,
+                              long long cache_batch, int batch, cudaStream_t s) {
   const long long total = (long long)rows * d;
-  if (total <= 0) return cudaSuccess;
+  if (total <= 0 || batch <= 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 4096) blocks = 4096;
-  pack_cache_kernel<<<int(blocks), 256, 0, s>>>(x, src, stride, cache, rows, d, cols, col);
+  pack_cache_kernel<<<dim3(int(blocks), batch), 256, 0, s>>>(x, src, stride, cache, rows, d, cols,
+                                                             col, x_batch, cache_batch);
   return cudaGetLastError();
 }
 
@@ -354,18 +361,20 @@ cudaError_t launch_attend(const float *q, long long q_stride, const uint32_t *kv
 }
 
 cudaError_t launch_rope(const float *table, void *qkv, int x_f16, long long stride, int rows,
-                        int pos, int heads, int hd, int rot, int neox, int sections,
-                        cudaStream_t s) {
+                        int pos, const int *positions, int heads, int hd, int rot, int neox,
+                        int sections, cudaStream_t s) {
   const long long total = (long long)rows * sections * heads * (rot / 2);
   if (total <= 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 4096) blocks = 4096;
   if (x_f16)
     rope_kernel<__half><<<int(blocks), 256, 0, s>>>(table, reinterpret_cast<__half *>(qkv), stride,
-                                                    rows, pos, heads, hd, rot, neox, sections);
+                                                    rows, pos, positions, heads, hd, rot, neox,
+                                                    sections);
   else
     rope_kernel<float><<<int(blocks), 256, 0, s>>>(table, reinterpret_cast<float *>(qkv), stride,
-                                                   rows, pos, heads, hd, rot, neox, sections);
+                                                   rows, pos, positions, heads, hd, rot, neox,
+                                                   sections);
   return cudaGetLastError();
 }
 

@@ -87,14 +87,16 @@ cudaError_t launch_pack_heads(const void *in, int in_f16, long long ld_in, const
 // ---- decoder (decode.cu) -----------------------------------------------------------------
 
 cudaError_t launch_pack_cache(const float *x, long long src, long long stride, uint32_t *cache,
-                              int rows, int d, int cols, int col, cudaStream_t s);
+                              int rows, int d, int cols, int col, long long x_batch,
+                              long long cache_batch, int batch, cudaStream_t s);
 cudaError_t launch_attend(const float *q, long long q_stride, const uint32_t *kv,
                           long long kv_stride, float *part, float *o, long long o_stride, int n,
                           int cols, int heads, int hd, int batch, cudaStream_t s);
 size_t attend_part_floats(int n, int heads, int hd, int batch);
+// positions (device, optional): the table row of each row; without it row r uses pos + r.
 cudaError_t launch_rope(const float *table, void *qkv, int x_f16, long long stride, int rows,
-                        int pos, int heads, int hd, int rot, int neox, int sections,
-                        cudaStream_t s);
+                        int pos, const int *positions, int heads, int hd, int rot, int neox,
+                        int sections, cudaStream_t s);
 // Rows (<= 32) of f32 a through W of type wtype (0 f32 [n][k], 1 f16 [n][k], 8 int8 [n][k] with
 // f32 scales [n][k/32]) in f32: the reference's gemv (W not rounded to f16).
 cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,

@@ -314,8 +314,8 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
   if (!ctx || !out || !data) return WAVO_EINVAL;
   *out = nullptr;
   // Argument checks as Gpu::upload_linear (src/gpu/mod.rs:775-827).
-  if (ty != WAVO_GGML_F32 && ty != WAVO_GGML_F16 && ty != WAVO_GGML_Q8_0)
-    return fail(ctx, WAVO_EINVAL, "linear layer: GGUF type %d is not F32, F16 or Q8_0", ty);
+  if (ty != WAVO_GGML_F32 && ty != WAVO_GGML_F16 && ty != WAVO_GGML_Q8_0 && ty != WAVO_GGML_BF16)
+    return fail(ctx, WAVO_EINVAL, "linear layer: GGUF type %d is not F32, F16, Q8_0 or BF16", ty);
   if (rows == 0 || k == 0 || k % 32 != 0)
     return fail(ctx, WAVO_EINVAL, "linear layer %u->%u: needs k %% 32 == 0", k, rows);
   const uint32_t dual = bias_len > rows ? uint32_t(bias_len - rows) : 0;
@@ -336,6 +336,16 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
     for (size_t i = 0; i < nk; ++i) w16[i] = f16_bits(f[i]);
   } else if (ty == WAVO_GGML_F16) {
     std::memcpy(w16.data(), data, nk * 2);
+  } else if (ty == WAVO_GGML_BF16) {
+    // bf16 is the high half of an f32: exact in f32 (the gemv operand), rounded to f16 for the
+    // GEMM as the reference rounds every W.
+    const uint16_t *b = static_cast<const uint16_t *>(data);
+    w32.assign(size_t(n) * k, 0.0f);
+    for (size_t i = 0; i < nk; ++i) {
+      const uint32_t bits = uint32_t(b[i]) << 16;
+      std::memcpy(&w32[i], &bits, 4);
+      w16[i] = f16_bits(w32[i]);
+    }
   } else {
     const uint8_t *b = static_cast<const uint8_t *>(data);
     q8.assign(size_t(n) * k, 0);
@@ -479,10 +489,11 @@ wavo_status wavo_gemv_rows(wavo_ctx *ctx, const float *a, uint32_t lda, const wa
     return fail(ctx, WAVO_EINVAL, "gemv: a rows need k floats, 16-byte aligned");
   if (rows > 1 && ldc < l->cols) return fail(ctx, WAVO_EINVAL, "gemv: ldc");
   cudaSetDevice(ctx->device);
-  const void *w = l->ty == WAVO_GGML_F32 ? static_cast<const void *>(l->w32)
+  const bool f32w = l->ty == WAVO_GGML_F32 || l->ty == WAVO_GGML_BF16;
+  const void *w = f32w ? static_cast<const void *>(l->w32)
                   : l->ty == WAVO_GGML_Q8_0 ? static_cast<const void *>(l->q8)
                                             : static_cast<const void *>(l->w16);
-  const int wt = l->ty == WAVO_GGML_F32 ? 0 : l->ty == WAVO_GGML_Q8_0 ? 8 : 1;
+  const int wt = f32w ? 0 : l->ty == WAVO_GGML_Q8_0 ? 8 : 1;
   // Pass::gemv writes l.cols outputs (src/gpu/mod.rs:1461-1467).
   CK(wv::launch_gemv(a, lda, wt, w, l->d8, l->bias, c, ldc, int(rows), int(l->cols), int(l->k),
                      epilogue, alpha, ctx->stream),
@@ -644,9 +655,9 @@ wavo_status wavo_attention_varlen(wavo_ctx *ctx, const void *qk, const void *v, 
 
 // ---- rope --------------------------------------------------------------------------------
 
-wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, uint32_t stride,
-                      uint32_t rows, uint32_t pos, uint32_t heads, uint32_t hd, uint32_t rot,
-                      int neox) {
+wavo_status wavo_rope_rows(wavo_ctx *ctx, const float *table, void *qkv, int dtype,
+                           uint32_t stride, uint32_t rows, uint32_t pos, const int32_t *positions,
+                           uint32_t heads, uint32_t hd, uint32_t rot, int neox) {
   if (!ctx) return WAVO_EINVAL;
   std::lock_guard<std::mutex> g(ctx->mu);
   if (rows == 0) return WAVO_OK;
@@ -654,28 +665,43 @@ wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, u
   if (rot > hd || rot % 2 || (dtype != WAVO_F32 && dtype != WAVO_F16))
     return fail(ctx, WAVO_EINVAL, "rope: rot %u of hd %u", rot, hd);
   if (stride == 0) stride = 3 * heads * hd;
+  if (stride < 2 * heads * hd) return fail(ctx, WAVO_EINVAL, "rope: stride %u", stride);
   cudaSetDevice(ctx->device);
-  CK(wv::launch_rope(table, qkv, dtype == WAVO_F16, stride, int(rows), int(pos), int(heads),
-                     int(hd), int(rot), neox ? 1 : 0, 2, ctx->stream),
+  CK(wv::launch_rope(table, qkv, dtype == WAVO_F16, stride, int(rows), int(pos), positions,
+                     int(heads), int(hd), int(rot), neox ? 1 : 0, 2, ctx->stream),
      "rope launch");
   return WAVO_OK;
 }
 
+wavo_status wavo_rope(wavo_ctx *ctx, const float *table, void *qkv, int dtype, uint32_t stride,
+                      uint32_t rows, uint32_t pos, uint32_t heads, uint32_t hd, uint32_t rot,
+                      int neox) {
+  return wavo_rope_rows(ctx, table, qkv, dtype, stride, rows, pos, nullptr, heads, hd, rot, neox);
+}
+
 // ---- decoder -----------------------------------------------------------------------------
 
-wavo_status wavo_pack(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride, void *cache,
-                      uint32_t rows, uint32_t d, uint32_t cols, uint32_t col) {
+wavo_status wavo_pack_batch(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride,
+                            uint64_t x_batch, void *cache, uint64_t cache_batch, uint32_t rows,
+                            uint32_t d, uint32_t cols, uint32_t col, uint32_t batch) {
   if (!ctx) return WAVO_EINVAL;
   std::lock_guard<std::mutex> g(ctx->mu);
-  if (rows == 0) return WAVO_OK;
+  if (rows == 0 || batch == 0) return WAVO_OK;
   if (!x || !cache) return fail(ctx, WAVO_EINVAL, "pack: NULL buffer");
   if (d % 2 || col + rows > cols)
     return fail(ctx, WAVO_EINVAL, "pack: rows %u at %u of %u positions, d %u", rows, col, cols, d);
+  if (batch > 65535) return fail(ctx, WAVO_EINVAL, "pack: batch %u (at most 65535)", batch);
   cudaSetDevice(ctx->device);
   CK(wv::launch_pack_cache(x, src, stride, static_cast<uint32_t *>(cache), int(rows), int(d),
-                           int(cols), int(col), ctx->stream),
+                           int(cols), int(col), (long long)x_batch, (long long)cache_batch,
+                           int(batch), ctx->stream),
      "pack launch");
   return WAVO_OK;
+}
+
+wavo_status wavo_pack(wavo_ctx *ctx, const float *x, uint32_t src, uint32_t stride, void *cache,
+                      uint32_t rows, uint32_t d, uint32_t cols, uint32_t col) {
+  return wavo_pack_batch(ctx, x, src, stride, 0, cache, 0, rows, d, cols, col, 1);
 }
 
 size_t wavo_attend_len(uint32_t n, uint32_t heads, uint32_t hd) {

@@ -212,6 +212,15 @@ class Pass:
         check(L.lib().wavo_rope(self.ctx, _ptr(table), _ptr(qkv), _dtype(qkv), stride, rows, pos,
                                 heads, hd, rot, int(neox)), self.ctx)
 
+    def rope_rows(self, table: torch.Tensor, qkv: torch.Tensor, rows: int,
+                  positions: torch.Tensor, shape: tuple[int, int, int], neox: bool,
+                  stride: int = 0) -> None:
+        """`rope` with each row's table row given (int32 device array)."""
+        heads, hd, rot = shape
+        assert positions.dtype == torch.int32
+        check(L.lib().wavo_rope_rows(self.ctx, _ptr(table), _ptr(qkv), _dtype(qkv), stride, rows,
+                                     0, _ptr(positions), heads, hd, rot, int(neox)), self.ctx)
+
     def pack(self, x: torch.Tensor, src_stride: tuple[int, int], cache: torch.Tensor, rows: int,
              d: int, cols_col: tuple[int, int]) -> None:
         """`Pass::pack` (src/gpu/mod.rs:1507-1522)."""
@@ -219,6 +228,16 @@ class Pass:
         cols, col = cols_col
         check(L.lib().wavo_pack(self.ctx, _ptr(x), src, stride, _ptr(cache), rows, d, cols, col),
               self.ctx)
+
+    def pack_batch(self, x: torch.Tensor, src_stride: tuple[int, int], x_batch: int,
+                   cache: torch.Tensor, cache_batch: int, rows: int, d: int,
+                   cols_col: tuple[int, int], batch: int) -> None:
+        """`pack` for `batch` segments: segment b's rows at x + b·x_batch floats, its cache at
+        cache + b·cache_batch words."""
+        src, stride = src_stride
+        cols, col = cols_col
+        check(L.lib().wavo_pack_batch(self.ctx, _ptr(x), src, stride, x_batch, _ptr(cache),
+                                      cache_batch, rows, d, cols, col, batch), self.ctx)
 
     def attend(self, q: torch.Tensor, kv: torch.Tensor, part: torch.Tensor, o: torch.Tensor,
                n: int, cols: int, heads: int, hd: int) -> None:
