@@ -207,6 +207,32 @@ wavo_status wavo_attend_batch(wavo_ctx *ctx, const float *q, uint64_t q_stride, 
                               uint32_t n, uint32_t cols, uint32_t heads, uint32_t hd,
                               uint32_t batch);
 
+/* Most floats of split scratch wavo_attend_batch_noalloc can use (1 MiB): enough for
+ * batch·heads·ceil(n/1024)·(hd+2) ≤ 262144, e.g. 99 Whisper-large segments × 20 heads over the
+ * 1500 encoder frames with heads of 64. */
+#define WAVO_ATTEND_NOALLOC_PART_FLOATS (1u << 18)
+
+/* wavo_attend_batch with no context and no caller scratch: the split partials live in a fixed
+ * device array inside the library (WAVO_ATTEND_NOALLOC_PART_FLOATS floats per device), and the
+ * launch goes to `stream` (a cudaStream_t; NULL = the default stream) on the calling thread's
+ * current device. No reference counterpart (the reference's Pass::attend, src/gpu/mod.rs:1485-1505,
+ * takes its `part` buffer from the caller). For callers that cannot allocate device memory at the
+ * call: a host that owns every device allocation itself, code recording a stream capture (no
+ * cudaMalloc there), a decode loop in which an allocation would synchronise the device.
+ * - Allocates nothing: no cudaMalloc / cudaFree, no context. The first call on each device does a
+ *   one-time set-up (it looks the array up, which may load the library's device code), so make it
+ *   before any stream capture that includes this call.
+ * - Calls that overlap on the GPU (on different streams, or from different threads without
+ *   ordering) share the array and race: order them on one stream or with events.
+ * - Nothing needs zeroing: every partial the combine step reads is written first in the same call.
+ * - Returns WAVO_EINVAL, with wavo_last_error(NULL) saying why, when the partials would exceed
+ *   WAVO_ATTEND_NOALLOC_PART_FLOATS (split the batch), and for the argument errors of
+ *   wavo_attend_batch. */
+wavo_status wavo_attend_batch_noalloc(const float *q, uint64_t q_stride, const void *kv,
+                                      uint64_t kv_stride, float *o, uint64_t o_stride, uint32_t n,
+                                      uint32_t cols, uint32_t heads, uint32_t hd, uint32_t batch,
+                                      void *stream);
+
 /* ---- graphs: record a sequence of calls once, replay it with one launch ----------------- */
 
 /* Starts capturing the context's stream (the context's own stream must be current; reserve the

@@ -16,6 +16,7 @@ STATUS = {0: "OK", 1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEDOUT", 5: "EUN
           6: "EDEVICE"}
 F32, F16 = 0, 1
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
+WAVO_ATTEND_NOALLOC_PART_FLOATS = 1 << 18  # the header's fixed scratch of the no-alloc attend
 EPILOGUES = {"bias": 0, "silu": 1, "relu": 2, "residual": 3, "gelu": 4, "gelu_residual": 5,
              "tanh": 6}
 
@@ -59,6 +60,8 @@ SIGNATURES = {
     "wavo_attend": ([_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32], _st),
     "wavo_attend_batch": ([_vp, _vp, _u64, _vp, _u64, _vp, _vp, _u64, _u32, _u32, _u32, _u32,
                            _u32], _st),
+    "wavo_attend_batch_noalloc": ([_vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _u32,
+                                   _u32, _vp], _st),
     "wavo_capture_begin": ([_vp], _st),
     "wavo_capture_end": ([_vp, ctypes.POINTER(_vp)], _st),
     "wavo_graph_launch": ([_vp, _vp], _st),

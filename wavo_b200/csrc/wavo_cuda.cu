@@ -799,3 +799,65 @@ wavo_status wavo_partition_lpt(const uint64_t *cost, uint32_t n, uint32_t parts,
 }
 
 }  // extern "C"
+
+// ---- decoder attention without allocation ------------------------------------------------
+
+namespace {
+
+// The split partials of wavo_attend_batch_noalloc: one fixed array per device, in the module's
+// own device memory (no cudaMalloc). Every element the combine step reads is written first by the
+// same call, so it needs no initial value.
+static __device__ __align__(256) float g_attend_noalloc_part[WAVO_ATTEND_NOALLOC_PART_FLOATS];
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[kNoAllocDevices] = {};
+
+// The device address of the array on the current device, looked up once per device (with that
+// device current) and cached.
+wavo_status noalloc_part(int device, float **out) {
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attend_noalloc_part);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "attend_noalloc: scratch address");
+    if (!p) return fail(nullptr, WAVO_ECUDA, "attend_noalloc: scratch address is NULL");
+    g_noalloc_ptr[device] = static_cast<float *>(p);
+  }
+  *out = g_noalloc_ptr[device];
+  return WAVO_OK;
+}
+
+}  // namespace
+
+extern "C" wavo_status wavo_attend_batch_noalloc(const float *q, uint64_t q_stride, const void *kv,
+                                                 uint64_t kv_stride, float *o, uint64_t o_stride,
+                                                 uint32_t n, uint32_t cols, uint32_t heads,
+                                                 uint32_t hd, uint32_t batch, void *stream) {
+  if (n == 0 || batch == 0) return WAVO_OK;
+  if (!q || !kv || !o) return fail(nullptr, WAVO_EINVAL, "attend_noalloc: NULL buffer");
+  if (n > cols || hd > 128 || hd % 2 || heads == 0)
+    return fail(nullptr, WAVO_EINVAL, "attend_noalloc: n %u of %u positions, heads %u of %u", n,
+                cols, heads, hd);
+  const size_t split_floats = size_t(batch) * heads * (hd + 2);
+  const size_t need = wv::attend_part_floats(int(n), int(heads), int(hd), int(batch));
+  // One split writes the output directly and uses no partials.
+  if (need > split_floats && need > WAVO_ATTEND_NOALLOC_PART_FLOATS)
+    return fail(nullptr, WAVO_EINVAL,
+                "attend_noalloc: %zu floats of partials needed (batch %u, heads %u of %u, %u "
+                "keys), the fixed scratch holds %u: split the batch",
+                need, batch, heads, hd, n, WAVO_ATTEND_NOALLOC_PART_FLOATS);
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "attend_noalloc: current device");
+  if (device < 0 || device >= kNoAllocDevices)
+    return fail(nullptr, WAVO_EUNSUPPORTED, "attend_noalloc: device %d", device);
+  float *part = nullptr;
+  wavo_status st = noalloc_part(device, &part);
+  if (st != WAVO_OK) return st;
+  e = wv::launch_attend(q, q_stride, static_cast<const uint32_t *>(kv), kv_stride, part, o,
+                        o_stride, int(n), int(cols), int(heads), int(hd), int(batch),
+                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "attend_noalloc launch");
+  return WAVO_OK;
+}
