@@ -148,6 +148,9 @@ class Workload:
     scaling = "weak"
     dtype = "f16 operands, f32 accumulate"
     bound = "tensor"
+    # DRAM bytes (read + write) per launch of an op's kernel from one ncu capture at the bench's
+    # shapes (dram__bytes_read.sum + dram__bytes_write.sum), when one was taken.
+    TRAFFIC: dict = {}
 
     def audio_s(self) -> float:  # audio seconds this rank processes per step
         raise NotImplementedError
@@ -159,6 +162,7 @@ class Workload:
 class C2(Workload):
     """Whisper large-v3-turbo encoder self-attention, 32 layers, batch 1, T=1500."""
     T, D, H, LAYERS = 1500, 1280, 20, 32
+    TRAFFIC = {"attention": 11578368 + 256, "gemm_qkv": 13716992, "gemm_out": 14840576}
 
     def __init__(self, gpu, rank, world, seed=2000):
         import torch
@@ -375,6 +379,7 @@ RelPosWorkload.cpu = staticmethod(
 
 class C5(RelPosWorkload):
     scaling = "strong"
+    TRAFFIC = {"attention": 697848832 + 162365696}
 
     def __init__(self, gpu, rank, world, seed=5000):
         super().__init__(gpu, rank, world, segment_lengths(seed, 400, 120, 300), 24, "q8_0", seed)
@@ -493,6 +498,7 @@ class C4(Workload):
     D, H, LAYERS, FRAMES, CONTEXT, STEPS, BATCH = 1280, 20, 4, 1500, 448, 224, 32
     scaling = "strong"
     bound = "hbm"
+    TRAFFIC = {"gemv_qkv": 10033152}
 
     def __init__(self, gpu, rank, world, seed=4000):
         import torch
@@ -575,9 +581,13 @@ class C4(Workload):
 
     def work(self):
         d, B, T = self.D, self.batch, self.FRAMES
-        # HBM bytes per launch: the cross cache of the batch (K and V, f16).
-        return {"attend_cross": 2.0 * B * T * d * 2, "attend_self": 0.0, "gemv_qkv": 0.0,
-                "pack": 0.0, "gemv_self_out": 0.0, "gemv_cross_q": 0.0, "gemv_cross_out": 0.0}
+        # HBM bytes per launch: the caches of the batch (K and V, f16; the self cache averaged
+        # over the steps), and for a projection its f16 weights plus the f32 rows in and out.
+        proj = lambda n, k: 2.0 * n * k + 4.0 * B * (n + k)  # noqa: E731
+        return {"attend_cross": 2.0 * B * T * d * 2,
+                "attend_self": 2.0 * B * (self.STEPS + 1) / 2 * d * 2,
+                "gemv_qkv": proj(3 * d, d), "gemv_self_out": proj(d, d),
+                "gemv_cross_q": proj(d, d), "gemv_cross_out": proj(d, d), "pack": 0.0}
 
     def audio_s(self):
         return self.batch * 30.0
@@ -743,23 +753,28 @@ def main():
     h2d = sum(t.numel() * t.element_size() for _, t in wl.inputs())
     d2h = sum(t.numel() * t.element_size() for t, _ in wl.outputs())
 
-    # ---- per-kernel durations (eager, CUDA events on the launch stream) for the roofline ----
-    events: dict[str, list] = {}
-
-    def timer(name, fn):
+    # ---- per-kernel durations for the roofline: each op's launches of one step, alone in a
+    # graph (same buffers, weights and order as in the step), replayed back to back and timed with
+    # CUDA events on the launching stream; per launch = elapsed / (replays x launches) ----
+    counts: dict[str, int] = {}
+    wl.record(gpu.pass_(), lambda name, fn: counts.__setitem__(name, counts.get(name, 0) + 1))
+    per = {}
+    for name in counts:
+        g = gpu.capture(lambda p: wl.record(p, lambda n, fn: fn() if n == name else None))
+        for _ in range(2):
+            g.launch()
+        gpu.sync()
+        reps = 3
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        fn()
+        for _ in range(reps):
+            g.launch()
         b.record(stream)
-        events.setdefault(name, []).append((a, b))
-
-    for _ in range(2):
-        events.clear()
-        wl.record(gpu.pass_(), timer)
         torch.cuda.synchronize()
-    gpu.sync()
-    per = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in events.items()}
-    totals = {k: per[k] * len(events[k]) for k in per}
+        gpu.sync()
+        per[name] = a.elapsed_time(b) / (reps * counts[name])
+        del g
+    totals = {k: per[k] * counts[k] for k in per}
     work = wl.work()
     top = max((k for k in totals if work.get(k, 0) > 0), key=totals.get)
 
@@ -796,7 +811,8 @@ def main():
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": wl.launches() * args.steps,
             "roofline": {"bound": wl.bound, "kernel": top, "achieved": achieved, "peak": peak,
-                         "unit": unit, "frac": achieved / peak, "traffic": None,
+                         "unit": unit, "frac": achieved / peak,
+                         "traffic": wl.TRAFFIC.get(top),
                          "peak_source": f"{peaks['source']} {src}"},
             "kernels_ms": per,
             "clocks": clocks.summary(),
