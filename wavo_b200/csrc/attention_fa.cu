@@ -4,17 +4,23 @@
 //
 // A CTA takes two 128-query tiles of one head of one segment, so that the tensor core works on one
 // tile while the other tile's softmax runs:
-//   warp 0     TMA: both Q tiles once, then K and V blocks through three-slot rings;
-//   warp 1     one thread issues the UMMAs: S_t = Q_t·K^T into TMEM, then O_t += P_t·V with P_t
-//              read from TMEM;
-//   warps 2-5  softmax of tile 0, warps 6-9 softmax of tile 1: one query row per thread, read from
-//              TMEM with tcgen05.ld in two passes (row maximum, then probabilities); a lagging
-//              maximum (the TMEM accumulator is rescaled only when a row maximum grows by more than
-//              2^8); a quarter of the exponentials on the FMA pipe (a degree-4 polynomial for 2^f
-//              on [-1/2, 1/2] fitted for this kernel, with the exponent added in the integer bits),
-//              the rest on the MUFU; probabilities written back to TMEM as f16 pairs with
-//              tcgen05.st (the UMMAs already use shared memory at its full read rate, so P stays
-//              out of it); at the end the accumulator row is normalised and stored.
+//   warp 0      TMA: both Q tiles once, then K and V blocks through three-slot rings;
+//   warps 1, 2  one thread each issues tile 0's / tile 1's UMMAs: S_t = Q_t·K^T into TMEM, then
+//               O_t += P_t·V with P_t read from TMEM (the A operand of a TS UMMA);
+//   warps 3-18  softmax, eight warps a tile: two warps share a 32-row quarter of the tile (the TMEM
+//               lanes a warp may read), 16 rows each, and two threads of a warp share a row, one
+//               half of its key columns each (the 16x32bx2 TMEM access shape). A thread loads its
+//               scores from TMEM into registers with one wait, hands the S columns back at once
+//               (the next S_t UMMA overlaps this block's exponentials), takes the row maximum
+//               with one shuffle, and writes its probabilities back to TMEM as f16 pairs.
+// The row maximum lags: the TMEM accumulator is rescaled only when a row maximum grows by more
+// than 2^8. Exponentials: 3 in 8 on the FMA pipe (a degree-4 polynomial for 2^f on [-1/2, 1/2]
+// fitted for this kernel, the exponent added in the integer bits), the rest on the MUFU; the
+// scale-and-shift and the row sums use the paired f32 instructions of sm_100 (fma/add .f32x2).
+// At the end the two threads of a row add their sums, normalise and store their halves of O.
+//
+// For heads of 64 the tensor core bounds the kernel: P·V is 8 UMMAs of N=64 per 128-key block
+// with A read from TMEM, each about 100 cycles (measured), against 4 UMMAs of N=128 for S.
 #include "kernels.cuh"
 #include "ptx.cuh"
 
@@ -22,9 +28,11 @@ namespace wv {
 namespace {
 
 constexpr int BM = 128;
-constexpr int NT = 2;  // query tiles per CTA
-constexpr int THREADS = 64 + NT * 128;
-constexpr int KVS = 3;  // K and V ring slots
+constexpr int NT = 2;                  // query tiles per CTA
+constexpr int CTRL_WARPS = 1 + NT;     // TMA producer, one UMMA issuer per tile
+constexpr int SOFT_WARPS = 8;          // softmax warps per tile
+constexpr int THREADS = 32 * (CTRL_WARPS + NT * SOFT_WARPS);
+constexpr int KVS = 3;                 // K and V ring slots
 
 template <int HD, int BN>
 struct Fa {
@@ -33,13 +41,14 @@ struct Fa {
   static constexpr int ATOM_KV = BN * 128;
   static constexpr int Q_BYTES = BM * HD * 2;
   static constexpr int KV_BYTES = BN * HD * 2;
+  static constexpr int CW = BN / 2;   // score columns per softmax thread (half a row)
+  static constexpr int OW = HD / 2;   // accumulator columns per softmax thread
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KVS * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + KVS * KV_BYTES;
   // TMEM columns of tile t, from t·256: the scores S (BN f32 columns), the probabilities P (BN
-  // f16, two per column: the A operand of P·V, read by the tensor core from TMEM, so that neither
-  // the softmax's writes nor the UMMA's reads of P touch shared memory), the accumulator O.
+  // f16, two per column), the accumulator O.
   static constexpr int T_TILE = 256;
   static constexpr int T_S = 0;
   static constexpr int T_P = BN;
@@ -48,6 +57,8 @@ struct Fa {
   static constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
   static constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
   static_assert(T_O + HD <= T_TILE && NT * T_TILE <= TMEM_COLS, "TMEM");
+  static_assert(CW == 32 || CW == 64, "score columns per thread");
+  static_assert(OW % 32 == 0, "accumulator columns per thread");
 };
 
 struct __align__(8) FaBarriers {
@@ -57,25 +68,49 @@ struct __align__(8) FaBarriers {
   uint64_t s_full[NT], s_free[NT];
   uint64_t p_full[NT], pv_done[NT];
   uint64_t o_full;
-  uint64_t drain;
+  uint64_t drain[NT];
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-// 2^x for x in [-125, 8] on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f by a
-// degree-4 polynomial (coefficients fitted here to the relative error of 2^f, max 7.7e-6 in f32),
-// 2^n added to the exponent bits.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;  // 1.5·2^23: rounds x to an integer in the low bits
-  const float n = t - 12582912.0f;
-  const float f = x - n;
-  float p = 0.009251425974071026f;
-  p = fmaf(p, f, 0.055853113532066345f);
-  p = fmaf(p, f, 0.24031664431095123f);
-  p = fmaf(p, f, 0.6931320428848267f);
-  p = fmaf(p, f, 0.9999976754188538f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// ---- paired f32 arithmetic (sm_100: fma/add .f32x2, two lanes of work per instruction) ----------
+
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1,
+                                     float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x for two x in [-125, 8] on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f by
+// a degree-4 polynomial (coefficients fitted here to the relative error of 2^f, max 7.7e-6 in
+// f32), 2^n added to the exponent bits.
+__device__ __forceinline__ void exp2_poly2(float &x0, float &x1) {
+  constexpr float kRound = 12582912.0f;  // 1.5·2^23: x + kRound holds round(x) in its low bits
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  float t0, t1, n0, n1, f0, f1;
+  add2(t0, t1, x0, x1, kRound, kRound);
+  add2(n0, n1, t0, t1, -kRound, -kRound);
+  add2(f0, f1, x0, x1, -n0, -n1);
+  float p0, p1;
+  fma2(p0, p1, 0.009251425974071026f, 0.009251425974071026f, f0, f1, 0.055853113532066345f,
+       0.055853113532066345f);
+  fma2(p0, p1, p0, p1, f0, f1, 0.24031664431095123f, 0.24031664431095123f);
+  fma2(p0, p1, p0, p1, f0, f1, 0.6931320428848267f, 0.6931320428848267f);
+  fma2(p0, p1, p0, p1, f0, f1, 0.9999976754188538f, 0.9999976754188538f);
+  x0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  x1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -89,6 +124,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fa_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
               const AttnArgs a) {
   using C = Fa<HD, BN>;
+  constexpr int CW = C::CW, OW = C::OW;
   const int seg = blockIdx.z, h = blockIdx.y;
   const int T = a.seg_len ? a.seg_len[seg] : a.single_t;
   const int row0 = a.seg_len ? a.seg_start[seg] : 0;
@@ -107,18 +143,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->q_full, 1);
     for (int i = 0; i < KVS; ++i) {
       mbar_init(&bar->k_full[i], 1);
-      mbar_init(&bar->k_empty[i], 1);
+      mbar_init(&bar->k_empty[i], nt);  // one commit from each live tile's issuer
       mbar_init(&bar->v_full[i], 1);
-      mbar_init(&bar->v_empty[i], 1);
+      mbar_init(&bar->v_empty[i], nt);
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&bar->s_full[t], 1);
-      mbar_init(&bar->s_free[t], 4);
-      mbar_init(&bar->p_full[t], 4);
+      mbar_init(&bar->s_free[t], SOFT_WARPS);
+      mbar_init(&bar->p_full[t], SOFT_WARPS);
       mbar_init(&bar->pv_done[t], 1);
+      mbar_init(&bar->drain[t], 1);
     }
-    mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->drain, 1);
+    mbar_init(&bar->o_full, nt);
     bar->abort = 0;
     fence_mbar_init();
   }
@@ -142,8 +178,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       bool ok = true;
       uint32_t k_last[KVS] = {}, v_last[KVS] = {};  // bit 1: armed; bit 0: parity
-      mbar_arrive_expect_tx(&bar->q_full, NT * C::Q_BYTES);
-      for (int t = 0; t < NT; ++t)
+      mbar_arrive_expect_tx(&bar->q_full, nt * C::Q_BYTES);
+      for (int t = 0; t < nt; ++t)
 #pragma unroll
         for (int b = 0; b < C::NBOX; ++b)
           tma_load_2d(smem + C::OFF_Q + t * C::Q_BYTES + b * C::ATOM_Q, &map_q, &bar->q_full,
@@ -180,189 +216,206 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer ----------------------------------------------------------------------------
-    if (lane == 0) {
+  } else if (warp < CTRL_WARPS) {
+    // ---- UMMA issuer of tile t -------------------------------------------------------------
+    // Per block j: S_t(j) = Q_t·K(j)^T as soon as the tile's softmax holds S_t(j-1) in registers,
+    // then O_t += P_t(j-1)·V(j-1) once P_t(j-1) is in TMEM. One issuing thread per tile, so that
+    // one thread's barrier waits and commits overlap the other tile's UMMAs.
+    const int t = int(warp) - 1;
+    if (lane == 0 && t < nt) {
       bool ok = mbar_wait(&bar->q_full, 0, ab, kErrTimeoutMma);
       bool issued = false;
       const int hsteps = (a.hd + 15) / 16;
-      const uint32_t sq = smem_u32(smem + C::OFF_Q), sk = smem_u32(smem + C::OFF_K);
-      const uint32_t sv = smem_u32(smem + C::OFF_V);
+      // Descriptors are linear in the start address (bits 0-13 hold address / 16), so every
+      // operand's descriptor is a base plus an offset / 16.
+      const uint64_t dq = sdesc_sw128(smem_u32(smem + C::OFF_Q + t * C::Q_BYTES), 16, 1024);
+      const uint64_t dk = sdesc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
+      const uint64_t dv = sdesc_sw128(smem_u32(smem + C::OFF_V), C::ATOM_KV, 1024);
+      const uint32_t tt = tmem + t * C::T_TILE;
       tc_fence_after();
-      // Per block j, tile by tile: S_t(j) as soon as tile t's softmax released S_t(j-1), then
-      // P_t(j-1)·V(j-1). Tiles advance independently, so one tile's softmax overlaps the other
-      // tile's UMMAs.
       for (int j = 0; j <= nb && ok; ++j) {
-        const int sk_slot = j % KVS, sv_slot = (j + KVS - 1) % KVS;
-        if (j < nb && !mbar_wait(&bar->k_full[sk_slot], (j / KVS) & 1, ab, kErrTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        if (j >= 1 &&
-            !mbar_wait(&bar->v_full[sv_slot], ((j - 1) / KVS) & 1, ab, kErrTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        for (int t = 0; t < nt && ok; ++t) {
-          if (j < nb) {
-            if (j >= 1 && !mbar_wait(&bar->s_free[t], (j - 1) & 1, ab, kErrTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            for (int kk = 0; kk < hsteps; ++kk) {
-              const uint64_t ad =
-                  sdesc_sw128(sq + t * C::Q_BYTES + (kk >> 2) * C::ATOM_Q + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = sdesc_sw128(
-                  sk + sk_slot * C::KV_BYTES + (kk >> 2) * C::ATOM_KV + (kk & 3) * 32, 16, 1024);
-              umma_f16(tmem + t * C::T_TILE + C::T_S, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
-            }
-            issued = true;
-            umma_commit(&bar->s_full[t]);
+        if (j < nb) {
+          const int ks = j % KVS;
+          if (!mbar_wait(&bar->k_full[ks], (j / KVS) & 1, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
           }
-          if (j >= 1) {
-            const int i = j - 1;
-            if (!mbar_wait(&bar->p_full[t], i & 1, ab, kErrTimeoutMma)) { ok = false; break; }
-            tc_fence_after();
+          if (j >= 1 && !mbar_wait(&bar->s_free[t], (j - 1) & 1, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bk0 = dk + uint64_t((ks * C::KV_BYTES) >> 4);
+          for (int kk = 0; kk < hsteps; ++kk) {
+            const uint32_t o_q = ((kk >> 2) * C::ATOM_Q + (kk & 3) * 32) >> 4;
+            const uint32_t o_k = ((kk >> 2) * C::ATOM_KV + (kk & 3) * 32) >> 4;
+            umma_f16(tt + C::T_S, dq + o_q, bk0 + o_k, C::IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&bar->s_full[t]);
+          umma_commit(&bar->k_empty[ks]);
+        }
+        if (j >= 1) {
+          const int i = j - 1, vs = i % KVS;
+          if (!mbar_wait(&bar->v_full[vs], (i / KVS) & 1, ab, kErrTimeoutMma) ||
+              !mbar_wait(&bar->p_full[t], i & 1, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bv0 = dv + uint64_t((vs * C::KV_BYTES) >> 4);
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              // A = P from TMEM: keys 16kk.. are columns 8kk.. of the P region.
-              const uint64_t bd =
-                  sdesc_sw128(sv + sv_slot * C::KV_BYTES + kk * 16 * 128, C::ATOM_KV, 1024);
-              umma_f16_ts(tmem + t * C::T_TILE + C::T_O, tmem + t * C::T_TILE + C::T_P + kk * 8,
-                          bd, C::IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(&bar->pv_done[t]);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            // A = P from TMEM: keys 16kk.. are columns 8kk.. of the P region; B = V rows 16kk..
+            umma_f16_ts(tt + C::T_O, tt + C::T_P + kk * 8, bv0 + uint64_t((kk * 16 * 128) >> 4),
+                        C::IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
           }
+          umma_commit(&bar->pv_done[t]);
+          umma_commit(&bar->v_empty[vs]);
         }
-        if (!ok) break;
-        if (j < nb) umma_commit(&bar->k_empty[sk_slot]);
-        if (j >= 1) umma_commit(&bar->v_empty[sv_slot]);
       }
       if (ok) {
         umma_commit(&bar->o_full);
       } else if (issued) {
-        umma_commit(&bar->drain);
+        umma_commit(&bar->drain[t]);
         const long long t0 = clock64();
-        while (!mbar_try_wait(&bar->drain, 0) && clock64() - t0 < kWaitCycles) {
+        while (!mbar_try_wait(&bar->drain[t], 0) && clock64() - t0 < kWaitCycles) {
         }
       }
     }
   } else {
-    // ---- softmax: warps 2..5 tile 0, warps 6..9 tile 1; one query row per thread ----------------
-    const int t = int(warp - 2) >> 2;
+    // ---- softmax: 8 warps a tile. The two warps of a quarter (the TMEM lanes 32·(w % 4) a warp
+    // may access) take 16 rows each; within a warp, threads t and t + 16 share row t % 16 and hold
+    // its two halves of the key columns (the 16x32bx2 TMEM access shape), so a row maximum or sum
+    // needs one shuffle.
+    const int w = int(warp) - CTRL_WARPS;
+    const int t = w >> 3, sub = (w >> 2) & 1;
     const uint32_t quarter = warp & 3u;
-    const int ii = int(quarter * 32 + lane);
-    const uint32_t tl = tmem + ((quarter * 32u) << 16);
-    const uint32_t ts = tl + t * C::T_TILE + C::T_S, tp = tl + t * C::T_TILE + C::T_P;
-    const uint32_t to = tl + t * C::T_TILE + C::T_O;
+    const int ch = int(lane >> 4);  // column half of this thread
+    const uint32_t tl = tmem + ((quarter * 32u + sub * 16u) << 16) + t * C::T_TILE;
+    const uint32_t ts = tl + C::T_S, tp = tl + C::T_P, to = tl + C::T_O;
     const float c = a.scale_log2;
-    float m_use = -INFINITY, l = 0.0f;
+    float m_use = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     bool ok = t < nt;
     for (int j = 0; j < nb && ok; ++j) {
       if (!mbar_wait(&bar->s_full[t], j & 1, ab, kErrTimeoutConsumer)) { ok = false; break; }
       tc_fence_after();
-      // Keys past the segment (last block only) are masked to -inf in both passes.
-      const int kvalid = T - j * BN;
-      // Pass 1: the block's row maximum, 32 columns at a time, the next load in flight.
-      float mx = -INFINITY;
+      float s[CW];
       {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(ts, ra);
-#pragma unroll
-        for (int q = 0; q < BN / 32; ++q) {
-          uint32_t(&cur)[32] = (q & 1) ? rb : ra;
-          uint32_t(&nxt)[32] = (q & 1) ? ra : rb;
+        uint32_t r[32];
+        tmem_ld_16x2_x32<CW>(ts, r);
+        if constexpr (CW == 64) {
+          uint32_t r2[32];
+          tmem_ld_16x2_x32<CW>(ts + 32, r2);
           tmem_wait_ld();
-          if (q + 1 < BN / 32) tmem_ld32(ts + (q + 1) * 32, nxt);
-          if (kvalid < BN) {
 #pragma unroll
-            for (int x = 0; x < 32; ++x)
-              if (q * 32 + x >= kvalid) cur[x] = __float_as_uint(-INFINITY);
-          }
-#pragma unroll
-          for (int x = 0; x < 32; x += 2)
-            mx = max3(mx, __uint_as_float(cur[x]), __uint_as_float(cur[x + 1]));
+          for (int x = 0; x < 32; ++x) s[32 + x] = __uint_as_float(r2[x]);
+        } else {
+          tmem_wait_ld();
         }
+#pragma unroll
+        for (int x = 0; x < 32; ++x) s[x] = __uint_as_float(r[x]);
+      }
+      // The scores are in registers: the issuer may overwrite S with the next block's.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->s_free[t]);
+      // Keys past the segment (last block only) are masked to -inf.
+      const int kvalid = T - j * BN - ch * CW;
+      if (kvalid < CW) {
+#pragma unroll
+        for (int x = 0; x < CW; ++x)
+          if (x >= kvalid) s[x] = -INFINITY;
+      }
+      float mx;
+      {
+        // Four independent chains of 3-input maxima, then the other half of the row.
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int x = 0; x < CW; x += 8) {
+          float &m = m4[(x / 8) & 3];
+          m = max3(m, s[x + 0], s[x + 1]);
+          m = max3(m, s[x + 2], s[x + 3]);
+          m = max3(m, s[x + 4], s[x + 5]);
+          m = max3(m, s[x + 6], s[x + 7]);
+        }
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       }
       const float m_blk = mx * c;
+      const bool need = m_blk > m_use + 8.0f;
+      const bool rescale = __any_sync(0xffffffffu, need) && j > 0;
+      const float alpha = need ? ex2(m_use - m_blk) : 1.0f;
+      if (rescale) {
+        l0 *= alpha;
+        l1 *= alpha;
+      }
+      if (need) m_use = m_blk;
+      const float nm = -m_use;
+      // Probabilities: 16 at a time, 6 of them on the FMA pipe.
+      uint32_t pk[CW / 2];
+#pragma unroll
+      for (int g = 0; g < CW; g += 16) {
+        float *p = s + g;  // in place: scores become exponents, then probabilities
+#pragma unroll
+        for (int x = 0; x < 16; x += 2) fma2(p[x], p[x + 1], p[x], p[x + 1], c, c, nm, nm);
+#pragma unroll
+        for (int x = 0; x < 10; ++x) p[x] = ex2(p[x]);
+        exp2_poly2(p[10], p[11]);
+        exp2_poly2(p[12], p[13]);
+        exp2_poly2(p[14], p[15]);
+#pragma unroll
+        for (int x = 0; x < 16; x += 4) {
+          float a0, a1;
+          add2(a0, a1, p[x], p[x + 1], p[x + 2], p[x + 3]);
+          add2(l0, l1, l0, l1, a0, a1);
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x) pk[g / 2 + x] = pack_half2(p[2 * x], p[2 * x + 1]);
+      }
       // P_t is free and O_t stable once P·V of block j - 1 landed.
       if (j >= 1 && !mbar_wait(&bar->pv_done[t], (j - 1) & 1, ab, kErrTimeoutConsumer)) {
         ok = false;
         break;
       }
-      const bool need = m_blk > m_use + 8.0f;
-      if (__any_sync(0xffffffffu, need) && j > 0) {
-        tc_fence_after();
-        const float alpha = need ? ex2(m_use - m_blk) : 1.0f;
-        uint32_t r[32];
-#pragma unroll
-        for (int q = 0; q < HD / 32; ++q) {
-          tmem_ld32(to + q * 32, r);
+      tc_fence_after();
+      if constexpr (CW == 64) {
+        tmem_st_16x2_x32<CW / 2>(tp, pk);
+      } else {
+        tmem_st_16x2_x16<CW / 2>(tp, pk);
+      }
+      if (rescale) {
+#pragma unroll 1
+        for (int q = 0; q < OW / 16; ++q) {
+          uint32_t r[16];
+          tmem_ld_16x2_x16<OW>(to + q * 16, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int x = 0; x < 32; ++x) r[x] = __float_as_uint(__uint_as_float(r[x]) * alpha);
-          tmem_st32(to + q * 32, r);
-        }
-        tmem_wait_st();
-        l *= alpha;
-      }
-      if (need) m_use = m_blk;
-      const float nm = -m_use;
-      // Pass 2: probabilities, 32 columns at a time, the next load in flight.
-      {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(ts, ra);
-#pragma unroll
-        for (int q = 0; q < BN / 32; ++q) {
-          uint32_t(&cur)[32] = (q & 1) ? rb : ra;
-          uint32_t(&nxt)[32] = (q & 1) ? ra : rb;
-          tmem_wait_ld();
-          if (q + 1 < BN / 32) tmem_ld32(ts + (q + 1) * 32, nxt);
-          if (kvalid < BN) {
-#pragma unroll
-            for (int x = 0; x < 32; ++x)
-              if (q * 32 + x >= kvalid) cur[x] = __float_as_uint(-INFINITY);
-          }
-          uint32_t pk[16];  // 32 probabilities as 16 f16 pairs: 16 columns of the P region
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float p[8];
-#pragma unroll
-            for (int x = 0; x < 8; ++x) {
-              const float e = fmaf(__uint_as_float(cur[8 * g + x]), c, nm);
-              p[x] = ((x & 3) == 3) ? exp2_poly(e) : ex2(e);
-            }
-            l += ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
-#pragma unroll
-            for (int x = 0; x < 4; ++x) pk[4 * g + x] = pack_half2(p[2 * x], p[2 * x + 1]);
-          }
-          tmem_st16(tp + q * 16, pk);
+          for (int x = 0; x < 16; ++x) r[x] = __float_as_uint(__uint_as_float(r[x]) * alpha);
+          tmem_st_16x2_x16<OW>(to + q * 16, r);
         }
       }
-      // The S columns are read and P is in TMEM: the next S of this tile may overwrite S, and the
-      // P·V UMMA may read P.
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar->s_free[t]);
-        mbar_arrive(&bar->p_full[t]);
-      }
+      if (lane == 0) mbar_arrive(&bar->p_full[t]);
     }
     if (ok && mbar_wait(&bar->o_full, 0, ab, kErrTimeoutConsumer)) {
+      // The row sum over both halves, then this thread's half of the row of O.
+      float l = l0 + l1;
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
       tc_fence_after();
       const float inv = 1.0f / l;
-      const int qrow = m0 + t * BM + ii;
+      const int qrow = m0 + t * BM + int(quarter * 32u + sub * 16u + (lane & 15u));
       const bool store = qrow < T;
       const long long orow = (long long)(row0 + qrow) * a.ldo + (long long)h * a.hd;
 #pragma unroll
-      for (int q = 0; q < HD / 32; ++q) {
+      for (int q = 0; q < OW / 32; ++q) {
         uint32_t r[32];
-        tmem_ld32(to + q * 32, r);
+        tmem_ld_16x2_x32<OW>(to + q * 32, r);
         tmem_wait_ld();
-        if (store) {
-          const int c0 = q * 32;
+        const int c0 = ch * OW + q * 32;
+        if (store && c0 < a.hd) {
           if (a.o_f16) {
             __half *o = reinterpret_cast<__half *>(a.o) + orow;
             if (c0 + 32 <= a.hd && ((reinterpret_cast<uintptr_t>(o + c0) & 15u) == 0)) {
