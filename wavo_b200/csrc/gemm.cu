@@ -19,12 +19,15 @@ namespace {
 
 constexpr int BM = kGemmBM, BK = kGemmBK;
 
-template <int BN>
+// KC: 64-column K chunks per pipeline stage. With KC = 2 each operand tile of a stage is one 3D
+// TMA box of two chunks: a TMA instruction costs an SM a fixed ~250 cycles besides its bytes, so
+// fewer, larger boxes keep the loads ahead of the UMMAs.
+template <int BN, int KC = 1>
 struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 160 ? 5 : 6);
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_BYTES = BM * BK * 2 * KC;
+  static constexpr int B_BYTES = BN * BK * 2 * KC;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (216 * 1024) / STAGE_BYTES > 6 ? 6 : (216 * 1024) / STAGE_BYTES;
   // Two accumulators of BN columns; tcgen05.alloc takes a power of two.
   static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static_assert(BN % 32 == 0 && STAGE_BYTES % 1024 == 0, "tile shape");
@@ -134,11 +137,11 @@ __device__ __forceinline__ void load_bias32(const float *bias, int lim, float (&
   }
 }
 
-template <int BN, int E>
+template <int BN, int E, int KC>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_w,
                 const GemmArgs g) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, KC>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -149,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_m = (g.m + BM - 1) / BM;
   const int num_n = (g.cols + BN - 1) / BN;
   const int tiles = num_m * num_n;
-  const int kblocks = (g.k + BK - 1) / BK;
+  const int kblocks = (g.k + BK * KC - 1) / (BK * KC);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -194,8 +197,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint8_t *sa = smem + stage * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&bar->full[stage], C::STAGE_BYTES);
-          tma_load_2d(sa, &tma_a, &bar->full[stage], kb * BK, m0);
-          tma_load_2d(sa + C::A_BYTES, &tma_w, &bar->full[stage], kb * BK, n0);
+          if constexpr (KC == 1) {
+            tma_load_2d(sa, &tma_a, &bar->full[stage], kb * BK, m0);
+            tma_load_2d(sa + C::A_BYTES, &tma_w, &bar->full[stage], kb * BK, n0);
+          } else {
+            tma_load_3d(sa, &tma_a, &bar->full[stage], 0, m0, kb * KC);
+            tma_load_3d(sa + C::A_BYTES, &tma_w, &bar->full[stage], 0, n0, kb * KC);
+          }
           armed |= 1u << stage;
           if (++stage == STAGES) {
             stage = 0;
@@ -239,10 +247,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t sb = sa + C::A_BYTES;
+          // Chunk c of a stage: BM (a) or BN (W) rows of 128 bytes.
 #pragma unroll
-          for (int ks = 0; ks < BK / 16; ++ks) {
-            umma_f16(d, sdesc_sw128(sa + ks * 32, 16, 1024), sdesc_sw128(sb + ks * 32, 16, 1024),
-                     C::IDESC, (kb | ks) != 0);
+          for (int ks = 0; ks < KC * BK / 16; ++ks) {
+            const uint32_t oa = (ks >> 2) * BM * 128 + (ks & 3) * 32;
+            const uint32_t ob = (ks >> 2) * BN * 128 + (ks & 3) * 32;
+            umma_f16(d, sdesc_sw128(sa + oa, 16, 1024), sdesc_sw128(sb + ob, 16, 1024), C::IDESC,
+                     (kb | ks) != 0);
           }
           issued = true;
           umma_commit(&bar->empty[stage]);
@@ -313,6 +324,323 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ---- pair GEMM: one tile of 256 rows x BN columns on a cluster of two CTAs ---------------------
+//
+// A single SM streams its operand tiles at about 80 bytes per cycle through TMA, so a 128 x 128
+// tile (32 KB per 64-deep k-block for 260 cycles of UMMAs) waits on its loads. A CTA pair shares
+// one UMMA of M=256: each CTA loads its 128 rows of a and half of the tile's W rows, so a k-block
+// costs each SM 16 KB + BN/2·128 bytes for 128·BN·64 multiply-adds, and the tensor core, not TMA,
+// sets the pace. The leader CTA (rank 0) issues the UMMAs for both; each CTA's epilogue reads its
+// own 128 accumulator rows from its own TMEM.
+
+template <int BN, int KC = 1>
+struct Gemm2Cfg {
+  static constexpr int BNH = BN / 2;  // W rows per CTA
+  static constexpr int A_BYTES = BM * BK * 2 * KC;
+  static constexpr int B_BYTES = BNH * BK * 2 * KC;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STG_BYTES = 8 * 4096;  // epilogue staging: 2 buffers of 32 rows per warp
+  static constexpr int STAGES = (200 * 1024 - STG_BYTES) / STAGE_BYTES > 8
+                                    ? 8
+                                    : (200 * 1024 - STG_BYTES) / STAGE_BYTES;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES;  // + barriers
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+  static_assert(BN % 32 == 0 && BNH % 16 == 0 && STAGE_BYTES % 1024 == 0, "pair tile shape");
+  static constexpr uint32_t IDESC = idesc_f16(2 * BM, BN, 0);
+};
+
+struct __align__(8) Gemm2Barriers {
+  uint64_t full[8];       // leader: both CTAs' loads of a stage landed
+  uint64_t empty[8];      // each CTA: the pair UMMAs reading its stage finished
+  uint64_t acc_full[2];   // each CTA: an accumulator is complete
+  uint64_t acc_empty[2];  // leader: both CTAs' epilogues have read an accumulator
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+template <int BN, int E, int KC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tma_a,
+                 const __grid_constant__ CUtensorMap tma_w,
+                 const __grid_constant__ CUtensorMap tma_c, const GemmArgs g) {
+  using C = Gemm2Cfg<BN, KC>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *stg = smem + STAGES * C::STAGE_BYTES;
+  Gemm2Barriers *bar = reinterpret_cast<Gemm2Barriers *>(stg + C::STG_BYTES);
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  const int num_m = (g.m + 2 * BM - 1) / (2 * BM);
+  const int num_n = (g.cols + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (g.k + BK * KC - 1) / (BK * KC);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar->full[s], 1);
+      mbar_init(&bar->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar->acc_full[b], 1);
+      mbar_init(&bar->acc_empty[b], 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(&bar->drain, 1);
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_w);
+    if (g.c_tma) prefetch_tmap(&tma_c);
+  }
+  // Both CTAs' barriers exist before either CTA signals one of the other's.
+  cluster_sync();
+  if (warp == 1) {
+    tmem_alloc_pair(&bar->tmem_base, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  const Abort ab{&bar->abort, g.err};
+
+  if (warp == 0) {
+    // ---- TMA producer (both CTAs): this CTA's rows of a and half of the W rows ---------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int m0 = (tile / num_n) * (2 * BM) + int(rank) * BM;
+        const int n0 = (tile % num_n) * BN + int(rank) * C::BNH;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bar->empty[stage], phase ^ 1u, ab, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + stage * C::STAGE_BYTES;
+          const uint32_t full = mapa_shared(&bar->full[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&bar->full[stage], 2 * C::STAGE_BYTES);
+          if constexpr (KC == 1) {
+            tma_load_2d_pair(sa, &tma_a, full, kb * BK, m0);
+            tma_load_2d_pair(sa + C::A_BYTES, &tma_w, full, kb * BK, n0);
+          } else {
+            tma_load_3d_pair(sa, &tma_a, full, 0, m0, kb * KC);
+            tma_load_3d_pair(sa + C::A_BYTES, &tma_w, full, 0, n0, kb * KC);
+          }
+          armed |= 1u << stage;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && leader) {
+        // Let the loads of every armed stage land (both CTAs' bytes count on these barriers).
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(armed & (1u << s))) continue;
+          const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&bar->full[s], par) && clock64() - t0 < kWaitCycles) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- UMMA issuer (leader only) -------------------------------------------------------------
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      const uint64_t d0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        if (!mbar_wait(&bar->acc_empty[acc], acc_phase ^ 1u, ab, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bar->full[stage], phase, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // Descriptors are linear in the start address (bits 0-13 hold address / 16).
+          const uint64_t da = d0 + uint64_t((stage * C::STAGE_BYTES) >> 4);
+          const uint64_t db = da + uint64_t(C::A_BYTES >> 4);
+#pragma unroll
+          for (int ks = 0; ks < KC * BK / 16; ++ks)
+            umma_f16_pair(d, da + uint64_t(((ks >> 2) * BM * 128 + (ks & 3) * 32) >> 4),
+                          db + uint64_t(((ks >> 2) * C::BNH * 128 + (ks & 3) * 32) >> 4),
+                          C::IDESC, (kb | ks) != 0);
+          issued = true;
+          umma_commit_pair(&bar->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&bar->acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_pair(&bar->drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&bar->drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {
+    // ---- epilogue (both CTAs): warps 2..5, one accumulator row per thread ---------------------
+    const uint32_t quarter = warp & 3u;
+    const int row_in_tile = int(rank) * BM + int(quarter * 32 + lane);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    if (g.c_tma) {
+      // Each warp stages 32 rows x 32 columns in shared memory (one row per thread, in the tensor
+      // map's swizzle, so the 32 threads' 16-byte writes spread over the banks) and one lane
+      // stores the box with TMA, coalesced and asynchronous; an epilogue that adds into c
+      // (residual) issues a TMA reduce-add instead, so c is never read into the SM.
+      constexpr bool resid = (E == kResidual || E == kGeluResidual);
+      uint8_t *sbuf = stg + (warp - 2) * 2 * 4096;
+      const int row_box = int(rank) * BM + int(quarter * 32);
+      int nbuf = 0;
+      // 32 values of this thread's row into the next staging buffer, then one lane stores (or
+      // reduce-adds) the warp's 32 x 32 box at column col, row row.
+      auto stage_store = [&](const float (&v)[32], int col, int row, bool reduce) {
+        uint8_t *buf = sbuf + nbuf * 4096;
+        if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+        __syncwarp();
+        if (g.c_f16) {
+          // 64-byte rows, 64-byte swizzle: 16-byte chunk c of row r at chunk c ^ ((r / 2) % 4).
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 q = make_uint4(pack_half2(v[8 * c], v[8 * c + 1]),
+                                       pack_half2(v[8 * c + 2], v[8 * c + 3]),
+                                       pack_half2(v[8 * c + 4], v[8 * c + 5]),
+                                       pack_half2(v[8 * c + 6], v[8 * c + 7]));
+            *reinterpret_cast<uint4 *>(buf + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)) = q;
+          }
+        } else {
+          // 128-byte rows, 128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8).
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4 *>(buf + lane * 128 + ((c ^ (lane & 7)) * 16)) =
+                make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (reduce) {
+            tma_reduce_add_2d(&tma_c, buf, col, row);
+          } else {
+            tma_store_2d(&tma_c, buf, col, row);
+          }
+          bulk_commit();
+        }
+        nbuf ^= 1;
+      };
+      for (int tile = pair; tile < tiles; tile += npairs) {
+        const int m0 = (tile / num_n) * (2 * BM), n0 = (tile % num_n) * BN;
+        if (!mbar_wait(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          const int col0 = n0 + chunk * 32;
+          if (col0 >= g.cols) break;
+          uint32_t r[32];
+          tmem_ld32(tmem + ((quarter * 32u) << 16) + uint32_t(acc * BN + chunk * 32), r);
+          float b[32];
+          load_bias32(g.bias + col0, min(32, g.cols - col0), b);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = __uint_as_float(r[j]) + b[j];
+            v[j] = E == kResidual ? g.alpha * x : E == kGeluResidual ? gelu_f(x) : epi<E>(x, 0.0f, g.alpha);
+          }
+          stage_store(v, col0, m0 + row_box, resid);
+          if (col0 < g.dual) {
+            // The dual copy (a bias longer than the rows): plain bias, columns cols + col0...
+            load_bias32(g.bias + g.cols + col0, min(32, g.dual - col0), b);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + b[j];
+            stage_store(v, g.cols + col0, m0 + row_box, false);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(&bar->acc_empty[acc], 0));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
+    } else
+    for (int tile = pair; tile < tiles; tile += npairs) {
+      const int m0 = (tile / num_n) * (2 * BM), n0 = (tile % num_n) * BN;
+      if (!mbar_wait(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+      tc_fence_after();
+      const long long row = m0 + row_in_tile;
+      const bool row_ok = row < g.m;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        const int col0 = n0 + chunk * 32;
+        if (col0 >= g.cols) break;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((quarter * 32u) << 16) + uint32_t(acc * BN + chunk * 32), r);
+        const int lim = min(32, g.cols - col0);
+        float b[32];
+        load_bias32(g.bias + col0, lim, b);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (row_ok) store_row32<E>(g, row, col0, lim, v, b);
+        if (col0 < g.dual) {
+          const int lim2 = min(lim, g.dual - col0);
+          load_bias32(g.bias + g.cols + col0, lim2, b);
+          if (row_ok) store_row32<kBias>(g, row, g.cols + col0, lim2, v, b);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(&bar->acc_empty[acc], 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  // Both CTAs' epilogues have read their accumulators and every pair UMMA has completed before
+  // the columns are released; neither CTA leaves while the other may still signal its barriers.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  cluster_sync();
+}
+
 // f32 rows to f16 rows, zero padded to ld_out columns.
 __global__ void cast_rows_kernel(const float *__restrict__ in, long long ld_in,
                                  __half *__restrict__ out, long long ld_out, int rows, int cols) {
@@ -332,39 +660,116 @@ __global__ void cast_rows_kernel(const float *__restrict__ in, long long ld_in,
   }
 }
 
-template <int BN, int E>
+template <int BN, int E, int KC>
 cudaError_t launch_bn_e(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int grid,
                         cudaStream_t s) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, KC>;
   const size_t smem = 1024 + C::STAGES * C::STAGE_BYTES + sizeof(GemmBarriers);
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[64] = {};
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, E>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, E, KC>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  gemm_kernel<BN, E><<<grid, kGemmThreads, smem, s>>>(a, w, g);
+  gemm_kernel<BN, E, KC><<<grid, kGemmThreads, smem, s>>>(a, w, g);
   return cudaGetLastError();
 }
 
-template <int BN>
+template <int BN, int KC>
 cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int grid,
                       cudaStream_t s) {
   switch (g.epilogue) {
-    case kBias: return launch_bn_e<BN, kBias>(a, w, g, grid, s);
-    case kSilu: return launch_bn_e<BN, kSilu>(a, w, g, grid, s);
-    case kRelu: return launch_bn_e<BN, kRelu>(a, w, g, grid, s);
-    case kResidual: return launch_bn_e<BN, kResidual>(a, w, g, grid, s);
-    case kGelu: return launch_bn_e<BN, kGelu>(a, w, g, grid, s);
-    case kGeluResidual: return launch_bn_e<BN, kGeluResidual>(a, w, g, grid, s);
-    default: return launch_bn_e<BN, kTanh>(a, w, g, grid, s);
+    case kBias: return launch_bn_e<BN, kBias, KC>(a, w, g, grid, s);
+    case kSilu: return launch_bn_e<BN, kSilu, KC>(a, w, g, grid, s);
+    case kRelu: return launch_bn_e<BN, kRelu, KC>(a, w, g, grid, s);
+    case kResidual: return launch_bn_e<BN, kResidual, KC>(a, w, g, grid, s);
+    case kGelu: return launch_bn_e<BN, kGelu, KC>(a, w, g, grid, s);
+    case kGeluResidual: return launch_bn_e<BN, kGeluResidual, KC>(a, w, g, grid, s);
+    default: return launch_bn_e<BN, kTanh, KC>(a, w, g, grid, s);
+  }
+}
+
+template <int BN, int E, int KC>
+cudaError_t launch2_bn_e(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &c,
+                         const GemmArgs &g, int pairs, cudaStream_t s) {
+  using C = Gemm2Cfg<BN, KC>;
+  const size_t smem = C::SMEM + sizeof(Gemm2Barriers);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<BN, E, KC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  gemm2_kernel<BN, E, KC><<<2 * pairs, kGemmThreads, smem, s>>>(a, w, c, g);
+  return cudaGetLastError();
+}
+
+template <int BN, int KC>
+cudaError_t launch2_bn(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &c,
+                       const GemmArgs &g, int pairs, cudaStream_t s) {
+  switch (g.epilogue) {
+    case kBias: return launch2_bn_e<BN, kBias, KC>(a, w, c, g, pairs, s);
+    case kSilu: return launch2_bn_e<BN, kSilu, KC>(a, w, c, g, pairs, s);
+    case kRelu: return launch2_bn_e<BN, kRelu, KC>(a, w, c, g, pairs, s);
+    case kResidual: return launch2_bn_e<BN, kResidual, KC>(a, w, c, g, pairs, s);
+    case kGelu: return launch2_bn_e<BN, kGelu, KC>(a, w, c, g, pairs, s);
+    case kGeluResidual: return launch2_bn_e<BN, kGeluResidual, KC>(a, w, c, g, pairs, s);
+    default: return launch2_bn_e<BN, kTanh, KC>(a, w, c, g, pairs, s);
   }
 }
 
 }  // namespace
+
+int gemm2_pick_bn(int m, int cols, int num_sms) {
+  // Waves of pair tiles times the tile width, over the relative rate of a wave: a tile of 128
+  // columns still waits on its loads (24 KB per k-block against 260 cycles of UMMAs).
+  const int mt = (m + 2 * BM - 1) / (2 * BM);
+  const int pairs = num_sms / 2;
+  auto cost = [&](int bn, double eff) {
+    const long long tiles = (long long)mt * ((cols + bn - 1) / bn);
+    const long long waves = (tiles + pairs - 1) / pairs;
+    return double(waves * bn) / eff;
+  };
+  int best = 256;
+  double c = cost(256, 1.0);
+  const int cand[3] = {192, 160, 128};
+  const double eff[3] = {1.0, 1.0, 0.87};
+  for (int i = 0; i < 3; ++i) {
+    const double ci = cost(cand[i], eff[i]);
+    if (ci < c) {
+      c = ci;
+      best = cand[i];
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_gemm2(const CUtensorMap &a, const CUtensorMap &w_half, const CUtensorMap &tma_c,
+                         const GemmArgs &g, int bn, int kc, int num_sms, cudaStream_t s) {
+  const int tiles = ((g.m + 2 * BM - 1) / (2 * BM)) * ((g.cols + bn - 1) / bn);
+  const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  if (pairs <= 0) return cudaSuccess;
+  if (kc == 2) {
+    switch (bn) {
+      case 128: return launch2_bn<128, 2>(a, w_half, tma_c, g, pairs, s);
+      case 160: return launch2_bn<160, 2>(a, w_half, tma_c, g, pairs, s);
+      case 192: return launch2_bn<192, 2>(a, w_half, tma_c, g, pairs, s);
+      default: return launch2_bn<256, 2>(a, w_half, tma_c, g, pairs, s);
+    }
+  }
+  switch (bn) {
+    case 128: return launch2_bn<128, 1>(a, w_half, tma_c, g, pairs, s);
+    case 160: return launch2_bn<160, 1>(a, w_half, tma_c, g, pairs, s);
+    case 192: return launch2_bn<192, 1>(a, w_half, tma_c, g, pairs, s);
+    default: return launch2_bn<256, 1>(a, w_half, tma_c, g, pairs, s);
+  }
+}
 
 int gemm_pick_bn(int m, int cols, int num_sms) {
   // Waves of tiles times the tile width: the cost of the last, partial wave included. The wider
@@ -382,19 +787,17 @@ int gemm_pick_bn(int m, int cols, int num_sms) {
   return c160 <= c128 ? 160 : 128;
 }
 
-size_t gemm_smem_bytes(int bn) {
-  if (bn == 160) return 1024 + GemmCfg<160>::STAGES * GemmCfg<160>::STAGE_BYTES + sizeof(GemmBarriers);
-  return bn == 256 ? 1024 + GemmCfg<256>::STAGES * GemmCfg<256>::STAGE_BYTES + sizeof(GemmBarriers)
-                   : 1024 + GemmCfg<128>::STAGES * GemmCfg<128>::STAGE_BYTES + sizeof(GemmBarriers);
-}
-
 cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int bn,
-                        int num_sms, cudaStream_t s) {
+                        int kc, int num_sms, cudaStream_t s) {
   const int tiles = ((g.m + BM - 1) / BM) * ((g.cols + bn - 1) / bn);
   const int grid = tiles < num_sms ? tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
-  if (bn == 160) return launch_bn<160>(a, w, g, grid, s);
-  return bn == 256 ? launch_bn<256>(a, w, g, grid, s) : launch_bn<128>(a, w, g, grid, s);
+  if (kc == 2) {
+    if (bn == 160) return launch_bn<160, 2>(a, w, g, grid, s);
+    return bn == 256 ? launch_bn<256, 2>(a, w, g, grid, s) : launch_bn<128, 2>(a, w, g, grid, s);
+  }
+  if (bn == 160) return launch_bn<160, 1>(a, w, g, grid, s);
+  return bn == 256 ? launch_bn<256, 1>(a, w, g, grid, s) : launch_bn<128, 1>(a, w, g, grid, s);
 }
 
 cudaError_t launch_cast_rows(const float *in, long long ld_in, __half *out, long long ld_out,

@@ -26,15 +26,26 @@ struct GemmArgs {
   int epilogue;
   float alpha;
   int *err;           // device error word
+  int c_tma;          // pair GEMM: store c through the tensor map tma_c (no dual outputs; f32 when
+                      // the epilogue adds into c: a TMA reduce-add)
 };
 
 constexpr int kGemmBM = 128, kGemmBK = 64;
 constexpr int kGemmThreads = 192;
-// Tile width (128 or 256) for an m x cols output on num_sms SMs; the W tensor map's box height.
+// kc: 64-column K chunks per pipeline stage. kc = 1 takes 2D tensor maps with boxes {64, rows};
+// kc = 2 takes 3D maps {64, rows, k / 64} (k a multiple of 64, chunk stride 128 bytes) with boxes
+// {64, rows, 2}. Tile width (128, 160 or 256) for an m x cols output on num_sms SMs; the W tensor
+// map's box height.
 int gemm_pick_bn(int m, int cols, int num_sms);
-size_t gemm_smem_bytes(int bn);
 cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int bn,
-                        int num_sms, cudaStream_t s);
+                        int kc, int num_sms, cudaStream_t s);
+// The pair GEMM (a cluster of two CTAs shares each UMMA of M=256): tile width BN (128, 160, 192
+// or 256) for an m x cols output; a's box height is 128 and W's BN / 2.
+int gemm2_pick_bn(int m, int cols, int num_sms);
+// tma_c (with g.c_tma): c as a 2D tensor {cols, m}, boxes {32, 32}, 128-byte swizzle for f32 and
+// 64-byte swizzle for f16.
+cudaError_t launch_gemm2(const CUtensorMap &a, const CUtensorMap &w_half, const CUtensorMap &tma_c,
+                         const GemmArgs &g, int bn, int kc, int num_sms, cudaStream_t s);
 
 // f32 rows -> f16 rows (round to nearest even), into a padded row stride; columns past `cols`
 // up to `ld_out` are zeroed.

@@ -44,6 +44,11 @@ struct wavo_linear {
   float *d8 = nullptr;       // [n][k/32] scales (Q8_0)
   float *bias = nullptr;     // max(n, cols + dual) floats
   CUtensorMap map_w128, map_w160, map_w256;  // W tiles of 128, 160 and 256 rows
+  // The pair GEMM's half tiles (64, 80, 96 rows; 128 is map_w128), 2D and, when k is a multiple
+  // of 64, 3D boxes of two 64-column chunks.
+  CUtensorMap map_h64, map_h80, map_h96;
+  CUtensorMap map3_h64, map3_h80, map3_h96;
+  bool has3 = false;
 };
 
 struct wavo_graph {
@@ -102,6 +107,15 @@ EncodeTiled encoder() {
   return fn;
 }
 
+// A 3D f16 view {64, rows, cols / 64} of rows x cols (row stride ld elements; cols a multiple of
+// 64; chunk c = columns 64c..): boxes {64, box_rows, 2}, two 64-column chunks per TMA load.
+bool make_map3(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
+               uint32_t box_rows);
+
+// The pair GEMM's output map: rows x cols of f16 or f32 (row stride ld elements), boxes of 32 x 32,
+// swizzle matching the epilogue's staging (64-byte rows for f16, 128-byte rows for f32).
+bool make_map_c(CUtensorMap *m, void *base, bool f16, uint64_t cols, uint64_t rows, uint64_t ld);
+
 // A 2D f16 tensor map over rows x cols (row stride ld elements), 64-column x box_rows boxes,
 // 128-byte swizzle, zero fill outside.
 bool make_map(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
@@ -116,6 +130,36 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, ui
   cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_map3(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
+               uint32_t box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15u) || cols % 64 || rows == 0)
+    return false;
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {ld * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_map_c(CUtensorMap *m, void *base, bool f16, uint64_t cols, uint64_t rows, uint64_t ld) {
+  EncodeTiled enc = encoder();
+  const uint64_t es = f16 ? 2 : 4;
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * es) & 15u) || rows == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * es};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base,
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             f16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -394,10 +438,14 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
     return cuda_fail(ctx, e, "linear upload");
   }
   if (!make_map(&l->map_w128, l->w16, k, n, k, 128) || !make_map(&l->map_w160, l->w16, k, n, k, 160) ||
-      !make_map(&l->map_w256, l->w16, k, n, k, 256)) {
+      !make_map(&l->map_w256, l->w16, k, n, k, 256) || !make_map(&l->map_h64, l->w16, k, n, k, 64) ||
+      !make_map(&l->map_h80, l->w16, k, n, k, 80) || !make_map(&l->map_h96, l->w16, k, n, k, 96)) {
     wavo_linear_destroy(l);
     return fail(ctx, WAVO_ECUDA, "linear: tensor map");
   }
+  l->has3 = k % 64 == 0 && make_map3(&l->map3_h64, l->w16, k, n, k, 64) &&
+            make_map3(&l->map3_h80, l->w16, k, n, k, 80) &&
+            make_map3(&l->map3_h96, l->w16, k, n, k, 96);
   *out = l;
   return WAVO_OK;
 }
@@ -453,9 +501,6 @@ wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, c
     a16 = static_cast<const __half *>(ws);
     lda16 = l->k;
   }
-  CUtensorMap map_a;
-  if (!make_map(&map_a, a16, l->k, m, lda16, wv::kGemmBM))
-    return fail(ctx, WAVO_ECUDA, "gemm: tensor map of a");
   wv::GemmArgs ga;
   ga.m = int(m);
   ga.cols = int(l->cols);
@@ -468,9 +513,34 @@ wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, c
   ga.epilogue = epilogue;
   ga.alpha = alpha;
   ga.err = ctx->dev_err;
+  ga.c_tma = 0;
+  CUtensorMap map_a;
+  if (m > uint32_t(wv::kGemmBM)) {
+    // Two or more row tiles: the pair GEMM (a CTA pair shares each UMMA of M=256).
+    const int bn = wv::gemm2_pick_bn(int(m), int(l->cols), ctx->sms);
+    const int kc = (l->has3 && bn <= 192) ? 2 : 1;
+    const bool ok_a = kc == 2 ? make_map3(&map_a, a16, l->k, m, lda16, wv::kGemmBM)
+                              : make_map(&map_a, a16, l->k, m, lda16, wv::kGemmBM);
+    if (!ok_a) return fail(ctx, WAVO_ECUDA, "gemm: tensor map of a");
+    const CUtensorMap &mw = kc == 2 ? (bn == 128 ? l->map3_h64 : bn == 160 ? l->map3_h80 : l->map3_h96)
+                                    : (bn == 128 ? l->map_h64 : bn == 160 ? l->map_h80
+                                       : bn == 192 ? l->map_h96 : l->map_w128);
+    // c through TMA stores (reduce-adds for the residual epilogues, which need f32 c), when c is
+    // 16-byte aligned and every 32-column box stays inside one output region.
+    const bool resid = epilogue == WAVO_EPI_RESIDUAL || epilogue == WAVO_EPI_GELU_RESIDUAL;
+    const bool f16 = c_dtype == WAVO_F16;
+    CUtensorMap map_c = map_a;
+    if ((!resid || !f16) && (!l->dual || (!resid && l->cols % 32 == 0 && l->dual % 32 == 0)) &&
+        make_map_c(&map_c, c, f16, l->cols + l->dual, m, ldc))
+      ga.c_tma = 1;
+    CK(wv::launch_gemm2(map_a, mw, map_c, ga, bn, kc, ctx->sms, ctx->stream), "gemm launch");
+    return WAVO_OK;
+  }
+  if (!make_map(&map_a, a16, l->k, m, lda16, wv::kGemmBM))
+    return fail(ctx, WAVO_ECUDA, "gemm: tensor map of a");
   const int bn = wv::gemm_pick_bn(int(m), int(l->cols), ctx->sms);
   const CUtensorMap &mw = bn == 256 ? l->map_w256 : bn == 160 ? l->map_w160 : l->map_w128;
-  CK(wv::launch_gemm(map_a, mw, ga, bn, ctx->sms, ctx->stream),
+  CK(wv::launch_gemm(map_a, mw, ga, bn, 1, ctx->sms, ctx->stream),
      "gemm launch");
   return WAVO_OK;
 }
