@@ -139,6 +139,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   const Abort ab{&bar->abort, a.err};
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   const int hoff = h * a.head_stride;
 
   if (warp == 0) {
@@ -455,8 +457,7 @@ cudaError_t launch_one(const CUtensorMap &q, const CUtensorMap &kv, const CUtens
     configured = true;
   }
   dim3 grid((max_len + BM - 1) / BM, a.heads, nseg);
-  attn_kernel<HD, REL><<<grid, kAttnThreads, smem, s>>>(q, kv, pos, a);
-  return cudaGetLastError();
+  return launch_pdl(attn_kernel<HD, REL>, grid, dim3(kAttnThreads), smem, s, q, kv, pos, a);
 }
 
 }  // namespace

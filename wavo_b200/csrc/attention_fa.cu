@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   const Abort ab{&bar->abort, a.err};
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   const int hoff = h * a.head_stride;
 
   if (warp == 0) {
@@ -465,8 +467,7 @@ cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const AttnArg
     configured[dev] = true;
   }
   dim3 grid((max_len + NT * BM - 1) / (NT * BM), a.heads, nseg);
-  fa_kernel<HD, BN><<<grid, THREADS, smem, s>>>(q, kv, a);
-  return cudaGetLastError();
+  return launch_pdl(fa_kernel<HD, BN>, grid, dim3(THREADS), smem, s, q, kv, a);
 }
 
 }  // namespace

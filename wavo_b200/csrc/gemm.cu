@@ -180,6 +180,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   const Abort ab{&bar->abort, g.err};
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
 
   if (warp == 0) {
     // ---- TMA producer --------------------------------------------------------------------
@@ -410,6 +412,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   const Abort ab{&bar->abort, g.err};
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
 
   if (warp == 0) {
     // ---- TMA producer (both CTAs): this CTA's rows of a and half of the W rows ---------------
@@ -674,8 +678,7 @@ cudaError_t launch_bn_e(const CUtensorMap &a, const CUtensorMap &w, const GemmAr
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  gemm_kernel<BN, E, KC><<<grid, kGemmThreads, smem, s>>>(a, w, g);
-  return cudaGetLastError();
+  return launch_pdl(gemm_kernel<BN, E, KC>, dim3(grid), dim3(kGemmThreads), smem, s, a, w, g);
 }
 
 template <int BN, int KC>
@@ -706,8 +709,8 @@ cudaError_t launch2_bn_e(const CUtensorMap &a, const CUtensorMap &w, const CUten
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  gemm2_kernel<BN, E, KC><<<2 * pairs, kGemmThreads, smem, s>>>(a, w, c, g);
-  return cudaGetLastError();
+  return launch_pdl(gemm2_kernel<BN, E, KC>, dim3(2 * pairs), dim3(kGemmThreads), smem, s, a, w, c,
+                    g);
 }
 
 template <int BN, int KC>

@@ -7,7 +7,28 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace wv {
+
+// Launches `kernel` with programmatic stream serialization: it may begin (and set itself up) while
+// the previous kernel of the stream is still running; the kernel itself waits for that grid
+// (griddepcontrol.wait) before it touches any data. Only kernels that do so are launched here.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Epilogue modes, the reference's `Epilogue` (src/gpu/mod.rs:431-456) in its kernel order.
 enum Epi : int { kBias = 0, kSilu, kRelu, kResidual, kGelu, kGeluResidual, kTanh };

@@ -350,6 +350,20 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start while the previous kernel of the stream still runs. It sets itself up (barriers, TMEM,
+// tensor-map prefetch), lets its own dependents be scheduled, then waits for the previous grid to
+// complete (its writes visible) before it touches any data that grid may write or read.
+// ------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------------------
 // CTA pairs (a cluster of 2 on neighbouring SMs): one UMMA of M=256 spans both SMs' tensor cores,
 // each CTA holding half of A (its 128 rows) and half of B (N/2 rows) in its own shared memory.
 // TMA loads here never use multicast: each CTA loads its own halves; only the tx-count completion
