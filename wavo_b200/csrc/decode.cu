@@ -326,6 +326,259 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+
+// Split-K form for the bias and residual epilogues: a CTA takes 64 output features and a range of
+// k; its W tile goes to shared memory once (as f32: W f16 exact, Q8_0 as q·d exact); lane r of a
+// warp is row r and holds 32 of its k values of a in registers, reused over the warp's 8 features
+// (each W value a shared-memory broadcast). Partial sums go to c with f32 atomics: c += alpha ·
+// (sum + bias) for the residual epilogue; for the bias epilogue c is cleared first and gets
+// sum + bias. (The full-k kernel above re-reads the rows of a for every feature.)
+constexpr int GS_F = 64;   // features per CTA
+constexpr int GS_KC = 32;  // k per register chunk
+
+template <int WT>
+__global__ void __launch_bounds__(256)
+    gemv_split_kernel(const float *__restrict__ a, long long lda, const void *__restrict__ w,
+                      const float *__restrict__ scales, const float *__restrict__ bias,
+                      float *__restrict__ c, long long ldc, int rows, int n, int k, int kr,
+                      int epi, float alpha) {
+  extern __shared__ float4 ws4[];
+  float *ws = reinterpret_cast<float *>(ws4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f0 = blockIdx.x * GS_F, k0 = blockIdx.y * kr;
+  const int kn = min(kr, k - k0);  // a multiple of 32 (k and kr are)
+  // W tile [64][kr] as f32: every load of the tile in flight at once (one memory latency), then
+  // the conversions and shared-memory stores.
+  constexpr int IT = GS_F * 256 / (256 * 8);  // loads of 8 values per thread (kr <= 256)
+  float wf[IT][8];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int i = (it * 256 + threadIdx.x) * 8;
+    const int f = i / kr, kk = i - f * kr;
+    if (i < GS_F * kr && f0 + f < n && kk < kn) {
+      load_w8<WT>(w, scales, f0 + f, k, k0 + kk, wf[it]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wf[it][j] = 0.0f;
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int i = (it * 256 + threadIdx.x) * 8;
+    if (i < GS_F * kr) {
+      *reinterpret_cast<float4 *>(ws + i) = make_float4(wf[it][0], wf[it][1], wf[it][2], wf[it][3]);
+      *reinterpret_cast<float4 *>(ws + i + 4) =
+          make_float4(wf[it][4], wf[it][5], wf[it][6], wf[it][7]);
+    }
+  }
+  __syncthreads();
+  float acc[8];
+#pragma unroll
+  for (int f = 0; f < 8; ++f) acc[f] = 0.0f;
+  const bool live = lane < rows;
+  const float *arow = a + (long long)lane * lda + k0;
+  for (int kc = 0; kc < kn; kc += GS_KC) {
+    float av[GS_KC];
+#pragma unroll
+    for (int j = 0; j < GS_KC; j += 4) {
+      const float4 t = live ? *reinterpret_cast<const float4 *>(arow + kc + j)
+                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      av[j] = t.x;
+      av[j + 1] = t.y;
+      av[j + 2] = t.z;
+      av[j + 3] = t.w;
+    }
+#pragma unroll
+    for (int f = 0; f < 8; ++f) {
+      const float *wr = ws + (warp * 8 + f) * kr + kc;
+      float sacc = acc[f];
+#pragma unroll
+      for (int j = 0; j < GS_KC; j += 4) {
+        const float4 wv = *reinterpret_cast<const float4 *>(wr + j);
+        sacc = fmaf(av[j], wv.x, sacc);
+        sacc = fmaf(av[j + 1], wv.y, sacc);
+        sacc = fmaf(av[j + 2], wv.z, sacc);
+        sacc = fmaf(av[j + 3], wv.w, sacc);
+      }
+      acc[f] = sacc;
+    }
+  }
+  if (!live) return;
+#pragma unroll
+  for (int f = 0; f < 8; ++f) {
+    const int feat = f0 + warp * 8 + f;
+    if (feat >= n) break;
+    float v = acc[f];
+    if (blockIdx.y == 0) v += bias[feat];
+    atomicAdd(c + (long long)lane * ldc + feat, epi == kResidual ? alpha * v : v);
+  }
+}
+
+
+// ---- gemv on the tensor core (F16 weights) -------------------------------------------------
+//
+// The rows of a (at most 32) in f32 are split exactly enough for f32 accuracy: a = hi + lo with
+// hi = f16(a), lo = f16(a - hi) (|a - hi - lo| <= 2^-22 |a|). One UMMA tile of M = 128 rows holds
+// hi in rows 0-31 and lo in rows 32-63 (rows 64-127 zero), so D rows r and r + 32 are hi·W^T and
+// lo·W^T with W exact in f16 and f32 accumulation — the reference's gemv (W not rounded, f32
+// sums) to within f32 rounding. A CTA takes 128 features and a range of k (split-K for about one
+// CTA per SM); W comes by TMA, the partial sums go to c with vector f32 reductions.
+constexpr int GT_N = 128;      // features per CTA (UMMA N)
+constexpr int GT_KMAX = 256;   // k per CTA
+
+struct __align__(8) GtBarriers {
+  uint64_t w_full;
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(128, 1)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const float *__restrict__ a,
+                   long long lda, const float *__restrict__ bias, float *__restrict__ c,
+                   long long ldc, int rows, int n, int k, int kr, int epi, float alpha, int vec,
+                   int *err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const int nch = kr / 64;  // 64-column chunks of k
+  uint8_t *sa = smem;                  // [nch][128 rows][128 B], 128-byte swizzle
+  uint8_t *sw = smem + nch * 16384;    // [nch][128 features][128 B]
+  GtBarriers *bar = reinterpret_cast<GtBarriers *>(sw + nch * 16384);
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const int f0 = blockIdx.x * GT_N, k0 = blockIdx.y * kr;
+  const int kn = min(kr, k - k0);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->w_full, 1);
+    mbar_init(&bar->mma_done, 1);
+    bar->abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&map_w);
+  }
+  if (warp == 0) {
+    tmem_alloc(&bar->tmem_base, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  const Abort ab{&bar->abort, err};
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar->w_full, nch * 16384);
+    for (int ch = 0; ch < nch; ++ch)
+      tma_load_2d(sw + ch * 16384, &map_w, &bar->w_full, k0 + ch * 64, f0);
+  }
+  // The A tile: thread t builds row t.
+  {
+    const int r = threadIdx.x;
+    const int src = r < 32 ? r : r - 32;
+    const bool live = r < 64 && src < rows;
+    const float *arow = a + (long long)src * lda + k0;
+    for (int ch = 0; ch < nch; ++ch) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kk = ch * 64 + u * 8;
+        float x[8];
+        if (live && kk < kn) {
+          const float4 p = *reinterpret_cast<const float4 *>(arow + kk);
+          const float4 q = *reinterpret_cast<const float4 *>(arow + kk + 4);
+          x[0] = p.x; x[1] = p.y; x[2] = p.z; x[3] = p.w;
+          x[4] = q.x; x[5] = q.y; x[6] = q.z; x[7] = q.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = 0.0f;
+        }
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float x0 = x[2 * j], x1 = x[2 * j + 1];
+          if (r >= 32) {  // the low part: what f16 rounding of a left out
+            x0 -= __half2float(__float2half_rn(x0));
+            x1 -= __half2float(__float2half_rn(x1));
+          }
+          h[j] = pack_half2(x0, x1);
+        }
+        *reinterpret_cast<uint4 *>(sa + ch * 16384 + r * 128 + ((u ^ (r & 7)) * 16)) =
+            make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  bool ok = true;
+  if (threadIdx.x == 0) {
+    ok = mbar_wait(&bar->w_full, 0, ab, kErrTimeoutMma);
+    if (ok) {
+      tc_fence_after();
+      const uint64_t da = sdesc_sw128(smem_u32(sa), 16, 1024);
+      const uint64_t dw = sdesc_sw128(smem_u32(sw), 16, 1024);
+      constexpr uint32_t IDESC = idesc_f16(128, GT_N, 0);
+      for (int st = 0; st < kr / 16; ++st) {
+        const uint64_t off = uint64_t(((st >> 2) * 16384 + (st & 3) * 32) >> 4);
+        umma_f16(tmem, da + off, dw + off, IDESC, st > 0 ? 1u : 0u);
+      }
+      umma_commit(&bar->mma_done);
+    }
+  }
+  ok = mbar_wait(&bar->mma_done, 0, ab, kErrTimeoutConsumer);
+  tc_fence_after();
+  // lo (TMEM lanes 32-63) into shared memory (the A tile is no longer read), then hi + lo.
+  float *dlo = reinterpret_cast<float *>(sa);  // [32 rows][129]
+  if (ok && warp == 1) {
+#pragma unroll 1
+    for (int q = 0; q < GT_N / 32; ++q) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((32u) << 16) + q * 32, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) dlo[lane * 129 + q * 32 + j] = __uint_as_float(v[j]);
+    }
+  }
+  __syncthreads();
+  if (ok && warp == 0) {
+    const bool live = int(lane) < rows;
+    float *crow = c + (long long)lane * ldc;
+#pragma unroll 1
+    for (int q = 0; q < GT_N / 32; ++q) {
+      uint32_t v[32];
+      tmem_ld32(tmem + q * 32, v);
+      tmem_wait_ld();
+      const int fb = f0 + q * 32;
+      float y[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float t = __uint_as_float(v[j]) + dlo[lane * 129 + q * 32 + j];
+        if (blockIdx.y == 0 && fb + j < n) t += bias[fb + j];
+        y[j] = epi == kResidual ? alpha * t : t;
+      }
+      if (live) {
+        if (vec && fb + 32 <= n) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) red_add_v4(crow + fb + j, y[j], y[j + 1], y[j + 2], y[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (fb + j < n) atomicAdd(crow + fb + j, y[j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
 }  // namespace
 
 cudaError_t launch_pack_cache(const float *x, long long src, long long stride, uint32_t *cache,
@@ -382,6 +635,40 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
                         const float *scales, const float *bias, float *c, long long ldc, int rows,
                         int n, int k, int epilogue, float alpha, cudaStream_t s) {
   if (rows <= 0 || n <= 0) return cudaSuccess;
+  if ((epilogue == kBias || epilogue == kResidual) && k % 32 == 0 && lda % 4 == 0) {
+    // Split-K: about two CTAs per SM over the feature groups and k ranges.
+    const int groups = (n + GS_F - 1) / GS_F;
+    int ks = (2 * 148 + groups - 1) / groups;
+    ks = ks < 1 ? 1 : (ks > k / 32 ? k / 32 : ks);
+    int kr = (k + ks - 1) / ks;
+    kr = (kr + 31) / 32 * 32;
+    if (kr > 256) kr = 256;  // 64 KB of W tile
+    ks = (k + kr - 1) / kr;
+    const size_t smem = size_t(GS_F) * kr * 4;
+    if (epilogue == kBias) {
+      cudaError_t e = cudaMemset2DAsync(c, size_t(ldc) * 4, 0, size_t(n) * 4, rows, s);
+      if (e != cudaSuccess) return e;
+    }
+    static bool configured[3][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int wi = wtype == 1 ? 0 : wtype == 0 ? 1 : 2;
+    if (dev < 64 && !configured[wi][dev]) {
+      cudaError_t e = wtype == 1 ? cudaFuncSetAttribute(gemv_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536)
+                      : wtype == 0 ? cudaFuncSetAttribute(gemv_split_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536)
+                                   : cudaFuncSetAttribute(gemv_split_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536);
+      if (e != cudaSuccess) return e;
+      configured[wi][dev] = true;
+    }
+    const dim3 grid(groups, ks);
+    if (wtype == 1)
+      gemv_split_kernel<1><<<grid, 256, smem, s>>>(a, lda, w, scales, bias, c, ldc, rows, n, k, kr, epilogue, alpha);
+    else if (wtype == 0)
+      gemv_split_kernel<0><<<grid, 256, smem, s>>>(a, lda, w, scales, bias, c, ldc, rows, n, k, kr, epilogue, alpha);
+    else
+      gemv_split_kernel<8><<<grid, 256, smem, s>>>(a, lda, w, scales, bias, c, ldc, rows, n, k, kr, epilogue, alpha);
+    return cudaGetLastError();
+  }
   const int grid = (n + 7) / 8;
   if (wtype == 1)
     gemv_kernel<1><<<grid, 256, 0, s>>>(a, lda, w, scales, bias, c, ldc, rows, n, k, epilogue, alpha);
@@ -389,6 +676,37 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
     gemv_kernel<0><<<grid, 256, 0, s>>>(a, lda, w, scales, bias, c, ldc, rows, n, k, epilogue, alpha);
   else
     gemv_kernel<8><<<grid, 256, 0, s>>>(a, lda, w, scales, bias, c, ldc, rows, n, k, epilogue, alpha);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map_w128,
+                           const float *bias, float *c, long long ldc, int rows, int n, int k,
+                           int epilogue, float alpha, int *err, cudaStream_t s) {
+  if (rows <= 0 || n <= 0) return cudaSuccess;
+  const int tiles = (n + GT_N - 1) / GT_N;
+  int ks = 148 / tiles;
+  if (ks < 1) ks = 1;
+  int kr = (k + ks - 1) / ks;
+  kr = (kr + 63) / 64 * 64;
+  if (kr > GT_KMAX) kr = GT_KMAX;
+  ks = (k + kr - 1) / kr;
+  if (epilogue == kBias) {
+    cudaError_t e = cudaMemset2DAsync(c, size_t(ldc) * 4, 0, size_t(n) * 4, rows, s);
+    if (e != cudaSuccess) return e;
+  }
+  const size_t smem = 1024 + size_t(kr / 64) * 2 * 16384 + sizeof(GtBarriers);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(1024 + 8 * 16384 + sizeof(GtBarriers)));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int vec = (reinterpret_cast<uintptr_t>(c) % 16 == 0) && (ldc % 4 == 0);
+  gemv_tc_kernel<<<dim3(tiles, ks), 128, smem, s>>>(map_w128, a, lda, bias, c, ldc, rows, n, k, kr,
+                                                   epilogue, alpha, vec, err);
   return cudaGetLastError();
 }
 
