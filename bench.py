@@ -162,7 +162,7 @@ class Workload:
 class C2(Workload):
     """Whisper large-v3-turbo encoder self-attention, 32 layers, batch 1, T=1500."""
     T, D, H, LAYERS = 1500, 1280, 20, 32
-    TRAFFIC = {"attention": 11578368 + 256, "gemm_qkv": 13716992, "gemm_out": 14840576}
+    TRAFFIC = {"attention": 11562240, "gemm_qkv": 13730560, "gemm_out": 14854400}
 
     def __init__(self, gpu, rank, world, seed=2000):
         import torch
@@ -379,7 +379,7 @@ RelPosWorkload.cpu = staticmethod(
 
 class C5(RelPosWorkload):
     scaling = "strong"
-    TRAFFIC = {"attention": 697848832 + 162365696}
+    TRAFFIC = {"attention": 697688320 + 163500288, "gemm_qkv": 180414720 + 644850432}
 
     def __init__(self, gpu, rank, world, seed=5000):
         super().__init__(gpu, rank, world, segment_lengths(seed, 400, 120, 300), 24, "q8_0", seed)
@@ -498,7 +498,7 @@ class C4(Workload):
     D, H, LAYERS, FRAMES, CONTEXT, STEPS, BATCH = 1280, 20, 4, 1500, 448, 224, 32
     scaling = "strong"
     bound = "hbm"
-    TRAFFIC = {"gemv_qkv": 10033152}
+    TRAFFIC = {"attend_cross": 245957376 + 3753216, "gemv_self_out": 3638016}
 
     def __init__(self, gpu, rank, world, seed=4000):
         import torch
