@@ -1,98 +1,97 @@
-// Encoder multi-head attention for sm_100a: the reference's `Pass::attention`
-// (src/gpu/mod.rs:1556-1605; attention.wgsl `flash` / `relative`, flash_f16.wgsl) re-designed as a
-// tcgen05 flash-attention kernel, over segments of any length in one launch.
+// Encoder multi-head attention with relative positions (Transformer-XL, Parakeet): the reference's
+// `Pass::attention` with [q+u | k | v | q+v] rows and a position table (src/gpu/mod.rs:1556-1605;
+// attention.wgsl `relative`, src/cpu/ops.rs:223-273), as a tcgen05 flash-attention kernel over
+// segments of any length in one launch. score(i, j) = ((q+u)_i·k_j + (q+v)_i·P[pos_t + 15 - (i - j)])
+// / sqrt(hd).
 //
-// A CTA takes 128 queries of one head of one segment. Warp 0 streams tiles with TMA (Q once, then
-// K/V blocks through two-deep rings), warp 1 issues the UMMAs (S = Q·K^T into a TMEM score buffer,
-// O += P·V into a TMEM accumulator), warps 2..5 own one query row per thread: they read the row's
-// scores with tcgen05.ld, run the online softmax in registers (exp2 on the MUFU, a lagging maximum
-// that rescales the TMEM accumulator only when the row maximum grows by more than 2^8), write the
-// probabilities as f16 into a 128-byte-swizzled shared tile (the A operand of P·V), and at the end
-// normalise the accumulator and store the row.
-//
-// With relative positions (Transformer-XL, Parakeet): score (i, j) = ((q+u)_i·k_j +
-// (q+v)_i·P[pos_t + 15 - (i - j)]) / sqrt(hd), the reference's score (src/cpu/ops.rs:223-273,
-// attention.wgsl:305-492). For a 128-query x 64-key block the needed position rows form a window
-// of 191 consecutive rows; BD' = (q+v)·window^T is one N=192 UMMA, and the rel-shift
-// BD[i][j] = BD'[i][j - i + 127] is a per-lane shift of a 96-column slice of each row, done in
-// registers by a 5-stage select network (no shared-memory round trip).
-//
-// Keys past a segment's length are masked; query rows past it are computed and not stored.
+// A CTA takes 128 queries of one head (of 128) of one segment and walks its keys in blocks of 64:
+//   warp 0      TMA: Q and Q+v once, then K, V and position windows through two-slot rings, each a
+//               single 3D box of the head's two 64-column chunks (a TMA instruction costs an SM
+//               ~300 cycles besides its bytes, and the loads set this kernel's pace);
+//   warp 1      one thread issues BD' = (q+v)·window^T over the 191 position rows a 128 x 64
+//               block needs (one N=192 UMMA group) and AC = (q+u)·K^T (N=64);
+//   warp 2      one thread issues O += P·V with P read from TMEM (TS UMMAs, N=128);
+//   warps 3-10  softmax, eight warps: two warps per 32-lane TMEM quarter (16 rows each), two
+//               threads per row, one half of the block's keys each (the 16x32bx2 TMEM access
+//               shape). A thread loads its 32 scores and a 48-column slice of its rows' BD'
+//               window, hands S and BD' back at once (the next block's UMMAs overlap this
+//               block's exponentials), applies the rel-shift BD[i][j] = BD'[i][j - i + 127] as a
+//               per-lane shift of 0-15 by a 4-stage select network, takes the row maximum with one
+//               shuffle, and writes its probabilities back to TMEM as f16 pairs.
+// Lagging maximum (the TMEM accumulator is rescaled only when a row maximum grows by more than
+// 2^8), 3 in 8 exponentials on the FMA pipe, paired f32 arithmetic, as the plain kernel
+// (attention_fa.cu). Keys past a segment's length are masked; query rows past it are computed and
+// not stored.
 #include "kernels.cuh"
 #include "ptx.cuh"
+#include "softmax.cuh"
 
 namespace wv {
 namespace {
 
-constexpr int BM = 128;
+constexpr int BM = 128;                  // queries per CTA
+constexpr int BN = 64;                   // keys per block
+constexpr int HD = 128;                  // head size (the relative path's)
+constexpr int PW_ROWS = BM + BN;         // position rows per block (191 used)
+constexpr int SOFT_WARPS = 8;
+constexpr int CTRL_WARPS = 3;            // TMA producer, S issuer, P·V issuer
+constexpr int THREADS = 32 * (CTRL_WARPS + SOFT_WARPS);
+constexpr int KVS = 2;                   // K / V ring slots
+constexpr int PWS = 2;                   // position window slots
 
-template <int HD, bool REL>
-struct Cfg {
-  static constexpr int BN = REL ? 64 : 128;          // keys per block
-  static constexpr int NBOX = HD / 64;               // 64-column TMA boxes per tile row
-  static constexpr int ATOM_Q = BM * 128;            // bytes of one 64-column block of a Q tile
-  static constexpr int ATOM_KV = BN * 128;
-  static constexpr int Q_BYTES = BM * HD * 2;
-  static constexpr int KV_BYTES = BN * HD * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
-  static constexpr int PW_ROWS = REL ? BM + BN : 0;  // position window rows (191 used)
-  static constexpr int PW_BYTES = PW_ROWS * HD * 2;
-  static constexpr int ATOM_PW = PW_ROWS * 128;
-  // Shared memory layout (every block 1024-aligned).
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_QV = OFF_Q + Q_BYTES;
-  static constexpr int OFF_K = OFF_QV + (REL ? Q_BYTES : 0);
-  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-  static constexpr int OFF_PW = OFF_P + 2 * P_BYTES;
-  static constexpr int OFF_BAR = OFF_PW + PW_BYTES;
-  // TMEM columns: score buffers, then (rel) the BD' block, then the accumulator.
-  static constexpr int T_S = 0;
-  static constexpr int T_BD = REL ? BN : 0;
-  static constexpr int T_O = 256;
-  static constexpr int TMEM_COLS = 512;
-  static constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
-  static constexpr uint32_t IDESC_BD = idesc_f16(BM, REL ? PW_ROWS : 64, 0);
-  static constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
-};
+constexpr int ATOM_Q = BM * 128;         // one 64-column block of a 128-row tile
+constexpr int ATOM_KV = BN * 128;
+constexpr int ATOM_PW = PW_ROWS * 128;
+constexpr int Q_BYTES = BM * HD * 2;
+constexpr int KV_BYTES = BN * HD * 2;
+constexpr int PW_BYTES = PW_ROWS * HD * 2;
+constexpr int OFF_Q = 0;
+constexpr int OFF_QV = OFF_Q + Q_BYTES;
+constexpr int OFF_K = OFF_QV + Q_BYTES;
+constexpr int OFF_V = OFF_K + KVS * KV_BYTES;
+constexpr int OFF_PW = OFF_V + KVS * KV_BYTES;
+constexpr int OFF_BAR = OFF_PW + PWS * PW_BYTES;
+// TMEM columns: S (64 f32), BD' (192 f32), P (64 keys as f16 pairs), O (128 f32).
+constexpr int T_S = 0;
+constexpr int T_BD = 64;
+constexpr int T_P = 256;
+constexpr int T_O = 384;
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
+constexpr uint32_t IDESC_BD = idesc_f16(BM, PW_ROWS, 0);
+constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
 
-struct __align__(8) AttnBarriers {
+struct __align__(8) RelBarriers {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
-  uint64_t pw_full, pw_empty;
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full[2], pv_done[2];
+  uint64_t k_full[KVS], k_empty[KVS];
+  uint64_t v_full[KVS], v_empty[KVS];
+  uint64_t pw_full[PWS], pw_empty[PWS];
+  uint64_t s_full, s_free;
+  uint64_t p_full, pv_done;
   uint64_t o_full;
-  uint64_t drain;
+  uint64_t drain[2];
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-// w[x] <- w[x + s] for x < 64, s in [0, 31]: a shift by a per-lane amount with static register
-// indices (a select per element and stage; the unused upper outputs are dead code).
+// w[x] <- w[x + s] for x < 32, s in [0, 15], with static register indices (a select per element and
+// stage; each stage makes just the outputs the later stages read).
 template <int SH, int OUT>
-__device__ __forceinline__ void shift_stage(float (&w)[96], bool take) {
+__device__ __forceinline__ void shift_stage(float (&w)[48], bool take) {
 #pragma unroll
   for (int x = 0; x < OUT; ++x) w[x] = take ? w[x + SH] : w[x];
 }
 
-__device__ __forceinline__ void shift_left(float (&w)[96], uint32_t s) {
-  // Each stage makes just the outputs the later stages read: 79, 71, 67, 65, 64.
-  shift_stage<16, 79>(w, (s >> 4) & 1u);
-  shift_stage<8, 71>(w, (s >> 3) & 1u);
-  shift_stage<4, 67>(w, (s >> 2) & 1u);
-  shift_stage<2, 65>(w, (s >> 1) & 1u);
-  shift_stage<1, 64>(w, s & 1u);
+__device__ __forceinline__ void shift_left16(float (&w)[48], uint32_t s) {
+  shift_stage<8, 39>(w, (s >> 3) & 1u);
+  shift_stage<4, 35>(w, (s >> 2) & 1u);
+  shift_stage<2, 33>(w, (s >> 1) & 1u);
+  shift_stage<1, 32>(w, s & 1u);
 }
 
-template <int HD, bool REL>
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
-                const __grid_constant__ CUtensorMap map_pos, const AttnArgs a) {
-  using C = Cfg<HD, REL>;
-  constexpr int BN = C::BN;
-
+__global__ void __launch_bounds__(THREADS, 1)
+    rel_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
+               const __grid_constant__ CUtensorMap map_pos, const AttnArgs a) {
   const int seg = blockIdx.z, h = blockIdx.y;
   const int T = a.seg_len ? a.seg_len[seg] : a.single_t;
   const int row0 = a.seg_len ? a.seg_start[seg] : 0;
@@ -103,35 +102,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  AttnBarriers *bar = reinterpret_cast<AttnBarriers *>(smem + C::OFF_BAR);
+  RelBarriers *bar = reinterpret_cast<RelBarriers *>(smem + OFF_BAR);
   const uint32_t warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KVS; ++i) {
       mbar_init(&bar->k_full[i], 1);
       mbar_init(&bar->k_empty[i], 1);
       mbar_init(&bar->v_full[i], 1);
       mbar_init(&bar->v_empty[i], 1);
-      mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->s_free[i], 128);
-      mbar_init(&bar->p_full[i], 128);
-      mbar_init(&bar->pv_done[i], 1);
     }
-    mbar_init(&bar->pw_full, 1);
-    mbar_init(&bar->pw_empty, 1);
+    for (int i = 0; i < PWS; ++i) {
+      mbar_init(&bar->pw_full[i], 1);
+      mbar_init(&bar->pw_empty[i], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, SOFT_WARPS);
+    mbar_init(&bar->p_full, SOFT_WARPS);
+    mbar_init(&bar->pv_done, 1);
     mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->drain, 1);
+    mbar_init(&bar->drain[0], 1);
+    mbar_init(&bar->drain[1], 1);
     bar->abort = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&map_q);
     prefetch_tmap(&map_kv);
-    if (REL) prefetch_tmap(&map_pos);
+    prefetch_tmap(&map_pos);
   }
   if (warp == 1) {
-    tmem_alloc(&bar->tmem_base, C::TMEM_COLS);
+    tmem_alloc(&bar->tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -144,265 +146,272 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int hoff = h * a.head_stride;
 
   if (warp == 0) {
-    // ---- TMA producer ----------------------------------------------------------------------
+    // ---- TMA producer ------------------------------------------------------------------------
     if (lane == 0) {
       bool ok = true;
-      // Parity of the last arm of each ring slot (bit 1: armed at least once).
-      uint32_t k_last[2] = {0, 0}, v_last[2] = {0, 0}, pw_last = 0;
-      mbar_arrive_expect_tx(&bar->q_full, (REL ? 2 : 1) * C::Q_BYTES);
-#pragma unroll
-      for (int b = 0; b < C::NBOX; ++b) {
-        tma_load_2d(smem + C::OFF_Q + b * C::ATOM_Q, &map_q, &bar->q_full, a.q_off + hoff + 64 * b,
-                    row0 + m0);
-        if (REL)
-          tma_load_2d(smem + C::OFF_QV + b * C::ATOM_Q, &map_q, &bar->q_full,
-                      a.qv_off + hoff + 64 * b, row0 + m0);
-      }
-      for (int j = 0; j < nb && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1u;
+      uint32_t k_last[KVS] = {}, v_last[KVS] = {}, p_last[PWS] = {};  // bit 1: armed; 0: parity
+      mbar_arrive_expect_tx(&bar->q_full, 2 * Q_BYTES);
+      // 3D maps {64, rows, columns / 64}: one box holds a head's two 64-column chunks.
+      tma_load_3d(smem + OFF_Q, &map_q, &bar->q_full, 0, row0 + m0, (a.q_off + hoff) / 64);
+      tma_load_3d(smem + OFF_QV, &map_q, &bar->q_full, 0, row0 + m0, (a.qv_off + hoff) / 64);
+      for (int j = 0; j < nb; ++j) {
+        const int s = j % KVS, ps = j % PWS;
+        const uint32_t par = ((j / KVS) & 1) ^ 1u, ppar = ((j / PWS) & 1) ^ 1u;
         if (!mbar_wait(&bar->k_empty[s], par, ab, kErrTimeoutProducer)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bar->k_full[s], C::KV_BYTES);
-#pragma unroll
-        for (int b = 0; b < C::NBOX; ++b)
-          tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + b * C::ATOM_KV, &map_kv, &bar->k_full[s],
-                      a.k_off + hoff + 64 * b, row0 + j * BN);
-        k_last[s] = 2u | ((j >> 1) & 1u);
-        if (REL) {
-          if (!mbar_wait(&bar->pw_empty, (j & 1) ^ 1u, ab, kErrTimeoutProducer)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bar->pw_full, C::PW_BYTES);
-          const int rho0 = a.pos_t + 15 + j * BN - m0 - (BM - 1);
-#pragma unroll
-          for (int b = 0; b < C::NBOX; ++b)
-            tma_load_2d(smem + C::OFF_PW + b * C::ATOM_PW, &map_pos, &bar->pw_full,
-                        a.pos_off + hoff + 64 * b, rho0);
-          pw_last = 2u | (j & 1u);
-        }
+        mbar_arrive_expect_tx(&bar->k_full[s], KV_BYTES);
+        tma_load_3d(smem + OFF_K + s * KV_BYTES, &map_kv, &bar->k_full[s], 0, row0 + j * BN,
+                    (a.k_off + hoff) / 64);
+        k_last[s] = 2u | ((j / KVS) & 1u);
+        if (!mbar_wait(&bar->pw_empty[ps], ppar, ab, kErrTimeoutProducer)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bar->pw_full[ps], PW_BYTES);
+        // Position rows of block j: row r is relative position pos_t + 15 - r; the window starts
+        // at the row of the largest i - j.
+        const int rho0 = a.pos_t + 15 + j * BN - m0 - (BM - 1);
+        tma_load_3d(smem + OFF_PW + ps * PW_BYTES, &map_pos, &bar->pw_full[ps], 0, rho0,
+                    (a.pos_off + hoff) / 64);
+        p_last[ps] = 2u | ((j / PWS) & 1u);
         if (!mbar_wait(&bar->v_empty[s], par, ab, kErrTimeoutProducer)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bar->v_full[s], C::KV_BYTES);
-#pragma unroll
-        for (int b = 0; b < C::NBOX; ++b)
-          tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + b * C::ATOM_KV, &map_kv, &bar->v_full[s],
-                      a.v_off + hoff + 64 * b, row0 + j * BN);
-        v_last[s] = 2u | ((j >> 1) & 1u);
+        mbar_arrive_expect_tx(&bar->v_full[s], KV_BYTES);
+        tma_load_3d(smem + OFF_V + s * KV_BYTES, &map_kv, &bar->v_full[s], 0, row0 + j * BN,
+                    (a.v_off + hoff) / 64);
+        v_last[s] = 2u | ((j / KVS) & 1u);
       }
       if (!ok) {
-        // Wait (bounded) for the loads already issued to land before the CTA may exit.
-        long long t0 = clock64();
+        const long long t0 = clock64();
         auto drain = [&](uint64_t *b, uint32_t last) {
           if (!(last & 2u)) return;
           while (!mbar_try_wait(b, last & 1u) && clock64() - t0 < kWaitCycles) {
           }
         };
         drain(&bar->q_full, 2u);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < KVS; ++s) {
           drain(&bar->k_full[s], k_last[s]);
           drain(&bar->v_full[s], v_last[s]);
         }
-        drain(&bar->pw_full, pw_last);
+        for (int s = 0; s < PWS; ++s) drain(&bar->pw_full[s], p_last[s]);
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer ------------------------------------------------------------------------
+  } else if (warp == 1 || warp == 2) {
+    // ---- UMMA issuers: warp 1 the scores (BD'(j), AC(j) as soon as the softmax holds block
+    // j - 1's S and BD' in registers), warp 2 the accumulator (P(j)·V(j) once P(j) is in TMEM).
+    // A tcgen05.mma blocks its thread while the tensor core is busy, so with one thread per
+    // stream one thread's barrier waits overlap the other's UMMAs.
     if (lane == 0) {
+      const bool is_s = warp == 1;
       bool ok = mbar_wait(&bar->q_full, 0, ab, kErrTimeoutMma);
       bool issued = false;
       const int hsteps = (a.hd + 15) / 16;
-      const uint32_t sq = smem_u32(smem + C::OFF_Q), sqv = smem_u32(smem + C::OFF_QV);
-      const uint32_t sk = smem_u32(smem + C::OFF_K), sv = smem_u32(smem + C::OFF_V);
-      const uint32_t sp = smem_u32(smem + C::OFF_P), spw = smem_u32(smem + C::OFF_PW);
+      // Descriptors are linear in the start address (bits 0-13 hold address / 16).
+      const uint64_t dq = sdesc_sw128(smem_u32(smem + OFF_Q), 16, 1024);
+      const uint64_t dqv = sdesc_sw128(smem_u32(smem + OFF_QV), 16, 1024);
+      const uint64_t dk = sdesc_sw128(smem_u32(smem + OFF_K), 16, 1024);
+      const uint64_t dpw = sdesc_sw128(smem_u32(smem + OFF_PW), 16, 1024);
+      const uint64_t dv = sdesc_sw128(smem_u32(smem + OFF_V), ATOM_KV, 1024);
       tc_fence_after();
-      auto pv = [&](int i) -> bool {
-        const int b = i & 1;
-        if (!mbar_wait(&bar->p_full[b], (i >> 1) & 1, ab, kErrTimeoutMma)) return false;
-        if (!mbar_wait(&bar->v_full[b], (i >> 1) & 1, ab, kErrTimeoutMma)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(sp + b * C::P_BYTES + (kk >> 2) * C::ATOM_Q + (kk & 3) * 32,
-                                          16, 1024);
-          const uint64_t bd = sdesc_sw128(sv + b * C::KV_BYTES + kk * 16 * 128, C::ATOM_KV, 1024);
-          umma_f16(tmem + C::T_O, ad, bd, C::IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&bar->v_empty[b]);
-        umma_commit(&bar->pv_done[b]);
-        return true;
-      };
-      for (int j = 0; j <= nb && ok; ++j) {
-        if (j < nb) {
-          const int s = j & 1;
-          if (!mbar_wait(&bar->k_full[s], (j >> 1) & 1, ab, kErrTimeoutMma)) { ok = false; break; }
-          if (REL) {
-            if (!mbar_wait(&bar->pw_full, j & 1, ab, kErrTimeoutMma)) { ok = false; break; }
-            if (j >= 1 && !mbar_wait(&bar->s_free[0], (j - 1) & 1, ab, kErrTimeoutMma)) {
-              ok = false;
-              break;
-            }
-          } else if (j >= 2 && !mbar_wait(&bar->s_free[s], ((j - 2) >> 1) & 1, ab, kErrTimeoutMma)) {
+      for (int j = 0; j < nb && ok; ++j) {
+        if (is_s) {
+          const int s = j % KVS, ps = j % PWS;
+          if (!mbar_wait(&bar->k_full[s], (j / KVS) & 1, ab, kErrTimeoutMma) ||
+              !mbar_wait(&bar->pw_full[ps], (j / PWS) & 1, ab, kErrTimeoutMma) ||
+              (j >= 1 && !mbar_wait(&bar->s_free, (j - 1) & 1, ab, kErrTimeoutMma))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t ts = tmem + C::T_S + (REL ? 0 : s * BN);
-          if (REL) {
-            for (int kk = 0; kk < hsteps; ++kk) {
-              const uint64_t ad = sdesc_sw128(sqv + (kk >> 2) * C::ATOM_Q + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = sdesc_sw128(spw + (kk >> 2) * C::ATOM_PW + (kk & 3) * 32, 16, 1024);
-              umma_f16(tmem + C::T_BD, ad, bd, C::IDESC_BD, kk > 0 ? 1u : 0u);
-            }
+          const uint64_t bpw = dpw + uint64_t((ps * PW_BYTES) >> 4);
+          const uint64_t bk = dk + uint64_t((s * KV_BYTES) >> 4);
+          for (int kk = 0; kk < hsteps; ++kk) {
+            const uint64_t oq = uint64_t(((kk >> 2) * ATOM_Q + (kk & 3) * 32) >> 4);
+            umma_f16(tmem + T_BD, dqv + oq,
+                     bpw + uint64_t(((kk >> 2) * ATOM_PW + (kk & 3) * 32) >> 4), IDESC_BD,
+                     kk > 0 ? 1u : 0u);
           }
           for (int kk = 0; kk < hsteps; ++kk) {
-            const uint64_t ad = sdesc_sw128(sq + (kk >> 2) * C::ATOM_Q + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd =
-                sdesc_sw128(sk + s * C::KV_BYTES + (kk >> 2) * C::ATOM_KV + (kk & 3) * 32, 16, 1024);
-            umma_f16(ts, ad, bd, C::IDESC_S, kk > 0 ? 1u : 0u);
+            const uint64_t oq = uint64_t(((kk >> 2) * ATOM_Q + (kk & 3) * 32) >> 4);
+            umma_f16(tmem + T_S, dq + oq,
+                     bk + uint64_t(((kk >> 2) * ATOM_KV + (kk & 3) * 32) >> 4), IDESC_S,
+                     kk > 0 ? 1u : 0u);
           }
           issued = true;
-          umma_commit(&bar->s_full[REL ? 0 : s]);
+          umma_commit(&bar->s_full);
           umma_commit(&bar->k_empty[s]);
-          if (REL) umma_commit(&bar->pw_empty);
-        }
-        if (j >= 1) {
-          if (!pv(j - 1)) { ok = false; break; }
+          umma_commit(&bar->pw_empty[ps]);
+        } else {
+          const int vs = j % KVS;
+          if (!mbar_wait(&bar->v_full[vs], (j / KVS) & 1, ab, kErrTimeoutMma) ||
+              !mbar_wait(&bar->p_full, j & 1, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bv = dv + uint64_t((vs * KV_BYTES) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            // A = P from TMEM: keys 16kk.. are columns 8kk.. of the P region; B = V rows 16kk..
+            umma_f16_ts(tmem + T_O, tmem + T_P + kk * 8, bv + uint64_t((kk * 16 * 128) >> 4),
+                        IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&bar->pv_done);
+          umma_commit(&bar->v_empty[vs]);
         }
       }
       if (ok) {
-        umma_commit(&bar->o_full);
+        if (!is_s) umma_commit(&bar->o_full);
       } else if (issued) {
-        umma_commit(&bar->drain);
-        long long t0 = clock64();
-        while (!mbar_try_wait(&bar->drain, 0) && clock64() - t0 < kWaitCycles) {
+        uint64_t *dr = &bar->drain[is_s ? 0 : 1];
+        umma_commit(dr);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(dr, 0) && clock64() - t0 < kWaitCycles) {
         }
       }
     }
   } else {
-    // ---- softmax / epilogue: warps 2..5, one query row per thread ---------------------------
+    // ---- softmax: warps 3..10; rows r0 + (lane % 16), key half lane / 16 ----------------------
+    const int w = int(warp) - CTRL_WARPS;
     const uint32_t quarter = warp & 3u;
-    const int ii = int(quarter * 32 + lane);
-    const uint32_t tl = tmem + ((quarter * 32u) << 16);
-    float m_use = -INFINITY, l = 0.0f;
+    const int sub = w >> 2;
+    const int ch = int(lane >> 4), d = int(lane & 15u);
+    const int r0 = int(quarter) * 32 + sub * 16;
+    const uint32_t tl = tmem + (uint32_t(r0) << 16);
+    // BD' column of the first key of this thread's half, before its row's shift of 15 - d.
+    const uint32_t bd0 = uint32_t(T_BD + (BM - 1) - r0 - 15);
+    const float c = a.scale_log2;
+    float m_use = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     bool ok = true;
-    for (int j = 0; j < nb; ++j) {
-      const int b = REL ? 0 : (j & 1);
-      const uint32_t spar = REL ? (j & 1) : ((j >> 1) & 1);
-      if (!mbar_wait(&bar->s_full[b], spar, ab, kErrTimeoutConsumer)) { ok = false; break; }
+    for (int j = 0; j < nb && ok; ++j) {
+      if (!mbar_wait(&bar->s_full, j & 1, ab, kErrTimeoutConsumer)) { ok = false; break; }
       tc_fence_after();
-      float s[BN];
-      if (REL) {
-        float w[96];
-        {
-          uint32_t r[32];
+      float sc[32], bw[48];
+      {
+        uint32_t r[32], q0[16], q1[16], q2[16];
+        tmem_ld_16x2_x32<32>(tl + T_S, r);
+        tmem_ld_16x2_x16<32>(tl + bd0, q0);
+        tmem_ld_16x2_x16<32>(tl + bd0 + 16, q1);
+        tmem_ld_16x2_x16<32>(tl + bd0 + 32, q2);
+        tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tl + C::T_S + c * 32, r);
-            tmem_wait_ld();
+        for (int x = 0; x < 32; ++x) sc[x] = __uint_as_float(r[x]);
 #pragma unroll
-            for (int x = 0; x < 32; ++x) s[c * 32 + x] = __uint_as_float(r[x]);
-          }
-          const uint32_t cb = 96u - 32u * quarter;
-#pragma unroll
-          for (int c = 0; c < 3; ++c) {
-            tmem_ld32(tl + C::T_BD + cb + c * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int x = 0; x < 32; ++x) w[c * 32 + x] = __uint_as_float(r[x]);
-          }
+        for (int x = 0; x < 16; ++x) {
+          bw[x] = __uint_as_float(q0[x]);
+          bw[16 + x] = __uint_as_float(q1[x]);
+          bw[32 + x] = __uint_as_float(q2[x]);
         }
-        tc_fence_before();
-        mbar_arrive(&bar->s_free[0]);
-        shift_left(w, 31u - lane);
+      }
+      // S and BD' are in registers: the issuer may overwrite them with the next block's.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->s_free);
+      shift_left16(bw, uint32_t(15 - d));
 #pragma unroll
-        for (int x = 0; x < BN; ++x) s[x] = s[x] + w[x];
-      } else {
-        uint32_t r[32];
+      for (int x = 0; x < 32; x += 2) add2(sc[x], sc[x + 1], sc[x], sc[x + 1], bw[x], bw[x + 1]);
+      // Keys past the segment (last block only) are masked to -inf.
+      const int kvalid = T - j * BN - ch * 32;
+      if (kvalid < 32) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(tl + C::T_S + b * BN + c * 32, r);
-          tmem_wait_ld();
+        for (int x = 0; x < 32; ++x)
+          if (x >= kvalid) sc[x] = -INFINITY;
+      }
+      float mx;
+      {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int x = 0; x < 32; ++x) s[c * 32 + x] = __uint_as_float(r[x]);
+        for (int x = 0; x < 32; x += 8) {
+          float &m = m4[(x / 8) & 3];
+          m = max3(m, sc[x + 0], sc[x + 1]);
+          m = max3(m, sc[x + 2], sc[x + 3]);
+          m = max3(m, sc[x + 4], sc[x + 5]);
+          m = max3(m, sc[x + 6], sc[x + 7]);
         }
-        tc_fence_before();
-        mbar_arrive(&bar->s_free[b]);
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       }
-      // Scale into log2 units, mask keys past the segment, block maximum.
-      const int kvalid = T - j * BN;
-      float mx = -INFINITY;
+      const float m_blk = mx * c;
+      const bool need = m_blk > m_use + 8.0f;
+      const bool rescale = __any_sync(0xffffffffu, need) && j > 0;
+      const float alpha = need ? ex2(m_use - m_blk) : 1.0f;
+      if (rescale) {
+        l0 *= alpha;
+        l1 *= alpha;
+      }
+      if (need) m_use = m_blk;
+      const float nm = -m_use;
+      uint32_t pk[16];
 #pragma unroll
-      for (int x = 0; x < BN; ++x) {
-        s[x] = (x < kvalid) ? s[x] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[x]);
+      for (int g = 0; g < 32; g += 16) {
+        float *p = sc + g;
+#pragma unroll
+        for (int x = 0; x < 16; x += 2) fma2(p[x], p[x + 1], p[x], p[x + 1], c, c, nm, nm);
+#pragma unroll
+        for (int x = 0; x < 10; ++x) p[x] = ex2(p[x]);
+        exp2_poly2(p[10], p[11]);
+        exp2_poly2(p[12], p[13]);
+        exp2_poly2(p[14], p[15]);
+#pragma unroll
+        for (int x = 0; x < 16; x += 4) {
+          float a0, a1;
+          add2(a0, a1, p[x], p[x + 1], p[x + 2], p[x + 3]);
+          add2(l0, l1, l0, l1, a0, a1);
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x) pk[g / 2 + x] = pack_half2(p[2 * x], p[2 * x + 1]);
       }
-      // The probability buffer b is free once P·V of block j - 2 completed.
-      const int pb = j & 1;
-      if (j >= 2 && !mbar_wait(&bar->pv_done[pb], ((j - 2) >> 1) & 1, ab, kErrTimeoutConsumer)) {
+      // P is free and O stable once P·V of block j - 1 landed.
+      if (j >= 1 && !mbar_wait(&bar->pv_done, (j - 1) & 1, ab, kErrTimeoutConsumer)) {
         ok = false;
         break;
       }
-      const float m_new = fmaxf(m_use, mx);
-      const bool need = m_new > m_use + 8.0f;
-      if (__any_sync(0xffffffffu, need) && j > 0) {
-        // Rescale the accumulator row once P·V of block j - 1 has landed in it.
-        if (!mbar_wait(&bar->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, ab, kErrTimeoutConsumer)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float alpha = need ? ex2(m_use - m_new) : 1.0f;
-        uint32_t r[32];
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          tmem_ld32(tl + C::T_O + c * 32, r);
+      tc_fence_after();
+      tmem_st_16x2_x16<16>(tl + T_P, pk);
+      if (rescale) {
+#pragma unroll 1
+        for (int q = 0; q < HD / 2 / 16; ++q) {
+          uint32_t r[16];
+          tmem_ld_16x2_x16<HD / 2>(tl + T_O + q * 16, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int x = 0; x < 32; ++x) r[x] = __float_as_uint(__uint_as_float(r[x]) * alpha);
-          tmem_st32(tl + C::T_O + c * 32, r);
+          for (int x = 0; x < 16; ++x) r[x] = __float_as_uint(__uint_as_float(r[x]) * alpha);
+          tmem_st_16x2_x16<HD / 2>(tl + T_O + q * 16, r);
         }
-        tmem_wait_st();
-        l *= alpha;
       }
-      if (need) m_use = m_new;
-      // Probabilities as f16 into the swizzled A tile of P·V.
-      uint8_t *prow = smem + C::OFF_P + pb * C::P_BYTES;
-#pragma unroll
-      for (int c = 0; c < BN / 8; ++c) {
-        float p[8];
-#pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          p[x] = ex2(s[8 * c + x] - m_use);
-          l += p[x];
-        }
-        uint4 v = make_uint4(pack_half2(p[0], p[1]), pack_half2(p[2], p[3]),
-                             pack_half2(p[4], p[5]), pack_half2(p[6], p[7]));
-        *reinterpret_cast<uint4 *>(prow + (c >> 3) * C::ATOM_Q + sw128_offset(ii, c & 7)) = v;
-      }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar->p_full[pb]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->p_full);
     }
     if (ok && mbar_wait(&bar->o_full, 0, ab, kErrTimeoutConsumer)) {
+      // The row sum over both halves, then this thread's half of the row of O.
+      float l = l0 + l1;
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
       tc_fence_after();
       const float inv = 1.0f / l;
-      const int qrow = m0 + ii;
+      const int qrow = m0 + r0 + d;
       const bool store = qrow < T;
       const long long orow = (long long)(row0 + qrow) * a.ldo + (long long)h * a.hd;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int q = 0; q < HD / 2 / 32; ++q) {
         uint32_t r[32];
-        tmem_ld32(tl + C::T_O + c * 32, r);
+        tmem_ld_16x2_x32<HD / 2>(tl + T_O + q * 32, r);
         tmem_wait_ld();
-        if (store) {
-          const int c0 = c * 32;
+        const int c0 = ch * (HD / 2) + q * 32;
+        if (store && c0 < a.hd) {
           if (a.o_f16) {
             __half *o = reinterpret_cast<__half *>(a.o) + orow;
+            if (c0 + 32 <= a.hd && ((reinterpret_cast<uintptr_t>(o + c0) & 15u) == 0)) {
 #pragma unroll
-            for (int x = 0; x < 32; x += 2) {
-              if (c0 + x + 1 < a.hd) {
-                *reinterpret_cast<__half2 *>(o + c0 + x) = __floats2half2_rn(
-                    __uint_as_float(r[x]) * inv, __uint_as_float(r[x + 1]) * inv);
-              } else if (c0 + x < a.hd) {
-                o[c0 + x] = __float2half_rn(__uint_as_float(r[x]) * inv);
+              for (int x = 0; x < 32; x += 8) {
+                const uint4 v = make_uint4(
+                    pack_half2(__uint_as_float(r[x]) * inv, __uint_as_float(r[x + 1]) * inv),
+                    pack_half2(__uint_as_float(r[x + 2]) * inv, __uint_as_float(r[x + 3]) * inv),
+                    pack_half2(__uint_as_float(r[x + 4]) * inv, __uint_as_float(r[x + 5]) * inv),
+                    pack_half2(__uint_as_float(r[x + 6]) * inv, __uint_as_float(r[x + 7]) * inv));
+                *reinterpret_cast<uint4 *>(o + c0 + x) = v;
               }
+            } else {
+#pragma unroll
+              for (int x = 0; x < 32; ++x)
+                if (c0 + x < a.hd) o[c0 + x] = __float2half_rn(__uint_as_float(r[x]) * inv);
             }
           } else {
             float *o = reinterpret_cast<float *>(a.o) + orow;
@@ -418,7 +427,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // f32 or f16 operand rows -> f16 rows with heads padded to hd_pad.
@@ -444,20 +453,20 @@ __global__ void pack_heads_kernel(const void *__restrict__ in, int in_f16, long 
   }
 }
 
-template <int HD, bool REL>
-cudaError_t launch_one(const CUtensorMap &q, const CUtensorMap &kv, const CUtensorMap &pos,
+cudaError_t launch_rel(const CUtensorMap &q, const CUtensorMap &kv, const CUtensorMap &pos,
                        const AttnArgs &a, int max_len, int nseg, cudaStream_t s) {
-  using C = Cfg<HD, REL>;
-  const size_t smem = 1024 + C::OFF_BAR + sizeof(AttnBarriers);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<HD, REL>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const size_t smem = 1024 + OFF_BAR + sizeof(RelBarriers);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(rel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[dev] = true;
   }
   dim3 grid((max_len + BM - 1) / BM, a.heads, nseg);
-  return launch_pdl(attn_kernel<HD, REL>, grid, dim3(kAttnThreads), smem, s, q, kv, pos, a);
+  return launch_pdl(rel_kernel, grid, dim3(THREADS), smem, s, q, kv, pos, a);
 }
 
 }  // namespace
@@ -466,14 +475,12 @@ cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv
                              const CUtensorMap &map_pos, const AttnArgs &a, int hd_pad, bool rel,
                              int max_len, int nseg, cudaStream_t s) {
   if (max_len <= 0 || nseg <= 0) return cudaSuccess;
-  if (rel) return launch_one<128, true>(map_q, map_kv, map_pos, a, max_len, nseg, s);
+  if (rel) return launch_rel(map_q, map_kv, map_pos, a, max_len, nseg, s);
   return launch_fa_attention(map_q, map_kv, a, hd_pad, max_len, nseg, s);
 }
 
-int attn_block_keys(bool rel, int hd_pad) {
-  return rel ? Cfg<128, true>::BN : fa_block_keys(hd_pad);
-}
-int attn_pos_window_rows() { return Cfg<128, true>::PW_ROWS; }
+int attn_block_keys(bool rel, int hd_pad) { return rel ? BN : fa_block_keys(hd_pad); }
+int attn_pos_window_rows() { return PW_ROWS; }
 
 cudaError_t launch_pack_heads(const void *in, int in_f16, long long ld_in, const int *in_off,
                               int sections, __half *out, long long ld_out, int rows, int heads,

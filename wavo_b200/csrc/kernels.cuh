@@ -94,7 +94,6 @@ struct AttnArgs {
   int *err;
 };
 
-constexpr int kAttnThreads = 192;
 constexpr int kAttnBlockQ = 128;  // queries per tile (the TMA box height of map_q)
 int attn_block_keys(bool rel, int hd_pad);  // keys per block (the TMA box height of map_kv)
 int attn_pos_window_rows();      // position rows per block (the TMA box height of map_pos)
@@ -103,8 +102,9 @@ int fa_block_keys(int hd_pad);
 cudaError_t launch_fa_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
                                 const AttnArgs &a, int hd_pad, int max_len, int nseg,
                                 cudaStream_t s);
-// hd_pad: 64 or 128 (the padded head size of the operand tiles). All maps are 2D f16 tensor maps
-// with 64-column (128-byte) boxes and 128-byte swizzle.
+// hd_pad: 64 or 128 (the padded head size of the operand tiles). Plain attention takes 2D f16
+// tensor maps with 64-column (128-byte) boxes; relative attention (heads of 128) 3D maps
+// {64, rows, columns / 64} with boxes {64, rows, 2}; all with 128-byte swizzle.
 cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
                              const CUtensorMap &map_pos, const AttnArgs &a, int hd_pad, bool rel,
                              int max_len, int nseg, cudaStream_t s);

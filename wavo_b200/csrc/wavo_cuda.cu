@@ -648,12 +648,14 @@ wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const v
     a.v_off = int(2 * ch);
     a.qv_off = int(3 * ch);
     a.pos_off = 0;
-    if (!make_map(&mq, qk, ld, rows, ld, wv::kAttnBlockQ) ||
-        !make_map(&mkv, qk, ld, rows, ld, uint32_t(bk)))
-      return fail(ctx, WAVO_ECUDA, "attention: tensor map");
+    const bool ok = rel ? make_map3(&mq, qk, ld, rows, ld, wv::kAttnBlockQ) &&
+                              make_map3(&mkv, qk, ld, rows, ld, uint32_t(bk))
+                        : make_map(&mq, qk, ld, rows, ld, wv::kAttnBlockQ) &&
+                              make_map(&mkv, qk, ld, rows, ld, uint32_t(bk));
+    if (!ok) return fail(ctx, WAVO_ECUDA, "attention: tensor map");
     mpos = mq;
-    if (rel && !make_map(&mpos, pos, ch, wavo_pos_rows(pos_t), ch,
-                         uint32_t(wv::attn_pos_window_rows())))
+    if (rel && !make_map3(&mpos, pos, ch, wavo_pos_rows(pos_t), ch,
+                          uint32_t(wv::attn_pos_window_rows())))
       return fail(ctx, WAVO_ECUDA, "attention: tensor map of pos");
   } else {
     // Repack into f16 rows [sections][heads][hd_pad] (zeros past hd) in the scratch.
@@ -687,9 +689,11 @@ wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const v
     a.k_off = int(heads * hd_pad);
     a.v_off = int(2 * heads * hd_pad);
     a.qv_off = int(3 * heads * hd_pad);
-    if (!make_map(&mq, pk, ldp, rows, ldp, wv::kAttnBlockQ) ||
-        !make_map(&mkv, pk, ldp, rows, ldp, uint32_t(bk)))
-      return fail(ctx, WAVO_ECUDA, "attention: tensor map");
+    const bool ok = rel ? make_map3(&mq, pk, ldp, rows, ldp, wv::kAttnBlockQ) &&
+                              make_map3(&mkv, pk, ldp, rows, ldp, uint32_t(bk))
+                        : make_map(&mq, pk, ldp, rows, ldp, wv::kAttnBlockQ) &&
+                              make_map(&mkv, pk, ldp, rows, ldp, uint32_t(bk));
+    if (!ok) return fail(ctx, WAVO_ECUDA, "attention: tensor map");
     mpos = mq;
     if (rel) {
       const int off1[1] = {0};
@@ -697,8 +701,8 @@ wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const v
                                int(heads), int(hd), hd_pad, ctx->stream),
          "attention repack pos");
       a.pos_off = 0;
-      if (!make_map(&mpos, pp, uint64_t(heads) * hd_pad, prow, uint64_t(heads) * hd_pad,
-                    uint32_t(wv::attn_pos_window_rows())))
+      if (!make_map3(&mpos, pp, uint64_t(heads) * hd_pad, prow, uint64_t(heads) * hd_pad,
+                     uint32_t(wv::attn_pos_window_rows())))
         return fail(ctx, WAVO_ECUDA, "attention: tensor map of pos");
     }
   }
