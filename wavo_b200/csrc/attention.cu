@@ -35,6 +35,7 @@ constexpr int HD = 128;                  // head size (the relative path's)
 constexpr int PW_ROWS = BM + BN;         // position rows per block (191 used)
 constexpr int SOFT_WARPS = 8;
 constexpr int CTRL_WARPS = 3;            // TMA producer, S issuer, P·V issuer
+constexpr int kRelPoly = 6;              // exponentials of 16 on the FMA pipe
 constexpr int THREADS = 32 * (CTRL_WARPS + SOFT_WARPS);
 constexpr int KVS = 2;                   // K / V ring slots
 constexpr int PWS = 2;                   // position window slots
@@ -343,11 +344,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         float *p = sc + g;
 #pragma unroll
         for (int x = 0; x < 16; x += 2) fma2(p[x], p[x + 1], p[x], p[x + 1], c, c, nm, nm);
-#pragma unroll
-        for (int x = 0; x < 10; ++x) p[x] = ex2(p[x]);
-        exp2_poly2(p[10], p[11]);
-        exp2_poly2(p[12], p[13]);
-        exp2_poly2(p[14], p[15]);
+        exp2_16<kRelPoly>(p);
 #pragma unroll
         for (int x = 0; x < 16; x += 4) {
           float a0, a1;

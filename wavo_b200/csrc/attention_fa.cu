@@ -14,13 +14,15 @@
 //               (the next S_t UMMA overlaps this block's exponentials), takes the row maximum
 //               with one shuffle, and writes its probabilities back to TMEM as f16 pairs.
 // The row maximum lags: the TMEM accumulator is rescaled only when a row maximum grows by more
-// than 2^8. Exponentials: 3 in 8 on the FMA pipe (a degree-4 polynomial for 2^f on [-1/2, 1/2]
-// fitted for this kernel, the exponent added in the integer bits), the rest on the MUFU; the
-// scale-and-shift and the row sums use the paired f32 instructions of sm_100 (fma/add .f32x2).
+// than 2^8. Scale/shift and row sums use the paired f32 instructions of sm_100 (fma/add .f32x2).
 // At the end the two threads of a row add their sums, normalise and store their halves of O.
 //
-// For heads of 64 the tensor core bounds the kernel: P·V is 8 UMMAs of N=64 per 128-key block
-// with A read from TMEM, each about 100 cycles (measured), against 4 UMMAs of N=128 for S.
+// Heads of 64: a 128 x 128 block of one tile is 16 384 exponentials against 4 S and 8 P·V UMMAs
+// (~640 tensor cycles). The MUFU's 16 exponentials per cycle per SM (measured) make the
+// exponentials, not the tensor core, the bound: ~2 050 of the ~2 600 cycles a block pair of the
+// two tiles takes (measured), so every exponential goes to the MUFU (an FMA-pipe polynomial for a
+// share of them costs more issue slots than the MUFU time it saves; measured). Heads of 128 put
+// 6 of 16 on the FMA pipe.
 #include "kernels.cuh"
 #include "ptx.cuh"
 #include "softmax.cuh"
@@ -316,11 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         float *p = s + g;  // in place: scores become exponents, then probabilities
 #pragma unroll
         for (int x = 0; x < 16; x += 2) fma2(p[x], p[x + 1], p[x], p[x + 1], c, c, nm, nm);
-#pragma unroll
-        for (int x = 0; x < 10; ++x) p[x] = ex2(p[x]);
-        exp2_poly2(p[10], p[11]);
-        exp2_poly2(p[12], p[13]);
-        exp2_poly2(p[14], p[15]);
+        exp2_16<(HD == 64 ? 0 : 6)>(p);
 #pragma unroll
         for (int x = 0; x < 16; x += 4) {
           float a0, a1;

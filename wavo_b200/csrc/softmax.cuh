@@ -4,6 +4,8 @@
 
 #include <stdint.h>
 
+#include "ptx.cuh"
+
 namespace wv {
 
 // ---- paired f32 arithmetic (sm_100: fma/add .f32x2, two lanes of work per instruction) ----------
@@ -44,6 +46,19 @@ __device__ __forceinline__ void exp2_poly2(float &x0, float &x1) {
   fma2(p0, p1, p0, p1, f0, f1, 0.9999976754188538f, 0.9999976754188538f);
   x0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
   x1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
+// Sixteen exponentials 2^p[x] in place: the first 16 - NPOLY on the MUFU (ex2.approx), the last
+// NPOLY (even) on the FMA pipe by exp2_poly2. Where the MUFU is not the bound (heads of 128, whose
+// tensor work per score is twice that of heads of 64) the polynomial share relieves it; with heads
+// of 64 the extra issue slots cost more than the MUFU time they save (measured).
+template <int NPOLY>
+__device__ __forceinline__ void exp2_16(float *p) {
+  static_assert(NPOLY % 2 == 0 && NPOLY <= 16, "polynomial share");
+#pragma unroll
+  for (int x = 0; x < 16 - NPOLY; ++x) p[x] = ex2(p[x]);
+#pragma unroll
+  for (int x = 16 - NPOLY; x < 16; x += 2) exp2_poly2(p[x], p[x + 1]);
 }
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
