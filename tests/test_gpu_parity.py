@@ -119,11 +119,13 @@ def test_relative_attention_matches_the_cpu_oracle(gpu):
 
 
 def test_varlen_segments(gpu):
-    # Independent segments in one launch equal each segment alone (plain and relative).
+    # Independent segments in one launch equal each segment alone (plain and relative); rows
+    # between segments (gaps of 5) are left as they were.
     rng = np.random.default_rng(3)
     lens = [200, 37, 129, 300, 1, 256]
-    starts = np.cumsum([0] + lens[:-1]).astype(np.int32)
-    rows = int(sum(lens))
+    gap = 5
+    starts = np.cumsum([0] + [n + gap for n in lens[:-1]]).astype(np.int32)
+    rows = int(starts[-1] + lens[-1] + gap)
     for rel in (False, True):
         heads, hd = (8, 128) if rel else (4, 64)
         ch = heads * hd
@@ -150,6 +152,10 @@ def test_varlen_segments(gpu):
                 want = O.attention(np.ascontiguousarray(seg.ravel()), 3 * ch,
                                    np.ascontiguousarray(seg.ravel()[2 * ch:]), 3 * ch, n, heads, ch)
             check(got[s:s + n], want)
+        inside = np.zeros(rows, dtype=bool)
+        for s, n in zip(starts, lens):
+            inside[s:s + n] = True
+        assert np.all(got[~inside] == 7.0), "rows outside the segments were written"
 
 
 @pytest.mark.parametrize("ty", [O.TY_F16, O.TY_Q8_0])

@@ -52,6 +52,7 @@ constexpr int OFF_K = OFF_QV + Q_BYTES;
 constexpr int OFF_V = OFF_K + KVS * KV_BYTES;
 constexpr int OFF_PW = OFF_V + KVS * KV_BYTES;
 constexpr int OFF_BAR = OFF_PW + PWS * PW_BYTES;
+static_assert(SOFT_WARPS * 16 * HD * 2 <= 2 * KVS * KV_BYTES, "output staging (K and V rings)");
 // TMEM columns: S (64 f32), BD' (192 f32), P (64 keys as f16 pairs), O (128 f32).
 constexpr int T_S = 0;
 constexpr int T_BD = 64;
@@ -92,7 +93,8 @@ __device__ __forceinline__ void shift_left16(float (&w)[48], uint32_t s) {
 
 __global__ void __launch_bounds__(THREADS, 1)
     rel_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
-               const __grid_constant__ CUtensorMap map_pos, const AttnArgs a) {
+               const __grid_constant__ CUtensorMap map_pos,
+               const __grid_constant__ CUtensorMap map_o, const AttnArgs a) {
   const int seg = blockIdx.z, h = blockIdx.y;
   const int T = a.seg_len ? a.seg_len[seg] : a.single_t;
   const int row0 = a.seg_len ? a.seg_start[seg] : 0;
@@ -132,6 +134,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&map_q);
     prefetch_tmap(&map_kv);
     prefetch_tmap(&map_pos);
+    if (a.o_tma) prefetch_tmap(&map_o);
   }
   if (warp == 1) {
     tmem_alloc(&bar->tmem_base, TMEM_COLS);
@@ -385,6 +388,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float inv = 1.0f / l;
       const int qrow = m0 + r0 + d;
       const bool store = qrow < T;
+      // A warp whose 16 rows all lie in the segment stages them in shared memory (the K ring,
+      // free once O is final) and stores them with one TMA box; a partial group row by row.
+      const bool via_tma = a.o_tma && m0 + r0 + 16 <= T;
+      uint8_t *stage = smem + OFF_K + w * (16 * HD * 2) + d * (a.hd * 2);
       const long long orow = (long long)(row0 + qrow) * a.ldo + (long long)h * a.hd;
 #pragma unroll
       for (int q = 0; q < HD / 2 / 32; ++q) {
@@ -392,7 +399,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_16x2_x32<HD / 2>(tl + T_O + q * 32, r);
         tmem_wait_ld();
         const int c0 = ch * (HD / 2) + q * 32;
-        if (store && c0 < a.hd) {
+        if (via_tma) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            if (c0 + x < a.hd) {  // the head size is a multiple of 8 on this path
+              const uint4 v = make_uint4(
+                  pack_half2(__uint_as_float(r[x]) * inv, __uint_as_float(r[x + 1]) * inv),
+                  pack_half2(__uint_as_float(r[x + 2]) * inv, __uint_as_float(r[x + 3]) * inv),
+                  pack_half2(__uint_as_float(r[x + 4]) * inv, __uint_as_float(r[x + 5]) * inv),
+                  pack_half2(__uint_as_float(r[x + 6]) * inv, __uint_as_float(r[x + 7]) * inv));
+              *reinterpret_cast<uint4 *>(stage + (c0 + x) * 2) = v;
+            }
+          }
+        } else if (store && c0 < a.hd) {
           if (a.o_f16) {
             __half *o = reinterpret_cast<__half *>(a.o) + orow;
             if (c0 + 32 <= a.hd && ((reinterpret_cast<uintptr_t>(o + c0) & 15u) == 0)) {
@@ -417,6 +436,17 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (c0 + x < a.hd) o[c0 + x] = __uint_as_float(r[x]) * inv;
           }
         }
+      }
+      if (via_tma) {
+        fence_proxy_async_smem();  // the staged rows are visible to the TMA (async proxy)
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_o, smem + OFF_K + w * (16 * HD * 2), h * a.hd, row0 + m0 + r0);
+          bulk_commit();
+          // Shared memory may go once the TMA has read it; the writes complete with the grid.
+          bulk_wait_read<0>();
+        }
+        __syncwarp();
       }
     }
   }
@@ -451,7 +481,8 @@ __global__ void pack_heads_kernel(const void *__restrict__ in, int in_f16, long 
 }
 
 cudaError_t launch_rel(const CUtensorMap &q, const CUtensorMap &kv, const CUtensorMap &pos,
-                       const AttnArgs &a, int max_len, int nseg, cudaStream_t s) {
+                       const CUtensorMap &o, const AttnArgs &a, int max_len, int nseg,
+                       cudaStream_t s) {
   const size_t smem = 1024 + OFF_BAR + sizeof(RelBarriers);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -463,17 +494,18 @@ cudaError_t launch_rel(const CUtensorMap &q, const CUtensorMap &kv, const CUtens
     configured[dev] = true;
   }
   dim3 grid((max_len + BM - 1) / BM, a.heads, nseg);
-  return launch_pdl(rel_kernel, grid, dim3(THREADS), smem, s, q, kv, pos, a);
+  return launch_pdl(rel_kernel, grid, dim3(THREADS), smem, s, q, kv, pos, o, a);
 }
 
 }  // namespace
 
 cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
-                             const CUtensorMap &map_pos, const AttnArgs &a, int hd_pad, bool rel,
-                             int max_len, int nseg, cudaStream_t s) {
+                             const CUtensorMap &map_pos, const CUtensorMap &map_o,
+                             const AttnArgs &a, int hd_pad, bool rel, int max_len, int nseg,
+                             cudaStream_t s) {
   if (max_len <= 0 || nseg <= 0) return cudaSuccess;
-  if (rel) return launch_rel(map_q, map_kv, map_pos, a, max_len, nseg, s);
-  return launch_fa_attention(map_q, map_kv, a, hd_pad, max_len, nseg, s);
+  if (rel) return launch_rel(map_q, map_kv, map_pos, map_o, a, max_len, nseg, s);
+  return launch_fa_attention(map_q, map_kv, map_o, a, hd_pad, max_len, nseg, s);
 }
 
 int attn_block_keys(bool rel, int hd_pad) { return rel ? BN : fa_block_keys(hd_pad); }

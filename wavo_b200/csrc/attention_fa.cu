@@ -62,6 +62,7 @@ struct Fa {
   static_assert(T_O + HD <= T_TILE && NT * T_TILE <= TMEM_COLS, "TMEM");
   static_assert(CW == 32 || CW == 64, "score columns per thread");
   static_assert(OW % 32 == 0, "accumulator columns per thread");
+  static_assert(NT * SOFT_WARPS * 16 * HD * 2 <= 2 * KVS * KV_BYTES, "output staging");
 };
 
 struct __align__(8) FaBarriers {
@@ -79,7 +80,7 @@ struct __align__(8) FaBarriers {
 template <int HD, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     fa_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
-              const AttnArgs a) {
+              const __grid_constant__ CUtensorMap map_o, const AttnArgs a) {
   using C = Fa<HD, BN>;
   constexpr int CW = C::CW, OW = C::OW;
   const int seg = blockIdx.z, h = blockIdx.y;
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&map_q);
     prefetch_tmap(&map_kv);
+    if (a.o_tma) prefetch_tmap(&map_o);
   }
   if (warp == 1) {
     tmem_alloc(&bar->tmem_base, C::TMEM_COLS);
@@ -361,8 +363,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       l += __shfl_xor_sync(0xffffffffu, l, 16);
       tc_fence_after();
       const float inv = 1.0f / l;
-      const int qrow = m0 + t * BM + int(quarter * 32u + sub * 16u + (lane & 15u));
+      const int rbase = m0 + t * BM + int(quarter * 32u + sub * 16u);  // this warp's 16 rows
+      const int qrow = rbase + int(lane & 15u);
       const bool store = qrow < T;
+      // A warp whose 16 rows all lie in the segment stages them in shared memory (the K ring,
+      // free once O is final: every load landed and every UMMA completed) and stores them with
+      // one TMA box; the segment's last partial group is stored row by row.
+      const bool via_tma = a.o_tma && rbase + 16 <= T;
+      uint8_t *stage = smem + C::OFF_K + w * (16 * HD * 2) + (lane & 15u) * (a.hd * 2);
       const long long orow = (long long)(row0 + qrow) * a.ldo + (long long)h * a.hd;
 #pragma unroll
       for (int q = 0; q < OW / 32; ++q) {
@@ -370,7 +378,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_16x2_x32<OW>(to + q * 32, r);
         tmem_wait_ld();
         const int c0 = ch * OW + q * 32;
-        if (store && c0 < a.hd) {
+        if (via_tma) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            if (c0 + x < a.hd) {  // the head size is a multiple of 8 on this path
+              const uint4 v = make_uint4(
+                  pack_half2(__uint_as_float(r[x]) * inv, __uint_as_float(r[x + 1]) * inv),
+                  pack_half2(__uint_as_float(r[x + 2]) * inv, __uint_as_float(r[x + 3]) * inv),
+                  pack_half2(__uint_as_float(r[x + 4]) * inv, __uint_as_float(r[x + 5]) * inv),
+                  pack_half2(__uint_as_float(r[x + 6]) * inv, __uint_as_float(r[x + 7]) * inv));
+              *reinterpret_cast<uint4 *>(stage + (c0 + x) * 2) = v;
+            }
+          }
+        } else if (store && c0 < a.hd) {
           if (a.o_f16) {
             __half *o = reinterpret_cast<__half *>(a.o) + orow;
             if (c0 + 32 <= a.hd && ((reinterpret_cast<uintptr_t>(o + c0) & 15u) == 0)) {
@@ -396,6 +416,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+      if (via_tma) {
+        fence_proxy_async_smem();  // the staged rows are visible to the TMA (async proxy)
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_o, smem + C::OFF_K + w * (16 * HD * 2), h * a.hd, row0 + rbase);
+          bulk_commit();
+          // Shared memory may go once the TMA has read it; the writes complete with the grid.
+          bulk_wait_read<0>();
+        }
+        __syncwarp();
+      }
     }
   }
 
@@ -406,8 +437,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int HD, int BN>
-cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const AttnArgs &a, int max_len,
-                      int nseg, cudaStream_t s) {
+cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const CUtensorMap &o,
+                      const AttnArgs &a, int max_len, int nseg, cudaStream_t s) {
   using C = Fa<HD, BN>;
   const size_t smem = 1024 + C::OFF_BAR + sizeof(FaBarriers);
   int dev = 0;
@@ -420,7 +451,7 @@ cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const AttnArg
     configured[dev] = true;
   }
   dim3 grid((max_len + NT * BM - 1) / (NT * BM), a.heads, nseg);
-  return launch_pdl(fa_kernel<HD, BN>, grid, dim3(THREADS), smem, s, q, kv, a);
+  return launch_pdl(fa_kernel<HD, BN>, grid, dim3(THREADS), smem, s, q, kv, o, a);
 }
 
 }  // namespace
@@ -428,11 +459,11 @@ cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const AttnArg
 int fa_block_keys(int hd_pad) { return hd_pad == 64 ? 128 : 64; }
 
 cudaError_t launch_fa_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
-                                const AttnArgs &a, int hd_pad, int max_len, int nseg,
-                                cudaStream_t s) {
+                                const CUtensorMap &map_o, const AttnArgs &a, int hd_pad,
+                                int max_len, int nseg, cudaStream_t s) {
   if (max_len <= 0 || nseg <= 0) return cudaSuccess;
-  if (hd_pad == 64) return launch_fa<64, 128>(map_q, map_kv, a, max_len, nseg, s);
-  return launch_fa<128, 64>(map_q, map_kv, a, max_len, nseg, s);
+  if (hd_pad == 64) return launch_fa<64, 128>(map_q, map_kv, map_o, a, max_len, nseg, s);
+  return launch_fa<128, 64>(map_q, map_kv, map_o, a, max_len, nseg, s);
 }
 
 }  // namespace wv

@@ -91,6 +91,7 @@ struct AttnArgs {
   void *o;          // output rows
   long long ldo;
   int o_f16;
+  int o_tma;        // 1: f16 output rows also reachable through map_o (boxes {hd, 16}, no swizzle)
   int *err;
 };
 
@@ -100,14 +101,16 @@ int attn_pos_window_rows();      // position rows per block (the TMA box height 
 // The plain-layout kernel (attention_fa.cu): two query tiles per CTA.
 int fa_block_keys(int hd_pad);
 cudaError_t launch_fa_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
-                                const AttnArgs &a, int hd_pad, int max_len, int nseg,
-                                cudaStream_t s);
+                                const CUtensorMap &map_o, const AttnArgs &a, int hd_pad,
+                                int max_len, int nseg, cudaStream_t s);
 // hd_pad: 64 or 128 (the padded head size of the operand tiles). Plain attention takes 2D f16
 // tensor maps with 64-column (128-byte) boxes; relative attention (heads of 128) 3D maps
-// {64, rows, columns / 64} with boxes {64, rows, 2}; all with 128-byte swizzle.
+// {64, rows, columns / 64} with boxes {64, rows, 2}; all with 128-byte swizzle. map_o (read with
+// a.o_tma): the f16 output as a 2D tensor {heads * hd, rows}, boxes {hd, 16}, no swizzle.
 cudaError_t launch_attention(const CUtensorMap &map_q, const CUtensorMap &map_kv,
-                             const CUtensorMap &map_pos, const AttnArgs &a, int hd_pad, bool rel,
-                             int max_len, int nseg, cudaStream_t s);
+                             const CUtensorMap &map_pos, const CUtensorMap &map_o,
+                             const AttnArgs &a, int hd_pad, bool rel, int max_len, int nseg,
+                             cudaStream_t s);
 
 // Repacks attention operands into f16 rows with heads padded to `hd_pad` (zeros past hd):
 // out[row][sec * heads * hd_pad + h * hd_pad + c] = in[row][in_off[sec] + h * hd + c], for

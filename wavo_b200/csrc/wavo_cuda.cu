@@ -148,6 +148,23 @@ bool make_map3(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, u
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The attention output as a TMA store target: f16 rows x cols (row stride ld elements), boxes of
+// {box_cols, 16} rows, no swizzle (box_cols x 2 bytes a multiple of 16).
+bool make_map_o(CUtensorMap *m, void *base, uint64_t cols, uint64_t rows, uint64_t ld,
+                uint32_t box_cols) {
+  EncodeTiled enc = encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15u) ||
+      ((box_cols * 2) & 15u) || box_cols > 256 || rows == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, 16};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map_c(CUtensorMap *m, void *base, bool f16, uint64_t cols, uint64_t rows, uint64_t ld) {
   EncodeTiled enc = encoder();
   const uint64_t es = f16 ? 2 : 4;
@@ -639,7 +656,9 @@ wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const v
   a.o_f16 = o_dtype == WAVO_F16;
   a.err = ctx->dev_err;
 
-  CUtensorMap mq, mkv, mpos;
+  CUtensorMap mq, mkv, mpos, mo;
+  // f16 output whose head boxes start on 16-byte boundaries: stored with TMA (16 rows a warp).
+  a.o_tma = a.o_f16 && (hd * 2) % 16 == 0 && make_map_o(&mo, o, ch, rows, ch, hd);
   const int bk = wv::attn_block_keys(rel, hd_pad);
   if (direct) {
     a.head_stride = int(hd);
@@ -706,7 +725,9 @@ wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const v
         return fail(ctx, WAVO_ECUDA, "attention: tensor map of pos");
     }
   }
-  CK(wv::launch_attention(mq, mkv, mpos, a, hd_pad, rel, int(max_len), int(nseg), ctx->stream),
+  if (!a.o_tma) mo = mq;  // not read
+  CK(wv::launch_attention(mq, mkv, mpos, mo, a, hd_pad, rel, int(max_len), int(nseg),
+                          ctx->stream),
      "attention launch");
   return WAVO_OK;
 }
