@@ -250,6 +250,25 @@ def test_rope(gpu, neox):
     assert_near(got, want, 2e-5)
 
 
+@pytest.mark.parametrize("neox,hd,rot", [(True, 48, 48), (False, 64, 32), (True, 128, 64)])
+def test_rope_f16_rows(gpu, neox, hd, rot):
+    # f16 q|k rows (the projection's output), four pairs a thread: as the oracle's rope on the
+    # same f16 values, each result rounded to f16 once.
+    rows, heads, pos = 37, 4, 3
+    stride = 3 * heads * hd
+    x = O.f16_round(O.random(rows * stride, 32))
+    table = O.random((pos + rows) * rot, 33)
+    want = x.copy()
+    O.rope(want, np.ascontiguousarray(table[pos * rot:]), rows, heads, hd, rot, neox)
+    xb = torch.from_numpy(x).cuda().half()
+    gpu.pass_().rope(gpu.upload(table), xb, rows, pos, (heads, hd, rot), neox)
+    gpu.sync()
+    got = xb.float().cpu().numpy()
+    # Only the q and k sections rotate; v stays bit for bit.
+    assert np.array_equal(got.reshape(rows, 3, -1)[:, 2], x.reshape(rows, 3, -1)[:, 2])
+    assert_near(got, O.f16_round(want), 1e-3)
+
+
 @pytest.mark.parametrize("ty", [O.TY_F32, O.TY_F16, O.TY_Q8_0])
 def test_gemv(gpu, ty):
     # src/cpu/gemm.rs:616-640 `gemv_matches_dot` and Pass::gemv: one row, W not rounded, f32 sums.

@@ -236,6 +236,49 @@ __global__ void rope_kernel(const float *__restrict__ table, T *__restrict__ x, 
   }
 }
 
+// f16 rows, four rotary pairs a thread (half = rot / 2 a multiple of 4, 8-byte aligned heads):
+// one row per grid row, the row's cos / sin read as float4, the pairs as 8- or 16-byte words.
+__device__ __forceinline__ void rot2(float a, float b, float c, float s, __half &x0, __half &x1) {
+  x0 = __float2half_rn(a * c - b * s);
+  x1 = __float2half_rn(a * s + b * c);
+}
+
+__global__ void rope4_kernel(const float *__restrict__ table, __half *__restrict__ x,
+                             long long stride, int rows, int pos, const int *__restrict__ positions,
+                             int heads, int hd, int rot, int neox, int sections) {
+  const int half = rot / 2, q4 = half / 4;
+  const int per_row = sections * heads * q4;
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const long long at = positions ? positions[r] : pos + (long long)r;
+    const float *cs = table + at * rot;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < per_row; t += gridDim.x * blockDim.x) {
+      const int hh = t / q4, i = (t - hh * q4) * 4;
+      __half *head = x + (long long)r * stride + (long long)hh * hd;
+      const float4 c = *reinterpret_cast<const float4 *>(cs + i);
+      const float4 sn = *reinterpret_cast<const float4 *>(cs + half + i);
+      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+      if (neox) {  // pairs (i + k, i + k + half)
+        uint2 lo = *reinterpret_cast<const uint2 *>(head + i);
+        uint2 hi = *reinterpret_cast<const uint2 *>(head + i + half);
+        __half *l = reinterpret_cast<__half *>(&lo), *u = reinterpret_cast<__half *>(&hi);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          rot2(__half2float(l[k]), __half2float(u[k]), cc[k], ss[k], l[k], u[k]);
+        *reinterpret_cast<uint2 *>(head + i) = lo;
+        *reinterpret_cast<uint2 *>(head + i + half) = hi;
+      } else {  // pairs (2(i + k), 2(i + k) + 1)
+        uint4 w = *reinterpret_cast<const uint4 *>(head + 2 * i);
+        __half *e = reinterpret_cast<__half *>(&w);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          rot2(__half2float(e[2 * k]), __half2float(e[2 * k + 1]), cc[k], ss[k], e[2 * k],
+               e[2 * k + 1]);
+        *reinterpret_cast<uint4 *>(head + 2 * i) = w;
+      }
+    }
+  }
+}
+
 // ---- gemv ------------------------------------------------------------------------------
 
 // c[r][n] = epilogue(Σ_k a[r][k]·W[n][k] + bias[n]) for r < rows, in f32 (W f16 exact), one warp
@@ -618,6 +661,16 @@ cudaError_t launch_rope(const float *table, void *qkv, int x_f16, long long stri
                         int sections, cudaStream_t s) {
   const long long total = (long long)rows * sections * heads * (rot / 2);
   if (total <= 0) return cudaSuccess;
+  const int half = rot / 2;
+  const auto a16 = [](const void *p, unsigned n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+  if (x_f16 && half % 4 == 0 && a16(qkv, 16) && a16(table, 16) && stride % 8 == 0 && hd % 8 == 0) {
+    const int per_row = sections * heads * (half / 4);
+    const int threads = per_row < 256 ? (per_row + 31) / 32 * 32 : 256;
+    const dim3 grid((per_row + threads - 1) / threads, rows < 65535 ? rows : 65535);
+    rope4_kernel<<<grid, threads, 0, s>>>(table, reinterpret_cast<__half *>(qkv), stride, rows,
+                                          pos, positions, heads, hd, rot, neox, sections);
+    return cudaGetLastError();
+  }
   long long blocks = (total + 255) / 256;
   if (blocks > 4096) blocks = 4096;
   if (x_f16)
