@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m_use = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     bool ok = t < nt;
     for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait(&bar->s_full[t], j & 1, ab, kErrTimeoutConsumer)) { ok = false; break; }
+      if (!mbar_wait_warp(&bar->s_full[t], j & 1, ab, kErrTimeoutConsumer)) { ok = false; break; }
       tc_fence_after();
       float s[CW];
       {
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int x = 0; x < 8; ++x) pk[g / 2 + x] = pack_half2(p[2 * x], p[2 * x + 1]);
       }
       // P_t is free and O_t stable once P·V of block j - 1 landed.
-      if (j >= 1 && !mbar_wait(&bar->pv_done[t], (j - 1) & 1, ab, kErrTimeoutConsumer)) {
+      if (j >= 1 && !mbar_wait_warp(&bar->pv_done[t], (j - 1) & 1, ab, kErrTimeoutConsumer)) {
         ok = false;
         break;
       }
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->p_full[t]);
     }
-    if (ok && mbar_wait(&bar->o_full, 0, ab, kErrTimeoutConsumer)) {
+    if (ok && mbar_wait_warp(&bar->o_full, 0, ab, kErrTimeoutConsumer)) {
       // The row sum over both halves, then this thread's half of the row of O.
       float l = l0 + l1;
       l += __shfl_xor_sync(0xffffffffu, l, 16);

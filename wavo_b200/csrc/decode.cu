@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(128, 1)
       umma_commit(&bar->mma_done);
     }
   }
-  ok = mbar_wait(&bar->mma_done, 0, ab, kErrTimeoutConsumer);
+  ok = mbar_wait_warp(&bar->mma_done, 0, ab, kErrTimeoutConsumer);
   tc_fence_after();
   // lo (TMEM lanes 32-63) into shared memory (the A tile is no longer read), then hi + lo.
   float *dlo = reinterpret_cast<float *>(sa);  // [32 rows][129]

@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
-      if (!mbar_wait(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+      if (!mbar_wait_warp(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
       tc_fence_after();
       const long long row = m0 + row_in_tile;
       const bool row_ok = row < g.m;
@@ -562,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       };
       for (int tile = pair; tile < tiles; tile += npairs) {
         const int m0 = (tile / num_n) * (2 * BM), n0 = (tile % num_n) * BN;
-        if (!mbar_wait(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+        if (!mbar_wait_warp(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
         tc_fence_after();
 #pragma unroll 1
         for (int chunk = 0; chunk < BN / 32; ++chunk) {
@@ -601,7 +601,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     } else
     for (int tile = pair; tile < tiles; tile += npairs) {
       const int m0 = (tile / num_n) * (2 * BM), n0 = (tile % num_n) * BN;
-      if (!mbar_wait(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+      if (!mbar_wait_warp(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
       tc_fence_after();
       const long long row = m0 + row_in_tile;
       const bool row_ok = row < g.m;

@@ -114,6 +114,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, const 
   }
 }
 
+// mbar_wait by every lane of a warp that goes on to warp-collective instructions (tcgen05.ld / st
+// are .sync.aligned: the whole warp must execute them together). The lanes leave the wait loop on
+// their own; the vote converges the warp again and gives every lane the same outcome.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, const Abort &ab,
+                                               int code) {
+  const bool ok = mbar_wait(bar, parity, ab, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------------------------------------------------------------
 // TMA (no cluster forms: every CTA loads its own tiles)
 // ------------------------------------------------------------------------------------------
