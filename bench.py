@@ -379,7 +379,7 @@ RelPosWorkload.cpu = staticmethod(
 
 class C5(RelPosWorkload):
     scaling = "strong"
-    TRAFFIC = {"attention": 697688320 + 163500288, "gemm_qkv": 180414720 + 644850432}
+    TRAFFIC = {"attention": 697896192 + 160284672, "gemm_qkv": 180414720 + 644850432}
 
     def __init__(self, gpu, rank, world, seed=5000):
         super().__init__(gpu, rank, world, segment_lengths(seed, 400, 120, 300), 24, "q8_0", seed)
@@ -403,6 +403,8 @@ class C3(Workload):
     D, H, LAYERS = 768, 16, 16
     FRAME_S = 0.04
     scaling = "strong"
+    # DRAM read + write of one attention launch at 1 GPU (ncu capture of this config).
+    TRAFFIC = {"attention": 40322048 + 291584}
 
     def __init__(self, gpu, rank, world, seed=3000):
         import torch
