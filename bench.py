@@ -379,7 +379,7 @@ RelPosWorkload.cpu = staticmethod(
 
 class C5(RelPosWorkload):
     scaling = "strong"
-    TRAFFIC = {"attention": 697896192 + 160284672, "gemm_qkv": 180414720 + 644850432}
+    TRAFFIC = {"attention": 708701440 + 159529728, "gemm_qkv": 180414720 + 644850432}
 
     def __init__(self, gpu, rank, world, seed=5000):
         super().__init__(gpu, rank, world, segment_lengths(seed, 400, 120, 300), 24, "q8_0", seed)
