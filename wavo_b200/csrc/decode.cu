@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(256)
 // sums) to within f32 rounding. A CTA takes 128 features and a range of k (split-K for about one
 // CTA per SM); W comes by TMA, the partial sums go to c with vector f32 reductions.
 constexpr int GT_N = 128;      // features per CTA (UMMA N)
-constexpr int GT_KMAX = 256;   // k per CTA
+constexpr int GT_KMAX = 384;   // k per CTA (A and W tiles: 2 x 6 x 16 KB of shared memory)
 
 struct __align__(8) GtBarriers {
   uint64_t w_full;
@@ -736,6 +736,8 @@ cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map
                            const float *bias, float *c, long long ldc, int rows, int n, int k,
                            int epilogue, float alpha, int *err, cudaStream_t s) {
   if (rows <= 0 || n <= 0) return cudaSuccess;
+  // One wave: tiles x k-splits CTAs on the 148 SMs (one CTA per SM), k per split a multiple of 64
+  // up to GT_KMAX.
   const int tiles = (n + GT_N - 1) / GT_N;
   int ks = 148 / tiles;
   if (ks < 1) ks = 1;
@@ -753,7 +755,7 @@ cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(1024 + 8 * 16384 + sizeof(GtBarriers)));
+                                         int(1024 + 2 * (GT_KMAX / 64) * 16384 + sizeof(GtBarriers)));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
