@@ -133,11 +133,8 @@ def segment_lengths(seed, n, lo, hi):
 
 def my_segments(lengths, rank, world, cost):
     """This rank's segments (LPT over the ranks, deterministic), in their original order."""
-    if world == 1:
-        return list(range(len(lengths)))
-    from wavo_b200.gpu import partition_lpt
-    assign = partition_lpt([cost(t) for t in lengths], world)
-    return [i for i, a in enumerate(assign) if a == rank]
+    from wavo_b200.runner import ShardPlan
+    return ShardPlan.for_lengths(lengths, world, cost).mine(rank)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -780,10 +777,8 @@ def main():
     work = wl.work()
     top = max((k for k in totals if work.get(k, 0) > 0), key=totals.get)
 
-    vals = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = vals.tolist()
+    from wavo_b200.runner import max_over_ranks
+    ms, ms_e2e = max_over_ranks([ms, ms_e2e], device="cuda")
 
     if rank == 0:
         peaks = load_peaks()
