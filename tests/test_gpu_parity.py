@@ -44,9 +44,11 @@ def qkv_like(rng, t, ch, sections, std=0.7):
     return (rng.standard_normal((t, sections * ch)) * std).astype(np.float32)
 
 
-@pytest.mark.parametrize("t,heads,hd", [(1500, 20, 64), (750, 16, 48), (300, 4, 128), (129, 2, 64)])
+@pytest.mark.parametrize("t,heads,hd", [(1500, 20, 64), (1000, 20, 64), (750, 16, 48),
+                                         (300, 4, 128), (129, 2, 64)])
 def test_plain_attention_level_i(gpu, t, heads, hd):
-    # C2 (Whisper turbo encoder), C3 (GigaAM heads of 48), and tile edges; f16 operands straight
+    # C2 (Whisper turbo encoder; 7 CTAs of 224 rows a head), 1000 rows (CTAs of 144 rows: one live
+    # row group in the second tile), C3 (GigaAM heads of 48), and tile edges; f16 operands straight
     # from a [t][q | k | v] f16 buffer (the fast path).
     rng = np.random.default_rng(t + hd)
     ch = heads * hd
