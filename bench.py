@@ -694,8 +694,20 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its banner to the process's stdout when it builds the communicator; rank 0's
+        # one JSON line must stand alone there, so stdout points at stderr meanwhile.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            import ctypes
+            ctypes.CDLL(None).fflush(None)  # C stdio buffers out before fd 1 is restored
+            os.dup2(saved, 1)
+            os.close(saved)
     from wavo_b200.gpu import Gpu
 
     gpu = Gpu(local)
