@@ -132,9 +132,10 @@ def segment_lengths(seed, n, lo, hi):
 
 
 def my_segments(lengths, rank, world, cost):
-    """This rank's segments (LPT over the ranks, deterministic), in their original order."""
+    """This rank's segments (LPT over the ranks, deterministic), costliest first: the order they
+    are packed and launched in."""
     from wavo_b200.runner import ShardPlan
-    return ShardPlan.for_lengths(lengths, world, cost).mine(rank)
+    return ShardPlan.for_lengths(lengths, world, cost).launch_order(rank)
 
 
 # ---------------------------------------------------------------------------------------------

@@ -43,12 +43,18 @@ def _rank(rank, world, port, out_dir):
         flat = sorted(i for s in seen for i in s)
         assert flat == list(range(len(lengths))), "a segment ran on no rank or on two"
 
-        # This rank's "device output": its segments packed one after another (as the varlen
-        # launches write them), each row tagged with its segment and row index.
+        # This rank's "device output": its segments packed one after another in launch order
+        # (costliest first, as the varlen launches take them), each row tagged with its segment
+        # and row index.
+        order = plan.launch_order(rank)
+        assert sorted(order) == mine
+        costs = [plan.costs[i] for i in order]
+        assert costs == sorted(costs, reverse=True)
         packed = np.concatenate([np.stack([np.full(lengths[i], i, np.float32),
                                            np.arange(lengths[i], dtype=np.float32)], 1)
-                                 for i in mine])
-        ordered = gather_in_order(plan, rank, split_rows(packed, [lengths[i] for i in mine]))
+                                 for i in order])
+        ordered = gather_in_order(plan, rank, split_rows(packed, [lengths[i] for i in order]),
+                                  order=order)
         if rank == 0:
             assert len(ordered) == len(lengths)
             for i, o in enumerate(ordered):
@@ -84,11 +90,15 @@ def test_plan_single_rank_keeps_everything_in_order():
     from wavo_b200.runner import ShardPlan, gather_in_order
     plan = ShardPlan([5, 3, 9], 1)
     assert plan.mine(0) == [0, 1, 2]
+    assert plan.launch_order(0) == [2, 0, 1]
     assert gather_in_order(plan, 0, ["a", "b", "c"]) == ["a", "b", "c"]
+    assert gather_in_order(plan, 0, ["c", "a", "b"], order=[2, 0, 1]) == ["a", "b", "c"]
     with pytest.raises(ValueError):
         plan.mine(1)
     with pytest.raises(ValueError):
         gather_in_order(plan, 0, ["a"])
+    with pytest.raises(ValueError):
+        gather_in_order(plan, 0, ["a", "b", "c"], order=[0, 1, 1])
 
 
 def test_split_rows_rejects_a_wrong_total():
