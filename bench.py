@@ -847,7 +847,12 @@ def main():
             peak, unit, src = peaks["hbm"], "GB/s", "HBM copy"
         else:
             achieved = work[top] / (per[top] * 1e-3) / 1e12
-            peak, unit, src = peaks["tensor_sustained"], "TFLOP/s", "bf16 sustained"
+            # The burst GEMM peak while the clocks ran free; the sustained one (the power-capped
+            # clock of a long dense loop) when the power cap held the clocks during the step.
+            if "sw_power_cap" in clocks.summary().get("reasons", []):
+                peak, unit, src = peaks["tensor_sustained"], "TFLOP/s", "bf16 sustained (power cap seen)"
+            else:
+                peak, unit, src = peaks["tensor"], "TFLOP/s", "bf16 burst (no power cap seen)"
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             from oracle import oracle as O
