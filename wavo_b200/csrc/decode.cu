@@ -465,7 +465,8 @@ __global__ void __launch_bounds__(256)
 // hi in rows 0-31 and lo in rows 32-63 (rows 64-127 zero), so D rows r and r + 32 are hi·W^T and
 // lo·W^T with W exact in f16 and f32 accumulation — the reference's gemv (W not rounded, f32
 // sums) to within f32 rounding. A CTA takes 128 features and a range of k (split-K for about one
-// CTA per SM); W comes by TMA, the partial sums go to c with vector f32 reductions.
+// CTA per SM); W comes by TMA while the CTA builds its A tile from coalesced loads of a, and the
+// partial sums go to c with f32 reductions, one 128-byte line of a row per warp instruction.
 constexpr int GT_N = 128;      // features per CTA (UMMA N)
 constexpr int GT_KMAX = 384;   // k per CTA (A and W tiles: 2 x 6 x 16 KB of shared memory)
 
@@ -476,16 +477,10 @@ struct __align__(8) GtBarriers {
   uint32_t abort;
 };
 
-__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
-
 __global__ void __launch_bounds__(128, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const float *__restrict__ a,
                    long long lda, const float *__restrict__ bias, float *__restrict__ c,
-                   long long ldc, int rows, int n, int k, int kr, int epi, float alpha, int vec,
+                   long long ldc, int rows, int n, int k, int kr, int epi, float alpha,
                    int *err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -519,38 +514,44 @@ __global__ void __launch_bounds__(128, 1)
     for (int ch = 0; ch < nch; ++ch)
       tma_load_2d(sw + ch * 16384, &map_w, &bar->w_full, k0 + ch * 64, f0);
   }
-  // The A tile: thread t builds row t.
+  // The A tile: rows 0-31 hi = f16(a), rows 32-63 lo = f16(a - hi). Warp w loads rows w, w + 4,
+  // ... of the CTA's k-slice, lane l the float4s l, l + 32, l + 64 of a row, so that each load
+  // instruction reads consecutive bytes and all 24 are in flight before the first conversion.
+  // Rows past `rows` and columns past the slice are zero; rows 64-127 are left as they are: they
+  // only feed accumulator rows that are never read.
   {
-    const int r = threadIdx.x;
-    const int src = r < 32 ? r : r - 32;
-    const bool live = r < 64 && src < rows;
-    const float *arow = a + (long long)src * lda + k0;
-    for (int ch = 0; ch < nch; ++ch) {
+    const int q4 = kr / 4;  // float4s per row of the slice (at most 96)
+    float4 v[8][3];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int kk = ch * 64 + u * 8;
-        float x[8];
-        if (live && kk < kn) {
-          const float4 p = *reinterpret_cast<const float4 *>(arow + kk);
-          const float4 q = *reinterpret_cast<const float4 *>(arow + kk + 4);
-          x[0] = p.x; x[1] = p.y; x[2] = p.z; x[3] = p.w;
-          x[4] = q.x; x[5] = q.y; x[6] = q.z; x[7] = q.w;
-        } else {
+    for (int i = 0; i < 8; ++i) {
+      const int row = int(warp) + 4 * i;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) x[j] = 0.0f;
-        }
-        uint32_t h[4];
+      for (int j = 0; j < 3; ++j) {
+        const int c4 = int(lane) + 32 * j;
+        v[i][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (row < rows && c4 < q4 && 4 * c4 < kn)
+          v[i][j] = *reinterpret_cast<const float4 *>(a + (long long)row * lda + k0 + 4 * c4);
+      }
+    }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float x0 = x[2 * j], x1 = x[2 * j + 1];
-          if (r >= 32) {  // the low part: what f16 rounding of a left out
-            x0 -= __half2float(__float2half_rn(x0));
-            x1 -= __half2float(__float2half_rn(x1));
-          }
-          h[j] = pack_half2(x0, x1);
-        }
-        *reinterpret_cast<uint4 *>(sa + ch * 16384 + r * 128 + ((u ^ (r & 7)) * 16)) =
-            make_uint4(h[0], h[1], h[2], h[3]);
+    for (int i = 0; i < 8; ++i) {
+      const int row = int(warp) + 4 * i;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int c4 = int(lane) + 32 * j;
+        if (c4 >= q4) continue;
+        const int kk = 4 * c4;
+        const float x[4] = {v[i][j].x, v[i][j].y, v[i][j].z, v[i][j].w};
+        float lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) lo[e] = x[e] - __half2float(__float2half_rn(x[e]));
+        // 16-byte chunk (kk % 64) / 8 of the row in the 128-byte swizzle, this float4's half of it.
+        const int off =
+            (kk >> 6) * 16384 + ((((kk & 63) >> 3) ^ (row & 7)) * 16) + ((kk >> 2) & 1) * 8;
+        *reinterpret_cast<uint2 *>(sa + off + row * 128) =
+            make_uint2(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]));
+        *reinterpret_cast<uint2 *>(sa + off + (row + 32) * 128) =
+            make_uint2(pack_half2(lo[0], lo[1]), pack_half2(lo[2], lo[3]));
       }
     }
   }
@@ -575,8 +576,11 @@ __global__ void __launch_bounds__(128, 1)
   }
   ok = mbar_wait_warp(&bar->mma_done, 0, ab, kErrTimeoutConsumer);
   tc_fence_after();
-  // lo (TMEM lanes 32-63) into shared memory (the A tile is no longer read), then hi + lo.
-  float *dlo = reinterpret_cast<float *>(sa);  // [32 rows][129]
+  // hi·W (TMEM lanes 0-31) and lo·W (lanes 32-63) meet in shared memory (the A tile is no longer
+  // read): warp 1 writes lo, warp 0 adds hi, the bias (first k-split only) and alpha. Then all four
+  // warps reduce into c, a row's 128 features per warp (lane l: features l, l + 32, l + 64,
+  // l + 96), so that each reduction instruction covers one 128-byte line of c.
+  float *sum = reinterpret_cast<float *>(sa);  // [32 rows][129]
   if (ok && warp == 1) {
 #pragma unroll 1
     for (int q = 0; q < GT_N / 32; ++q) {
@@ -584,35 +588,36 @@ __global__ void __launch_bounds__(128, 1)
       tmem_ld32(tmem + ((32u) << 16) + q * 32, v);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) dlo[lane * 129 + q * 32 + j] = __uint_as_float(v[j]);
+      for (int j = 0; j < 32; ++j) sum[lane * 129 + q * 32 + j] = __uint_as_float(v[j]);
     }
   }
   __syncthreads();
   if (ok && warp == 0) {
-    const bool live = int(lane) < rows;
-    float *crow = c + (long long)lane * ldc;
 #pragma unroll 1
     for (int q = 0; q < GT_N / 32; ++q) {
       uint32_t v[32];
       tmem_ld32(tmem + q * 32, v);
       tmem_wait_ld();
       const int fb = f0 + q * 32;
-      float y[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        float t = __uint_as_float(v[j]) + dlo[lane * 129 + q * 32 + j];
+        float t = __uint_as_float(v[j]) + sum[lane * 129 + q * 32 + j];
         if (blockIdx.y == 0 && fb + j < n) t += bias[fb + j];
-        y[j] = epi == kResidual ? alpha * t : t;
+        sum[lane * 129 + q * 32 + j] = epi == kResidual ? alpha * t : t;
       }
-      if (live) {
-        if (vec && fb + 32 <= n) {
+    }
+  }
+  __syncthreads();
+  if (ok) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i) {
+      const int row = int(warp) * 8 + i;
+      if (row >= rows) break;
+      float *crow = c + (long long)row * ldc + f0;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) red_add_v4(crow + fb + j, y[j], y[j + 1], y[j + 2], y[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (fb + j < n) atomicAdd(crow + fb + j, y[j]);
-        }
+      for (int j = 0; j < GT_N / 32; ++j) {
+        const int f = int(lane) + 32 * j;
+        if (f0 + f < n) atomicAdd(crow + f, sum[row * 129 + f]);
       }
     }
   }
@@ -759,9 +764,8 @@ cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const int vec = (reinterpret_cast<uintptr_t>(c) % 16 == 0) && (ldc % 4 == 0);
   gemv_tc_kernel<<<dim3(tiles, ks), 128, smem, s>>>(map_w128, a, lda, bias, c, ldc, rows, n, k, kr,
-                                                   epilogue, alpha, vec, err);
+                                                   epilogue, alpha, err);
   return cudaGetLastError();
 }
 
