@@ -62,7 +62,7 @@ __device__ __forceinline__ float2 h2f(uint32_t w) {
 
 // CTA (split, head, segment): keys split·ATT_KEYS .. of head h of segment b. Writes the partial
 // (Σ e·V, m, l) to part, or with one split the normalised output directly.
-__global__ void __launch_bounds__(ATT_THREADS)
+__global__ void __launch_bounds__(ATT_THREADS, 5)
     attend_kernel(const float *__restrict__ q, long long q_stride, const uint32_t *__restrict__ kv,
                   long long kv_stride, float *__restrict__ part, float *__restrict__ o,
                   long long o_stride, int n, int cols, int hd, float scale) {
@@ -91,7 +91,51 @@ __global__ void __launch_bounds__(ATT_THREADS)
   const bool vec = aligned && ((cols & 3) == 0);
 #pragma unroll
   for (int u = 0; u < 4; ++u) sc[u] = 0.0f;
-  if (jt < nk) {
+  if (vec && nk <= 4 * (ATT_THREADS / 4)) {
+    // At most 256 keys (a decoder's self-attention): thread t takes key quad t % 64 over a quarter
+    // of the pairs (8 at hd 64), its loads issued four at a time; the quarters meet in ps.
+    const int kq = threadIdx.x % (ATT_THREADS / 4), pg = threadIdx.x / (ATT_THREADS / 4);
+    const int jq = 4 * kq, ppg = (pairs + 3) / 4;
+    const int i0 = pg * ppg, i1 = min(pairs, i0 + ppg);
+    float pa[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (jq < nk) {
+      for (int i = i0; i < i1; i += 4) {
+        uint32_t w[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (i + u >= i1) break;
+          const uint32_t *row = kt + (long long)(i + u) * cols + j0 + jq;
+          if (jq + 3 < nk) {
+            const uint4 x = *reinterpret_cast<const uint4 *>(row);
+            w[u][0] = x.x; w[u][1] = x.y; w[u][2] = x.z; w[u][3] = x.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w[u][e] = jq + e < nk ? row[e] : 0u;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (i + u >= i1) break;
+          const float q0 = qs[2 * (i + u)], q1 = qs[2 * (i + u) + 1];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 k = h2f(w[u][e]);
+            pa[e] = fmaf(q1, k.y, fmaf(q0, k.x, pa[e]));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ps[pg * (ATT_KEYS / 4) + jq + e] = pa[e];
+    __syncthreads();
+    if (jt < nk) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        sc[e] = ps[jt + e] + ps[ATT_KEYS / 4 + jt + e] + ps[2 * (ATT_KEYS / 4) + jt + e] +
+                ps[3 * (ATT_KEYS / 4) + jt + e];
+    }
+    __syncthreads();  // ps is rewritten with the probabilities below
+  } else if (jt < nk) {
     if (vec && jt + 3 < nk) {
       for (int i = 0; i < pairs; ++i) {
         const uint4 w = *reinterpret_cast<const uint4 *>(kt + (long long)i * cols + j0 + jt);
