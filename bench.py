@@ -13,9 +13,11 @@ A step is one pass of the config's unit of work (c2: one 30 s window through 32 
 whole 224-token decode of the batch; c3/c5: the whole batch of segments), captured once as a CUDA
 graph and replayed. Every layer's input is a pre-LayerNorm activation ~N(0,1) and its output is
 added into an f32 residual stream (the LayerNorm and FFN around the attention are out of scope).
-The default is c2; the multi-segment configs shard their segments over the ranks by
-longest-processing-time-first (strong scaling, no collective), c1/c2 run one unit per rank
-(replicas, weak scaling).
+The default is c5, the long-form config: the largest one that fits one GPU and the one whose
+1 -> 8 GPU scaling is the target. The multi-segment configs (c3, c4, c5) shard their segments over
+the ranks by longest-processing-time-first (strong scaling, no collective) and gather every
+segment's output to one host buffer in segment order inside the end-to-end timed region; c1/c2
+run one unit per rank (replicas, weak scaling).
 """
 
 from __future__ import annotations
@@ -131,11 +133,12 @@ def segment_lengths(seed, n, lo, hi):
     return np.random.default_rng(seed).integers(lo, hi + 1, size=n).tolist()
 
 
-def my_segments(lengths, rank, world, cost):
-    """This rank's segments (LPT over the ranks, deterministic), costliest first: the order they
-    are packed and launched in."""
+def shard(lengths, rank, world, cost):
+    """The plan (LPT over the ranks, deterministic) and this rank's segments costliest first: the
+    order they are packed and launched in."""
     from wavo_b200.runner import ShardPlan
-    return ShardPlan.for_lengths(lengths, world, cost).launch_order(rank)
+    plan = ShardPlan.for_lengths(lengths, world, cost)
+    return plan, plan.launch_order(rank)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -155,6 +158,21 @@ class Workload:
 
     def total_audio_s(self, world) -> float:  # whole job per step
         return self.audio_s() * world
+
+    # Segment workloads set these: the plan over the ranks, this rank's segments in packed order,
+    # every segment's length in rows of the output, and the output's width.
+    plan = None
+    order = None
+    seg_rows = None
+    out_width = None
+
+    def host_gather(self, rank):
+        """The node-wide segment-ordered host output of this workload's result, or None."""
+        if self.plan is None:
+            return None
+        from wavo_b200.runner import HostGather
+        hg = HostGather(self.plan, self.seg_rows, self.out_width, rank, order=self.order)
+        return hg if hg.available else None
 
 
 class C2(Workload):
@@ -252,7 +270,8 @@ class RelPosWorkload(Workload):
         D = self.D
         self.all_lengths = lengths
         cost = lambda t: 24 * (6 * t * t * D + 10 * t * D * D)  # noqa: E731
-        mine = my_segments(lengths, rank, world, cost)
+        self.plan, mine = shard(lengths, rank, world, cost)
+        self.order, self.seg_rows, self.out_width = mine, list(lengths), D
         self.lengths = [lengths[i] for i in mine]
         rng = np.random.default_rng(seed)  # the same weights on every rank
         ty = GGML_Q8_0 if ty_name == "q8_0" else GGML_F32
@@ -322,7 +341,9 @@ class C1(RelPosWorkload):
     scaling = "weak"
 
     def __init__(self, gpu, rank, world, seed=1000):
-        super().__init__(gpu, rank, 1, [138], 1, "f32", seed)
+        # One unit per rank (replicas): every rank runs the same single segment on its own.
+        super().__init__(gpu, 0, 1, [138], 1, "f32", seed)
+        self.plan = None
 
     def total_audio_s(self, world):
         return self.audio_s() * world
@@ -391,8 +412,10 @@ class C5(RelPosWorkload):
                 f"{self.world} GPU(s), no collective"}
 
     @staticmethod
-    def cpu_sample(layers=1, seed=5000):
-        lens = segment_lengths(seed, 400, 120, 300)[:2]
+    def cpu_sample(layers=2, seed=5000):
+        # Every 25th of the 400 segments (16, spanning the length distribution) through 2 of the
+        # 24 identical layers, scaled to the set by their audio seconds.
+        lens = segment_lengths(seed, 400, 120, 300)[::25]
         return RelPosWorkload.cpu(seed, lens, layers, "q8_0", 1)
 
 
@@ -412,8 +435,9 @@ class C3(Workload):
         D = self.D
         self.all_lengths = segment_lengths(seed, 16, 400, 750)
         cost = lambda t: 16 * (4 * t * t * D + 8 * t * D * D)  # noqa: E731
-        self.lengths = [self.all_lengths[i] for i in my_segments(self.all_lengths, rank, world,
-                                                                 cost)]
+        self.plan, mine = shard(self.all_lengths, rank, world, cost)
+        self.order, self.seg_rows, self.out_width = mine, list(self.all_lengths), D
+        self.lengths = [self.all_lengths[i] for i in mine]
         rng = np.random.default_rng(seed)
         self.blocks = [RotaryAttention(gpu, GGML_BF16, D, self.H, bf16_weights(rng, 3 * D, D, 0.02),
                                        bf16_weights(rng, D, D, 0.02), theta=10000.0,
@@ -506,8 +530,11 @@ class C4(Workload):
         from wavo_b200.blocks import DecoderAttention
         self.gpu, self.world = gpu, world
         D = self.D
-        per = [len(range(r, self.BATCH, world)) for r in range(world)]
-        self.batch = per[rank]
+        # Decode streams of equal cost: longest-first over the ranks deals them round-robin.
+        self.plan, _ = shard([1] * self.BATCH, rank, world, lambda t: 1)
+        self.order = self.plan.mine(rank)
+        self.seg_rows, self.out_width = [1] * self.BATCH, D
+        self.batch = len(self.order)
         rng = np.random.default_rng(seed)
         self.layers = []
         for _ in range(self.LAYERS):
@@ -660,7 +687,10 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
             "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD_NAMES[args.config]},
+            "config": {"workload": WORKLOAD_NAMES[args.config],
+                       "sample": sample + " per step; value = the sample's audio seconds over "
+                                 "its CPU time (the layers and segments are alike, so the rate "
+                                 "carries over to the whole workload)"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
                              "sample": sample + " per step (CPU oracle restating the "
                              "reference's src/cpu attention path)"},
@@ -674,7 +704,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default="c5", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="wavo", choices=["wavo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -743,13 +773,27 @@ def main():
     barrier()
 
     # ---- end to end: H2D of the step's inputs (pinned), the step, D2H of its result ----
-    # Serial: the copies and the step one after another on the launching stream.
+    # Serial: the copies and the step one after another on the launching stream. Segment
+    # workloads read their result back segment by segment into one node-wide host buffer in
+    # segment order (every rank over its own host link), and the step ends when every rank's rows
+    # are there (each rank's stream drained, then a barrier): the ordered gather to the host.
+    hg = wl.host_gather(rank)
+
+    def read_back():
+        if hg is not None:
+            for _, dev_t in wl.outputs():
+                hg.copy_from(dev_t)
+        else:
+            for host_t, dev_t in wl.outputs():
+                host_t.copy_(dev_t, non_blocking=True)
+
     def e2e_step():
         for dev_t, host_t in wl.inputs():
             dev_t.copy_(host_t, non_blocking=True)
         graph.launch()
-        for host_t, dev_t in wl.outputs():
-            host_t.copy_(dev_t, non_blocking=True)
+        read_back()
+        if hg is not None:
+            hg.wait(stream)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -771,6 +815,8 @@ def main():
     h2d_s, d2h_s = torch.cuda.Stream(local), torch.cuda.Stream(local)
     in_stage = [(dev_t, host_t, torch.empty_like(dev_t)) for dev_t, host_t in wl.inputs()]
     out_stage = [(host_t, dev_t, torch.empty_like(dev_t)) for host_t, dev_t in wl.outputs()]
+    if hg is not None:
+        hg.wait(stream)  # the serial loop's last rows are in place before the buffer is reused
     in_free, in_ready = torch.cuda.Event(), torch.cuda.Event()
     out_free, out_ready = torch.cuda.Event(), torch.cuda.Event()
 
@@ -792,7 +838,10 @@ def main():
         with torch.cuda.stream(d2h_s):
             d2h_s.wait_event(out_ready)
             for host_t, _, st in out_stage:
-                host_t.copy_(st, non_blocking=True)
+                if hg is not None:
+                    hg.copy_from(st)
+                else:
+                    host_t.copy_(st, non_blocking=True)
             out_free.record(d2h_s)
 
     for _ in range(args.warmup):
@@ -805,6 +854,8 @@ def main():
     for _ in range(args.steps):
         pipelined_step()
     stream.wait_event(out_free)  # the last result is in host memory
+    if hg is not None:
+        hg.wait(stream)  # and every rank's
     f1.record(stream)
     torch.cuda.synchronize()
     gpu.sync()
@@ -842,17 +893,19 @@ def main():
 
     if rank == 0:
         peaks = load_peaks()
+        clk = clocks.summary()
+        clock_frac = None
         if wl.bound == "hbm":
             achieved = work[top] / (per[top] * 1e-3) / 1e9
             peak, unit, src = peaks["hbm"], "GB/s", "HBM copy"
         else:
             achieved = work[top] / (per[top] * 1e-3) / 1e12
-            # The burst GEMM peak while the clocks ran free; the sustained one (the power-capped
-            # clock of a long dense loop) when the power cap held the clocks during the step.
-            if "sw_power_cap" in clocks.summary().get("reasons", []):
-                peak, unit, src = peaks["tensor_sustained"], "TFLOP/s", "bf16 sustained (power cap seen)"
-            else:
-                peak, unit, src = peaks["tensor"], "TFLOP/s", "bf16 burst (no power cap seen)"
+            # The burst GEMM peak (cuBLAS at free-running clocks) is the denominator; the tensor
+            # peak scales with the SM clock, so the fraction at the clock sampled during the
+            # timed region is reported beside it.
+            peak, unit, src = peaks["tensor"], "TFLOP/s", "bf16 burst"
+            if clk.get("sm_mhz") and clk.get("sm_max_mhz"):
+                clock_frac = achieved / (peak * clk["sm_mhz"] / clk["sm_max_mhz"])
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             from oracle import oracle as O
@@ -872,22 +925,30 @@ def main():
             "e2e": {"value": total_audio / (ms_e2e_serial * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "copies": "serial: each step's H2D, the step, its D2H, one after another",
+                    "gather": ("every segment's output rows to their place in one node-wide "
+                               "host buffer in segment order (each rank over its own host "
+                               "link), every rank's copies done and a barrier, each step")
+                              if hg is not None else "none (one unit per rank)",
                     "pipelined_value": total_audio / (ms_e2e * 1e-3),
                     "pipelined": "step k+1's H2D and step k's D2H on two copy streams overlap "
                                  "step k (pinned staging, device copies in and out)"},
             "gpu_launches": wl.launches() * args.steps,
             "roofline": {"bound": wl.bound, "kernel": top, "achieved": achieved, "peak": peak,
                          "unit": unit, "frac": achieved / peak,
+                         "frac_at_sampled_clock": clock_frac,
                          "traffic": wl.TRAFFIC.get(top),
                          "peak_source": f"{peaks['source']} {src}"},
             "kernels_ms": per,
-            "clocks": clocks.summary(),
+            "clocks": clk,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     del graph
+    if hg is not None:
+        hg.close()
     gpu.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -76,7 +76,9 @@ int wavo_device_count(void);
 wavo_status wavo_create(int device, wavo_ctx **out);
 void wavo_destroy(wavo_ctx *ctx);
 
-/* The last error message of the context (or of the last failed wavo_create when ctx is NULL). */
+/* The last error message of the context. With ctx NULL: the last error of a call without a
+ * context (wavo_create, wavo_attend_batch_noalloc) made by the calling thread; each thread has
+ * its own, valid until that thread's next such call fails. */
 const char *wavo_last_error(const wavo_ctx *ctx);
 
 /* Runs the context's work on `stream` (a cudaStream_t; NULL is the CUDA default stream). A new
@@ -241,6 +243,19 @@ wavo_status wavo_capture_begin(wavo_ctx *ctx);
 wavo_status wavo_capture_end(wavo_ctx *ctx, wavo_graph **out);
 wavo_status wavo_graph_launch(wavo_ctx *ctx, const wavo_graph *g);
 void wavo_graph_destroy(wavo_graph *g);
+
+/* ---- self-checks of the device building blocks (no reference counterpart) -------------- */
+
+/* Test support for the completion check (Gpu::run, src/gpu/mod.rs:969-1003): enqueues one warp
+ * that waits on an mbarrier nothing arms, through the same bounded wait every kernel of this
+ * library uses, with a limit of `limit_cycles` SM cycles (1 .. the kernels' ~1 s default). The
+ * wait gives up, the kernel returns, and the next wavo_sync reports WAVO_EDEVICE; the context
+ * stays usable. */
+wavo_status wavo_selftest_wait_timeout(wavo_ctx *ctx, uint64_t limit_cycles);
+
+/* y[i] = 2^x[i] (device buffers of n floats) by the FMA-pipe polynomial the attention softmax
+ * computes part of its exponentials with, for x in [-125, 8] (below -125 it returns 2^-125). */
+wavo_status wavo_selftest_exp2(wavo_ctx *ctx, const float *x, float *y, uint32_t n);
 
 /* ---- sharding: the segment partition of the multi-GPU runner ---------------------------- */
 

@@ -81,3 +81,29 @@ def test_partition_lpt(parts):
     for c, p in zip(costs, got):
         loads[p] += c
     assert loads.max() / loads.mean() < 1.02
+
+
+def test_context_free_errors_are_per_thread():
+    # Two threads fail context-free calls (argument errors, returned before any CUDA call) with
+    # different messages and read wavo_last_error(NULL) many times: each thread reads its own
+    # message, never the other thread's or a freed one.
+    import threading
+
+    lib = L.lib()
+    bad = {}
+
+    def worker(tag, heads):
+        for _ in range(2000):
+            # hd 3 is odd: rejected with the thread's own head count in the message.
+            st = lib.wavo_attend_batch_noalloc(1, 0, 1, 0, 1, 0, 10, 10, heads, 3, 1, None)
+            msg = lib.wavo_last_error(None).decode()
+            if st != L.EINVAL or f"heads {heads} of 3" not in msg:
+                bad[tag] = msg
+                return
+
+    ts = [threading.Thread(target=worker, args=(i, h)) for i, h in enumerate((7, 11))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not bad, bad

@@ -62,20 +62,38 @@ def test_plain_attention_level_i(gpu, t, heads, hd):
     check(o.float().cpu().numpy(), want)
 
 
+def grid(rng, shape, step, bound):
+    """Values on a grid of `step` (a power of two) within (-bound, bound): sums of such values stay
+    exact in f16 and f32, so that the GPU's f16 operands and the oracle's f32 operands agree."""
+    x = np.clip(rng.standard_normal(shape) * bound / 3, -bound + step, bound - step)
+    return (np.round(x / step) * step).astype(np.float32)
+
+
+def rel_inputs(rng, t, heads, hd, pos_rows):
+    """q, k, v, u, v_bias and a position table on which q+u and q+v are exact in f16: the GPU's
+    [q+u | k | v | q+v] rows and the oracle's own sums of q [q | k | v] with u and v are the same
+    values (level (i))."""
+    ch = heads * hd
+    q = grid(rng, (t, ch), 2.0 ** -8, 4.0)
+    kv = f16(qkv_like(rng, t, ch, 2))
+    u = grid(rng, ch, 2.0 ** -8, 0.25)
+    vb = grid(rng, ch, 2.0 ** -8, 0.25)
+    pos = f16(rng.standard_normal((pos_rows, ch)) * 0.5)
+    qkv = np.ascontiguousarray(np.concatenate([q, kv], axis=1))
+    quv = np.ascontiguousarray(np.concatenate([q + u, kv, q + vb], axis=1))
+    assert np.array_equal(f16(quv), quv)
+    return qkv, quv, u, vb, pos
+
+
 @pytest.mark.parametrize("t", [138, 300, 64, 1])
 def test_relative_attention_level_i(gpu, t):
-    # C1 / C5 shapes: 8 heads of 128, positions pos_rows(t); inputs rounded to f16 for the oracle.
+    # C1 / C5 shapes, 8 heads of 128, positions pos_rows(t), against the oracle's
+    # relative_attention (src/cpu/ops.rs:223-273) on identical values; f32 and f16 operand rows.
     heads, hd = 8, 128
     ch = heads * hd
     rng = np.random.default_rng(t)
-    qkv = f16(qkv_like(rng, t, ch, 3))
-    u = f16(rng.standard_normal(ch) * 0.02)
-    vb = f16(rng.standard_normal(ch) * 0.02)
-    pos = f16(rng.standard_normal((O.pos_rows(t), ch)) * 0.5)
-    # The oracle forms q+u and q+v in f32; the kernel reads them as f16, so round them first.
-    q = qkv[:, :ch]
-    quv = np.concatenate([f16(q + u), qkv[:, ch:], f16(q + vb)], axis=1)
-    want = naive_rel(quv, pos, t, heads, hd)
+    qkv, quv, u, vb, pos = rel_inputs(rng, t, heads, hd, O.pos_rows(t))
+    want = O.relative_attention(qkv.ravel(), pos.ravel(), u, vb, t, heads, ch)
     for dtype in (torch.float32, torch.float16):
         xb = torch.from_numpy(quv).cuda().to(dtype)
         pb = torch.from_numpy(pos).cuda().to(dtype)
@@ -83,21 +101,6 @@ def test_relative_attention_level_i(gpu, t):
         gpu.pass_().attention(xb, None, pb, o, t, heads, hd)
         gpu.sync()
         check(o.float().cpu().numpy(), want)
-
-
-def naive_rel(quv, pos, t, heads, hd):
-    d = heads * hd
-    i = np.arange(t)[:, None]
-    j = np.arange(t)[None, :]
-    out = np.zeros((t, d))
-    for h in range(heads):
-        sl = slice(h * hd, (h + 1) * hd)
-        qu, k, v, qv = (quv[:, s * d:(s + 1) * d][:, sl].astype(np.float64) for s in range(4))
-        bd = np.take_along_axis(qv @ pos[:, sl].astype(np.float64).T, j + t + 15 - i, axis=1)
-        s = (qu @ k.T + bd) / np.sqrt(hd)
-        e = np.exp(s - s.max(axis=1, keepdims=True))
-        out[:, sl] = (e / e.sum(axis=1, keepdims=True)) @ v
-    return out
 
 
 def test_relative_attention_matches_the_cpu_oracle(gpu):
@@ -121,8 +124,9 @@ def test_relative_attention_matches_the_cpu_oracle(gpu):
 
 
 def test_varlen_segments(gpu):
-    # Independent segments in one launch equal each segment alone (plain and relative); rows
-    # between segments (gaps of 5) are left as they were.
+    # Independent segments in one launch equal each segment alone through the oracle (plain and
+    # relative, the relative ones sharing one position table); rows between segments (gaps of 5)
+    # are left as they were.
     rng = np.random.default_rng(3)
     lens = [200, 37, 129, 300, 1, 256]
     gap = 5
@@ -131,10 +135,12 @@ def test_varlen_segments(gpu):
     for rel in (False, True):
         heads, hd = (8, 128) if rel else (4, 64)
         ch = heads * hd
-        secs = 4 if rel else 3
-        x = f16(qkv_like(rng, rows, ch, secs))
         pos_t = max(lens)
-        pos = f16(rng.standard_normal((O.pos_rows(pos_t), ch)) * 0.5) if rel else None
+        if rel:
+            qkv, x, u, vb, pos = rel_inputs(rng, rows, heads, hd, O.pos_rows(pos_t))
+        else:
+            x = f16(qkv_like(rng, rows, ch, 3))
+            pos = None
         xb = torch.from_numpy(x).cuda().half()
         pb = torch.from_numpy(pos).cuda().half() if rel else None
         o = torch.full((rows, ch), 7.0, dtype=torch.float16, device="cuda")
@@ -144,13 +150,14 @@ def test_varlen_segments(gpu):
         gpu.sync()
         got = o.float().cpu().numpy()
         for s, n in zip(starts, lens):
-            seg = x[s:s + n]
             if rel:
                 # The shared table: row r is position pos_t + 15 - r; this segment's rows r' =
                 # r - (pos_t - n) give its own pos_rows(n) table.
-                p = pos[pos_t - n: pos_t - n + O.pos_rows(n)]
-                want = naive_rel(seg, p, n, heads, hd)
+                p = np.ascontiguousarray(pos[pos_t - n: pos_t - n + O.pos_rows(n)])
+                want = O.relative_attention(np.ascontiguousarray(qkv[s:s + n]).ravel(), p.ravel(),
+                                            u, vb, n, heads, ch)
             else:
+                seg = x[s:s + n]
                 want = O.attention(np.ascontiguousarray(seg.ravel()), 3 * ch,
                                    np.ascontiguousarray(seg.ravel()[2 * ch:]), 3 * ch, n, heads, ch)
             check(got[s:s + n], want)

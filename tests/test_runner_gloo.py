@@ -63,6 +63,21 @@ def _rank(rank, world, port, out_dir):
         else:
             assert ordered is None
 
+        # The same outputs through the node-wide shared host buffer: each rank writes its own
+        # segments' rows to their places; rank 0 reads them all in segment order.
+        from wavo_b200.runner import HostGather
+        import torch
+        hg = HostGather(plan, lengths, 2, rank, order=order)
+        assert hg.available
+        hg.copy_from(torch.from_numpy(packed))
+        hg.wait()
+        if rank == 0:
+            for i, t in enumerate(lengths):
+                seg = hg.segment(i).numpy()
+                assert (seg[:, 0] == i).all() and (seg[:, 1] == np.arange(t)).all(), i
+        dist.barrier()
+        hg.close()
+
         # Step timing: the slowest rank sets the time.
         got = max_over_ranks([1.0 + rank, 10.0 - rank])
         assert got == [float(world), 10.0]

@@ -1,7 +1,8 @@
 """wavo_attend_batch_noalloc (no reference counterpart): the decoder attention with its split
 partials in the library's fixed device array, against wavo_attend_batch with a caller-provided
-`part` buffer (the entry point of Pass::attend, src/gpu/mod.rs:1485-1505), through the C ABI.
-Collected last so that it also runs after every other GPU test in one process."""
+`part` buffer (the entry point of Pass::attend, src/gpu/mod.rs:1485-1505) and against the CPU
+oracle's attend (src/cpu/ops.rs:300-337), through the C ABI. Collected last so that it also runs
+after every other GPU test in one process."""
 
 import ctypes
 
@@ -10,6 +11,17 @@ import pytest
 import torch
 
 from wavo_b200 import _lib as L
+
+
+def oracle_cache(kv_words: np.ndarray, d: int, cols: int, heads: int, hd: int) -> np.ndarray:
+    """The cache of one segment in the oracle's layout ([K heads][cols][hd] then the same for V,
+    f32) from the GPU layout (f16 pairs in 32-bit words: K transposed, pair i of position j at
+    word i·cols + j, then V by position at word d/2·cols + j·d/2 + i)."""
+    h = kv_words.view(np.float16).astype(np.float32)
+    k = h[:d * cols].reshape(d // 2, cols, 2).transpose(1, 0, 2).reshape(cols, d)
+    v = h[d * cols:2 * d * cols].reshape(cols, d)
+    to_heads = lambda m: m.reshape(cols, heads, hd).transpose(1, 0, 2).ravel()  # noqa: E731
+    return np.ascontiguousarray(np.concatenate([to_heads(k), to_heads(v)]))
 
 
 def _ptr(t: torch.Tensor) -> int:
@@ -64,6 +76,16 @@ def test_noalloc_matches_attend_batch(n, cols, heads, hd, batch):
             o = got[:, :d].cpu().numpy()
             assert np.isfinite(w).all() and np.isfinite(o).all(), f"call {call}"
             assert np.abs(o - w).max() <= 2e-5, f"call {call}: {np.abs(o - w).max():.3g}"
+            # And the oracle, within the BASELINE tolerance (max-abs 2e-3, relative-L2 1e-3).
+            from oracle import oracle as O
+            kv_h = kv.cpu().numpy()
+            q_h = q.cpu().numpy()
+            for b in range(batch):
+                ref = O.attend(np.ascontiguousarray(q_h[b, :d]),
+                               oracle_cache(kv_h[b], d, cols, heads, hd), cols, n, heads, hd)
+                err = np.abs(o[b] - ref).max()
+                rel = np.linalg.norm(o[b] - ref) / np.linalg.norm(ref)
+                assert err <= 2e-3 and rel <= 1e-3, f"call {call} segment {b}: {err:.3g} {rel:.3g}"
             # The padding between rows is not written.
             assert torch.isnan(got[:, d:]).all(), f"call {call}"
     finally:

@@ -67,6 +67,8 @@ SIGNATURES = {
     "wavo_graph_launch": ([_vp, _vp], _st),
     "wavo_graph_destroy": ([_vp], None),
     "wavo_partition_lpt": ([_vp, _u32, _u32, _vp], _st),
+    "wavo_selftest_wait_timeout": ([_vp, _u64], _st),
+    "wavo_selftest_exp2": ([_vp, _vp, _vp, _u32], _st),
 }
 
 _lib = None

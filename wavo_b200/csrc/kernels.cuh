@@ -143,4 +143,11 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
                         const float *scales, const float *bias, float *c, long long ldc, int rows,
                         int n, int k, int epilogue, float alpha, cudaStream_t s);
 
+// ---- self-checks (selftest.cu) -------------------------------------------------------------
+
+// One warp waits on an mbarrier nothing arms, giving up after `limit` cycles (raises *err).
+cudaError_t launch_wait_probe(int *err, long long limit, cudaStream_t s);
+// y[i] = 2^x[i] by the softmax's FMA-pipe polynomial (x in [-125, 8]).
+cudaError_t launch_exp2_probe(const float *x, float *y, int n, cudaStream_t s);
+
 }  // namespace wv

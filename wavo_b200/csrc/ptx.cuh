@@ -44,6 +44,10 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -85,10 +89,12 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
   return ok != 0;
 }
 
-// Per-CTA abort word in shared memory plus the launch's device error word in global memory.
+// Per-CTA abort word in shared memory plus the launch's device error word in global memory, and
+// the cycles a wait may take before it gives up (kWaitCycles unless a launch asks for less).
 struct Abort {
   volatile uint32_t *flag;  // shared
   int *err;                 // global
+  long long limit = kWaitCycles;
   __device__ __forceinline__ bool raised() const { return *flag != 0; }
   __device__ __forceinline__ void raise(int code) const {
     *flag = 1u;
@@ -97,17 +103,18 @@ struct Abort {
 };
 
 // Waits for the phase of `bar` with parity `parity` to complete. Returns false (and raises the
-// abort) if the CTA aborted meanwhile or the wait ran past kWaitCycles.
+// abort) if the CTA aborted meanwhile or the wait ran past ab.limit cycles.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, const Abort &ab,
                                           int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
 #pragma unroll 1
   while (true) {
-    // Each try sleeps until the phase completes, 100 us at most, then the limits are checked.
-    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    // Each try sleeps until the phase completes, 100 us at most (less under a short limit), then
+    // the limits are checked.
+    if (mbar_try_wait_sleep(bar, parity, ab.limit < 200000000ll ? 1000u : 100000u)) return true;
     if (ab.raised()) return false;
-    if (clock64() - start > kWaitCycles) {
+    if (clock64() - start > ab.limit) {
       ab.raise(code);
       return false;
     }

@@ -58,8 +58,10 @@ struct wavo_graph {
 
 namespace {
 
-std::mutex g_create_mu;
-std::string g_create_err;
+// The last error of the calls that have no context (a failed wavo_create, the context-free
+// wavo_attend_batch_noalloc), one per thread: a failing call on one thread never replaces the
+// message another thread is reading.
+thread_local std::string t_last_err;
 
 wavo_status fail(wavo_ctx *c, wavo_status s, const char *fmt, ...) {
   char buf[512];
@@ -67,12 +69,10 @@ wavo_status fail(wavo_ctx *c, wavo_status s, const char *fmt, ...) {
   va_start(ap, fmt);
   vsnprintf(buf, sizeof buf, fmt, ap);
   va_end(ap);
-  if (c) {
+  if (c)
     c->err = buf;
-  } else {
-    std::lock_guard<std::mutex> g(g_create_mu);
-    g_create_err = buf;
-  }
+  else
+    t_last_err = buf;
   return s;
 }
 
@@ -228,8 +228,7 @@ int wavo_device_count(void) {
 
 const char *wavo_last_error(const wavo_ctx *ctx) {
   if (ctx) return ctx->err.c_str();
-  std::lock_guard<std::mutex> g(g_create_mu);
-  return g_create_err.c_str();
+  return t_last_err.c_str();
 }
 
 wavo_status wavo_create(int device, wavo_ctx **out) {
@@ -877,6 +876,30 @@ void wavo_graph_destroy(wavo_graph *gr) {
   if (gr->exec) cudaGraphExecDestroy(gr->exec);
   if (gr->graph) cudaGraphDestroy(gr->graph);
   delete gr;
+}
+
+// ---- self-checks ---------------------------------------------------------------------------
+
+wavo_status wavo_selftest_wait_timeout(wavo_ctx *ctx, uint64_t limit_cycles) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (limit_cycles == 0 || limit_cycles > uint64_t(wv::kWaitCycles))
+    return fail(ctx, WAVO_EINVAL, "selftest_wait_timeout: limit of %llu cycles (1 .. %lld)",
+                (unsigned long long)limit_cycles, wv::kWaitCycles);
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_wait_probe(ctx->dev_err, (long long)limit_cycles, ctx->stream), "wait probe");
+  return WAVO_OK;
+}
+
+wavo_status wavo_selftest_exp2(wavo_ctx *ctx, const float *x, float *y, uint32_t n) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (n == 0) return WAVO_OK;
+  if (!x || !y) return fail(ctx, WAVO_EINVAL, "selftest_exp2: NULL buffer");
+  if (n > 0x7fffffffu) return fail(ctx, WAVO_EINVAL, "selftest_exp2: n %u", n);
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_exp2_probe(x, y, int(n), ctx->stream), "exp2 probe");
+  return WAVO_OK;
 }
 
 // ---- sharding ----------------------------------------------------------------------------

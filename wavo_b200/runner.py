@@ -4,13 +4,16 @@ wavo's long-audio path runs the pieces that src/split.rs cut at pauses one after
 (src/lib.rs:844-900); the pieces share nothing, so they partition across devices with no exchange
 on the data path. Every rank builds the same `ShardPlan` (longest processing time first through
 `wavo_partition_lpt`, deterministic), runs its own segments as varlen launches on its own stream,
-and copies each segment's output rows to the host. `gather_in_order` then hands rank 0 every
-segment's output in the original segment order, the order wavo concatenates transcripts in.
-The only cross-rank traffic is that host-side gather and `max_over_ranks` of the step timings.
+and copies each segment's output rows to the host. `HostGather` puts every rank's segment rows
+straight into one node-wide host buffer in the original segment order (the order wavo
+concatenates transcripts in), each GPU over its own host link; `gather_in_order` does the same
+through the process group's object gather where shared memory is short. The only cross-rank
+traffic is a barrier and `max_over_ranks` of the step timings.
 """
 
 from __future__ import annotations
 
+import os
 from typing import Callable, Sequence
 
 from .gpu import partition_lpt
@@ -114,3 +117,120 @@ def max_over_ranks(values: Sequence[float], device=None, group=None) -> list[flo
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return t.tolist()
+
+
+class HostGather:
+    """The segment outputs of every rank of one node, in segment order, in one host buffer.
+
+    Rank 0 creates a shared-memory buffer of Σ len rows of `width` values; every rank maps it,
+    registers it with CUDA (page-locked, so device-to-host copies run asynchronously at full PCIe
+    rate), and copies each of its own segments' rows from its packed device output straight to the
+    segment's place — each GPU over its own host link, nothing between GPUs. After `wait` (the
+    copies done on every rank, then a barrier) rank 0 reads every segment's output in segment
+    order from `rows()`; `segment(i)` is segment i's rows. With one rank the buffer is private.
+
+    When the node's shared memory cannot hold the buffer, `available` is False and the caller
+    falls back to `gather_in_order`.
+    """
+
+    def __init__(self, plan: ShardPlan, lengths: Sequence[int], width: int, rank: int,
+                 order: Sequence[int] | None = None, group=None):
+        import numpy as np
+        import torch
+
+        self.plan, self.rank, self.group = plan, rank, group
+        self.lengths = [int(t) for t in lengths]
+        self.width = int(width)
+        self.order = list(order) if order is not None else plan.mine(rank)
+        if sorted(self.order) != plan.mine(rank):
+            raise ValueError(f"rank {rank}: the order lists other segments than the plan gives it")
+        self.offsets = [0]
+        for t in self.lengths:
+            self.offsets.append(self.offsets[-1] + t)
+        total = self.offsets[-1]
+        nbytes = max(total * self.width * 4, 4)
+        self._shm = None
+        self._registered = None
+        self.available = True
+        if plan.world > 1:
+            import torch.distributed as dist
+            from multiprocessing import shared_memory
+            name = [None]
+            if rank == 0:
+                st = os.statvfs("/dev/shm") if os.path.isdir("/dev/shm") else None
+                if st is None or st.f_bavail * st.f_frsize < nbytes + (64 << 20):
+                    name[0] = ""
+                else:
+                    self._shm = shared_memory.SharedMemory(create=True, size=nbytes)
+                    name[0] = self._shm.name
+            dist.broadcast_object_list(name, src=0, group=group)
+            if not name[0]:
+                self.available = False
+                return
+            if rank != 0:
+                self._shm = shared_memory.SharedMemory(name=name[0])
+                # Rank 0 created the segment and removes it; the others only map it.
+                from multiprocessing import resource_tracker
+                resource_tracker.unregister(self._shm._name, "shared_memory")
+            buf = np.ndarray((total, self.width), np.float32, buffer=self._shm.buf)
+            self.host = torch.from_numpy(buf)
+        else:
+            self.host = torch.empty((total, self.width), dtype=torch.float32)
+        if torch.cuda.is_available():
+            if plan.world > 1:
+                err = torch.cuda.cudart().cudaHostRegister(self.host.data_ptr(), nbytes, 0)
+                if int(err) != 0:
+                    raise RuntimeError(f"cudaHostRegister of the shared output: error {int(err)}")
+                self._registered = self.host.data_ptr()
+            else:
+                self.host = self.host.pin_memory()
+        # (packed row, output row, rows) of each of this rank's segments; adjacent runs merged.
+        runs, at = [], 0
+        for i in self.order:
+            t = self.lengths[i]
+            if runs and runs[-1][0] + runs[-1][2] == at and runs[-1][1] + runs[-1][2] == \
+                    self.offsets[i]:
+                runs[-1][2] += t
+            else:
+                runs.append([at, self.offsets[i], t])
+            at += t
+        self.runs = [tuple(r) for r in runs]
+        self.packed_rows = at
+
+    def copy_from(self, packed) -> None:
+        """Enqueues the copies of this rank's packed output rows ([Σ its len][width], in `order`)
+        to their places (device tensors: asynchronous on the current stream)."""
+        if packed.shape[0] != self.packed_rows or packed.shape[1] != self.width:
+            raise ValueError(f"packed output {tuple(packed.shape)}, expected "
+                             f"({self.packed_rows}, {self.width})")
+        nb = packed.is_cuda
+        for src, dst, n in self.runs:
+            self.host[dst:dst + n].copy_(packed[src:src + n], non_blocking=nb)
+
+    def wait(self, stream=None) -> None:
+        """The copies of every rank have landed: this rank's stream drained, then a barrier."""
+        import torch
+        if torch.cuda.is_available():
+            (stream or torch.cuda.current_stream()).synchronize()
+        if self.plan.world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
+
+    def rows(self):
+        """All segments' rows in segment order (rank 0, after `wait`)."""
+        return self.host
+
+    def segment(self, i: int):
+        return self.host[self.offsets[i]:self.offsets[i + 1]]
+
+    def close(self) -> None:
+        import torch
+        if self._registered is not None:
+            torch.cuda.cudart().cudaHostUnregister(self._registered)
+            self._registered = None
+        self.host = None
+        if self._shm is not None:
+            self._shm.close()
+            if self.rank == 0:
+                self._shm.unlink()
+            self._shm = None
