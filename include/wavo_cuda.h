@@ -128,6 +128,16 @@ uint32_t wavo_linear_k(const wavo_linear *l);
 wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, const wavo_linear *l,
                       void *c, int c_dtype, uint32_t ldc, uint32_t m, int epilogue, float alpha);
 
+/* How wavo_gemm reads a Q8_0 layer's weights. The reference's GEMM dequantises Q8_0 blocks as it
+ * stages each K-step (src/gpu/gemm.wgsl:105-130); WAVO_Q8_PROLOGUE does the same (int8 values and
+ * scales by TMA, converted to f16 tiles in shared memory: one byte a weight from HBM), while
+ * WAVO_Q8_DEQUANT reads the f16 copy made at wavo_linear_create. Both give bit-identical results.
+ * WAVO_Q8_AUTO (the default) is the faster of the two at every measured shape, the f16 copy: the
+ * converters' shared-memory traffic costs more than the halved weight bytes save (the weights are
+ * L2-resident across row tiles). Returns the previous mode. */
+enum { WAVO_Q8_AUTO = 0, WAVO_Q8_DEQUANT = 1, WAVO_Q8_PROLOGUE = 2 };
+int wavo_set_q8_gemm(wavo_ctx *ctx, int mode);
+
 /* Pass::gemv: c[offset..] = epilogue(a·W^T + b) for one f32 row, W not rounded (f32 sums). */
 wavo_status wavo_gemv(wavo_ctx *ctx, const float *a, const wavo_linear *l, float *c, int epilogue,
                       float alpha, uint32_t offset);

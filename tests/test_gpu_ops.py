@@ -289,3 +289,63 @@ def test_gemv(gpu, ty):
     want = O.Linear(ty, n, k, data, bias).gemv(x, epilogue="gelu")
     got = run_out(gpu, np.zeros(lin.cols + 3), lambda p, c: p.gemv(xb, lin, c, "gelu", offset=3))
     assert_near(got[3:3 + n], want, 2e-5)
+
+
+@pytest.mark.parametrize("m,n,k,dual", [
+    (1, 164, 96, 0),        # k % 64 == 32: the last K-step's second half is the TMA's zero fill
+    (37, 288, 96, 64),      # dual outputs
+    (138, 3072, 1024, 1024),  # C1: the rel-pos layer's [q+u | k | v | q+v] projection
+    (300, 1024, 1024, 0),   # three row tiles
+    (2100, 1024, 256, 0),   # many row tiles: the persistent tile loop
+])
+def test_gemm_q8_prologue_matches_dequant(gpu, m, n, k, dual):
+    # Q8_0 dequantised in the GEMM's prologue (src/gpu/gemm.wgsl:105-130) against the layer's
+    # load-time f16 copy: the converters round q·d to f16 as the load does, so the outputs are
+    # bit-identical.
+    from wavo_b200 import _lib as L
+    w = O.random(n * k, 11) * 0.05
+    b = O.random(n + dual, 12)
+    lin = gpu.linear(O.TY_Q8_0, n, k, O.q8_0_bytes(w), b)
+    width = lin.width()
+    a = gpu.upload(O.random(m * k, 13))
+    c0 = O.random(m * width, 14)
+    outs = {}
+    old = gpu.set_q8_gemm(L.Q8_AUTO)
+    try:
+        for mode in (L.Q8_DEQUANT, L.Q8_PROLOGUE):
+            gpu.set_q8_gemm(mode)
+            for e in ("bias", "residual", "gelu"):
+                outs[mode, e] = run_out(gpu, c0, lambda p, out: p.gemm(a, lin, out, m, e, 0.5))
+    finally:
+        gpu.set_q8_gemm(old)
+    for e in ("bias", "residual", "gelu"):
+        np.testing.assert_array_equal(outs[L.Q8_PROLOGUE, e], outs[L.Q8_DEQUANT, e])
+
+
+@pytest.mark.parametrize("vnni", [0, -1])
+def test_gemm_q8_prologue_vs_oracle(gpu, vnni):
+    # The C1/C5 projection shape through the prologue path against the CPU oracle's Q8_0 GEMM, in
+    # its f16-rounded mode and in the mode the reference picks on this host (i16 VNNI on AVX-VNNI,
+    # src/cpu/gemm.rs:129-161), at the model tolerance.
+    from wavo_b200 import _lib as L
+    m, n, k = 138, 1024, 1024
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal(n * k) * 0.02).astype(np.float32)
+    data = O.q8_0_bytes(w)
+    lin = gpu.linear(O.TY_Q8_0, n, k, data, None)
+    a = rng.standard_normal(m * k).astype(np.float32)
+    old = gpu.set_q8_gemm(L.Q8_PROLOGUE)
+    try:
+        got = run_out(gpu, np.zeros(m * n, np.float32),
+                      lambda p, out: p.gemm(gpu.upload(a), lin, out, m, "bias"))
+    finally:
+        gpu.set_q8_gemm(old)
+    prev = O.vnni()
+    O.set_vnni(vnni)
+    try:
+        want = O.Linear(O.TY_Q8_0, n, k, data, np.zeros(n, np.float32)).gemm(a, m)
+    finally:
+        O.set_vnni(prev)
+    err = np.abs(got - want)
+    rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err.max() <= 2e-3 and rel <= 1e-3, f"max-abs {err.max():.3g}, rel-L2 {rel:.3g}"

@@ -16,6 +16,7 @@ STATUS = {0: "OK", 1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEDOUT", 5: "EUN
           6: "EDEVICE"}
 F32, F16 = 0, 1
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
+Q8_AUTO, Q8_DEQUANT, Q8_PROLOGUE = 0, 1, 2  # wavo_set_q8_gemm modes
 WAVO_ATTEND_NOALLOC_PART_FLOATS = 1 << 18  # the header's fixed scratch of the no-alloc attend
 EPILOGUES = {"bias": 0, "silu": 1, "relu": 2, "residual": 3, "gelu": 4, "gelu_residual": 5,
              "tanh": 6}
@@ -45,6 +46,7 @@ SIGNATURES = {
     "wavo_linear_width": ([_vp], _u32),
     "wavo_linear_k": ([_vp], _u32),
     "wavo_gemm": ([_vp, _vp, _i32, _u32, _vp, _vp, _i32, _u32, _u32, _i32, _f32], _st),
+    "wavo_set_q8_gemm": ([_vp, _i32], _i32),
     "wavo_gemv": ([_vp, _vp, _vp, _vp, _i32, _f32, _u32], _st),
     "wavo_gemv_rows": ([_vp, _vp, _u32, _vp, _vp, _u32, _u32, _i32, _f32], _st),
     "wavo_attention": ([_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i32], _st),

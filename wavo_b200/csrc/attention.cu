@@ -267,8 +267,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool is_s = warp == 1;
       bool ok = true;
       bool issued = false;
-      const int hsteps = (a.hd + 15) / 16;
-      // Descriptors are linear in the start address (bits 0-13 hold address / 16).
+      // Descriptors are linear in the start address (bits 0-13 hold address / 16). Heads are 128
+      // wide on this path (the host zero-pads narrower ones), so the score loops issue all eight
+      // K-steps, unrolled and unconditional: issue loops with a guard on each UMMA produced wrong
+      // scores, the unguarded and the rolled forms are exact.
       const uint64_t dq = sdesc_sw128(smem_u32(smem + OFF_Q), 16, 1024);
       const uint64_t dqv = sdesc_sw128(smem_u32(smem + OFF_QV), 16, 1024);
       const uint64_t dk = sdesc_sw128(smem_u32(smem + OFF_K), 16, 1024);
@@ -289,13 +291,15 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const uint64_t bpw = dpw + uint64_t((ps * PW_BYTES) >> 4);
             const uint64_t bk = dk + uint64_t((s * KV_BYTES) >> 4);
-            for (int kk = 0; kk < hsteps; ++kk) {
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
               const uint64_t oq = uint64_t(((kk >> 2) * ATOM_Q + (kk & 3) * 32) >> 4);
               umma_f16(tmem + T_BD, dqv + oq,
                        bpw + uint64_t(((kk >> 2) * ATOM_PW + (kk & 3) * 32) >> 4), IDESC_BD,
                        kk > 0 ? 1u : 0u);
             }
-            for (int kk = 0; kk < hsteps; ++kk) {
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
               const uint64_t oq = uint64_t(((kk >> 2) * ATOM_Q + (kk & 3) * 32) >> 4);
               umma_f16(tmem + T_S, dq + oq,
                        bk + uint64_t(((kk >> 2) * ATOM_KV + (kk & 3) * 32) >> 4), IDESC_S,

@@ -77,7 +77,9 @@ struct __align__(8) FaBarriers {
   uint32_t abort;
 };
 
-template <int HD, int BN>
+// KS: K-steps of 16 columns in a score UMMA group (the head's width in 16s; all HD / 16 when the
+// host zero-padded the heads).
+template <int HD, int BN, int KS>
 __global__ void __launch_bounds__(THREADS, 1)
     fa_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
               const __grid_constant__ CUtensorMap map_o, const AttnArgs a) {
@@ -186,9 +188,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0 && t < nt) {
       bool ok = mbar_wait(&bar->q_full, 0, ab, kErrTimeoutMma);
       bool issued = false;
-      const int hsteps = (a.hd + 15) / 16;
       // Descriptors are linear in the start address (bits 0-13 hold address / 16), so every
-      // operand's descriptor is a base plus an offset / 16.
+      // operand's descriptor is a base plus an offset / 16. The score loop is unrolled over a
+      // compile-time count of K-steps and issues every UMMA unconditionally: the same loop with a
+      // guard on each UMMA (k-step < the head's steps) produced wrong scores; the unguarded and
+      // the rolled forms are exact.
       const uint64_t dq = sdesc_sw128(smem_u32(smem + C::OFF_Q + t * C::Q_BYTES), 16, 1024);
       const uint64_t dk = sdesc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
       const uint64_t dv = sdesc_sw128(smem_u32(smem + C::OFF_V), C::ATOM_KV, 1024);
@@ -207,7 +211,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
           const uint64_t bk0 = dk + uint64_t((ks * C::KV_BYTES) >> 4);
-          for (int kk = 0; kk < hsteps; ++kk) {
+#pragma unroll
+          for (int kk = 0; kk < KS; ++kk) {
             const uint32_t o_q = ((kk >> 2) * C::ATOM_Q + (kk & 3) * 32) >> 4;
             const uint32_t o_k = ((kk >> 2) * C::ATOM_KV + (kk & 3) * 32) >> 4;
             umma_f16(tt + C::T_S, dq + o_q, bk0 + o_k, C::IDESC_S, kk > 0 ? 1u : 0u);
@@ -436,7 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-template <int HD, int BN>
+template <int HD, int BN, int KS>
 cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const CUtensorMap &o,
                       const AttnArgs &a, int max_len, int nseg, cudaStream_t s) {
   using C = Fa<HD, BN>;
@@ -445,13 +450,13 @@ cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const CUtenso
   cudaGetDevice(&dev);
   static bool configured[64] = {};
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fa_kernel<HD, BN>,
+    cudaError_t e = cudaFuncSetAttribute(fa_kernel<HD, BN, KS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   dim3 grid((max_len + NT * BM - 1) / (NT * BM), a.heads, nseg);
-  return launch_pdl(fa_kernel<HD, BN>, grid, dim3(THREADS), smem, s, q, kv, o, a);
+  return launch_pdl(fa_kernel<HD, BN, KS>, grid, dim3(THREADS), smem, s, q, kv, o, a);
 }
 
 }  // namespace
@@ -462,8 +467,15 @@ cudaError_t launch_fa_attention(const CUtensorMap &map_q, const CUtensorMap &map
                                 const CUtensorMap &map_o, const AttnArgs &a, int hd_pad,
                                 int max_len, int nseg, cudaStream_t s) {
   if (max_len <= 0 || nseg <= 0) return cudaSuccess;
-  if (hd_pad == 64) return launch_fa<64, 128>(map_q, map_kv, map_o, a, max_len, nseg, s);
-  return launch_fa<128, 64>(map_q, map_kv, map_o, a, max_len, nseg, s);
+  if (hd_pad == 128) return launch_fa<128, 64, 8>(map_q, map_kv, map_o, a, max_len, nseg, s);
+  // Heads read in place (a head stride below 64): the head's own K-steps; zero-padded heads: all.
+  const int ks = a.head_stride < 64 ? (a.hd + 15) / 16 : 4;
+  switch (ks) {
+    case 1: return launch_fa<64, 128, 1>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    case 2: return launch_fa<64, 128, 2>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    case 3: return launch_fa<64, 128, 3>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    default: return launch_fa<64, 128, 4>(map_q, map_kv, map_o, a, max_len, nseg, s);
+  }
 }
 
 }  // namespace wv

@@ -326,6 +326,287 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ---- Q8_0 GEMM: W dequantised in the prologue -------------------------------------------------
+//
+// The reference's GPU GEMM reads Q8_0 blocks (int8 values, one f16 scale per 32) and dequantises
+// them as it stages each K-step (src/gpu/gemm.wgsl:105-130, WTYPE = Q8_0). Here the int8 values of
+// a 64-column K-step stream by TMA into a raw staging area of the stage (64 bytes a row, no
+// swizzle); four converter warps turn them into the f16 W tile the UMMA reads (the canonical
+// 128-byte-swizzled K-major layout), q·d rounded to f16 exactly as the load-time dequantisation
+// (an f16 multiply of an exact integer and an exact scale is the correctly rounded product), so the
+// results are bit-identical to the f16-weight GEMM. W moves through HBM and L2 at one byte per
+// weight plus 2 bytes of scale per 32; the f16 tile never exists in global memory.
+//   warp 0      TMA: a (f16, swizzled), the int8 block values of W and their two rows of scales
+//               (a transposed f16 copy [k / 32][n] made at load, so that a K-step's scales are one
+//               box)
+//   warp 1      one thread issues the UMMAs of a stage once the converters finished its W tile
+//   warps 2-5   epilogue (as gemm_kernel)
+//   warps 6-13  converters: thread t converts 16-byte chunks (8 values) c = t % 8 of rows t / 8 +
+//               32 i; a warp reads 256 contiguous staging bytes and writes four whole 128-byte rows
+//               of the swizzled tile (no bank conflicts either way)
+constexpr int kQ8ConvWarps = 8;
+constexpr int kQ8Threads = 32 * (6 + kQ8ConvWarps);
+
+template <int BN>
+struct GemmQ8Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;  // the converted f16 tile
+  static constexpr int Q_BYTES = BN * BK;      // int8 staging
+  static constexpr int S_BYTES = 2 * BN * 2;   // the K-step's two scale rows (f16)
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES + Q_BYTES + S_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGES = (208 * 1024) / STAGE_BYTES > 6 ? 6 : (208 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+  static_assert(BN % 32 == 0 && STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "tile shape");
+  static constexpr uint32_t IDESC = idesc_f16(BM, BN, 0);
+};
+
+struct __align__(8) GemmQ8Barriers {
+  uint64_t full[6];     // a and the int8 values landed (TMA)
+  uint64_t conv[6];     // the f16 W tile is written (four converter warps)
+  uint64_t empty[6];    // the stage's UMMAs completed
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+// Two f16 values of signed bytes b0, b1 of x: 0x6400 | (b ^ 0x80) is the f16 1024 + (b + 128),
+// exact; subtracting 1152 leaves b.
+__device__ __forceinline__ __half2 i8x2_to_h2(uint32_t x, uint32_t sel) {
+  const uint32_t v = __byte_perm(x ^ 0x80808080u, 0x64646464u, sel);
+  return __hsub2(*reinterpret_cast<const __half2 *>(&v), __float2half2_rn(1152.0f));
+}
+
+template <int BN, int E>
+__global__ void __launch_bounds__(kQ8Threads, 1)
+    gemm_q8_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_q,
+                   const __grid_constant__ CUtensorMap tma_s, const GemmArgs g) {
+  using C = GemmQ8Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  GemmQ8Barriers *bar = reinterpret_cast<GemmQ8Barriers *>(smem + STAGES * C::STAGE_BYTES);
+  const uint32_t warp = warp_id(), lane = lane_id();
+
+  const int num_m = (g.m + BM - 1) / BM;
+  const int num_n = (g.cols + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (g.k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar->full[s], 1);
+      mbar_init(&bar->conv[s], kQ8ConvWarps);
+      mbar_init(&bar->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar->acc_full[b], 1);
+      mbar_init(&bar->acc_empty[b], 4);
+    }
+    mbar_init(&bar->drain, 1);
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_q);
+    prefetch_tmap(&tma_s);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  const Abort ab{&bar->abort, g.err};
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
+
+  if (warp == 0) {
+    // ---- TMA producer --------------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&bar->empty[stage], phase ^ 1u, ab, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + stage * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&bar->full[stage], C::A_BYTES + C::Q_BYTES + C::S_BYTES);
+          tma_load_2d(sa, &tma_a, &bar->full[stage], kb * BK, m0);
+          tma_load_2d(sa + C::A_BYTES + C::B_BYTES, &tma_q, &bar->full[stage], kb * BK, n0);
+          // Scale rows 2 kb, 2 kb + 1 (k % 64 == 32: the second is the TMA's zero fill).
+          tma_load_2d(sa + C::A_BYTES + C::B_BYTES + C::Q_BYTES, &tma_s, &bar->full[stage], n0,
+                      2 * kb);
+          armed |= 1u << stage;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(armed & (1u << s))) continue;
+          const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&bar->full[s], par) && clock64() - t0 < kWaitCycles) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----------------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&bar->acc_empty[acc], acc_phase ^ 1u, ab, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          // The converters waited for the stage's loads: their arrival covers a as well.
+          if (!mbar_wait(&bar->conv[stage], phase, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks)
+            umma_f16(d, sdesc_sw128(sa + ks * 32, 16, 1024), sdesc_sw128(sb + ks * 32, 16, 1024),
+                     C::IDESC, (kb | ks) != 0);
+          issued = true;
+          umma_commit(&bar->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&bar->acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued) {
+        umma_commit(&bar->drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&bar->drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ---- epilogue: warps 2..5, one accumulator row per thread -----------------------------
+    const uint32_t quarter = warp & 3u;
+    const int row_in_tile = int(quarter * 32 + lane);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+      if (!mbar_wait_warp(&bar->acc_full[acc], acc_phase, ab, kErrTimeoutConsumer)) break;
+      tc_fence_after();
+      const long long row = m0 + row_in_tile;
+      const bool row_ok = row < g.m;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        const int col0 = n0 + chunk * 32;
+        if (col0 >= g.cols) break;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((quarter * 32u) << 16) + uint32_t(acc * BN + chunk * 32), r);
+        const int lim = min(32, g.cols - col0);
+        float b[32];
+        load_bias32(g.bias + col0, lim, b);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (row_ok) store_row32<E>(g, row, col0, lim, v, b);
+        if (col0 < g.dual) {
+          const int lim2 = min(lim, g.dual - col0);
+          load_bias32(g.bias + g.cols + col0, lim2, b);
+          if (row_ok) store_row32<kBias>(g, row, g.cols + col0, lim2, v, b);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---- converters: warps 6..13 -----------------------------------------------------------
+    const int t = int(threadIdx.x) - 6 * 32;  // 0..255
+    const int c = t & 7;                      // 16-byte chunk of a 128-byte row (8 values)
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int n0 = (tile % num_n) * BN;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait_warp(&bar->full[stage], phase, ab, kErrTimeoutConsumer)) {
+          ok = false;
+          break;
+        }
+        uint8_t *sb = smem + stage * C::STAGE_BYTES + C::A_BYTES;
+        const uint8_t *sq = sb + C::B_BYTES;
+        // Chunk c's scale: Q8 block 2 kb + c / 4 of the row, scale row c / 4 of the stage.
+        const __half *ss = reinterpret_cast<const __half *>(sq + C::Q_BYTES) + (c >> 2) * BN;
+#pragma unroll
+        for (int r = t >> 3; r < BN; r += 32) {
+          const __half2 d2 = __half2half2(ss[r]);
+          const uint2 q = *reinterpret_cast<const uint2 *>(sq + r * BK + c * 8);
+          const __half2 h0 = __hmul2(i8x2_to_h2(q.x, 0x4140u), d2);
+          const __half2 h1 = __hmul2(i8x2_to_h2(q.x, 0x4342u), d2);
+          const __half2 h2 = __hmul2(i8x2_to_h2(q.y, 0x4140u), d2);
+          const __half2 h3 = __hmul2(i8x2_to_h2(q.y, 0x4342u), d2);
+          uint4 o;
+          o.x = *reinterpret_cast<const uint32_t *>(&h0);
+          o.y = *reinterpret_cast<const uint32_t *>(&h1);
+          o.z = *reinterpret_cast<const uint32_t *>(&h2);
+          o.w = *reinterpret_cast<const uint32_t *>(&h3);
+          // 128-byte swizzle: chunk c of row r at chunk c ^ (r % 8) of its 128-byte line.
+          *reinterpret_cast<uint4 *>(sb + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = o;
+        }
+        fence_proxy_async_smem();  // the generic-proxy writes are visible to the UMMA
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->conv[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
 // ---- pair GEMM: one tile of 256 rows x BN columns on a cluster of two CTAs ---------------------
 //
 // A single SM streams its operand tiles at about 80 bytes per cycle through TMA, so a 128 x 128
@@ -695,6 +976,37 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs
   }
 }
 
+template <int BN, int E>
+cudaError_t launch_q8_e(const CUtensorMap &a, const CUtensorMap &q, const CUtensorMap &sc,
+                        const GemmArgs &g, int grid, cudaStream_t s) {
+  using C = GemmQ8Cfg<BN>;
+  const size_t smem = 1024 + C::STAGES * C::STAGE_BYTES + sizeof(GemmQ8Barriers);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel<BN, E>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  return launch_pdl(gemm_q8_kernel<BN, E>, dim3(grid), dim3(kQ8Threads), smem, s, a, q, sc, g);
+}
+
+template <int BN>
+cudaError_t launch_q8(const CUtensorMap &a, const CUtensorMap &q, const CUtensorMap &sc,
+                      const GemmArgs &g, int grid, cudaStream_t s) {
+  switch (g.epilogue) {
+    case kBias: return launch_q8_e<BN, kBias>(a, q, sc, g, grid, s);
+    case kSilu: return launch_q8_e<BN, kSilu>(a, q, sc, g, grid, s);
+    case kRelu: return launch_q8_e<BN, kRelu>(a, q, sc, g, grid, s);
+    case kResidual: return launch_q8_e<BN, kResidual>(a, q, sc, g, grid, s);
+    case kGelu: return launch_q8_e<BN, kGelu>(a, q, sc, g, grid, s);
+    case kGeluResidual: return launch_q8_e<BN, kGeluResidual>(a, q, sc, g, grid, s);
+    default: return launch_q8_e<BN, kTanh>(a, q, sc, g, grid, s);
+  }
+}
+
 template <int BN, int E, int KC>
 cudaError_t launch2_bn_e(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &c,
                          const GemmArgs &g, int pairs, cudaStream_t s) {
@@ -801,6 +1113,15 @@ cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmAr
   }
   if (bn == 160) return launch_bn<160, 1>(a, w, g, grid, s);
   return bn == 256 ? launch_bn<256, 1>(a, w, g, grid, s) : launch_bn<128, 1>(a, w, g, grid, s);
+}
+
+cudaError_t launch_gemm_q8(const CUtensorMap &a, const CUtensorMap &q, const CUtensorMap &sc,
+                           const GemmArgs &g, int bn, int num_sms, cudaStream_t s) {
+  const int tiles = ((g.m + BM - 1) / BM) * ((g.cols + bn - 1) / bn);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  if (grid <= 0) return cudaSuccess;
+  if (bn == 160) return launch_q8<160>(a, q, sc, g, grid, s);
+  return bn == 256 ? launch_q8<256>(a, q, sc, g, grid, s) : launch_q8<128>(a, q, sc, g, grid, s);
 }
 
 cudaError_t launch_cast_rows(const float *in, long long ld_in, __half *out, long long ld_out,

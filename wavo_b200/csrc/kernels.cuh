@@ -60,6 +60,11 @@ constexpr int kGemmThreads = 192;
 int gemm_pick_bn(int m, int cols, int num_sms);
 cudaError_t launch_gemm(const CUtensorMap &a, const CUtensorMap &w, const GemmArgs &g, int bn,
                         int kc, int num_sms, cudaStream_t s);
+// The Q8_0 GEMM (W dequantised in the prologue): q is an int8 tensor map over W's block values
+// [rows][k] (boxes {64, bn}, no swizzle), sc an f16 map over the scales transposed, [k / 32][rows]
+// (boxes {bn, 2}). Tile widths as gemm_pick_bn.
+cudaError_t launch_gemm_q8(const CUtensorMap &a, const CUtensorMap &q, const CUtensorMap &sc,
+                           const GemmArgs &g, int bn, int num_sms, cudaStream_t s);
 // The pair GEMM (a cluster of two CTAs shares each UMMA of M=256): tile width BN (128, 160, 192
 // or 256) for an m x cols output; a's box height is 128 and W's BN / 2.
 int gemm2_pick_bn(int m, int cols, int num_sms);

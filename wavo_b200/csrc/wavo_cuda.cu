@@ -30,6 +30,7 @@ struct wavo_ctx {
   void *ws = nullptr;        // scratch for casts and repacks
   size_t ws_bytes = 0;
   bool capturing = false;
+  int q8_mode = WAVO_Q8_AUTO;  // wavo_set_q8_gemm
   std::mutex mu;
   std::string err;
 };
@@ -42,6 +43,7 @@ struct wavo_linear {
   float *w32 = nullptr;      // [n][k] f32 (F32 weights), the gemv operand
   int8_t *q8 = nullptr;      // [n][k] int8 (Q8_0 weights), the gemv operand
   float *d8 = nullptr;       // [n][k/32] scales (Q8_0)
+  __half *s16t = nullptr;    // the same scales as f16, transposed: [k/32][n] (the prologue GEMM)
   float *bias = nullptr;     // max(n, cols + dual) floats
   CUtensorMap map_w128, map_w160, map_w256;  // W tiles of 128, 160 and 256 rows
   // The pair GEMM's half tiles (64, 80, 96 rows; 128 is map_w128), 2D and, when k is a multiple
@@ -49,6 +51,11 @@ struct wavo_linear {
   CUtensorMap map_h64, map_h80, map_h96;
   CUtensorMap map3_h64, map3_h80, map3_h96;
   bool has3 = false;
+  // Q8_0: int8 block values [n][k] as TMA boxes of {64, 128 / 160 / 256 rows}, and the transposed
+  // scales as boxes of {128 / 160 / 256, 2} (the prologue GEMM).
+  CUtensorMap map_q128, map_q160, map_q256;
+  CUtensorMap map_s128, map_s160, map_s256;
+  bool has_q8map = false;
 };
 
 struct wavo_graph {
@@ -111,6 +118,38 @@ EncodeTiled encoder() {
 // 64; chunk c = columns 64c..): boxes {64, box_rows, 2}, two 64-column chunks per TMA load.
 bool make_map3(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
                uint32_t box_rows);
+
+// An int8 tensor map over rows x cols bytes (row stride ld bytes), boxes of 64 x box_rows, no
+// swizzle, zero fill outside: the Q8_0 GEMM's raw block values.
+bool make_map_i8(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
+                 uint32_t box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || (ld & 15u) || cols == 0 || rows == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The Q8_0 scales transposed, [rows][cols] f16 (cols = the layer's padded rows n, rows = k / 32),
+// boxes of box_cols x 2: one K-step's two scale rows of a W tile.
+bool make_map_s16(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows,
+                  uint32_t box_cols) {
+  EncodeTiled enc = encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || ((cols * 2) & 15u) || rows == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, 2};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 // The pair GEMM's output map: rows x cols of f16 or f32 (row stride ld elements), boxes of 32 x 32,
 // swizzle matching the epilogue's staging (64-byte rows for f16, 128-byte rows for f32).
@@ -447,6 +486,11 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
   if (!q8.empty()) {
     up(reinterpret_cast<void **>(&l->q8), q8.data(), q8.size());
     up(reinterpret_cast<void **>(&l->d8), d8.data(), d8.size() * 4);
+    std::vector<uint16_t> s16t(d8.size());
+    const size_t kq = k / 32;
+    for (size_t r = 0; r < n; ++r)
+      for (size_t b = 0; b < kq; ++b) s16t[b * n + r] = f16_bits(d8[r * kq + b]);  // exact
+    up(reinterpret_cast<void **>(&l->s16t), s16t.data(), s16t.size() * 2);
   }
   if (e != cudaSuccess) {
     wavo_linear_destroy(l);
@@ -459,6 +503,12 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
     wavo_linear_destroy(l);
     return fail(ctx, WAVO_ECUDA, "linear: tensor map");
   }
+  l->has_q8map = l->q8 && make_map_i8(&l->map_q128, l->q8, k, n, k, 128) &&
+                 make_map_i8(&l->map_q160, l->q8, k, n, k, 160) &&
+                 make_map_i8(&l->map_q256, l->q8, k, n, k, 256) &&
+                 make_map_s16(&l->map_s128, l->s16t, n, k / 32, 128) &&
+                 make_map_s16(&l->map_s160, l->s16t, n, k / 32, 160) &&
+                 make_map_s16(&l->map_s256, l->s16t, n, k / 32, 256);
   l->has3 = k % 64 == 0 && make_map3(&l->map3_h64, l->w16, k, n, k, 64) &&
             make_map3(&l->map3_h80, l->w16, k, n, k, 80) &&
             make_map3(&l->map3_h96, l->w16, k, n, k, 96);
@@ -473,6 +523,7 @@ void wavo_linear_destroy(wavo_linear *l) {
   cudaFree(l->w32);
   cudaFree(l->q8);
   cudaFree(l->d8);
+  cudaFree(l->s16t);
   cudaFree(l->bias);
   delete l;
 }
@@ -531,6 +582,18 @@ wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, c
   ga.err = ctx->dev_err;
   ga.c_tma = 0;
   CUtensorMap map_a;
+  const bool q8_prologue =
+      l->ty == WAVO_GGML_Q8_0 && l->has_q8map && ctx->q8_mode == WAVO_Q8_PROLOGUE;
+  if (q8_prologue) {
+    // W dequantised as it is staged: int8 values by TMA, f16 tiles built in shared memory.
+    if (!make_map(&map_a, a16, l->k, m, lda16, wv::kGemmBM))
+      return fail(ctx, WAVO_ECUDA, "gemm: tensor map of a");
+    const int bn = wv::gemm_pick_bn(int(m), int(l->cols), ctx->sms);
+    const CUtensorMap &mq = bn == 256 ? l->map_q256 : bn == 160 ? l->map_q160 : l->map_q128;
+    const CUtensorMap &ms = bn == 256 ? l->map_s256 : bn == 160 ? l->map_s160 : l->map_s128;
+    CK(wv::launch_gemm_q8(map_a, mq, ms, ga, bn, ctx->sms, ctx->stream), "gemm launch");
+    return WAVO_OK;
+  }
   if (m > uint32_t(wv::kGemmBM)) {
     // Two or more row tiles: the pair GEMM (a CTA pair shares each UMMA of M=256).
     const int bn = wv::gemm2_pick_bn(int(m), int(l->cols), ctx->sms);
@@ -559,6 +622,15 @@ wavo_status wavo_gemm(wavo_ctx *ctx, const void *a, int a_dtype, uint32_t lda, c
   CK(wv::launch_gemm(map_a, mw, ga, bn, 1, ctx->sms, ctx->stream),
      "gemm launch");
   return WAVO_OK;
+}
+
+int wavo_set_q8_gemm(wavo_ctx *ctx, int mode) {
+  if (!ctx) return -1;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  const int old = ctx->q8_mode;
+  if (mode == WAVO_Q8_AUTO || mode == WAVO_Q8_DEQUANT || mode == WAVO_Q8_PROLOGUE)
+    ctx->q8_mode = mode;
+  return old;
 }
 
 wavo_status wavo_gemv_rows(wavo_ctx *ctx, const float *a, uint32_t lda, const wavo_linear *l,

@@ -124,6 +124,11 @@ class Gpu:
     def reserve(self, nbytes: int) -> None:
         check(L.lib().wavo_reserve(self.ctx, nbytes), self.ctx)
 
+    def set_q8_gemm(self, mode: int) -> int:
+        """How Q8_0 layers' GEMMs read W (L.Q8_AUTO, L.Q8_DEQUANT, L.Q8_PROLOGUE); returns the
+        previous mode."""
+        return int(L.lib().wavo_set_q8_gemm(self.ctx, mode))
+
     def sync(self, timeout_ms: int = 60000) -> None:
         """Completion check (src/gpu/mod.rs:969-1003): device errors raise here."""
         check(L.lib().wavo_sync(self.ctx, timeout_ms), self.ctx)
