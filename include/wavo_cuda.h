@@ -171,6 +171,20 @@ wavo_status wavo_attention_varlen(wavo_ctx *ctx, const void *qk, const void *v, 
                                   uint32_t pos_t, uint32_t heads, uint32_t hd, int dtype,
                                   int o_dtype);
 
+/* wavo_attention_varlen over f16 rows [q | k | v] with rotary positions on q and k applied inside
+ * the attention kernel: the reference rotates the rows first (Pass::rope, src/gpu/mod.rs:1630-1649,
+ * then Pass::attention); here each Q tile and K block is rotated as the kernel stages it, and the
+ * rows in memory are left as they are. Row i of a segment takes table row pos + i (rot / 2 cosines,
+ * then as many sines; table_rows >= pos + max_len); NEOX pairs (i, i + rot/2) or adjacent pairs
+ * (2i, 2i + 1), as wavo_rope. Needs 16-byte aligned rows, heads of 16, 32, 48, 64 or 128, rot / 2
+ * (neox) or rot a multiple of 8; other shapes return WAVO_EUNSUPPORTED (use wavo_rope_rows, then
+ * wavo_attention_varlen). */
+wavo_status wavo_attention_rope_varlen(wavo_ctx *ctx, const void *qkv, void *o, uint32_t rows,
+                                       const int32_t *seg_start, const int32_t *seg_len,
+                                       uint32_t nseg, uint32_t max_len, uint32_t heads,
+                                       uint32_t hd, const float *table, uint32_t table_rows,
+                                       uint32_t pos, uint32_t rot, int neox, int o_dtype);
+
 /* pos_rows (src/gpu/mod.rs:1060-1065): 2t + 15. */
 uint32_t wavo_pos_rows(uint32_t t);
 

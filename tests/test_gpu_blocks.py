@@ -83,7 +83,8 @@ def oracle_linear_gemm(ty, rows, k, data, bias, a, m, c=None, epi="bias"):
         O.set_vnni(-1)
 
 
-def test_rotary_block(gpu):
+@pytest.mark.parametrize("fuse", [False, True])
+def test_rotary_block(gpu, fuse):
     from wavo_b200 import GGML_F16
     from wavo_b200.blocks import RotaryAttention, Segments, rope_table
     d, heads = 96, 2
@@ -94,7 +95,8 @@ def test_rotary_block(gpu):
     wo = (rng.standard_normal((d, d)) * 0.05).astype(np.float16)
     bq = (rng.standard_normal(3 * d) * 0.05).astype(np.float32)
     blk = RotaryAttention(gpu, GGML_F16, d, heads, wq.tobytes(), wo.tobytes(), bq, None,
-                          theta=10000.0, max_frames=256)
+                          theta=10000.0, max_frames=256, fuse_rope=fuse)
+    assert blk.fused() == fuse
     segs = Segments(lens, "cuda")
     y = rng.standard_normal((segs.rows, d)).astype(np.float32)
     x = torch.ones(segs.rows, d, device="cuda")

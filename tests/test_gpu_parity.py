@@ -206,3 +206,45 @@ def test_layer_level_ii(gpu, ty):
         check(x.cpu().numpy(), want)
     finally:
         O.set_vnni(-1)
+
+
+@pytest.mark.parametrize("hd,heads,neox,lens,pos", [
+    (48, 4, True, [37, 129, 300], 0),     # C3's heads (GigaAM: 16 x 48, NEOX, base 10000)
+    (64, 3, True, [200, 5], 0),
+    (64, 2, False, [70, 129], 7),        # adjacent pairs, table rows from 7
+    (128, 2, True, [150, 64], 0),
+    (16, 2, True, [33], 0),
+    (32, 2, False, [50, 257], 0),
+])
+def test_rotary_attention_fused(gpu, hd, heads, neox, lens, pos):
+    # Rotary positions inside the attention kernel against the oracle's rope (src/cpu/ops.rs:339-355)
+    # then attention (ops.rs:184-221) per segment; the rows in memory stay unrotated.
+    from wavo_b200 import _lib as L
+    from wavo_b200.blocks import Segments, rope_table
+    d = heads * hd
+    rng = np.random.default_rng(hd + heads + len(lens))
+    segs = Segments(lens, "cuda")
+    x = f16(qkv_like(rng, segs.rows, d, 3))
+    table = rope_table(pos + max(lens), hd, 10000.0)
+    qkv = torch.from_numpy(x).to("cuda", torch.float16)
+    before = qkv.clone()
+    o = torch.zeros(segs.rows, d, dtype=torch.float32, device="cuda")
+    gpu.pass_().attention_rope_varlen(qkv, o, segs.rows, segs.start_t, segs.len_t, segs.max_len,
+                                      heads, hd, torch.from_numpy(table).cuda(), hd, neox, pos)
+    gpu.sync()
+    assert torch.equal(qkv, before)
+    got = o.cpu().numpy()
+    for st, n in zip(segs.starts, lens):
+        q = np.ascontiguousarray(x[st:st + n].copy())
+        O.rope(q, np.ascontiguousarray(table[pos:pos + n]), n, heads, hd, hd, neox)
+        q = f16(q)  # the kernel rotates the f16 tiles and rounds the result to f16
+        q = q.ravel()
+        want = O.attention(q, 3 * d, np.ascontiguousarray(q[2 * d:]), 3 * d, n, heads, d)
+        check(got[st:st + n], want)
+    # Shapes the kernel cannot rotate in its tiles are refused, not computed another way.
+    lib = L.lib()
+    st = lib.wavo_attention_rope_varlen(gpu.ctx, qkv.data_ptr(), o.data_ptr(), segs.rows,
+                                        segs.start_t.data_ptr(), segs.len_t.data_ptr(), len(lens),
+                                        segs.max_len, heads, hd, table.ctypes.data, 1, pos, hd,
+                                        int(neox), L.F32)
+    assert st == L.EINVAL  # a table shorter than the segments

@@ -52,6 +52,8 @@ SIGNATURES = {
     "wavo_attention": ([_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i32], _st),
     "wavo_attention_varlen": ([_vp, _vp, _vp, _vp, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32,
                                _u32, _i32, _i32], _st),
+    "wavo_attention_rope_varlen": ([_vp, _vp, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _vp,
+                                    _u32, _u32, _u32, _i32, _i32], _st),
     "wavo_pos_rows": ([_u32], _u32),
     "wavo_rope": ([_vp, _vp, _vp, _i32, _u32, _u32, _u32, _u32, _u32, _u32, _i32], _st),
     "wavo_rope_rows": ([_vp, _vp, _vp, _i32, _u32, _u32, _u32, _vp, _u32, _u32, _u32, _i32], _st),

@@ -35,6 +35,9 @@ constexpr int NT = 2;                  // query tiles per CTA
 constexpr int CTRL_WARPS = 1 + NT;     // TMA producer, one UMMA issuer per tile
 constexpr int SOFT_WARPS = 8;          // softmax warps per tile
 constexpr int THREADS = 32 * (CTRL_WARPS + NT * SOFT_WARPS);
+constexpr int ROPE_WARPS = 4;           // with rotary positions: the warps that rotate Q and K
+template <bool ROPE>
+constexpr int fa_threads() { return THREADS + (ROPE ? 32 * ROPE_WARPS : 0); }
 constexpr int KVS = 3;                 // K and V ring slots
 
 template <int HD, int BN>
@@ -50,6 +53,14 @@ struct Fa {
   static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KVS * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + KVS * KV_BYTES;
+  // Rotary positions at heads of 64: each K block's table rows (rot <= 64 f32 a key) staged
+  // beside it in shared memory, one slot per K slot.
+  static constexpr int T_SLOT = BN * 64 * 4;
+  static constexpr int OFF_T = OFF_V + KVS * KV_BYTES;
+  template <bool ROPE>
+  __host__ __device__ static constexpr int off_bar() {
+    return ROPE && HD == 64 ? OFF_T + KVS * T_SLOT : OFF_BAR;
+  }
   // TMEM columns of tile t, from t·256: the scores S (BN f32 columns), the probabilities P (BN
   // f16, two per column), the accumulator O.
   static constexpr int T_TILE = 256;
@@ -67,6 +78,7 @@ struct Fa {
 
 struct __align__(8) FaBarriers {
   uint64_t q_full;
+  uint64_t q_ready[NT], k_ready[KVS];  // rotary positions: the tile / block is rotated
   uint64_t k_full[KVS], k_empty[KVS];
   uint64_t v_full[KVS], v_empty[KVS];
   uint64_t s_full[NT], s_free[NT];
@@ -77,10 +89,86 @@ struct __align__(8) FaBarriers {
   uint32_t abort;
 };
 
+// Rotates one f16 row of a 128-byte-swizzled tile in shared memory ([64-column block][rows][128
+// bytes], `atom` bytes a block) by the table row `cs` (rot / 2 cosines, then as many sines): NEOX
+// pairs (i, i + rot / 2) or adjacent pairs (2i, 2i + 1), eight columns (one 16-byte chunk) at a
+// time; rot / 2 (NEOX) or rot a multiple of 8. The arithmetic of the separate rotary pass:
+// a·cos − b·sin, a·sin + b·cos in f32, rounded to f16.
+__device__ __forceinline__ uint4 *tile_chunk(uint8_t *tile, int atom, int r, int c) {
+  const int cc = c & 63;
+  return reinterpret_cast<uint4 *>(tile + (c >> 6) * atom + r * 128 + (((cc >> 3) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void rot_pair(__half &x0, __half &x1, float c, float s) {
+  const float a = __half2float(x0), b = __half2float(x1);
+  x0 = __float2half_rn(a * c - b * s);
+  x1 = __float2half_rn(a * s + b * c);
+}
+
+// One rotation unit: 8 NEOX pairs (chunk i of the first half with chunk i + half) or 4 adjacent
+// pairs (chunk c), at column `col` of row r. Loads first, then the arithmetic, so that a thread's
+// table reads of several units are in flight together.
+struct RopeUnit {
+  uint4 lo, hi;
+  float4 c0, c1, s0, s1;
+};
+
+__device__ __forceinline__ void rope_load(RopeUnit &u, uint8_t *tile, int atom, int r, int col,
+                                          const float *cs, int half, bool neox) {
+  if (neox) {
+    u.lo = *tile_chunk(tile, atom, r, col);
+    u.hi = *tile_chunk(tile, atom, r, col + half);
+    u.c0 = *reinterpret_cast<const float4 *>(cs + col);
+    u.c1 = *reinterpret_cast<const float4 *>(cs + col + 4);
+    u.s0 = *reinterpret_cast<const float4 *>(cs + half + col);
+    u.s1 = *reinterpret_cast<const float4 *>(cs + half + col + 4);
+  } else {
+    u.lo = *tile_chunk(tile, atom, r, col);
+    u.c0 = *reinterpret_cast<const float4 *>(cs + col / 2);
+    u.s0 = *reinterpret_cast<const float4 *>(cs + half + col / 2);
+  }
+}
+
+__device__ __forceinline__ void rope_store(RopeUnit &u, uint8_t *tile, int atom, int r, int col,
+                                           int half, bool neox) {
+  if (neox) {
+    const float cc[8] = {u.c0.x, u.c0.y, u.c0.z, u.c0.w, u.c1.x, u.c1.y, u.c1.z, u.c1.w};
+    const float ss[8] = {u.s0.x, u.s0.y, u.s0.z, u.s0.w, u.s1.x, u.s1.y, u.s1.z, u.s1.w};
+    __half *l = reinterpret_cast<__half *>(&u.lo), *h = reinterpret_cast<__half *>(&u.hi);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) rot_pair(l[k], h[k], cc[k], ss[k]);
+    *tile_chunk(tile, atom, r, col) = u.lo;
+    *tile_chunk(tile, atom, r, col + half) = u.hi;
+  } else {
+    const float cc[4] = {u.c0.x, u.c0.y, u.c0.z, u.c0.w}, ss[4] = {u.s0.x, u.s0.y, u.s0.z, u.s0.w};
+    __half *e = reinterpret_cast<__half *>(&u.lo);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rot_pair(e[2 * k], e[2 * k + 1], cc[k], ss[k]);
+    *tile_chunk(tile, atom, r, col) = u.lo;
+  }
+}
+
+// Rotates units part, part + parts, .. of row r (table row cs), two units at a time.
+__device__ void rope_tile_row(uint8_t *tile, int atom, int r, const float *cs, int rot,
+                              bool neox, int part, int parts) {
+  const int half = rot / 2;
+  const int units = neox ? half / 8 : rot / 8;
+#pragma unroll 1
+  for (int k = part; k < units; k += 2 * parts) {
+    const bool two = k + parts < units;
+    RopeUnit u0, u1;
+    rope_load(u0, tile, atom, r, 8 * k, cs, half, neox);
+    if (two) rope_load(u1, tile, atom, r, 8 * (k + parts), cs, half, neox);
+    rope_store(u0, tile, atom, r, 8 * k, half, neox);
+    if (two) rope_store(u1, tile, atom, r, 8 * (k + parts), half, neox);
+  }
+}
+
 // KS: K-steps of 16 columns in a score UMMA group (the head's width in 16s; all HD / 16 when the
-// host zero-padded the heads).
-template <int HD, int BN, int KS>
-__global__ void __launch_bounds__(THREADS, 1)
+// host zero-padded the heads). ROPE: rotary positions on q and k (a.rope_table), applied to each Q
+// tile and K block in shared memory by four more warps before the UMMAs read them.
+template <int HD, int BN, int KS, bool ROPE>
+__global__ void __launch_bounds__(fa_threads<ROPE>(), 1)
     fa_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
               const __grid_constant__ CUtensorMap map_o, const AttnArgs a) {
   using C = Fa<HD, BN>;
@@ -96,12 +184,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  FaBarriers *bar = reinterpret_cast<FaBarriers *>(smem + C::OFF_BAR);
+  FaBarriers *bar = reinterpret_cast<FaBarriers *>(smem + C::template off_bar<ROPE>());
   const uint32_t warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
+    for (int t = 0; t < NT; ++t) mbar_init(&bar->q_ready[t], SOFT_WARPS);
     for (int i = 0; i < KVS; ++i) {
+      mbar_init(&bar->k_ready[i], ROPE_WARPS);
       mbar_init(&bar->k_full[i], 1);
       mbar_init(&bar->k_empty[i], nt);  // one commit from each live tile's issuer
       mbar_init(&bar->v_full[i], 1);
@@ -151,11 +241,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = j % KVS;
         const uint32_t par = ((j / KVS) & 1) ^ 1u;
         if (!mbar_wait(&bar->k_empty[s], par, ab, kErrTimeoutProducer)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bar->k_full[s], C::KV_BYTES);
+        // Rotary positions at heads of 64: the table rows of the block's keys in the segment
+        // (contiguous, rot f32 each) come with K on the same barrier.
+        const uint32_t tbytes =
+            ROPE && HD == 64 ? uint32_t(min(BN, T - j * BN) * a.rope_rot * 4) : 0u;
+        mbar_arrive_expect_tx(&bar->k_full[s], C::KV_BYTES + tbytes);
 #pragma unroll
         for (int b = 0; b < C::NBOX; ++b)
           tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + b * C::ATOM_KV, &map_kv, &bar->k_full[s],
                       a.k_off + hoff + 64 * b, row0 + j * BN);
+        if (tbytes)
+          bulk_load(smem + C::OFF_T + s * C::T_SLOT,
+                    a.rope_table + (long long)(a.rope_pos + j * BN) * a.rope_rot, tbytes,
+                    &bar->k_full[s]);
         k_last[s] = 2u | ((j / KVS) & 1u);
         if (!mbar_wait(&bar->v_empty[s], par, ab, kErrTimeoutProducer)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar->v_full[s], C::KV_BYTES);
@@ -186,7 +284,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // one thread's barrier waits and commits overlap the other tile's UMMAs.
     const int t = int(warp) - 1;
     if (lane == 0 && t < nt) {
-      bool ok = mbar_wait(&bar->q_full, 0, ab, kErrTimeoutMma);
+      bool ok = mbar_wait(ROPE ? &bar->q_ready[t] : &bar->q_full, 0, ab, kErrTimeoutMma);
       bool issued = false;
       // Descriptors are linear in the start address (bits 0-13 hold address / 16), so every
       // operand's descriptor is a base plus an offset / 16. The score loop is unrolled over a
@@ -201,7 +299,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j <= nb && ok; ++j) {
         if (j < nb) {
           const int ks = j % KVS;
-          if (!mbar_wait(&bar->k_full[ks], (j / KVS) & 1, ab, kErrTimeoutMma)) {
+          if (!mbar_wait(ROPE ? &bar->k_ready[ks] : &bar->k_full[ks], (j / KVS) & 1, ab,
+                         kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -249,6 +348,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+  } else if (ROPE && warp >= CTRL_WARPS + NT * SOFT_WARPS) {
+    // ---- rotary positions: thread t rotates rows t, t + 128, .. of each K block as it lands (key
+    // j of the segment at table row rope_pos + j); rows past the segment are left as they are
+    // (their keys are masked). The softmax warps rotate their tile's Q rows at the start.
+    const int t = int(threadIdx.x) - 32 * (CTRL_WARPS + NT * SOFT_WARPS);
+    const int rot = a.rope_rot;
+    const bool neox = a.rope_neox != 0;
+    for (int j = 0; j < nb; ++j) {
+      const int ks = j % KVS;
+      if (!mbar_wait_warp(&bar->k_full[ks], (j / KVS) & 1, ab, kErrTimeoutConsumer)) break;
+      for (int r = t; r < BN; r += 32 * ROPE_WARPS) {
+        const int kj = j * BN + r;
+        if (kj < T)
+          rope_tile_row(smem + C::OFF_K + ks * C::KV_BYTES, C::ATOM_KV, r,
+                        HD == 64 ? reinterpret_cast<const float *>(smem + C::OFF_T + ks * C::T_SLOT) +
+                                       r * rot
+                                 : a.rope_table + (long long)(a.rope_pos + kj) * rot,
+                        rot, neox, 0, 1);
+      }
+      fence_proxy_async_smem();  // the rotated rows are visible to the UMMAs (async proxy)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->k_ready[ks]);
+    }
   } else {
     // ---- softmax: 8 warps a tile. The two warps of a quarter (the TMEM lanes 32·(w % 4) a warp
     // may access) take 16 rows each; within a warp, threads t and t + 16 share row t % 16 and hold
@@ -263,6 +385,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float c = a.scale_log2;
     float m_use = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     bool ok = t < nt;
+    if (ROPE && ok) {
+      // The tile's 128 Q rows, two threads a row (alternate rotation units), before its issuer's
+      // first UMMA (query i of the segment at table row rope_pos + i).
+      ok = mbar_wait_warp(&bar->q_full, 0, ab, kErrTimeoutConsumer);
+      if (ok) {
+        const int tw = (w & 7) * 32 + int(lane);  // 0..255 within the tile's softmax warps
+        const int r = tw >> 1, qi = m0 + t * BM + r;
+        if (qi < T)
+          rope_tile_row(smem + C::OFF_Q + t * C::Q_BYTES, C::ATOM_Q, r,
+                        a.rope_table + (long long)(a.rope_pos + qi) * a.rope_rot, a.rope_rot,
+                        a.rope_neox != 0, tw & 1, 2);
+        fence_proxy_async_smem();  // the rotated rows are visible to the UMMAs (async proxy)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->q_ready[t]);
+      }
+    }
     for (int j = 0; j < nb && ok; ++j) {
       if (!mbar_wait_warp(&bar->s_full[t], j & 1, ab, kErrTimeoutConsumer)) { ok = false; break; }
       tc_fence_after();
@@ -441,22 +579,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-template <int HD, int BN, int KS>
+template <int HD, int BN, int KS, bool ROPE>
 cudaError_t launch_fa(const CUtensorMap &q, const CUtensorMap &kv, const CUtensorMap &o,
                       const AttnArgs &a, int max_len, int nseg, cudaStream_t s) {
   using C = Fa<HD, BN>;
-  const size_t smem = 1024 + C::OFF_BAR + sizeof(FaBarriers);
+  const size_t smem = 1024 + C::template off_bar<ROPE>() + sizeof(FaBarriers);
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[64] = {};
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fa_kernel<HD, BN, KS>,
+    cudaError_t e = cudaFuncSetAttribute(fa_kernel<HD, BN, KS, ROPE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   dim3 grid((max_len + NT * BM - 1) / (NT * BM), a.heads, nseg);
-  return launch_pdl(fa_kernel<HD, BN, KS>, grid, dim3(THREADS), smem, s, q, kv, o, a);
+  return launch_pdl(fa_kernel<HD, BN, KS, ROPE>, grid, dim3(fa_threads<ROPE>()), smem, s, q, kv, o,
+                    a);
 }
 
 }  // namespace
@@ -467,14 +606,23 @@ cudaError_t launch_fa_attention(const CUtensorMap &map_q, const CUtensorMap &map
                                 const CUtensorMap &map_o, const AttnArgs &a, int hd_pad,
                                 int max_len, int nseg, cudaStream_t s) {
   if (max_len <= 0 || nseg <= 0) return cudaSuccess;
-  if (hd_pad == 128) return launch_fa<128, 64, 8>(map_q, map_kv, map_o, a, max_len, nseg, s);
   // Heads read in place (a head stride below 64): the head's own K-steps; zero-padded heads: all.
   const int ks = a.head_stride < 64 ? (a.hd + 15) / 16 : 4;
+  if (a.rope_table) {
+    if (hd_pad == 128) return launch_fa<128, 64, 8, true>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    switch (ks) {
+      case 1: return launch_fa<64, 128, 1, true>(map_q, map_kv, map_o, a, max_len, nseg, s);
+      case 2: return launch_fa<64, 128, 2, true>(map_q, map_kv, map_o, a, max_len, nseg, s);
+      case 3: return launch_fa<64, 128, 3, true>(map_q, map_kv, map_o, a, max_len, nseg, s);
+      default: return launch_fa<64, 128, 4, true>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    }
+  }
+  if (hd_pad == 128) return launch_fa<128, 64, 8, false>(map_q, map_kv, map_o, a, max_len, nseg, s);
   switch (ks) {
-    case 1: return launch_fa<64, 128, 1>(map_q, map_kv, map_o, a, max_len, nseg, s);
-    case 2: return launch_fa<64, 128, 2>(map_q, map_kv, map_o, a, max_len, nseg, s);
-    case 3: return launch_fa<64, 128, 3>(map_q, map_kv, map_o, a, max_len, nseg, s);
-    default: return launch_fa<64, 128, 4>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    case 1: return launch_fa<64, 128, 1, false>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    case 2: return launch_fa<64, 128, 2, false>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    case 3: return launch_fa<64, 128, 3, false>(map_q, map_kv, map_o, a, max_len, nseg, s);
+    default: return launch_fa<64, 128, 4, false>(map_q, map_kv, map_o, a, max_len, nseg, s);
   }
 }
 

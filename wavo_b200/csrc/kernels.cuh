@@ -98,6 +98,11 @@ struct AttnArgs {
   int o_f16;
   int o_tma;        // 1: f16 output rows also reachable through map_o (boxes {hd, 16}, no swizzle)
   int *err;
+  // Rotary positions on q and k inside the plain kernel (rope_table NULL: none): row i of a
+  // segment takes table row rope_pos + i (rope_rot / 2 cosines, then as many sines); NEOX pairs
+  // (i, i + rot / 2) or adjacent pairs.
+  const float *rope_table;
+  int rope_rot, rope_neox, rope_pos;
 };
 
 constexpr int kAttnBlockQ = 128;  // queries per tile (the TMA box height of map_q)

@@ -442,6 +442,17 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Untiled bulk copy of `bytes` contiguous bytes global -> shared (both 16-byte aligned, bytes a
+// multiple of 16), completion counted on `bar` (no cluster multicast).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 3D form of tma_load_2d (a box of several 64-column chunks: one instruction, fewer per byte).
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t x, int32_t y, int32_t z) {

@@ -685,10 +685,17 @@ struct AttnLayout {
   bool rel;
 };
 
+// Rotary positions applied inside the plain attention kernel (wavo_attention_rope_varlen).
+struct RopeSpec {
+  const float *table;
+  uint32_t rot, pos;
+  int neox;
+};
+
 wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const void *pos, void *o,
                            const int32_t *seg_start, const int32_t *seg_len, uint32_t nseg,
                            uint32_t max_len, uint32_t pos_t, uint32_t single_t, uint32_t heads,
-                           uint32_t hd, int dtype, int o_dtype) {
+                           uint32_t hd, int dtype, int o_dtype, const RopeSpec *rope = nullptr) {
   if (!qk || !o) return fail(ctx, WAVO_EINVAL, "attention: NULL buffer");
   if (dtype != WAVO_F32 && dtype != WAVO_F16) return fail(ctx, WAVO_EINVAL, "attention: dtype");
   if (o_dtype != WAVO_F32 && o_dtype != WAVO_F16) return fail(ctx, WAVO_EINVAL, "attention: o dtype");
@@ -726,6 +733,18 @@ wavo_status attention_impl(wavo_ctx *ctx, const void *qk, const void *v, const v
   a.ldo = ch;
   a.o_f16 = o_dtype == WAVO_F16;
   a.err = ctx->dev_err;
+  if (rope) {
+    // The rotation happens on the f16 tiles the kernel stages from the operand rows, so the rows
+    // must be the kernel's operands as they are (no repack).
+    if (!direct || rel)
+      return fail(ctx, WAVO_EUNSUPPORTED,
+                  "attention with rotary positions: needs f16 [q | k | v] rows, 16-byte aligned, "
+                  "heads of 16, 32, 48, 64 or 128");
+    a.rope_table = rope->table;
+    a.rope_rot = int(rope->rot);
+    a.rope_neox = rope->neox;
+    a.rope_pos = int(rope->pos);
+  }
 
   CUtensorMap mq, mkv, mpos, mo;
   // f16 output whose head boxes start on 16-byte boundaries: stored with TMA (16 rows a warp).
@@ -824,6 +843,30 @@ wavo_status wavo_attention_varlen(wavo_ctx *ctx, const void *qk, const void *v, 
   if (nseg > 65535) return fail(ctx, WAVO_EINVAL, "attention: %u segments (at most 65535)", nseg);
   return attention_impl(ctx, qk, v, pos, o, seg_start, seg_len, nseg, max_len, pos ? pos_t : 0,
                         rows, heads, hd, dtype, o_dtype);
+}
+
+wavo_status wavo_attention_rope_varlen(wavo_ctx *ctx, const void *qkv, void *o, uint32_t rows,
+                                       const int32_t *seg_start, const int32_t *seg_len,
+                                       uint32_t nseg, uint32_t max_len, uint32_t heads,
+                                       uint32_t hd, const float *table, uint32_t table_rows,
+                                       uint32_t pos, uint32_t rot, int neox, int o_dtype) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (!seg_start || !seg_len || !table)
+    return fail(ctx, WAVO_EINVAL, "attention with rotary positions: NULL segment arrays or table");
+  if (max_len > rows) return fail(ctx, WAVO_EINVAL, "attention: max_len %u > rows %u", max_len, rows);
+  if (nseg > 65535) return fail(ctx, WAVO_EINVAL, "attention: %u segments (at most 65535)", nseg);
+  if (rot == 0 || rot > hd || rot % 2 || (neox ? (rot / 2) % 8 : rot % 8) ||
+      (reinterpret_cast<uintptr_t>(table) & 15u))
+    return fail(ctx, WAVO_EINVAL,
+                "attention with rotary positions: rot %u of hd %u (rot / 2 a multiple of 8 with "
+                "neox, rot a multiple of 8 without; table 16-byte aligned)", rot, hd);
+  if (uint64_t(pos) + max_len > table_rows)
+    return fail(ctx, WAVO_EINVAL, "attention with rotary positions: table of %u rows < %u + %u",
+                table_rows, pos, max_len);
+  const RopeSpec rs{table, rot, pos, neox};
+  return attention_impl(ctx, qkv, nullptr, nullptr, o, seg_start, seg_len, nseg, max_len, 0, rows,
+                        heads, hd, WAVO_F16, o_dtype, &rs);
 }
 
 // ---- rope --------------------------------------------------------------------------------

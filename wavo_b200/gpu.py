@@ -210,6 +210,18 @@ class Pass:
                                             max_len, pos_t, heads, hd, _dtype(qk), _dtype(o)),
               self.ctx)
 
+    def attention_rope_varlen(self, qkv, o, rows: int, seg_start: torch.Tensor,
+                              seg_len: torch.Tensor, max_len: int, heads: int, hd: int,
+                              table: torch.Tensor, rot: int, neox: bool, pos: int = 0) -> None:
+        """Attention over segments of f16 [q | k | v] rows with rotary positions applied inside the
+        kernel (row i of a segment at table row pos + i); the rows are left unrotated."""
+        assert seg_start.dtype == torch.int32 and seg_len.dtype == torch.int32
+        assert qkv.dtype == torch.float16 and table.dtype == torch.float32
+        check(L.lib().wavo_attention_rope_varlen(
+            self.ctx, _ptr(qkv), _ptr(o), rows, _ptr(seg_start), _ptr(seg_len), seg_len.numel(),
+            max_len, heads, hd, _ptr(table), table.shape[0], pos, rot, int(neox), _dtype(o)),
+            self.ctx)
+
     def rope(self, table: torch.Tensor, qkv: torch.Tensor, rows: int, pos: int,
              shape: tuple[int, int, int], neox: bool, stride: int = 0) -> None:
         """`Pass::rope` (src/gpu/mod.rs:1630-1649): shape = [heads, hd, rot]."""
