@@ -185,6 +185,36 @@ wavo_status wavo_attention_rope_varlen(wavo_ctx *ctx, const void *qkv, void *o, 
                                        uint32_t hd, const float *table, uint32_t table_rows,
                                        uint32_t pos, uint32_t rot, int neox, int o_dtype);
 
+/* ---- the rest of the encoder block around the attention ----------------------------------- */
+
+/* Pass::layer_norm (src/gpu/mod.rs:1431-1449; CPU src/cpu/ops.rs:65-110): per row of f32 x
+ * [rows][cols], y = (x - mean)·rstd·w + b with rstd = 1/sqrt(variance + 1e-5), into y (y_dtype).
+ * With a table (NULL: none), yr (y_dtype) gets y with NEOX rotary pairs (i, i + hd/2) rotated inside
+ * each head of hd: table row positions[r] (device int32; NULL: r) of hd/2 cosines, then hd/2 sines
+ * (GigaAM's rotary input to its Q/K projection). cols <= 2048. */
+wavo_status wavo_layer_norm(wavo_ctx *ctx, const float *x, const float *w, const float *b, void *y,
+                            int y_dtype, uint32_t rows, uint32_t cols, const float *table,
+                            const int32_t *positions, void *yr, uint32_t hd);
+
+/* Pass::conv_glu (src/gpu/mod.rs:1538-1566; CPU src/cpu/ops.rs:133-182): the Conformer conv module
+ * between its pointwise convs. From h [t][2·ch] (f32, left as it is): GLU (first half ·
+ * sigmoid(second half)), the depthwise conv over frames (odd kernel <= 63, centred; dw_w
+ * [ch][kernel] as the GGUF tensor stores it, dw_b [ch]), then LayerNorm over the channels
+ * (WAVO_CONV_LAYER_NORM: n_w, n_b as its weight and bias) or the per-channel affine n_w·x + n_b
+ * (WAVO_CONV_AFFINE, a folded batch norm), then SiLU, into y [t][ch] (y_dtype). */
+enum { WAVO_CONV_LAYER_NORM = 0, WAVO_CONV_AFFINE = 1 };
+wavo_status wavo_conv_glu(wavo_ctx *ctx, const float *h, const float *dw_w, const float *dw_b,
+                          uint32_t kernel, const float *n_w, const float *n_b, int norm, void *y,
+                          int y_dtype, uint32_t t, uint32_t ch);
+/* The same over nseg independent segments packed in `rows` rows (device int32 seg_start, seg_len;
+ * max_len >= every seg_len): the conv does not reach across a segment's ends. Rows of y outside
+ * every segment are overwritten (with the norm of zeros). */
+wavo_status wavo_conv_glu_varlen(wavo_ctx *ctx, const float *h, const float *dw_w,
+                                 const float *dw_b, uint32_t kernel, const float *n_w,
+                                 const float *n_b, int norm, void *y, int y_dtype, uint32_t rows,
+                                 const int32_t *seg_start, const int32_t *seg_len, uint32_t nseg,
+                                 uint32_t max_len, uint32_t ch);
+
 /* pos_rows (src/gpu/mod.rs:1060-1065): 2t + 15. */
 uint32_t wavo_pos_rows(uint32_t t);
 

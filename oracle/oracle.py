@@ -56,6 +56,8 @@ def lib():
         L.wo_pack_cache.argtypes = [_f, _sz, _sz, _sz, _f, _sz, _sz]
         L.wo_rope.argtypes = [_f, _f, _sz, _sz, _sz, _sz, ctypes.c_int]
         L.wo_rope_table.argtypes = [_sz, _sz, ctypes.c_double, _f]
+        L.wo_layer_norm.argtypes = [_f, _f, _f, _f, _sz, _sz, _f, _f, _sz]
+        L.wo_conv_glu.argtypes = [_f, _f, _f, _f, _f, ctypes.c_int, _f, _sz, _sz, _sz]
         L.wo_rel_positions.argtypes = [_sz, ctypes.c_int64, _sz, _f]
         L.wo_pos_rows.argtypes = [_sz]
         L.wo_pos_rows.restype = _sz
@@ -135,6 +137,28 @@ def pack_cache(kv, rows, d, hd, cache, cols, col) -> None:
 def rope(qkv, table, rows, heads, hd, rot, neox) -> None:
     """src/cpu/ops.rs:339-355 `rope` (in place)."""
     lib().wo_rope(_p(qkv), _p(table), rows, heads, hd, rot, int(neox))
+
+
+def layer_norm(x, w, b, rows, cols, table=None, hd=0):
+    """src/cpu/ops.rs:65-110 `layer_norm` (eps 1e-5); with a table (row r for row r) also the
+    rotated copy yr. Returns y, or (y, yr)."""
+    y = np.zeros(rows * cols, np.float32)
+    yr = np.zeros(rows * cols, np.float32) if table is not None else None
+    lib().wo_layer_norm(_p(np.ascontiguousarray(x, np.float32)), _p(np.ascontiguousarray(w, np.float32)),
+                        _p(np.ascontiguousarray(b, np.float32)), _p(y), rows, cols,
+                        _p(np.ascontiguousarray(table, np.float32)) if table is not None else None,
+                        _p(yr) if yr is not None else None, hd)
+    return y if yr is None else (y, yr)
+
+
+def conv_glu(h, taps, bias, g, beta, layer_norm, t, ch, kernel):
+    """src/cpu/ops.rs:133-182 `conv_glu`: h [t][2ch] is updated in place (GLU into its first
+    halves); returns y [t][ch]."""
+    y = np.zeros(t * ch, np.float32)
+    lib().wo_conv_glu(_p(h), _p(np.ascontiguousarray(taps, np.float32)),
+                      _p(np.ascontiguousarray(bias, np.float32)), _p(np.ascontiguousarray(g, np.float32)),
+                      _p(np.ascontiguousarray(beta, np.float32)), int(layer_norm), _p(y), t, ch, kernel)
+    return y
 
 
 def rope_table(frames, hd, theta) -> np.ndarray:

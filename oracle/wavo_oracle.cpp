@@ -432,6 +432,73 @@ void wo_rope(float *qkv, const float *table, size_t rows, size_t heads, size_t h
   }
 }
 
+// src/cpu/ops.rs:47-53 `moments`: mean and 1/sqrt(variance + 1e-5) of a row, both sums by `sum`.
+static void moments(const float *x, size_t n, float &mean, float &rstd) {
+  const float fn = float(n);
+  mean = sum8(x, n) / fn;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (size_t i = 0; i < n; ++i) {
+    const float d = x[i] - mean;
+    acc[i % 8] += d * d;
+  }
+  float var = 0.0f;
+  for (int i = 0; i < 8; ++i) var += acc[i];
+  var /= fn;
+  rstd = 1.0f / std::sqrt(var + 1e-5f);
+}
+
+// src/cpu/ops.rs:65-110 `layer_norm`: y = (x - mean)·rstd·w + b per row of `cols`; with a table
+// (rows of hd / 2 cosines then as many sines, row r for row r) also yr = y with NEOX rotary pairs
+// (i, i + hd/2) rotated inside each head of hd.
+void wo_layer_norm(const float *x, const float *w, const float *b, float *y, size_t rows,
+                   size_t cols, const float *table, float *yr, size_t hd) {
+  par_each(rows, [&](size_t r) {
+    const float *xr = x + r * cols;
+    float *yy = y + r * cols;
+    float mean, rstd;
+    moments(xr, cols, mean, rstd);
+    for (size_t c = 0; c < cols; ++c) yy[c] = (xr[c] - mean) * rstd * w[c] + b[c];
+    if (!table) return;
+    const size_t half = hd / 2;
+    const float *cs = table + r * hd, *sn = cs + half;
+    for (size_t h0 = 0; h0 + hd <= cols; h0 += hd) {
+      const float *y0 = yy + h0, *y1 = yy + h0 + half;
+      float *r0 = yr + r * cols + h0, *r1 = r0 + half;
+      for (size_t i = 0; i < half; ++i) {
+        r0[i] = y0[i] * cs[i] - y1[i] * sn[i];
+        r1[i] = y1[i] * cs[i] + y0[i] * sn[i];
+      }
+    }
+  });
+}
+
+// src/cpu/ops.rs:133-182 `conv_glu`: the Conformer conv module between the pointwise convs. GLU of
+// h [t][2·ch] in place into its first halves (x /= 1 + exp(-gate)), the depthwise conv (odd
+// kernel, centred, taps [kernel][ch] and bias) over frames of the segment, then LayerNorm over the
+// channels (`moments`) or the per-channel affine (g, beta), SiLU, into y [t][ch].
+void wo_conv_glu(float *h, const float *taps, const float *bias, const float *g, const float *beta,
+                 int layer_norm, float *y, size_t t, size_t ch, size_t kernel) {
+  par_each(t, [&](size_t i) {
+    float *x = h + i * 2 * ch;
+    const float *gate = x + ch;
+    for (size_t c = 0; c < ch; ++c) x[c] /= 1.0f + cephes_exp(-gate[c]);
+  });
+  par_each(t, [&](size_t i) {
+    std::vector<float> acc(bias, bias + ch);
+    for (size_t k = 0; k < kernel; ++k) {
+      if (i + k < kernel / 2) continue;
+      const size_t src = i + k - kernel / 2;
+      if (src >= t) continue;
+      const float *tk = taps + k * ch, *xs = h + src * 2 * ch;
+      for (size_t c = 0; c < ch; ++c) acc[c] += tk[c] * xs[c];
+    }
+    float mean = 0.0f, rstd = 1.0f;
+    if (layer_norm) moments(acc.data(), ch, mean, rstd);
+    float *yy = y + i * ch;
+    for (size_t c = 0; c < ch; ++c) yy[c] = silu((acc[c] - mean) * rstd * g[c] + beta[c]);
+  });
+}
+
 // src/gigaam/mod.rs:88-96 `rope`: per position hd/2 cosines then hd/2 sines, angles in f64.
 void wo_rope_table(size_t frames, size_t hd, double theta, float *out) {
   for (size_t t = 0; t < frames; ++t)

@@ -305,3 +305,55 @@ def test_rel_positions_and_rope_table():
     ang = np.arange(9)[:, None] * 10000.0 ** (-2.0 * np.arange(24) / 48)
     assert np.allclose(tab[:, :24], np.cos(ang), atol=1e-7)
     assert np.allclose(tab[:, 24:], np.sin(ang), atol=1e-7)
+
+
+def test_layer_norm_and_conv_glu_restatements():
+    # The oracle's layer_norm (src/cpu/ops.rs:65-110) and conv_glu (133-182) against the naive
+    # references of the reference's GPU tests (src/gpu/mod.rs:1753-1763, 1947-1973, 2131-2160) on
+    # their inputs, at their tolerance (2e-5 · max(1, max|want|)).
+    def close(got, want):
+        got, want = np.asarray(got, np.float64).ravel(), np.asarray(want, np.float64).ravel()
+        assert np.abs(got - want).max() <= 2e-5 * max(1.0, np.abs(want).max())
+
+    def naive_ln(x, g, b):
+        x = x.reshape(-1, g.size).astype(np.float64)
+        mean = x.mean(axis=1, keepdims=True)
+        var = ((x - mean) ** 2).mean(axis=1, keepdims=True)
+        return (x - mean) / np.sqrt(var + 1e-5) * g + b
+
+    rows, cols, hd = 37, 192, 48
+    x, g, b = O.random(rows * cols, 5), O.random(cols, 6), O.random(cols, 7)
+    rope = O.random(rows * hd, 8)
+    y = naive_ln(x, g, b).ravel()
+    half = hd // 2
+    idx = np.arange(rows * cols)
+    t, dd = idx // cols, idx % hd
+    cos, sin = rope[t * hd + dd % half], rope[t * hd + half + dd % half]
+    partner = np.where(dd < half, idx + half, idx - half)
+    yr = np.where(dd < half, y * cos - y[partner] * sin, y * cos + y[partner] * sin)
+    oy, oyr = O.layer_norm(x, g, b, rows, cols, rope, hd)
+    close(oy, y)
+    close(oyr, yr)
+    close(O.layer_norm(x, g, b, rows, cols), y)
+
+    t, ch = 37, 192
+    h = O.random(t * 2 * ch, 10)
+    g, b = O.random(ch, 13), O.random(ch, 14)
+    hh = h.reshape(t, 2 * ch).astype(np.float64)
+    glu = hh[:, :ch] / (1.0 + np.exp(-hh[:, ch:]))
+    for kernel, ln in [(5, True), (9, False)]:
+        w, wb = O.random(ch * kernel, 11), O.random(ch, 12)
+        wk = w.reshape(ch, kernel).astype(np.float64)
+        dw = np.tile(wb.astype(np.float64), (t, 1))
+        for r in range(t):
+            for k in range(kernel):
+                if 0 <= r + k - kernel // 2 < t:
+                    dw[r] += wk[:, k] * glu[r + k - kernel // 2]
+        want = naive_ln(dw, g, b) if ln else dw * g + b
+        want = want / (1.0 + np.exp(-want))
+        hc = h.copy()
+        got = O.conv_glu(hc, np.ascontiguousarray(wk.T.astype(np.float32)), wb, g, b, ln, t, ch,
+                         kernel)
+        close(got, want)
+        # The CPU conv_glu leaves the GLU in h's first halves (src/cpu/ops.rs:146-156).
+        close(hc.reshape(t, 2 * ch)[:, :ch], glu)

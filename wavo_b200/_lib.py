@@ -17,6 +17,7 @@ STATUS = {0: "OK", 1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEDOUT", 5: "EUN
 F32, F16 = 0, 1
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
 Q8_AUTO, Q8_DEQUANT, Q8_PROLOGUE = 0, 1, 2  # wavo_set_q8_gemm modes
+CONV_LAYER_NORM, CONV_AFFINE = 0, 1        # wavo_conv_glu norms
 WAVO_ATTEND_NOALLOC_PART_FLOATS = 1 << 18  # the header's fixed scratch of the no-alloc attend
 EPILOGUES = {"bias": 0, "silu": 1, "relu": 2, "residual": 3, "gelu": 4, "gelu_residual": 5,
              "tanh": 6}
@@ -55,6 +56,10 @@ SIGNATURES = {
     "wavo_attention_rope_varlen": ([_vp, _vp, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _vp,
                                     _u32, _u32, _u32, _i32, _i32], _st),
     "wavo_pos_rows": ([_u32], _u32),
+    "wavo_layer_norm": ([_vp, _vp, _vp, _vp, _vp, _i32, _u32, _u32, _vp, _vp, _vp, _u32], _st),
+    "wavo_conv_glu": ([_vp, _vp, _vp, _vp, _u32, _vp, _vp, _i32, _vp, _i32, _u32, _u32], _st),
+    "wavo_conv_glu_varlen": ([_vp, _vp, _vp, _vp, _u32, _vp, _vp, _i32, _vp, _i32, _u32, _vp, _vp,
+                              _u32, _u32, _u32], _st),
     "wavo_rope": ([_vp, _vp, _vp, _i32, _u32, _u32, _u32, _u32, _u32, _u32, _i32], _st),
     "wavo_rope_rows": ([_vp, _vp, _vp, _i32, _u32, _u32, _u32, _vp, _u32, _u32, _u32, _i32], _st),
     "wavo_pack": ([_vp, _vp, _u32, _u32, _vp, _u32, _u32, _u32, _u32], _st),

@@ -219,3 +219,62 @@ class DecoderAttention:
         p.attend_batch(self.q_buf, d, self.cross, d * self.frames, self.part, self.att, d,
                        self.frames, self.frames, self.heads, self.hd, B)
         p.gemv_rows(self.att, self.cross_out, x, B, "residual", 1.0, ldc=d)
+
+
+class ConformerBlock:
+    """A whole FastConformer block with relative-position attention (Parakeet; the reference's
+    `Block::record`, src/conformer.rs:232-265, CPU `Block::run`, src/cpu/conformer.rs:159-199), over
+    packed segments: half-step FFN, MHSA, conv module, half-step FFN, then norm_out. `norms` maps
+    "ff1", "attn", "conv", "ff2", "out" to (weight, bias) f32 arrays of d; the conv module's norm is
+    a LayerNorm (`conv_norm` (weight, bias), conv_ln=True) or a folded batch norm (per-channel
+    scale, shift). Weights are GGUF tensor bytes of `ty`: ff*_1 [f][d], ff*_2 [d][f], pw1 [2d][d],
+    pw2 [d][d]; dw [d][kernel] f32 (as the GGUF tensor stores it) with bias dw_b.
+
+    Every GEMM input is f16 (the reference GPU GEMM rounds a to f16); the residual stream x is
+    f32; the block output (norm_out) goes to an f32 buffer, as the reference's."""
+
+    def __init__(self, gpu: Gpu, ty: int, d: int, f: int, heads: int, kernel: int, w: dict,
+                 norms: dict, conv_ln: bool):
+        self.gpu, self.d, self.f, self.heads, self.kernel, self.conv_ln = gpu, d, f, heads, kernel, conv_ln
+        up = lambda a: gpu.upload(np.asarray(a, np.float32))  # noqa: E731
+        self.norms = {k: (up(wb[0]), up(wb[1])) for k, wb in norms.items()}
+        self.ff1 = (gpu.linear(ty, f, d, w["ff1_1"], w.get("ff1_1_b")),
+                    gpu.linear(ty, d, f, w["ff1_2"], w.get("ff1_2_b")))
+        self.ff2 = (gpu.linear(ty, f, d, w["ff2_1"], w.get("ff2_1_b")),
+                    gpu.linear(ty, d, f, w["ff2_2"], w.get("ff2_2_b")))
+        self.attn = RelPosAttention(gpu, ty, d, heads, w["qkv"], w["pos"], w["out"], w["u"], w["v"],
+                                    w.get("qkv_b"), w.get("out_b"))
+        self.pw1 = gpu.linear(ty, 2 * d, d, w["pw1"], w.get("pw1_b"))
+        self.pw2 = gpu.linear(ty, d, d, w["pw2"], w.get("pw2_b"))
+        self.dw = up(w["dw"])
+        self.dw_b = up(w.get("dw_b", np.zeros(d, np.float32)))
+
+    def scratch(self, rows: int, t_pos: int):
+        dev = self.gpu.torch_device
+        s = self.attn.scratch(rows, t_pos)
+        s["y"] = torch.empty(rows, self.d, dtype=torch.float16, device=dev)
+        s["h"] = torch.empty(rows, self.f, dtype=torch.float16, device=dev)
+        s["pw"] = torch.empty(rows, 2 * self.d, dtype=torch.float32, device=dev)
+        return s
+
+    def record(self, p: Pass, x: torch.Tensor, out: torch.Tensor, segs: Segments,
+               table: torch.Tensor, t_pos: int, s: dict) -> None:
+        """x: the f32 block input [rows][d] (updated in place as the residual stream); out: the
+        f32 block output norm_out(x); table: the f16 sinusoid rows (pos_rows(t_pos))."""
+        rows, d = segs.rows, self.d
+        y, h = s["y"], s["h"]
+        n = self.norms
+        p.layer_norm(x, *n["ff1"], y, rows, d)
+        p.gemm(y, self.ff1[0], h, rows, "silu")
+        p.gemm(h, self.ff1[1], x, rows, "residual", 0.5)
+        p.layer_norm(x, *n["attn"], y, rows, d)
+        self.attn.record(p, y, x, segs, table, t_pos, s)
+        p.layer_norm(x, *n["conv"], y, rows, d)
+        p.gemm(y, self.pw1, s["pw"], rows, "bias")
+        p.conv_glu(s["pw"], self.dw, self.dw_b, self.kernel, *n["conv_norm"], self.conv_ln, y,
+                   rows, d, segs)
+        p.gemm(y, self.pw2, x, rows, "residual", 1.0)
+        p.layer_norm(x, *n["ff2"], y, rows, d)
+        p.gemm(y, self.ff2[0], h, rows, "silu")
+        p.gemm(h, self.ff2[1], x, rows, "residual", 0.5)
+        p.layer_norm(x, *n["out"], out, rows, d)

@@ -105,6 +105,22 @@ struct AttnArgs {
   int rope_rot, rope_neox, rope_pos;
 };
 
+// ---- encoder block around the attention (encoder.cu) ----
+enum { kLnNorm = 0, kLnNormSilu = 1, kLnAffineSilu = 2 };
+// Row-wise LayerNorm of f32 x [rows][cols] into y (f16 or f32); mode kLnNormSilu adds SiLU,
+// kLnAffineSilu is w·x + b then SiLU; with a table, yr = y with NEOX rotary pairs inside heads of hd
+// (table row positions[r], or r).
+cudaError_t launch_layer_norm(const float *x, const float *w, const float *b, void *y, int y_f16,
+                              int rows, int cols, int mode, const float *table,
+                              const int *positions, void *yr, int hd, cudaStream_t s);
+int layer_norm_max_cols();
+// GLU of h [rows][2ch] and the depthwise conv over each segment's frames into z [rows][ch] (taps
+// [ch][kernel], odd kernel, centred).
+cudaError_t launch_dwconv(const float *h, const float *taps, const float *bias, float *z, int ch,
+                          int kernel, const int *seg_start, const int *seg_len, int nseg,
+                          int max_len, cudaStream_t s);
+int dwconv_max_kernel();
+
 constexpr int kAttnBlockQ = 128;  // queries per tile (the TMA box height of map_q)
 int attn_block_keys(bool rel, int hd_pad);  // keys per block (the TMA box height of map_kv)
 int attn_pos_window_rows();      // position rows per block (the TMA box height of map_pos)

@@ -869,6 +869,88 @@ wavo_status wavo_attention_rope_varlen(wavo_ctx *ctx, const void *qkv, void *o, 
                         heads, hd, WAVO_F16, o_dtype, &rs);
 }
 
+// ---- encoder block: LayerNorm and the conv module ---------------------------------------------
+
+wavo_status wavo_layer_norm(wavo_ctx *ctx, const float *x, const float *w, const float *b, void *y,
+                            int y_dtype, uint32_t rows, uint32_t cols, const float *table,
+                            const int32_t *positions, void *yr, uint32_t hd) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (rows == 0) return WAVO_OK;
+  if (!x || !w || !b || !y) return fail(ctx, WAVO_EINVAL, "layer_norm: NULL buffer");
+  if (y_dtype != WAVO_F32 && y_dtype != WAVO_F16) return fail(ctx, WAVO_EINVAL, "layer_norm: dtype");
+  if (cols == 0 || cols > uint32_t(wv::layer_norm_max_cols()))
+    return fail(ctx, WAVO_EINVAL, "layer_norm: %u columns (1..%d)", cols, wv::layer_norm_max_cols());
+  if (table && (!yr || hd == 0 || hd % 2 || cols % hd))
+    return fail(ctx, WAVO_EINVAL, "layer_norm: rotary copy needs yr and even hd dividing %u", cols);
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_layer_norm(x, w, b, y, y_dtype == WAVO_F16, int(rows), int(cols), wv::kLnNorm,
+                           table, positions, table ? yr : nullptr, int(hd), ctx->stream),
+     "layer_norm launch");
+  return WAVO_OK;
+}
+
+namespace {
+
+wavo_status conv_glu_impl(wavo_ctx *ctx, const float *h, const float *dw_w, const float *dw_b,
+                          uint32_t kernel, const float *n_w, const float *n_b, int norm, void *y,
+                          int y_dtype, uint32_t rows, const int32_t *seg_start,
+                          const int32_t *seg_len, uint32_t nseg, uint32_t max_len, uint32_t ch) {
+  if (rows == 0 || nseg == 0 || max_len == 0) return WAVO_OK;
+  if (!h || !dw_w || !dw_b || !n_w || !n_b || !y) return fail(ctx, WAVO_EINVAL, "conv_glu: NULL buffer");
+  if (y_dtype != WAVO_F32 && y_dtype != WAVO_F16) return fail(ctx, WAVO_EINVAL, "conv_glu: dtype");
+  if (norm != WAVO_CONV_LAYER_NORM && norm != WAVO_CONV_AFFINE)
+    return fail(ctx, WAVO_EINVAL, "conv_glu: norm %d", norm);
+  if (kernel == 0 || kernel % 2 == 0 || kernel > uint32_t(wv::dwconv_max_kernel()))
+    return fail(ctx, WAVO_EINVAL, "conv_glu: kernel %u (odd, at most %d)", kernel,
+                wv::dwconv_max_kernel());
+  if (ch == 0 || ch > uint32_t(wv::layer_norm_max_cols()))
+    return fail(ctx, WAVO_EINVAL, "conv_glu: %u channels (1..%d)", ch, wv::layer_norm_max_cols());
+  if (max_len > rows) return fail(ctx, WAVO_EINVAL, "conv_glu: max_len %u > rows %u", max_len, rows);
+  cudaSetDevice(ctx->device);
+  // The depthwise output (before the norm) in the context's scratch, then the row pass.
+  void *ws;
+  wavo_status st = workspace(ctx, size_t(rows) * ch * 4, &ws);
+  if (st) return st;
+  float *z = static_cast<float *>(ws);
+  if (seg_len) {
+    // Rows outside every segment are normalised too (the caller ignores them): clear them once.
+    CK(cudaMemsetAsync(z, 0, size_t(rows) * ch * 4, ctx->stream), "conv_glu clear");
+  }
+  CK(wv::launch_dwconv(h, dw_w, dw_b, z, int(ch), int(kernel), seg_start, seg_len, int(nseg),
+                       int(max_len), ctx->stream),
+     "conv_glu depthwise launch");
+  CK(wv::launch_layer_norm(z, n_w, n_b, y, y_dtype == WAVO_F16, int(rows), int(ch),
+                           norm == WAVO_CONV_LAYER_NORM ? wv::kLnNormSilu : wv::kLnAffineSilu,
+                           nullptr, nullptr, nullptr, 0, ctx->stream),
+     "conv_glu norm launch");
+  return WAVO_OK;
+}
+
+}  // namespace
+
+wavo_status wavo_conv_glu(wavo_ctx *ctx, const float *h, const float *dw_w, const float *dw_b,
+                          uint32_t kernel, const float *n_w, const float *n_b, int norm, void *y,
+                          int y_dtype, uint32_t t, uint32_t ch) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  return conv_glu_impl(ctx, h, dw_w, dw_b, kernel, n_w, n_b, norm, y, y_dtype, t, nullptr, nullptr,
+                       1, t, ch);
+}
+
+wavo_status wavo_conv_glu_varlen(wavo_ctx *ctx, const float *h, const float *dw_w,
+                                 const float *dw_b, uint32_t kernel, const float *n_w,
+                                 const float *n_b, int norm, void *y, int y_dtype, uint32_t rows,
+                                 const int32_t *seg_start, const int32_t *seg_len, uint32_t nseg,
+                                 uint32_t max_len, uint32_t ch) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (!seg_start || !seg_len) return fail(ctx, WAVO_EINVAL, "conv_glu: NULL segment arrays");
+  if (nseg > 65535) return fail(ctx, WAVO_EINVAL, "conv_glu: %u segments (at most 65535)", nseg);
+  return conv_glu_impl(ctx, h, dw_w, dw_b, kernel, n_w, n_b, norm, y, y_dtype, rows, seg_start,
+                       seg_len, nseg, max_len, ch);
+}
+
 // ---- rope --------------------------------------------------------------------------------
 
 wavo_status wavo_rope_rows(wavo_ctx *ctx, const float *table, void *qkv, int dtype,

@@ -222,6 +222,34 @@ class Pass:
             max_len, heads, hd, _ptr(table), table.shape[0], pos, rot, int(neox), _dtype(o)),
             self.ctx)
 
+    def layer_norm(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, y: torch.Tensor,
+                   rows: int, cols: int, rope=None) -> None:
+        """`Pass::layer_norm` (src/gpu/mod.rs:1431-1449): f32 x into y (f32 or f16); rope =
+        (table, yr, head_dim[, positions]) also writes the rotary copy yr."""
+        table = yr = positions = None
+        hd = 0
+        if rope is not None:
+            table, yr, hd = rope[:3]
+            positions = rope[3] if len(rope) > 3 else None
+            assert yr.dtype == y.dtype
+        check(L.lib().wavo_layer_norm(self.ctx, _ptr(x), _ptr(w), _ptr(b), _ptr(y), _dtype(y), rows,
+                                      cols, _ptr(table), _ptr(positions), _ptr(yr), hd), self.ctx)
+
+    def conv_glu(self, h: torch.Tensor, dw_w: torch.Tensor, dw_b: torch.Tensor, kernel: int,
+                 n_w: torch.Tensor, n_b: torch.Tensor, layer_norm: bool, y: torch.Tensor, t: int,
+                 ch: int, segs=None) -> None:
+        """`Pass::conv_glu` (src/gpu/mod.rs:1538-1566); with segs (a Segments) over packed
+        segments."""
+        norm = L.CONV_LAYER_NORM if layer_norm else L.CONV_AFFINE
+        if segs is None:
+            check(L.lib().wavo_conv_glu(self.ctx, _ptr(h), _ptr(dw_w), _ptr(dw_b), kernel, _ptr(n_w),
+                                        _ptr(n_b), norm, _ptr(y), _dtype(y), t, ch), self.ctx)
+        else:
+            check(L.lib().wavo_conv_glu_varlen(
+                self.ctx, _ptr(h), _ptr(dw_w), _ptr(dw_b), kernel, _ptr(n_w), _ptr(n_b), norm,
+                _ptr(y), _dtype(y), t, _ptr(segs.start_t), _ptr(segs.len_t), segs.len_t.numel(),
+                segs.max_len, ch), self.ctx)
+
     def rope(self, table: torch.Tensor, qkv: torch.Tensor, rows: int, pos: int,
              shape: tuple[int, int, int], neox: bool, stride: int = 0) -> None:
         """`Pass::rope` (src/gpu/mod.rs:1630-1649): shape = [heads, hd, rot]."""
