@@ -419,6 +419,137 @@ class C5(RelPosWorkload):
         return RelPosWorkload.cpu(seed, lens, layers, "q8_0", 1)
 
 
+class C5Block(Workload):
+    """Whole Parakeet 0.6B FastConformer blocks (the caller side of the attention path, the
+    reference's Block::record, src/conformer.rs:232-265) over C5's 400 segments: 24 blocks of
+    d 1024, FFN 4096, 8 heads of 128, conv kernel 9 with the folded batch norm, Q8_0 weights."""
+    D, H, F, KERNEL, LAYERS = 1024, 8, 4096, 9, 24
+    FRAME_S = 0.08
+    scaling = "strong"
+    METRIC = "encoder-block audio-sec/sec"
+
+    def __init__(self, gpu, rank, world, seed=5000):
+        import torch
+        from wavo_b200 import GGML_Q8_0
+        from wavo_b200.blocks import ConformerBlock, Segments, rel_positions
+        self.gpu, self.world = gpu, world
+        D, F = self.D, self.F
+        lengths = segment_lengths(seed, 400, 120, 300)
+        self.all_lengths = lengths
+        cost = lambda t: 24 * (6 * t * t * D + (12 + 8 * F // D) * t * D * D)  # noqa: E731
+        self.plan, mine = shard(lengths, rank, world, cost)
+        self.order, self.seg_rows, self.out_width = mine, list(lengths), D
+        self.lengths = [lengths[i] for i in mine]
+        rng = np.random.default_rng(seed)
+        self.blocks = []
+        for _ in range(self.LAYERS):
+            w = {"ff1_1": q8_0_weights(rng, F, D), "ff1_2": q8_0_weights(rng, D, F),
+                 "ff2_1": q8_0_weights(rng, F, D), "ff2_2": q8_0_weights(rng, D, F),
+                 "qkv": q8_0_weights(rng, 3 * D, D), "pos": q8_0_weights(rng, D, D),
+                 "out": q8_0_weights(rng, D, D), "pw1": q8_0_weights(rng, 2 * D, D),
+                 "pw2": q8_0_weights(rng, D, D),
+                 "u": rng.standard_normal(D, dtype=np.float32) * 0.02,
+                 "v": rng.standard_normal(D, dtype=np.float32) * 0.02,
+                 "dw": rng.standard_normal((D, self.KERNEL), dtype=np.float32) * 0.2,
+                 "dw_b": rng.standard_normal(D, dtype=np.float32) * 0.02}
+            norms = {k: (1.0 + rng.standard_normal(D, dtype=np.float32) * 0.1,
+                         rng.standard_normal(D, dtype=np.float32) * 0.1)
+                     for k in ("ff1", "attn", "conv", "ff2", "out", "conv_norm")}
+            self.blocks.append(ConformerBlock(gpu, GGML_Q8_0, D, F, self.H, self.KERNEL, w, norms,
+                                              conv_ln=False))
+        dev = gpu.torch_device
+        self.segs = Segments(self.lengths, dev)
+        rows = self.segs.rows
+        self.t_pos = max(lengths)
+        self.table = gpu.upload(rel_positions(D, self.t_pos + 15, 2 * self.t_pos + 15),
+                                torch.float16)
+        drng = np.random.default_rng(seed + 1 + rank)
+        self.y_host = torch.from_numpy(drng.standard_normal((rows, D), dtype=np.float32)).pin_memory()
+        self.x_host = torch.empty((rows, D), dtype=torch.float32).pin_memory()
+        self.y = self.y_host.to(dev)
+        self.xa = torch.zeros((rows, D), dtype=torch.float32, device=dev)
+        self.xb = torch.zeros((rows, D), dtype=torch.float32, device=dev)
+        self.s = self.blocks[0].scratch(rows, self.t_pos)
+
+    def record(self, p, timer=None):
+        tick = timer or (lambda name, fn: fn())
+        tick("cast", lambda: self.xa.copy_(self.y))
+        src, dst = self.xa, self.xb
+        for b in self.blocks:
+            b.record(p, src, dst, self.segs, self.table, self.t_pos, self.s, tick)
+            src, dst = dst, src
+        self.result = src
+
+    def inputs(self):
+        return [(self.y, self.y_host)]
+
+    def outputs(self):
+        return [(self.x_host, self.xa if self.LAYERS % 2 == 0 else self.xb)]
+
+    def launches(self):
+        return 1 + sum(b.launches() for b in self.blocks)
+
+    def work(self):
+        D, F, rows = self.D, self.F, self.segs.rows
+        return {"gemm_ff1": 2.0 * rows * D * F, "gemm_ff2": 2.0 * rows * D * F,
+                "gemm_qkv": 2.0 * rows * D * 4 * D, "gemm_out": 2.0 * rows * D * D,
+                "gemm_pos": 2.0 * (2 * self.t_pos + 15) * D * D,
+                "attention": sum(6.0 * t * t * D for t in self.lengths),
+                "gemm_pw1": 2.0 * rows * D * 2 * D, "gemm_pw2": 2.0 * rows * D * D,
+                "layer_norm": 0.0, "conv_glu": 0.0, "cast": 0.0}
+
+    def audio_s(self):
+        return sum(self.lengths) * self.FRAME_S
+
+    def total_audio_s(self, world):
+        return sum(self.all_lengths) * self.FRAME_S
+
+    def config(self):
+        return {"workload": "C5 blocks: Parakeet-0.6B FastConformer blocks (FFN, rel-pos MHSA, "
+                "conv module, norms), 24 blocks, 400 segments of U[120,300] frames, Q8_0 weights",
+                "global_batch": 400, "seq_len": "120-300",
+                "total_frames": int(sum(self.all_lengths)), "d_model": 1024, "d_ff": 4096,
+                "heads": 8, "head_dim": 128, "conv_kernel": 9, "layers": 24,
+                "weights": "GGUF Q8_0 (dequantized to f16 at load)", "l2": "inputs larger than L2",
+                "parallelism": f"segments sharded LPT over {self.world} GPU(s), no collective"}
+
+    @staticmethod
+    def cpu_sample(layers=1, seed=5000):
+        # Every 50th of the 400 segments (8, spanning the length distribution) through one block
+        # of the CPU oracle (src/cpu/conformer.rs:159-199), scaled to the set by audio seconds.
+        from oracle import oracle as O
+        D, F, H, K = 1024, 4096, 8, 9
+        lens = segment_lengths(seed, 400, 120, 300)[::50]
+        rng = np.random.default_rng(seed)
+        lin = lambda n, k: O.Linear(O.TY_Q8_0, n, k, q8_0_weights(rng, n, k))  # noqa: E731
+        ff = [lin(F, D), lin(D, F), lin(F, D), lin(D, F)]
+        lq, lp, lo, l1, l2 = lin(3 * D, D), lin(D, D), lin(D, D), lin(2 * D, D), lin(D, D)
+        u, v = (rng.standard_normal(D, dtype=np.float32) * 0.02 for _ in range(2))
+        taps = np.ascontiguousarray(rng.standard_normal((K, D), dtype=np.float32) * 0.2)
+        dw_b = np.zeros(D, np.float32)
+        nw, nb = np.ones(D, np.float32), np.zeros(D, np.float32)
+        xs = [rng.standard_normal(t * D, dtype=np.float32) for t in lens]
+        t0 = time.perf_counter()
+        for x, t in zip(xs, lens):
+            for _ in range(layers):
+                y = O.layer_norm(x, nw, nb, t, D)
+                ff[1].gemm(ff[0].gemm(y, t, epilogue="silu"), t, x, "residual", 0.5)
+                y = O.layer_norm(x, nw, nb, t, D)
+                pos = lp.gemm(np.ascontiguousarray(O.rel_positions(D, t + 15, O.pos_rows(t)).ravel()),
+                              O.pos_rows(t))
+                o = O.relative_attention(lq.gemm(y, t), pos, u, v, t, H, D)
+                lo.gemm(np.ascontiguousarray(o.ravel()), t, x, "residual", 1.0)
+                y = O.layer_norm(x, nw, nb, t, D)
+                yc = O.conv_glu(l1.gemm(y, t), taps, dw_b, nw, nb, False, t, D, K)
+                l2.gemm(yc, t, x, "residual", 1.0)
+                y = O.layer_norm(x, nw, nb, t, D)
+                ff[3].gemm(ff[2].gemm(y, t, epilogue="silu"), t, x, "residual", 0.5)
+                x = O.layer_norm(x, nw, nb, t, D)
+        dt = time.perf_counter() - t0
+        audio = sum(lens) * 0.08 * layers / 24
+        return dt, audio, f"{len(lens)} of 400 segments through {layers} of 24 blocks"
+
+
 class C3(Workload):
     """GigaAM-v3-shaped attention with RoPE: 16 layers, d 768, 16 x 48, 16 segments."""
     D, H, LAYERS = 768, 16, 16
@@ -655,7 +786,7 @@ class C4(Workload):
         return dt, 30.0 * steps / (224 * 4), f"{steps} cross-attention steps of one segment"
 
 
-WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5}
+WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5, "c5block": C5Block}
 WORKLOAD_NAMES = {
     "c1": "C1: Parakeet rel-pos MHSA layer, f32 weights, batch 1, T=138",
     "c2": "C2: Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500",
@@ -665,6 +796,8 @@ WORKLOAD_NAMES = {
           "cross attention over F16 caches",
     "c5": "C5: Parakeet-0.6B long form, 24 rel-pos layers, 400 segments of U[120,300] frames, "
           "Q8_0 weights",
+    "c5block": "C5 blocks: Parakeet-0.6B FastConformer blocks (FFN, rel-pos MHSA, conv module, "
+               "norms), 24 blocks, 400 segments of U[120,300] frames, Q8_0 weights",
 }
 
 
@@ -686,7 +819,7 @@ def run_reference(args):
         times.append(dt)
     t = float(np.mean(times))
     value = audio / t
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+    line = {"metric": getattr(W, "METRIC", METRIC), "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
             "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
@@ -920,7 +1053,8 @@ def main():
                    "sample": sample + " (CPU oracle restating the reference's src/cpu path)"}
         total_audio = wl.total_audio_s(world)
         line = {
-            "metric": METRIC, "value": total_audio / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "metric": getattr(wl, "METRIC", METRIC), "value": total_audio / (ms * 1e-3), "unit": UNIT,
+            "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE.json shapes/distributions)",

@@ -208,7 +208,7 @@ wavo_status wavo_conv_glu(wavo_ctx *ctx, const float *h, const float *dw_w, cons
                           int y_dtype, uint32_t t, uint32_t ch);
 /* The same over nseg independent segments packed in `rows` rows (device int32 seg_start, seg_len;
  * max_len >= every seg_len): the conv does not reach across a segment's ends. Rows of y outside
- * every segment are overwritten (with the norm of zeros). */
+ * every segment are overwritten with unspecified values. */
 wavo_status wavo_conv_glu_varlen(wavo_ctx *ctx, const float *h, const float *dw_w,
                                  const float *dw_b, uint32_t kernel, const float *n_w,
                                  const float *n_b, int norm, void *y, int y_dtype, uint32_t rows,

@@ -134,7 +134,7 @@ def test_conv_glu(gpu):
         assert_close(oy, want)
 
 
-@pytest.mark.parametrize("kernel,ln", [(9, True), (31, False)])
+@pytest.mark.parametrize("kernel,ln", [(9, True), (31, False), (7, True)])
 def test_conv_glu_segments(gpu, kernel, ln):
     # Packed segments: the depthwise conv stops at each segment's ends.
     from wavo_b200.blocks import Segments

@@ -86,15 +86,17 @@ class RelPosAttention:
                 "o": torch.empty(rows, self.d, dtype=torch.float16, device=dev)}
 
     def record(self, p: Pass, y: torch.Tensor, x: torch.Tensor, segs: Segments,
-               table: torch.Tensor, t_pos: int, s: dict) -> None:
+               table: torch.Tensor, t_pos: int, s: dict, tick=None) -> None:
         """y: the layer input rows (LayerNorm output); x: the f32 residual stream; table: the
         sinusoids of positions t_pos + 15 down to -t_pos (pos_rows(t_pos) rows)."""
         rows = segs.rows
-        p.gemm(y, self.qkv, s["qkv"], rows, "bias")
-        p.gemm(table, self.pos, s["p"], pos_rows(t_pos), "bias")
-        p.attention_varlen(s["qkv"], None, s["p"], s["o"], rows, segs.start_t, segs.len_t,
-                           segs.max_len, self.heads, self.hd, t_pos)
-        p.gemm(s["o"], self.out, x, rows, "residual", 1.0)
+        tick = tick or (lambda name, fn: fn())
+        tick("gemm_qkv", lambda: p.gemm(y, self.qkv, s["qkv"], rows, "bias"))
+        tick("gemm_pos", lambda: p.gemm(table, self.pos, s["p"], pos_rows(t_pos), "bias"))
+        tick("attention", lambda: p.attention_varlen(
+            s["qkv"], None, s["p"], s["o"], rows, segs.start_t, segs.len_t, segs.max_len,
+            self.heads, self.hd, t_pos))
+        tick("gemm_out", lambda: p.gemm(s["o"], self.out, x, rows, "residual", 1.0))
 
 
 class RotaryAttention:
@@ -258,23 +260,30 @@ class ConformerBlock:
         return s
 
     def record(self, p: Pass, x: torch.Tensor, out: torch.Tensor, segs: Segments,
-               table: torch.Tensor, t_pos: int, s: dict) -> None:
+               table: torch.Tensor, t_pos: int, s: dict, tick=None) -> None:
         """x: the f32 block input [rows][d] (updated in place as the residual stream); out: the
-        f32 block output norm_out(x); table: the f16 sinusoid rows (pos_rows(t_pos))."""
+        f32 block output norm_out(x); table: the f16 sinusoid rows (pos_rows(t_pos)). tick(name,
+        fn) runs each launch (a timer may wrap it)."""
         rows, d = segs.rows, self.d
         y, h = s["y"], s["h"]
         n = self.norms
-        p.layer_norm(x, *n["ff1"], y, rows, d)
-        p.gemm(y, self.ff1[0], h, rows, "silu")
-        p.gemm(h, self.ff1[1], x, rows, "residual", 0.5)
-        p.layer_norm(x, *n["attn"], y, rows, d)
-        self.attn.record(p, y, x, segs, table, t_pos, s)
-        p.layer_norm(x, *n["conv"], y, rows, d)
-        p.gemm(y, self.pw1, s["pw"], rows, "bias")
-        p.conv_glu(s["pw"], self.dw, self.dw_b, self.kernel, *n["conv_norm"], self.conv_ln, y,
-                   rows, d, segs)
-        p.gemm(y, self.pw2, x, rows, "residual", 1.0)
-        p.layer_norm(x, *n["ff2"], y, rows, d)
-        p.gemm(y, self.ff2[0], h, rows, "silu")
-        p.gemm(h, self.ff2[1], x, rows, "residual", 0.5)
-        p.layer_norm(x, *n["out"], out, rows, d)
+        tick = tick or (lambda name, fn: fn())
+        tick("layer_norm", lambda: p.layer_norm(x, *n["ff1"], y, rows, d))
+        tick("gemm_ff1", lambda: p.gemm(y, self.ff1[0], h, rows, "silu"))
+        tick("gemm_ff2", lambda: p.gemm(h, self.ff1[1], x, rows, "residual", 0.5))
+        tick("layer_norm", lambda: p.layer_norm(x, *n["attn"], y, rows, d))
+        self.attn.record(p, y, x, segs, table, t_pos, s, tick)
+        tick("layer_norm", lambda: p.layer_norm(x, *n["conv"], y, rows, d))
+        tick("gemm_pw1", lambda: p.gemm(y, self.pw1, s["pw"], rows, "bias"))
+        tick("conv_glu", lambda: p.conv_glu(s["pw"], self.dw, self.dw_b, self.kernel,
+                                            *n["conv_norm"], self.conv_ln, y, rows, d, segs))
+        tick("gemm_pw2", lambda: p.gemm(y, self.pw2, x, rows, "residual", 1.0))
+        tick("layer_norm", lambda: p.layer_norm(x, *n["ff2"], y, rows, d))
+        tick("gemm_ff1", lambda: p.gemm(y, self.ff2[0], h, rows, "silu"))
+        tick("gemm_ff2", lambda: p.gemm(h, self.ff2[1], x, rows, "residual", 0.5))
+        tick("layer_norm", lambda: p.layer_norm(x, *n["out"], out, rows, d))
+
+    def launches(self) -> int:
+        """Kernels the block launches: 5 LayerNorms, 9 GEMMs, the attention and the conv module
+        (one kernel with the affine norm, two with the LayerNorm)."""
+        return 15 + (2 if self.conv_ln else 1)

@@ -50,13 +50,15 @@ __device__ __forceinline__ float gelu_f(float x) {
   float t = 1.0f / (1.0f + 0.3275911f * z);
   float p = (((1.0614054f * t - 1.453152f) * t + 1.4214138f) * t - 0.28449674f) * t + 0.2548296f;
   float s = signbit(x) ? -1.0f : 1.0f;
-  return 0.5f * x * (1.0f + s * (1.0f - p * t * expf(-z * z)));
+  return 0.5f * x * (1.0f + s * (1.0f - p * t * __expf(-z * z)));
 }
 
 template <int E>
 __device__ __forceinline__ float epi(float v, float c, float alpha) {
   if (E == kBias) return v;
-  if (E == kSilu) return v / (1.0f + expf(-v));
+  // SiLU with the hardware exponential and reciprocal: the epilogue of a wide GEMM (FFN, N = 4d)
+  // runs one per output, and the accurate forms cost it more issue slots than the UMMAs take.
+  if (E == kSilu) return __fdividef(v, 1.0f + __expf(-v));
   if (E == kRelu) return fmaxf(v, 0.0f);
   if (E == kResidual) return c + alpha * v;
   if (E == kGelu) return gelu_f(v);

@@ -114,11 +114,13 @@ cudaError_t launch_layer_norm(const float *x, const float *w, const float *b, vo
                               int rows, int cols, int mode, const float *table,
                               const int *positions, void *yr, int hd, cudaStream_t s);
 int layer_norm_max_cols();
-// GLU of h [rows][2ch] and the depthwise conv over each segment's frames into z [rows][ch] (taps
-// [ch][kernel], odd kernel, centred).
-cudaError_t launch_dwconv(const float *h, const float *taps, const float *bias, float *z, int ch,
+// GLU of h [rows][2ch] and the depthwise conv over each segment's frames into z [rows][ch] f32
+// (taps [ch][kernel], odd kernel, centred); with n_w (an affine norm) y = SiLU(n_w·z + n_b) into z
+// instead, f16 when y_f16.
+cudaError_t launch_dwconv(const float *h, const float *taps, const float *bias, void *z, int ch,
                           int kernel, const int *seg_start, const int *seg_len, int nseg,
-                          int max_len, cudaStream_t s);
+                          int max_len, const float *n_w, const float *n_b, int y_f16,
+                          cudaStream_t s);
 int dwconv_max_kernel();
 
 constexpr int kAttnBlockQ = 128;  // queries per tile (the TMA box height of map_q)

@@ -908,21 +908,23 @@ wavo_status conv_glu_impl(wavo_ctx *ctx, const float *h, const float *dw_w, cons
     return fail(ctx, WAVO_EINVAL, "conv_glu: %u channels (1..%d)", ch, wv::layer_norm_max_cols());
   if (max_len > rows) return fail(ctx, WAVO_EINVAL, "conv_glu: max_len %u > rows %u", max_len, rows);
   cudaSetDevice(ctx->device);
+  if (norm == WAVO_CONV_AFFINE) {
+    // One pass: the per-channel affine and SiLU need no other channel of the frame.
+    CK(wv::launch_dwconv(h, dw_w, dw_b, y, int(ch), int(kernel), seg_start, seg_len, int(nseg),
+                         int(max_len), n_w, n_b, y_dtype == WAVO_F16, ctx->stream),
+       "conv_glu launch");
+    return WAVO_OK;
+  }
   // The depthwise output (before the norm) in the context's scratch, then the row pass.
   void *ws;
   wavo_status st = workspace(ctx, size_t(rows) * ch * 4, &ws);
   if (st) return st;
   float *z = static_cast<float *>(ws);
-  if (seg_len) {
-    // Rows outside every segment are normalised too (the caller ignores them): clear them once.
-    CK(cudaMemsetAsync(z, 0, size_t(rows) * ch * 4, ctx->stream), "conv_glu clear");
-  }
   CK(wv::launch_dwconv(h, dw_w, dw_b, z, int(ch), int(kernel), seg_start, seg_len, int(nseg),
-                       int(max_len), ctx->stream),
+                       int(max_len), nullptr, nullptr, 0, ctx->stream),
      "conv_glu depthwise launch");
   CK(wv::launch_layer_norm(z, n_w, n_b, y, y_dtype == WAVO_F16, int(rows), int(ch),
-                           norm == WAVO_CONV_LAYER_NORM ? wv::kLnNormSilu : wv::kLnAffineSilu,
-                           nullptr, nullptr, nullptr, 0, ctx->stream),
+                           wv::kLnNormSilu, nullptr, nullptr, nullptr, 0, ctx->stream),
      "conv_glu norm launch");
   return WAVO_OK;
 }
