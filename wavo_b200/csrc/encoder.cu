@@ -10,9 +10,9 @@
 //   dwconv_kernel      the GLU and depthwise conv over frames of packed segments: a CTA takes 32
 //                      frames x 128 channels, stages the GLU of its window (32 + kernel - 1 frames,
 //                      zero outside the segment) in shared memory, one column per thread, and sums
-//                      the taps in the reference's order (bias first, taps k = 0..kernel-1,
-//                      separately rounded products and sums); kernels of 5, 9, 15 and 31 taps
-//                      compiled with the taps in registers. With the affine norm (a folded batch
+//                      the taps in the reference's order (bias first, taps k = 0..kernel-1, one
+//                      fused multiply-add each); kernels of 5, 9, 15 and 31 taps compiled with the
+//                      taps in registers and eight outputs at a time from a register window. With the affine norm (a folded batch
 //                      norm) the CTA also applies it and SiLU and writes y; the LayerNorm form
 //                      writes the conv output for a row pass.
 #include "kernels.cuh"
@@ -204,18 +204,24 @@ __global__ void __launch_bounds__(DW_CH)
     float tk[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) tk[k] = __ldg(tc + k);
-    for (int fo = 0; fo < nf; ++fo) {
-      float acc = b;
+    // Eight outputs at a time from a register copy of the 8 + K - 1 window frames they read.
+    for (int fo0 = 0; fo0 < nf; fo0 += 8) {
+      float wv[8 + K - 1];
 #pragma unroll
-      for (int k = 0; k < K; ++k)
-        acc = __fadd_rn(acc, __fmul_rn(tk[k], dw_win[(fo + k) * DW_CH + cl]));
-      emit(fo, acc);
+      for (int i = 0; i < 8 + K - 1; ++i) wv[i] = dw_win[(fo0 + i) * DW_CH + cl];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float acc = b;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(tk[k], wv[u + k], acc);
+        if (fo0 + u < nf) emit(fo0 + u, acc);
+      }
     }
   } else {
     for (int fo = 0; fo < nf; ++fo) {
       float acc = b;
       for (int k = 0; k < kernel; ++k)
-        acc = __fadd_rn(acc, __fmul_rn(__ldg(tc + k), dw_win[(fo + k) * DW_CH + cl]));
+        acc = fmaf(__ldg(tc + k), dw_win[(fo + k) * DW_CH + cl], acc);
       emit(fo, acc);
     }
   }
