@@ -327,7 +327,9 @@ class RelPosWorkload(Workload):
         D = self.D
         rows = self.segs.rows
         att = sum(6.0 * t * t * D for t in self.lengths)  # AC + BD + PV (the reference's count)
-        return {"gemm_qkv": 2.0 * rows * D * 4 * D, "gemm_out": 2.0 * rows * D * D,
+        # The QKV GEMM multiplies 3D columns; its fourth section (q + v) is the epilogue writing q
+        # a second time with the other bias (the reference's dual outputs).
+        return {"gemm_qkv": 2.0 * rows * D * 3 * D, "gemm_out": 2.0 * rows * D * D,
                 "gemm_pos": 2.0 * (2 * self.t_pos + 15) * D * D, "attention": att, "cast": 0.0}
 
     def audio_s(self):
@@ -492,7 +494,7 @@ class C5Block(Workload):
     def work(self):
         D, F, rows = self.D, self.F, self.segs.rows
         return {"gemm_ff1": 2.0 * rows * D * F, "gemm_ff2": 2.0 * rows * D * F,
-                "gemm_qkv": 2.0 * rows * D * 4 * D, "gemm_out": 2.0 * rows * D * D,
+                "gemm_qkv": 2.0 * rows * D * 3 * D, "gemm_out": 2.0 * rows * D * D,
                 "gemm_pos": 2.0 * (2 * self.t_pos + 15) * D * D,
                 "attention": sum(6.0 * t * t * D for t in self.lengths),
                 "gemm_pw1": 2.0 * rows * D * 2 * D, "gemm_pw2": 2.0 * rows * D * D,

@@ -215,6 +215,33 @@ wavo_status wavo_conv_glu_varlen(wavo_ctx *ctx, const float *h, const float *dw_
                                  const int32_t *seg_start, const int32_t *seg_len, uint32_t nseg,
                                  uint32_t max_len, uint32_t ch);
 
+/* ---- the decoder step's ends: a greedy decode that stays on the device ----------------------- */
+
+/* Pass::embed (src/gpu/mod.rs:1471-1484) for a batch: x[b] (f32, row stride ldx; 0 means k) =
+ * row tokens[b] of the layer's weights (device int32 token ids) + row `pos` of the f32 positions
+ * table [.][k] (NULL: none) + the layer's bias. The weights as stored: F32/BF16 and F16 exact, Q8_0
+ * as q·d. */
+wavo_status wavo_embed_rows(wavo_ctx *ctx, const wavo_linear *l, const float *positions,
+                            const int32_t *tokens, uint32_t rows, uint32_t pos, float *x,
+                            uint32_t ldx);
+
+/* The next token of each of `rows` rows, on the device (no reference counterpart on the GPU: the
+ * reference picks on the CPU between steps, src/whisper/search.rs:46-59, 76-107, 111-123): per row
+ * b, logits[b] (f32 [vocab], row stride ld; edited in place as the reference edits its vector) get
+ * the suppression lists (suppress; begin_suppress while the row has generated nothing), the
+ * timestamp rules over the row's generated tokens history[b][0 .. hist_len[b]) (no
+ * <|notimestamps|>; timestamps in pairs, never decreasing; the first token a timestamp of at most
+ * max_initial steps; timestamps only when their total probability beats every other token), then
+ * the first maximum. tokens[b] gets it (and logprobs[b], if non-NULL, its log-softmax), and it is
+ * appended to the row's history unless it is EOT. A row whose tokens[b] is EOT on entry is
+ * finished and stays so. Token ids: `eot`, `no_timestamps`, and timestamps from `begin`. */
+wavo_status wavo_pick(wavo_ctx *ctx, float *logits, uint32_t ld, uint32_t rows, uint32_t vocab,
+                      int32_t *history, int32_t *hist_len, uint32_t max_hist,
+                      const int32_t *suppress, uint32_t n_suppress,
+                      const int32_t *begin_suppress, uint32_t n_begin, uint32_t eot,
+                      uint32_t no_timestamps, uint32_t begin, uint32_t max_initial,
+                      int32_t *tokens, float *logprobs);
+
 /* pos_rows (src/gpu/mod.rs:1060-1065): 2t + 15. */
 uint32_t wavo_pos_rows(uint32_t t);
 

@@ -57,6 +57,10 @@ def lib():
         L.wo_rope.argtypes = [_f, _f, _sz, _sz, _sz, _sz, ctypes.c_int]
         L.wo_rope_table.argtypes = [_sz, _sz, ctypes.c_double, _f]
         L.wo_layer_norm.argtypes = [_f, _f, _f, _f, _sz, _sz, _f, _f, _sz]
+        _i = ctypes.POINTER(ctypes.c_int32)
+        L.wo_pick.argtypes = [_f, _sz, _i, _sz, _i, _sz, _i, _sz, _sz, _sz, _sz, _sz, ctypes.c_int,
+                              _f]
+        L.wo_pick.restype = ctypes.c_int
         L.wo_conv_glu.argtypes = [_f, _f, _f, _f, _f, ctypes.c_int, _f, _sz, _sz, _sz]
         L.wo_rel_positions.argtypes = [_sz, ctypes.c_int64, _sz, _f]
         L.wo_pos_rows.argtypes = [_sz]
@@ -159,6 +163,19 @@ def conv_glu(h, taps, bias, g, beta, layer_norm, t, ch, kernel):
                       _p(np.ascontiguousarray(bias, np.float32)), _p(np.ascontiguousarray(g, np.float32)),
                       _p(np.ascontiguousarray(beta, np.float32)), int(layer_norm), _p(y), t, ch, kernel)
     return y
+
+
+def pick(logits, generated, suppress, begin_suppress, eot, no_timestamps, begin,
+         max_initial=50, logprob=True):
+    """src/whisper/search.rs:46-59 `pick` (suppression, timestamp rules, argmax): logits (f32,
+    edited in place) of one row, the window's generated tokens; returns (token, log-probability)."""
+    i32 = lambda a: np.ascontiguousarray(np.asarray(a, np.int32))  # noqa: E731
+    gen, sup, bsup = i32(generated), i32(suppress), i32(begin_suppress)
+    ip = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))  # noqa: E731
+    lp = np.zeros(1, np.float32)
+    tok = lib().wo_pick(_p(logits), logits.size, ip(gen), gen.size, ip(sup), sup.size, ip(bsup),
+                        bsup.size, eot, no_timestamps, begin, max_initial, int(logprob), _p(lp))
+    return int(tok), float(lp[0])
 
 
 def rope_table(frames, hd, theta) -> np.ndarray:

@@ -24,6 +24,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <limits>
 #include <mutex>
 #include <thread>
 #include <vector>
@@ -497,6 +498,70 @@ void wo_conv_glu(float *h, const float *taps, const float *bias, const float *g,
     float *yy = y + i * ch;
     for (size_t c = 0; c < ch; ++c) yy[c] = silu((acc[c] - mean) * rstd * g[c] + beta[c]);
   });
+}
+
+// src/whisper/search.rs:46-59 `pick` with `timestamp_rules` (76-107) and `argmax` (111-123): the
+// suppression lists, the timestamp rules over the window's generated tokens, the first maximum and
+// (with logprob) its log-softmax; logits edited in place. Returns the token.
+int wo_pick(float *logits, size_t vocab, const int32_t *generated, size_t n,
+            const int32_t *suppress, size_t n_suppress, const int32_t *begin_suppress,
+            size_t n_begin, size_t eot, size_t no_ts, size_t begin, size_t max_initial,
+            int logprob, float *lp_out) {
+  const float ninf = -std::numeric_limits<float>::infinity();
+  for (size_t i = 0; i < n_suppress; ++i) logits[suppress[i]] = ninf;
+  if (n == 0)
+    for (size_t i = 0; i < n_begin; ++i) logits[begin_suppress[i]] = ninf;
+  // timestamp_rules
+  auto is_ts = [&](int32_t id) { return size_t(id) >= begin; };
+  logits[no_ts] = ninf;
+  const bool last = n > 0 && is_ts(generated[n - 1]);
+  const bool penultimate = n < 2 || is_ts(generated[n - 2]);
+  if (last) {
+    const size_t lo = penultimate ? begin : 0, hi = penultimate ? vocab : eot;
+    for (size_t i = lo; i < hi; ++i) logits[i] = ninf;
+  }
+  for (size_t i = n; i-- > 0;) {
+    if (is_ts(generated[i])) {
+      const size_t ts = size_t(generated[i]);
+      const size_t low = (last && !penultimate) ? ts : ts + 1;
+      for (size_t j = begin; j < low; ++j) logits[j] = ninf;
+      break;
+    }
+  }
+  if (n == 0) {
+    for (size_t i = 0; i < begin; ++i) logits[i] = ninf;
+    const size_t end = std::min(begin + max_initial + 1, vocab);
+    for (size_t i = end; i < vocab; ++i) logits[i] = ninf;
+  }
+  float mx = ninf;
+  for (size_t i = begin; i < vocab; ++i) mx = std::max(mx, logits[i]);
+  float mass = ninf;
+  if (std::isfinite(mx)) {
+    double sum = 0.0;
+    for (size_t i = begin; i < vocab; ++i)
+      if (std::isfinite(logits[i])) sum += std::exp(double(logits[i] - mx));
+    if (sum > 0.0) mass = mx + float(std::log(sum));
+  }
+  float text = ninf;
+  for (size_t i = 0; i < begin; ++i) text = std::max(text, logits[i]);
+  if (mass > text)
+    for (size_t i = 0; i < begin; ++i) logits[i] = ninf;
+  // argmax
+  size_t best = 0;
+  for (size_t i = 0; i < vocab; ++i)
+    if (logits[i] > logits[best]) best = i;
+  float lp = 0.0f;
+  if (logprob) {
+    float m = ninf;
+    for (size_t i = 0; i < vocab; ++i)
+      if (std::isfinite(logits[i])) m = std::max(m, logits[i]);
+    double sum = 0.0;
+    for (size_t i = 0; i < vocab; ++i)
+      if (std::isfinite(logits[i])) sum += std::exp(double(logits[i] - m));
+    lp = logits[best] - (m + float(std::log(sum)));
+  }
+  if (lp_out) *lp_out = lp;
+  return int(best);
 }
 
 // src/gigaam/mod.rs:88-96 `rope`: per position hd/2 cosines then hd/2 sines, angles in f64.

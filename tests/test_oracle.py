@@ -357,3 +357,32 @@ def test_layer_norm_and_conv_glu_restatements():
         close(got, want)
         # The CPU conv_glu leaves the GLU in h's first halves (src/cpu/ops.rs:146-156).
         close(hc.reshape(t, 2 * ch)[:, :ch], glu)
+
+
+def test_pick_restates_reference_rules():
+    # src/whisper/search.rs:180-225 (tests): a vocabulary of 20 (text 0..10, EOT 10,
+    # <|notimestamps|> 12, timestamps 13..20); with all logits equal, which tokens the timestamp
+    # rules leave open, and the scripted greedy decode T, 3, T + 4, EOT.
+    T = 13
+
+    def rules(generated):
+        lg = np.zeros(20, np.float32)
+        O.pick(lg, generated, [], [], 10, 12, T)
+        return list(np.isfinite(lg))
+
+    allowed = lambda s: [i in s for i in range(20)]  # noqa: E731
+    assert rules([]) == allowed(range(T, 20))
+    assert rules([T, 3, T + 2]) == allowed(range(T + 2, 20))
+    assert rules([T, 3, T + 2, T + 2]) == allowed(range(0, 12))
+    assert rules([T + 1, 3]) == allowed(range(T + 2, 20))
+
+    one_hot = lambda i: np.array([5.0 if j == i else 0.0 for j in range(20)], np.float32)  # noqa: E731
+    gen, lps = [], []
+    for logits in (one_hot(T), one_hot(3), one_hot(T + 4), one_hot(10)):
+        tok, lp = O.pick(logits, gen, [11], [1, 10], 10, 12, T)
+        lps.append(lp)
+        if tok == 10:
+            break
+        gen.append(tok)
+    assert gen == [T, 3, T + 4]
+    assert -1.0 < float(np.mean(lps)) < 0.0

@@ -57,6 +57,9 @@ SIGNATURES = {
                                     _u32, _u32, _u32, _i32, _i32], _st),
     "wavo_pos_rows": ([_u32], _u32),
     "wavo_layer_norm": ([_vp, _vp, _vp, _vp, _vp, _i32, _u32, _u32, _vp, _vp, _vp, _u32], _st),
+    "wavo_embed_rows": ([_vp, _vp, _vp, _vp, _u32, _u32, _vp, _u32], _st),
+    "wavo_pick": ([_vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _vp, _u32, _vp, _u32, _u32, _u32,
+                   _u32, _u32, _vp, _vp], _st),
     "wavo_conv_glu": ([_vp, _vp, _vp, _vp, _u32, _vp, _vp, _i32, _vp, _i32, _u32, _u32], _st),
     "wavo_conv_glu_varlen": ([_vp, _vp, _vp, _vp, _u32, _vp, _vp, _i32, _vp, _i32, _u32, _vp, _vp,
                               _u32, _u32, _u32], _st),

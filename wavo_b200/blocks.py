@@ -210,6 +210,12 @@ class DecoderAttention:
                     pos: int) -> None:
         """One token per segment at position `pos`: y_self / y_cross are the LayerNorm outputs
         feeding the self and cross projections ([batch][d]); x the residual stream."""
+        self.record_self(p, y_self, x, pos)
+        self.record_cross_attend(p, y_cross, x)
+
+    def record_self(self, p: Pass, y_self: torch.Tensor, x: torch.Tensor, pos: int) -> None:
+        """The self-attention half of a step: q|k|v, k and v into the cache at `pos`, attention
+        over 0..pos, the output projection added into x."""
         d, B = self.d, self.batch
         p.gemv_rows(y_self, self.qkv, self.qkv_buf, B, "bias", ldc=3 * d)
         p.pack_batch(self.qkv_buf, (d, 0), 3 * d, self.own, d * self.context, 1, d,
@@ -217,6 +223,11 @@ class DecoderAttention:
         p.attend_batch(self.qkv_buf, 3 * d, self.own, d * self.context, self.part, self.att, d,
                        pos + 1, self.context, self.heads, self.hd, B)
         p.gemv_rows(self.att, self.self_out, x, B, "residual", 1.0, ldc=d)
+
+    def record_cross_attend(self, p: Pass, y_cross: torch.Tensor, x: torch.Tensor) -> None:
+        """The cross-attention half: the query, attention over the encoder frames, the output
+        projection added into x."""
+        d, B = self.d, self.batch
         p.gemv_rows(y_cross, self.cross_q, self.q_buf, B, "bias", ldc=d)
         p.attend_batch(self.q_buf, d, self.cross, d * self.frames, self.part, self.att, d,
                        self.frames, self.frames, self.heads, self.hd, B)
@@ -287,3 +298,83 @@ class ConformerBlock:
         """Kernels the block launches: 5 LayerNorms, 9 GEMMs, the attention and the conv module
         (one kernel with the affine norm, two with the LayerNorm)."""
         return 15 + (2 if self.conv_ln else 1)
+
+
+class WhisperDecoder:
+    """The whole Whisper decoder step for a batch of segments, on the device (the reference's
+    `Decoder::record_step`, src/transformer.rs:254-290, with the token picked by `wavo_pick` instead
+    of the CPU's search, src/whisper/search.rs:35-123): embed the batch's tokens at the step's
+    position, per layer LayerNorm -> self attention -> LayerNorm -> cross attention -> LayerNorm ->
+    FFN (GELU), the final LayerNorm, the logits through the tied embedding, the greedy pick with
+    the suppression and timestamp rules. The tokens, the generated histories and the logits stay in
+    device memory, so a whole decode runs without a host round trip per token (and can be one CUDA
+    graph).
+
+    w: "embed" [vocab][d] GGUF bytes of `ty`, "positions" [context][d] f32, "norm" (weight, bias),
+    "layers": one dict per layer with the DecoderAttention weights and biases ("qkv", "self_out",
+    "cross_q", "cross_kv", "cross_out"; biases under "b"), "fc1" [d_ff][d], "fc2" [d][d_ff] (biases
+    "fc1_b", "fc2_b") and the norms "norm_self", "norm_cross", "norm_ffn" as (weight, bias).
+    ids: "eot", "no_timestamps", "begin" (the first timestamp), "suppress", "begin_suppress"."""
+
+    def __init__(self, gpu: Gpu, ty: int, d: int, heads: int, d_ff: int, vocab: int,
+                 context: int, frames: int, batch: int, w: dict, ids: dict, max_initial: int = 50):
+        self.gpu, self.d, self.heads, self.d_ff, self.vocab = gpu, d, heads, d_ff, vocab
+        self.context, self.frames, self.batch, self.ids = context, frames, batch, ids
+        self.max_initial = max_initial
+        dev = gpu.torch_device
+        up = lambda a: gpu.upload(np.asarray(a, np.float32))  # noqa: E731
+        self.embed = gpu.linear(ty, vocab, d, w["embed"], None)
+        self.positions = up(w["positions"])
+        self.norm = tuple(up(v) for v in w["norm"])
+        self.layers = []
+        for lw in w["layers"]:
+            att = DecoderAttention(gpu, ty, d, heads, context, frames, batch, lw, lw.get("b", {}))
+            self.layers.append({
+                "att": att,
+                "fc1": gpu.linear(ty, d_ff, d, lw["fc1"], lw.get("fc1_b")),
+                "fc2": gpu.linear(ty, d, d_ff, lw["fc2"], lw.get("fc2_b")),
+                **{k: tuple(up(v) for v in lw[k]) for k in ("norm_self", "norm_cross", "norm_ffn")},
+            })
+        self.x = torch.zeros(batch, d, dtype=torch.float32, device=dev)
+        self.y = torch.zeros(batch, d, dtype=torch.float32, device=dev)
+        self.h = torch.zeros(batch, d_ff, dtype=torch.float32, device=dev)
+        self.logits = torch.zeros(batch, self.embed.width(), dtype=torch.float32, device=dev)
+        i32 = lambda a: torch.tensor(np.asarray(a, np.int32), dtype=torch.int32, device=dev)  # noqa: E731
+        self.suppress = i32(ids.get("suppress", []) or [0])
+        self.n_suppress = len(ids.get("suppress", []))
+        self.begin_suppress = i32(ids.get("begin_suppress", []) or [0])
+        self.n_begin = len(ids.get("begin_suppress", []))
+        self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.history = torch.zeros(batch, context, dtype=torch.int32, device=dev)
+        self.hist_len = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.logprobs = torch.zeros(batch, dtype=torch.float32, device=dev)
+
+    def start(self, last_prompt_tokens) -> None:
+        """A new window: each row's last prompt token, empty histories."""
+        self.tokens.copy_(torch.as_tensor(np.asarray(last_prompt_tokens, np.int32)))
+        self.hist_len.zero_()
+
+    def record_cross(self, p: Pass, enc: torch.Tensor) -> None:
+        """The cross-attention caches of every layer from the encoder output [batch][frames][d]."""
+        for lay in self.layers:
+            lay["att"].record_cross(p, enc)
+
+    def record_step(self, p: Pass, pos: int) -> None:
+        """The batch's current tokens at position `pos` through the decoder; the picked tokens
+        replace them (and are appended to the histories)."""
+        d, B = self.d, self.batch
+        p.embed_rows(self.embed, self.positions, self.tokens, B, pos, self.x)
+        for lay in self.layers:
+            p.layer_norm(self.x, *lay["norm_self"], self.y, B, d)
+            lay["att"].record_self(p, self.y, self.x, pos)
+            p.layer_norm(self.x, *lay["norm_cross"], self.y, B, d)
+            lay["att"].record_cross_attend(p, self.y, self.x)
+            p.layer_norm(self.x, *lay["norm_ffn"], self.y, B, d)
+            p.gemv_rows(self.y, lay["fc1"], self.h, B, "gelu", ldc=self.d_ff)
+            p.gemv_rows(self.h, lay["fc2"], self.x, B, "residual", 1.0, ldc=d)
+        p.layer_norm(self.x, *self.norm, self.y, B, d)
+        p.gemv_rows(self.y, self.embed, self.logits, B, "bias", ldc=self.embed.width())
+        ids = self.ids
+        p.pick(self.logits, B, self.vocab, self.history, self.hist_len, self.suppress,
+               self.n_suppress, self.begin_suppress, self.n_begin, ids["eot"],
+               ids["no_timestamps"], ids["begin"], self.max_initial, self.tokens, self.logprobs)

@@ -123,6 +123,18 @@ cudaError_t launch_dwconv(const float *h, const float *taps, const float *bias, 
                           cudaStream_t s);
 int dwconv_max_kernel();
 
+// ---- the decoder step's ends (decoder.cu) ----
+// x[b] = W[tokens[b]] + positions[pos] + bias for b < rows (wtype 0: f32 W, 1: f16, 8: int8 with
+// f32 scales d8 a block of 32); positions may be NULL.
+cudaError_t launch_embed(const void *w, int wtype, const float *d8, const float *bias,
+                         const float *positions, const int *tokens, int rows, int k, int pos,
+                         float *x, long long ldx, cudaStream_t s);
+// Greedy pick with Whisper's suppression and timestamp rules, one CTA a row (see decoder.cu).
+cudaError_t launch_pick(float *logits, long long ld, int rows, int vocab, int *history,
+                        int *hist_len, int max_hist, const int *suppress, int n_suppress,
+                        const int *begin_suppress, int n_begin, int eot, int no_ts, int begin,
+                        int max_initial, int *tokens, float *logprobs, cudaStream_t s);
+
 constexpr int kAttnBlockQ = 128;  // queries per tile (the TMA box height of map_q)
 int attn_block_keys(bool rel, int hd_pad);  // keys per block (the TMA box height of map_kv)
 int attn_pos_window_rows();      // position rows per block (the TMA box height of map_pos)

@@ -953,6 +953,57 @@ wavo_status wavo_conv_glu_varlen(wavo_ctx *ctx, const float *h, const float *dw_
                        seg_len, nseg, max_len, ch);
 }
 
+// ---- the decoder step's ends -----------------------------------------------------------------
+
+wavo_status wavo_embed_rows(wavo_ctx *ctx, const wavo_linear *l, const float *positions,
+                            const int32_t *tokens, uint32_t rows, uint32_t pos, float *x,
+                            uint32_t ldx) {
+  if (!ctx || !l) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (rows == 0) return WAVO_OK;
+  if (!tokens || !x) return fail(ctx, WAVO_EINVAL, "embed: NULL buffer");
+  if (l->device != ctx->device) return fail(ctx, WAVO_EINVAL, "embed: layer of another device");
+  if (ldx == 0) ldx = l->k;
+  if (ldx < l->k) return fail(ctx, WAVO_EINVAL, "embed: ldx %u < k %u", ldx, l->k);
+  cudaSetDevice(ctx->device);
+  const bool f32w = l->ty == WAVO_GGML_F32 || l->ty == WAVO_GGML_BF16;
+  const void *w = f32w ? static_cast<const void *>(l->w32)
+                  : l->ty == WAVO_GGML_Q8_0 ? static_cast<const void *>(l->q8)
+                                            : static_cast<const void *>(l->w16);
+  const int wt = f32w ? 0 : l->ty == WAVO_GGML_Q8_0 ? 8 : 1;
+  // Token ids index the layer's rows; an id past them reads the zero padding rows (up to n) at
+  // most: the kernel does not check ids, so callers pass ids below the layer's rows.
+  CK(wv::launch_embed(w, wt, l->d8, l->bias, positions, tokens, int(rows), int(l->k), int(pos), x,
+                      ldx, ctx->stream),
+     "embed launch");
+  return WAVO_OK;
+}
+
+wavo_status wavo_pick(wavo_ctx *ctx, float *logits, uint32_t ld, uint32_t rows, uint32_t vocab,
+                      int32_t *history, int32_t *hist_len, uint32_t max_hist,
+                      const int32_t *suppress, uint32_t n_suppress,
+                      const int32_t *begin_suppress, uint32_t n_begin, uint32_t eot,
+                      uint32_t no_timestamps, uint32_t begin, uint32_t max_initial,
+                      int32_t *tokens, float *logprobs) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (rows == 0) return WAVO_OK;
+  if (!logits || !history || !hist_len || !tokens || (n_suppress && !suppress) ||
+      (n_begin && !begin_suppress))
+    return fail(ctx, WAVO_EINVAL, "pick: NULL buffer");
+  if (ld == 0) ld = vocab;
+  if (vocab == 0 || ld < vocab || begin > vocab || eot >= vocab || max_hist == 0 ||
+      vocab > 0x7fffffffu)
+    return fail(ctx, WAVO_EINVAL, "pick: vocab %u, ld %u, begin %u, eot %u, history %u", vocab,
+                ld, begin, eot, max_hist);
+  cudaSetDevice(ctx->device);
+  CK(wv::launch_pick(logits, ld, int(rows), int(vocab), history, hist_len, int(max_hist), suppress,
+                     int(n_suppress), begin_suppress, int(n_begin), int(eot), int(no_timestamps),
+                     int(begin), int(max_initial), tokens, logprobs, ctx->stream),
+     "pick launch");
+  return WAVO_OK;
+}
+
 // ---- rope --------------------------------------------------------------------------------
 
 wavo_status wavo_rope_rows(wavo_ctx *ctx, const float *table, void *qkv, int dtype,

@@ -250,6 +250,23 @@ class Pass:
                 _ptr(y), _dtype(y), t, _ptr(segs.start_t), _ptr(segs.len_t), segs.len_t.numel(),
                 segs.max_len, ch), self.ctx)
 
+    def embed_rows(self, l: Linear, positions: torch.Tensor | None, tokens: torch.Tensor,
+                   rows: int, pos: int, x: torch.Tensor, ldx: int = 0) -> None:
+        """`Pass::embed` (src/gpu/mod.rs:1471-1484) for `rows` token ids (device int32)."""
+        assert tokens.dtype == torch.int32
+        check(L.lib().wavo_embed_rows(self.ctx, l.h, _ptr(positions), _ptr(tokens), rows, pos,
+                                      _ptr(x), ldx), self.ctx)
+
+    def pick(self, logits: torch.Tensor, rows: int, vocab: int, history: torch.Tensor,
+             hist_len: torch.Tensor, suppress: torch.Tensor, n_suppress: int,
+             begin_suppress: torch.Tensor, n_begin: int, eot: int, no_timestamps: int, begin: int,
+             max_initial: int, tokens: torch.Tensor, logprobs: torch.Tensor | None = None) -> None:
+        """The greedy pick with Whisper's suppression and timestamp rules (wavo_pick)."""
+        check(L.lib().wavo_pick(self.ctx, _ptr(logits), logits.shape[-1], rows, vocab,
+                                _ptr(history), _ptr(hist_len), history.shape[-1], _ptr(suppress),
+                                n_suppress, _ptr(begin_suppress), n_begin, eot, no_timestamps,
+                                begin, max_initial, _ptr(tokens), _ptr(logprobs)), self.ctx)
+
     def rope(self, table: torch.Tensor, qkv: torch.Tensor, rows: int, pos: int,
              shape: tuple[int, int, int], neox: bool, stride: int = 0) -> None:
         """`Pass::rope` (src/gpu/mod.rs:1630-1649): shape = [heads, hd, rot]."""
