@@ -788,7 +788,157 @@ class C4(Workload):
         return dt, 30.0 * steps / (224 * 4), f"{steps} cross-attention steps of one segment"
 
 
-WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5, "c5block": C5Block}
+class C4Full(Workload):
+    """The whole Whisper large-v3-turbo decoder for a batch of 32 windows, kept on the device: 224
+    greedy steps of embedding, 4 decoder layers (LayerNorms, self attention over the growing F16
+    cache, cross attention over the 1500 encoder frames, FFN 5120 with GELU), final LayerNorm,
+    logits over the 51 866-token vocabulary through the tied embedding, and the greedy pick with
+    the suppression and timestamp rules (src/transformer.rs:254-290, src/whisper/search.rs:35-123);
+    tokens never leave the GPU. EOT is in the suppression list so that every window runs all 224
+    steps (the config's fixed decode length)."""
+    D, H, F, LAYERS, FRAMES, CONTEXT, STEPS, BATCH, VOCAB = 1280, 20, 5120, 4, 1500, 448, 224, 32, 51866
+    EOT, NO_TS, BEGIN = 50257, 50364, 50365
+    scaling = "strong"
+    bound = "hbm"
+    METRIC = "decoder audio-sec/sec"
+
+    def __init__(self, gpu, rank, world, seed=4100):
+        import torch
+        from wavo_b200 import GGML_F16
+        from wavo_b200.blocks import WhisperDecoder
+        self.gpu, self.world = gpu, world
+        D, F = self.D, self.F
+        self.plan, _ = shard([1] * self.BATCH, rank, world, lambda t: 1)
+        self.order = self.plan.mine(rank)
+        self.seg_rows, self.out_width = [1] * self.BATCH, 1
+        self.batch = len(self.order)
+        rng = np.random.default_rng(seed)
+        vec = lambda n: rng.standard_normal(n, dtype=np.float32) * 0.02  # noqa: E731
+        norm = lambda: (1.0 + vec(D), vec(D))  # noqa: E731
+        layers = []
+        for _ in range(self.LAYERS):
+            lw = {"qkv": normal_f16(rng, (3 * D, D), 0.02).tobytes(),
+                  "self_out": normal_f16(rng, (D, D), 0.02).tobytes(),
+                  "cross_q": normal_f16(rng, (D, D), 0.02).tobytes(),
+                  "cross_kv": normal_f16(rng, (2 * D, D), 0.02).tobytes(),
+                  "cross_out": normal_f16(rng, (D, D), 0.02).tobytes(),
+                  "fc1": normal_f16(rng, (F, D), 0.02).tobytes(),
+                  "fc2": normal_f16(rng, (D, F), 0.02).tobytes(),
+                  "b": {"qkv": np.concatenate([vec(D), np.zeros(D, np.float32), vec(D)]),
+                        "self_out": vec(D), "cross_q": vec(D),
+                        "cross_kv": np.concatenate([np.zeros(D, np.float32), vec(D)]),
+                        "cross_out": vec(D)},
+                  "fc1_b": vec(F), "fc2_b": vec(D),
+                  "norm_self": norm(), "norm_cross": norm(), "norm_ffn": norm()}
+            layers.append(lw)
+        w = {"embed": normal_f16(rng, (self.VOCAB, D), 0.02).tobytes(),
+             "positions": rng.standard_normal((self.CONTEXT, D), dtype=np.float32) * 0.02,
+             "norm": norm(), "layers": layers}
+        suppress = sorted(set(int(i) for i in rng.integers(0, self.EOT, 88)) | {self.EOT})
+        ids = {"eot": self.EOT, "no_timestamps": self.NO_TS, "begin": self.BEGIN,
+               "suppress": suppress, "begin_suppress": [220]}
+        self.dec = WhisperDecoder(gpu, GGML_F16, D, self.H, F, self.VOCAB, self.CONTEXT,
+                                  self.FRAMES, self.batch, w, ids)
+        dev = gpu.torch_device
+        drng = np.random.default_rng(seed + 1 + rank)
+        enc = torch.from_numpy(drng.standard_normal((self.batch, self.FRAMES, D),
+                                                    dtype=np.float32)).to(dev)
+        self.dec.record_cross(gpu.pass_(), enc)
+        gpu.sync()
+        del enc
+        # Inputs: each window's last prompt token; result: the generated tokens.
+        self.tok_host = torch.full((self.batch,), 50360, dtype=torch.int32).pin_memory()
+        self.out_host = torch.empty((self.batch, self.CONTEXT), dtype=torch.int32).pin_memory()
+
+    def record(self, p, timer=None):
+        tick = timer or (lambda name, fn: fn())
+        tick("reset", lambda: self.dec.hist_len.zero_())
+        for pos in range(self.STEPS):
+            self.dec.record_step(p, pos, tick)
+
+    def host_gather(self, rank):
+        return None  # each rank reads back its own windows' tokens
+
+    def inputs(self):
+        return [(self.dec.tokens, self.tok_host)]
+
+    def outputs(self):
+        return [(self.out_host, self.dec.history)]
+
+    def launches(self):
+        return self.STEPS * self.dec.launches_per_step()
+
+    def work(self):
+        # HBM bytes a call of each group reads and writes (f16 weights, f16 caches, f32 rows).
+        D, F, B = self.D, self.F, self.batch
+        mean_n = (self.STEPS + 1) / 2  # self-attention keys, averaged over the steps
+        return {"cross_attention": 2.0 * D * D * 2 + B * self.FRAMES * D * 2 * 2,
+                "self_attention": 2.0 * 4 * D * D + B * mean_n * D * 2 * 2,
+                "ffn": 2.0 * 2 * D * F, "logits": 2.0 * self.VOCAB * D + 4.0 * B * self.VOCAB,
+                "pick": 4.0 * B * self.VOCAB, "layer_norm": 4.0 * 2 * B * D,
+                "embed": 2.0 * B * D + 4.0 * B * D, "reset": 0.0}
+
+    def audio_s(self):
+        return self.batch * 30.0
+
+    def total_audio_s(self, world):
+        return self.BATCH * 30.0
+
+    def config(self):
+        return {"workload": "C4 full decoder: Whisper large-v3-turbo decoder (4 layers, d 1280, "
+                "FFN 5120, vocabulary 51866), batch 32, 224 greedy steps on the device",
+                "global_batch": self.BATCH, "seq_len": self.STEPS, "d_model": self.D,
+                "heads": self.H, "layers": self.LAYERS, "frames": self.FRAMES,
+                "weights": "f16 ~N(0,0.02)", "l2": "inputs larger than L2 (the cross caches)",
+                "eot": "suppressed, so that every window decodes all 224 steps",
+                "parallelism": f"windows dealt over {self.world} GPU(s), no collective"}
+
+    @staticmethod
+    def cpu_sample(steps=4, seed=4100):
+        # One window through `steps` greedy steps of the oracle's CPU decoder (f32 gemv, f16
+        # caches) and search, scaled to 32 windows x 224 steps by tokens.
+        from oracle import oracle as O
+        D, F, H, L, V, frames = 1280, 5120, 20, 4, 51866, 1500
+        hd = D // H
+        rng = np.random.default_rng(seed)
+        lin = lambda n, k: O.Linear(O.TY_F16, n, k, normal_f16(rng, (n, k), 0.02).tobytes())  # noqa: E731
+        emb = normal_f16(rng, (V, D), 0.02)
+        E = O.Linear(O.TY_F16, V, D, emb.tobytes())
+        lay = [{k: lin(*sh) for k, sh in {"qkv": (3 * D, D), "self_out": (D, D),
+                                          "cross_q": (D, D), "cross_out": (D, D),
+                                          "fc1": (F, D), "fc2": (D, F)}.items()}
+               for _ in range(L)]
+        one, zero = np.ones(D, np.float32), np.zeros(D, np.float32)
+        cross = [rng.standard_normal(frames * 2 * D, dtype=np.float32) for _ in range(L)]
+        own = [np.zeros(448 * 2 * D, np.float32) for _ in range(L)]
+        pos_t = rng.standard_normal((448, D), dtype=np.float32) * 0.02
+        token, gen = 50360, []
+        t0 = time.perf_counter()
+        for pos in range(steps):
+            x = (emb[token].astype(np.float32) + pos_t[pos]).astype(np.float32)
+            for l in range(L):
+                w = lay[l]
+                y = O.layer_norm(x, one, zero, 1, D)
+                qkv = w["qkv"].gemv(y)
+                O.pack_cache(np.ascontiguousarray(qkv[D:]), 1, D, hd, own[l], 448, pos)
+                att = O.attend(np.ascontiguousarray(qkv[:D]), own[l], 448, pos + 1, H, hd)
+                w["self_out"].gemv(att, x, "residual", 1.0)
+                y = O.layer_norm(x, one, zero, 1, D)
+                att = O.attend(w["cross_q"].gemv(y), cross[l], frames, frames, H, hd)
+                w["cross_out"].gemv(att, x, "residual", 1.0)
+                y = O.layer_norm(x, one, zero, 1, D)
+                w["fc2"].gemv(w["fc1"].gemv(y, None, "gelu"), x, "residual", 1.0)
+            y = O.layer_norm(x, one, zero, 1, D)
+            logits = E.gemv(y)[:V].copy()
+            token, _ = O.pick(logits, gen, [50257], [220], 50257, 50364, 50365)
+            gen.append(token)
+        dt = time.perf_counter() - t0
+        audio = 30.0 * steps / 224
+        return dt, audio, f"1 window through {steps} of 224 steps"
+
+
+WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c4full": C4Full, "c5": C5,
+             "c5block": C5Block}
 WORKLOAD_NAMES = {
     "c1": "C1: Parakeet rel-pos MHSA layer, f32 weights, batch 1, T=138",
     "c2": "C2: Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500",
@@ -798,6 +948,8 @@ WORKLOAD_NAMES = {
           "cross attention over F16 caches",
     "c5": "C5: Parakeet-0.6B long form, 24 rel-pos layers, 400 segments of U[120,300] frames, "
           "Q8_0 weights",
+    "c4full": "C4 full decoder: Whisper large-v3-turbo decoder, batch 32, 224 greedy steps on the "
+              "device (LayerNorms, attention, FFN, logits, pick)",
     "c5block": "C5 blocks: Parakeet-0.6B FastConformer blocks (FFN, rel-pos MHSA, conv module, "
                "norms), 24 blocks, 400 segments of U[120,300] frames, Q8_0 weights",
 }

@@ -359,22 +359,35 @@ class WhisperDecoder:
         for lay in self.layers:
             lay["att"].record_cross(p, enc)
 
-    def record_step(self, p: Pass, pos: int) -> None:
+    # Kernels a step launches: the embedding, per layer 3 LayerNorms + the self attention's 5
+    # (q|k|v, pack, attend, combine, output) + the cross attention's 4 + the FFN's 2, then the
+    # final LayerNorm, the logits and the pick.
+    def launches_per_step(self) -> int:
+        return 1 + 14 * len(self.layers) + 3
+
+    def record_step(self, p: Pass, pos: int, tick=None) -> None:
         """The batch's current tokens at position `pos` through the decoder; the picked tokens
-        replace them (and are appended to the histories)."""
+        replace them (and are appended to the histories). tick(name, fn) runs each group of
+        launches (a timer may wrap it)."""
         d, B = self.d, self.batch
-        p.embed_rows(self.embed, self.positions, self.tokens, B, pos, self.x)
+        tick = tick or (lambda name, fn: fn())
+        tick("embed", lambda: p.embed_rows(self.embed, self.positions, self.tokens, B, pos, self.x))
         for lay in self.layers:
-            p.layer_norm(self.x, *lay["norm_self"], self.y, B, d)
-            lay["att"].record_self(p, self.y, self.x, pos)
-            p.layer_norm(self.x, *lay["norm_cross"], self.y, B, d)
-            lay["att"].record_cross_attend(p, self.y, self.x)
-            p.layer_norm(self.x, *lay["norm_ffn"], self.y, B, d)
-            p.gemv_rows(self.y, lay["fc1"], self.h, B, "gelu", ldc=self.d_ff)
-            p.gemv_rows(self.h, lay["fc2"], self.x, B, "residual", 1.0, ldc=d)
-        p.layer_norm(self.x, *self.norm, self.y, B, d)
-        p.gemv_rows(self.y, self.embed, self.logits, B, "bias", ldc=self.embed.width())
+            tick("layer_norm", lambda: p.layer_norm(self.x, *lay["norm_self"], self.y, B, d))
+            tick("self_attention", lambda: lay["att"].record_self(p, self.y, self.x, pos))
+            tick("layer_norm", lambda: p.layer_norm(self.x, *lay["norm_cross"], self.y, B, d))
+            tick("cross_attention", lambda: lay["att"].record_cross_attend(p, self.y, self.x))
+            tick("layer_norm", lambda: p.layer_norm(self.x, *lay["norm_ffn"], self.y, B, d))
+
+            def ffn():
+                p.gemv_rows(self.y, lay["fc1"], self.h, B, "gelu", ldc=self.d_ff)
+                p.gemv_rows(self.h, lay["fc2"], self.x, B, "residual", 1.0, ldc=d)
+            tick("ffn", ffn)
+        tick("layer_norm", lambda: p.layer_norm(self.x, *self.norm, self.y, B, d))
+        tick("logits", lambda: p.gemv_rows(self.y, self.embed, self.logits, B, "bias",
+                                           ldc=self.embed.width()))
         ids = self.ids
-        p.pick(self.logits, B, self.vocab, self.history, self.hist_len, self.suppress,
-               self.n_suppress, self.begin_suppress, self.n_begin, ids["eot"],
-               ids["no_timestamps"], ids["begin"], self.max_initial, self.tokens, self.logprobs)
+        tick("pick", lambda: p.pick(
+            self.logits, B, self.vocab, self.history, self.hist_len, self.suppress,
+            self.n_suppress, self.begin_suppress, self.n_begin, ids["eot"], ids["no_timestamps"],
+            ids["begin"], self.max_initial, self.tokens, self.logprobs))
