@@ -291,6 +291,33 @@ def test_gemv(gpu, ty):
     assert_near(got[3:3 + n], want, 2e-5)
 
 
+@pytest.mark.parametrize("rows,n,k", [
+    (3, 96, 224),         # one ragged tile, k over a cluster of four (k % 64 == 32: zero fill)
+    (32, 1280, 1280),     # Whisper's d x d projections: k over a cluster of seven
+    (5, 5120, 1280),      # the FFN's first projection: clusters of three
+    (32, 1280, 5120),     # the FFN's second: clusters of eight
+    (17, 40000, 256),     # many tiles: persistent CTAs, two accumulators, the ring across tiles
+])
+@pytest.mark.parametrize("epi", ["bias", "gelu", "residual", "gelu_residual", "silu", "tanh"])
+def test_gemv_rows_tc(gpu, rows, n, k, epi):
+    # Pass::gemv over a batch of rows (src/gpu/mod.rs:1461-1467) with F16 weights, on the tensor
+    # core with every epilogue, against the oracle's gemv of each row (W exact, f32 sums).
+    rng = np.random.default_rng(n + k + rows)
+    data = (rng.standard_normal(n * k) * 0.05).astype(np.float16).tobytes()
+    bias = rng.standard_normal(n).astype(np.float32)
+    x = rng.standard_normal(rows * k).astype(np.float32)
+    c0 = rng.standard_normal(rows * n).astype(np.float32)
+    lin = gpu.linear(O.TY_F16, n, k, data, bias)
+    assert lin.cols == n  # c rows of n floats
+    ref = O.Linear(O.TY_F16, n, k, data, bias)
+    want = c0.reshape(rows, n).copy()
+    for r in range(rows):
+        ref.gemv(np.ascontiguousarray(x[r * k:(r + 1) * k]), want[r], epi, 0.5)
+    xb = gpu.upload(x)
+    got = run_out(gpu, c0, lambda p, c: p.gemv_rows(xb, lin, c, rows, epi, 0.5))
+    assert_near(got, want, 2e-5)
+
+
 @pytest.mark.parametrize("m,n,k,dual", [
     (1, 164, 96, 0),        # k % 64 == 32: the last K-step's second half is the TMA's zero fill
     (37, 288, 96, 64),      # dual outputs

@@ -504,98 +504,173 @@ __global__ void __launch_bounds__(256)
 
 // ---- gemv on the tensor core (F16 weights) -------------------------------------------------
 //
-// The rows of a (at most 32) in f32 are split exactly enough for f32 accuracy: a = hi + lo with
-// hi = f16(a), lo = f16(a - hi) (|a - hi - lo| <= 2^-22 |a|). One UMMA tile of M = 128 rows holds
-// hi in rows 0-31 and lo in rows 32-63 (rows 64-127 zero), so D rows r and r + 32 are hi·W^T and
-// lo·W^T with W exact in f16 and f32 accumulation — the reference's gemv (W not rounded, f32
-// sums) to within f32 rounding. A CTA takes 128 features and a range of k (split-K for about one
-// CTA per SM); W comes by TMA while the CTA builds its A tile from coalesced loads of a, and the
-// partial sums go to c with f32 reductions, one 128-byte line of a row per warp instruction.
-constexpr int GT_N = 128;      // features per CTA (UMMA N)
-constexpr int GT_KMAX = 384;   // k per CTA (A and W tiles: 2 x 6 x 16 KB of shared memory)
+// c[r][f] = epilogue(Σ_k a[r][k]·W[f][k] + bias[f]) for rows r < rows (at most 32), W f16 [n][k].
+// The rows of a are split exactly enough for f32 accuracy: a = hi + lo with hi = f16(a), lo =
+// f16(a - hi) (|a - hi - lo| <= 2^-22 |a|). The product is taken transposed, D = W · X^T: W's 128
+// features of a tile are the UMMA's M = 128 rows (the A operand, straight from W's TMA tiles) and
+// X = [hi rows 0-31; lo rows 32-63] is the N = 64 operand, so that no UMMA row is wasted and TMEM
+// lane f holds feature f with hi·W in columns 0-31 and lo·W in columns 32-63: each epilogue thread
+// owns one feature of all 32 rows and adds its two halves in registers. W (exact in f16) streams
+// through a ring of 64-column chunks; X is built once per CTA from coalesced loads of a.
+//
+// Work split: with at least about one 128-feature tile per SM (the logits over a vocabulary) the
+// grid is persistent, one CTA per SM looping over tiles with the whole k, two TMEM accumulators so
+// that the epilogue of one tile overlaps the UMMAs of the next, and the ring running ahead across
+// tiles. With fewer tiles, k is split over a cluster of up to 8 CTAs (one tile each); the CTAs stage
+// their partial sums in shared memory and reduce them through distributed shared memory, each CTA
+// finishing a share of the rows in a fixed order, so that every epilogue (GELU, SiLU, the residual
+// add) sees the whole sum and the result does not depend on timing.
+//
+// Roles (256 threads): warp 4 lane 0 loads W, warp 5 lane 0 issues the UMMAs, warps 0-3 (TMEM
+// subpartitions 0-3) run the epilogue; all eight warps build X. The W loads before the first tile
+// do not depend on the previous kernel of the stream and start before griddepcontrol.wait.
+constexpr int GT_N = 128;           // features per tile (UMMA M)
+constexpr int GT_KMAX = 1280;       // k per CTA: X is kr / 64 chunks of [64 rows][128 B]
+constexpr int GT_THREADS = 256;
+constexpr int GT_MAX_CLUSTER = 8;   // portable cluster size
+constexpr int GT_MAX_STAGES = 4;
+constexpr int GT_SMEM_MAX = 232448; // 227 KB per CTA
+constexpr uint32_t GT_X_CHUNK = 8192, GT_W_CHUNK = 16384;
 
 struct __align__(8) GtBarriers {
-  uint64_t w_full;
-  uint64_t mma_done;
+  uint64_t full[GT_MAX_STAGES];
+  uint64_t empty[GT_MAX_STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-__global__ void __launch_bounds__(128, 1)
+__host__ __device__ constexpr size_t gt_smem_bytes(int nch, int stages) {
+  return 1024 + size_t(nch) * GT_X_CHUNK + size_t(stages) * GT_W_CHUNK + sizeof(GtBarriers);
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float gemv_epilogue(int epi, float v, float old, float alpha) {
+  switch (epi) {
+    case kBias: return v;
+    case kSilu: return v / (1.0f + expf(-v));
+    case kRelu: return fmaxf(v, 0.0f);
+    case kResidual: return old + alpha * v;
+    case kGelu: return gelu_g(v);
+    case kGeluResidual: return old + gelu_g(v);
+    default: return tanhf(fminf(fmaxf(v, -10.0f), 10.0f));
+  }
+}
+
+__device__ __forceinline__ bool gemv_reads_c(int epi) {
+  return epi == kResidual || epi == kGeluResidual;
+}
+
+__global__ void __launch_bounds__(GT_THREADS, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const float *__restrict__ a,
                    long long lda, const float *__restrict__ bias, float *__restrict__ c,
-                   long long ldc, int rows, int n, int k, int kr, int epi, float alpha,
-                   int *err) {
+                   long long ldc, int rows, int n, int k, int kr, int stages, int tiles, int epi,
+                   float alpha, int *err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  const int nch = kr / 64;  // 64-column chunks of k
-  uint8_t *sa = smem;                  // [nch][128 rows][128 B], 128-byte swizzle
-  uint8_t *sw = smem + nch * 16384;    // [nch][128 features][128 B]
-  GtBarriers *bar = reinterpret_cast<GtBarriers *>(sw + nch * 16384);
-  const uint32_t warp = warp_id(), lane = lane_id();
-  const int f0 = blockIdx.x * GT_N, k0 = blockIdx.y * kr;
+  const int ks = int(gridDim.y);  // CTAs of a cluster along k (1: persistent over the tiles)
+  const int k0 = int(blockIdx.y) * kr;
   const int kn = min(kr, k - k0);
+  const int nch = (kn + 63) / 64;
+  uint8_t *sx = smem;                            // X: [nch][64 rows][128 B], 128-byte swizzle
+  uint8_t *sw = smem + (kr / 64) * GT_X_CHUNK;   // W ring: [stages][128 features][128 B]
+  GtBarriers *bar = reinterpret_cast<GtBarriers *>(sw + stages * GT_W_CHUNK);
+  const uint32_t warp = warp_id(), lane = lane_id();
+  // This CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ... (exactly one when k is split).
+  const int my_tiles =
+      ks > 1 ? 1 : (tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+  const int total = my_tiles * nch;  // W chunks through the ring
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar->w_full, 1);
-    mbar_init(&bar->mma_done, 1);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&bar->full[s], 1);
+      mbar_init(&bar->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar->acc_full[b], 1);
+      mbar_init(&bar->acc_empty[b], 4);
+    }
     bar->abort = 0;
     fence_mbar_init();
-    prefetch_tmap(&map_w);
   }
   if (warp == 0) {
-    tmem_alloc(&bar->tmem_base, 128);
+    tmem_alloc(&bar->tmem_base, 128);  // two accumulators of 64 columns
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch_dependents();
   const uint32_t tmem = bar->tmem_base;
   const Abort ab{&bar->abort, err};
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&bar->w_full, nch * 16384);
-    for (int ch = 0; ch < nch; ++ch)
-      tma_load_2d(sw + ch * 16384, &map_w, &bar->w_full, k0 + ch * 64, f0);
+  // W chunk g of this CTA: tile g / nch, k chunk g % nch, into ring slot g % stages.
+  const auto w_load = [&](int g) {
+    const int slot = g % stages;
+    const int tile = int(blockIdx.x) + (g / nch) * int(gridDim.x);
+    mbar_arrive_expect_tx(&bar->full[slot], GT_W_CHUNK);
+    tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], k0 + (g % nch) * 64,
+                tile * GT_N);
+  };
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&map_w);
+    for (int g = 0; g < stages && g < total; ++g) w_load(g);  // W does not wait for the stream
   }
-  // The A tile: rows 0-31 hi = f16(a), rows 32-63 lo = f16(a - hi). Warp w loads rows w, w + 4,
-  // ... of the CTA's k-slice, lane l the float4s l, l + 32, l + 64 of a row, so that each load
-  // instruction reads consecutive bytes and all 24 are in flight before the first conversion.
-  // Rows past `rows` and columns past the slice are zero; rows 64-127 are left as they are: they
-  // only feed accumulator rows that are never read.
+  griddep_wait();  // the previous kernel of the stream has completed (a and c are ready)
+
+  // X: row r < 32 of the CTA's k-range as hi = f16(a) in X row r and lo = f16(a - hi) in X row
+  // r + 32; zeros past `rows` and past k. Warp w takes rows w, w + 8, w + 16, w + 24 (two at a
+  // time, every load of the pair in flight before the first conversion), lane l the float4s l,
+  // l + 32, ... of a row, so that each load instruction reads consecutive bytes.
   {
-    const int q4 = kr / 4;  // float4s per row of the slice (at most 96)
-    float4 v[8][3];
+    const int q4 = nch * 16;  // float4 columns of the chunks (up to 320)
+#pragma unroll 1
+    for (int i = 0; i < 4; i += 2) {
+      float4 v[2][10];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int row = int(warp) + 4 * i;
+      for (int h = 0; h < 2; ++h) {
+        const int row = int(warp) + 8 * (i + h);
+        const float *ar = a + (long long)row * lda + k0;
 #pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int c4 = int(lane) + 32 * j;
-        v[i][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (row < rows && c4 < q4 && 4 * c4 < kn)
-          v[i][j] = *reinterpret_cast<const float4 *>(a + (long long)row * lda + k0 + 4 * c4);
+        for (int j = 0; j < 10; ++j) {
+          const int kk = 4 * (int(lane) + 32 * j);
+          v[h][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          if (row < rows && kk < kn) {
+            v[h][j] = *reinterpret_cast<const float4 *>(ar + kk);
+            if (kk + 4 > kn) {  // k not a multiple of 4: the tail of the last float4 is zero
+              if (kk + 1 >= kn) v[h][j].y = 0.0f;
+              if (kk + 2 >= kn) v[h][j].z = 0.0f;
+              v[h][j].w = 0.0f;
+            }
+          }
+        }
       }
-    }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int row = int(warp) + 4 * i;
+      for (int h = 0; h < 2; ++h) {
+        const int row = int(warp) + 8 * (i + h);
 #pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int c4 = int(lane) + 32 * j;
-        if (c4 >= q4) continue;
-        const int kk = 4 * c4;
-        const float x[4] = {v[i][j].x, v[i][j].y, v[i][j].z, v[i][j].w};
-        float lo[4];
+        for (int j = 0; j < 10; ++j) {
+          const int c4 = int(lane) + 32 * j;
+          if (c4 >= q4) continue;
+          const int kk = 4 * c4;
+          const float x[4] = {v[h][j].x, v[h][j].y, v[h][j].z, v[h][j].w};
+          float lo[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) lo[e] = x[e] - __half2float(__float2half_rn(x[e]));
-        // 16-byte chunk (kk % 64) / 8 of the row in the 128-byte swizzle, this float4's half of it.
-        const int off =
-            (kk >> 6) * 16384 + ((((kk & 63) >> 3) ^ (row & 7)) * 16) + ((kk >> 2) & 1) * 8;
-        *reinterpret_cast<uint2 *>(sa + off + row * 128) =
-            make_uint2(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]));
-        *reinterpret_cast<uint2 *>(sa + off + (row + 32) * 128) =
-            make_uint2(pack_half2(lo[0], lo[1]), pack_half2(lo[2], lo[3]));
+          for (int e = 0; e < 4; ++e) lo[e] = x[e] - __half2float(__float2half_rn(x[e]));
+          // 16-byte unit (kk % 64) / 8 of the row in the 128-byte swizzle, this float4's half.
+          const int off = (kk >> 6) * int(GT_X_CHUNK) + ((((kk & 63) >> 3) ^ (row & 7)) * 16) +
+                          ((kk >> 2) & 1) * 8;
+          *reinterpret_cast<uint2 *>(sx + off + row * 128) =
+              make_uint2(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]));
+          *reinterpret_cast<uint2 *>(sx + off + (row + 32) * 128) =
+              make_uint2(pack_half2(lo[0], lo[1]), pack_half2(lo[2], lo[3]));
+        }
       }
     }
   }
@@ -603,67 +678,117 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  bool ok = true;
-  if (threadIdx.x == 0) {
-    ok = mbar_wait(&bar->w_full, 0, ab, kErrTimeoutMma);
-    if (ok) {
+
+  float *part = reinterpret_cast<float *>(sw);  // split k: this CTA's partial sums [32][128]
+  if (warp == 4) {
+    if (lane == 0) {
+#pragma unroll 1
+      for (int g = stages; g < total; ++g) {
+        if (!mbar_wait(&bar->empty[g % stages], ((g / stages) - 1) & 1, ab, kErrTimeoutProducer))
+          break;
+        w_load(g);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint64_t dx0 = sdesc_sw128(smem_u32(sx), 16, 1024);
+      const uint64_t dw0 = sdesc_sw128(smem_u32(sw), 16, 1024);
+      constexpr uint32_t IDESC = idesc_f16(128, 64, 0);
+      int g = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int buf = i & 1;
+        if (i >= 2 && !mbar_wait(&bar->acc_empty[buf], ((i >> 1) - 1) & 1, ab, kErrTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(buf * 64);
+#pragma unroll 1
+        for (int ch = 0; ch < nch; ++ch, ++g) {
+          const int slot = g % stages;
+          if (!mbar_wait(&bar->full[slot], (g / stages) & 1, ab, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t dw = dw0 + uint64_t((slot * GT_W_CHUNK) >> 4);
+          const uint64_t dx = dx0 + uint64_t((ch * GT_X_CHUNK) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // 16 columns of k = 32 bytes a step
+            umma_f16(d, dw + 2 * kk, dx + 2 * kk, IDESC, (ch > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&bar->empty[slot]);
+        }
+        if (ok) umma_commit(&bar->acc_full[buf]);
+      }
+    }
+  } else if (warp < 4) {
+    // Epilogue: lane l of warp w is feature 32w + l of the tile; TMEM columns 0-31 hold its hi·W
+    // of rows 0-31, columns 32-63 its lo·W.
+#pragma unroll 1
+    for (int i = 0; i < my_tiles; ++i) {
+      const int buf = i & 1;
+      const int tile = int(blockIdx.x) + i * int(gridDim.x);
+      if (!mbar_wait_warp(&bar->acc_full[buf], (i >> 1) & 1, ab, kErrTimeoutConsumer)) break;
       tc_fence_after();
-      const uint64_t da = sdesc_sw128(smem_u32(sa), 16, 1024);
-      const uint64_t dw = sdesc_sw128(smem_u32(sw), 16, 1024);
-      constexpr uint32_t IDESC = idesc_f16(128, GT_N, 0);
-      for (int st = 0; st < kr / 16; ++st) {
-        const uint64_t off = uint64_t(((st >> 2) * 16384 + (st & 3) * 32) >> 4);
-        umma_f16(tmem, da + off, dw + off, IDESC, st > 0 ? 1u : 0u);
-      }
-      umma_commit(&bar->mma_done);
-    }
-  }
-  ok = mbar_wait_warp(&bar->mma_done, 0, ab, kErrTimeoutConsumer);
-  tc_fence_after();
-  // hi·W (TMEM lanes 0-31) and lo·W (lanes 32-63) meet in shared memory (the A tile is no longer
-  // read): warp 1 writes lo, warp 0 adds hi, the bias (first k-split only) and alpha. Then all four
-  // warps reduce into c, a row's 128 features per warp (lane l: features l, l + 32, l + 64,
-  // l + 96), so that each reduction instruction covers one 128-byte line of c.
-  float *sum = reinterpret_cast<float *>(sa);  // [32 rows][129]
-  if (ok && warp == 1) {
-#pragma unroll 1
-    for (int q = 0; q < GT_N / 32; ++q) {
-      uint32_t v[32];
-      tmem_ld32(tmem + ((32u) << 16) + q * 32, v);
+      uint32_t hi[32], lo[32];
+      const uint32_t taddr = tmem + ((warp * 32u) << 16) + uint32_t(buf * 64);
+      tmem_ld32(taddr, hi);
+      tmem_ld32(taddr + 32, lo);
       tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->acc_empty[buf]);
+      const int fl = int(warp) * 32 + int(lane);
+      if (ks == 1) {
+        const int f = tile * GT_N + fl;
+        if (f < n) {
+          const float b = bias[f];
+          const bool rd = gemv_reads_c(epi);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) sum[lane * 129 + q * 32 + j] = __uint_as_float(v[j]);
-    }
-  }
-  __syncthreads();
-  if (ok && warp == 0) {
-#pragma unroll 1
-    for (int q = 0; q < GT_N / 32; ++q) {
-      uint32_t v[32];
-      tmem_ld32(tmem + q * 32, v);
-      tmem_wait_ld();
-      const int fb = f0 + q * 32;
+          for (int r = 0; r < 32; ++r) {
+            if (r < rows) {
+              float *cp = c + (long long)r * ldc + f;
+              const float v = (__uint_as_float(hi[r]) + __uint_as_float(lo[r])) + b;
+              *cp = gemv_epilogue(epi, v, rd ? *cp : 0.0f, alpha);
+            }
+          }
+        }
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float t = __uint_as_float(v[j]) + sum[lane * 129 + q * 32 + j];
-        if (blockIdx.y == 0 && fb + j < n) t += bias[fb + j];
-        sum[lane * 129 + q * 32 + j] = epi == kResidual ? alpha * t : t;
+        for (int r = 0; r < 32; ++r)
+          part[r * GT_N + fl] = __uint_as_float(hi[r]) + __uint_as_float(lo[r]);
       }
     }
   }
-  __syncthreads();
-  if (ok) {
-#pragma unroll 1
-    for (int i = 0; i < 8; ++i) {
-      const int row = int(warp) * 8 + i;
-      if (row >= rows) break;
-      float *crow = c + (long long)row * ldc + f0;
+  if (ks > 1) {
+    // Every CTA of the cluster has its partial sums in shared memory; CTA q finishes rows q,
+    // q + ks, ... (threads 0-127 and 128-255 take alternate rows of that set), adding the CTAs'
+    // sums in rank order.
+    __syncwarp();
+    cluster_sync();
+    const uint32_t rank = cluster_ctarank();
+    const int fl = int(threadIdx.x) & (GT_N - 1);
+    const int f = int(blockIdx.x) * GT_N + fl;
+    if (f < n) {
+      const float b = bias[f];
+      const bool rd = gemv_reads_c(epi);
+      uint32_t peer[GT_MAX_CLUSTER];
 #pragma unroll
-      for (int j = 0; j < GT_N / 32; ++j) {
-        const int f = int(lane) + 32 * j;
-        if (f0 + f < n) atomicAdd(crow + f, sum[row * 129 + f]);
+      for (int p = 0; p < GT_MAX_CLUSTER; ++p)
+        peer[p] = p < ks ? mapa_shared(part + fl, uint32_t(p)) : 0u;
+#pragma unroll 1
+      for (int r = int(rank) + ks * int(threadIdx.x >> 7); r < rows; r += 2 * ks) {
+        float v = 0.0f;
+#pragma unroll
+        for (int p = 0; p < GT_MAX_CLUSTER; ++p)
+          if (p < ks) v += ld_cluster_f32(peer[p] + uint32_t(r * GT_N * 4));
+        v += b;
+        float *cp = c + (long long)r * ldc + f;
+        *cp = gemv_epilogue(epi, v, rd ? *cp : 0.0f, alpha);
       }
     }
+    __syncwarp();
+    cluster_sync();  // the peers' shared memory stays until every CTA has read it
   }
   tc_fence_before();
   __syncthreads();
@@ -783,34 +908,50 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
 
 cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map_w128,
                            const float *bias, float *c, long long ldc, int rows, int n, int k,
-                           int epilogue, float alpha, int *err, cudaStream_t s) {
+                           int epilogue, float alpha, int sms, int *err, cudaStream_t s) {
   if (rows <= 0 || n <= 0) return cudaSuccess;
-  // One wave: tiles x k-splits CTAs on the 148 SMs (one CTA per SM), k per split a multiple of 64
-  // up to GT_KMAX.
+  if (rows > 32 || k <= 0 || sms <= 0) return cudaErrorInvalidValue;
+  // About one CTA per SM: tiles x k-splits, the splits of a tile one cluster (at most 8 CTAs); with
+  // a tile per SM or more, one persistent CTA per SM over the tiles with the whole k.
   const int tiles = (n + GT_N - 1) / GT_N;
-  int ks = 148 / tiles;
+  int ks = tiles < sms ? sms / tiles : 1;
+  if (ks > GT_MAX_CLUSTER) ks = GT_MAX_CLUSTER;
   if (ks < 1) ks = 1;
-  int kr = (k + ks - 1) / ks;
-  kr = (kr + 63) / 64 * 64;
+  int kr = ((k + ks - 1) / ks + 63) / 64 * 64;
   if (kr > GT_KMAX) kr = GT_KMAX;
   ks = (k + kr - 1) / kr;
-  if (epilogue == kBias) {
-    cudaError_t e = cudaMemset2DAsync(c, size_t(ldc) * 4, 0, size_t(n) * 4, rows, s);
-    if (e != cudaSuccess) return e;
-  }
-  const size_t smem = 1024 + size_t(kr / 64) * 2 * 16384 + sizeof(GtBarriers);
+  if (ks > GT_MAX_CLUSTER) return cudaErrorNotSupported;  // k above 8 x 1280
+  kr = ((k + ks - 1) / ks + 63) / 64 * 64;                // the same splits, evenly
+  const int nch = kr / 64;
+  int stages = int((GT_SMEM_MAX - gt_smem_bytes(nch, 0)) / GT_W_CHUNK);
+  if (stages > GT_MAX_STAGES) stages = GT_MAX_STAGES;
+  if (stages < 2) return cudaErrorNotSupported;
+  const size_t smem = gt_smem_bytes(nch, stages);
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(1024 + 2 * (GT_KMAX / 64) * 16384 + sizeof(GtBarriers)));
+                                         GT_SMEM_MAX);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  gemv_tc_kernel<<<dim3(tiles, ks), 128, smem, s>>>(map_w128, a, lda, bias, c, ldc, rows, n, k, kr,
-                                                   epilogue, alpha, err);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = ks > 1 ? dim3(tiles, ks) : dim3(tiles < sms ? tiles : sms, 1);
+  cfg.blockDim = dim3(GT_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = unsigned(ks);
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ks > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel, map_w128, a, lda, bias, c, ldc, rows, n, k, kr,
+                            stages, tiles, epilogue, alpha, err);
 }
 
 }  // namespace wv

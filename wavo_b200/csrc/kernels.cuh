@@ -174,11 +174,12 @@ cudaError_t launch_rope(const float *table, void *qkv, int x_f16, long long stri
                         int sections, cudaStream_t s);
 // Rows (<= 32) of f32 a through W of type wtype (0 f32 [n][k], 1 f16 [n][k], 8 int8 [n][k] with
 // f32 scales [n][k/32]) in f32: the reference's gemv (W not rounded to f16).
-// F16 weights, bias or residual epilogue, rows <= 32, lda % 4 == 0 and a 16-byte aligned: the
-// tensor-core gemv (split f16 rows of a, f32 accuracy) over W's 128-row 2D tensor map.
+// F16 weights, any epilogue, rows <= 32, lda % 4 == 0 and a 16-byte aligned: the tensor-core
+// gemv (split f16 rows of a, f32 accuracy) over W's 128-row 2D tensor map. Returns
+// cudaErrorNotSupported, launching nothing, for k above 8 x 1280.
 cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map_w128,
                            const float *bias, float *c, long long ldc, int rows, int n, int k,
-                           int epilogue, float alpha, int *err, cudaStream_t s);
+                           int epilogue, float alpha, int sms, int *err, cudaStream_t s);
 cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
                         const float *scales, const float *bias, float *c, long long ldc, int rows,
                         int n, int k, int epilogue, float alpha, cudaStream_t s);

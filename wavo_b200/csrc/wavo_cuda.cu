@@ -653,12 +653,15 @@ wavo_status wavo_gemv_rows(wavo_ctx *ctx, const float *a, uint32_t lda, const wa
                                             : static_cast<const void *>(l->w16);
   const int wt = f32w ? 0 : l->ty == WAVO_GGML_Q8_0 ? 8 : 1;
   // Pass::gemv writes l.cols outputs (src/gpu/mod.rs:1461-1467).
-  if (wt == 1 && (epilogue == WAVO_EPI_BIAS || epilogue == WAVO_EPI_RESIDUAL)) {
+  if (wt == 1) {
     // F16 weights are exact in f16: the tensor-core form (split f16 rows, f32 accuracy).
-    CK(wv::launch_gemv_tc(a, lda, l->map_w128, l->bias, c, ldc, int(rows), int(l->cols),
-                          int(l->k), epilogue, alpha, ctx->dev_err, ctx->stream),
-       "gemv launch");
-    return WAVO_OK;
+    const cudaError_t e =
+        wv::launch_gemv_tc(a, lda, l->map_w128, l->bias, c, ldc, int(rows), int(l->cols),
+                           int(l->k), epilogue, alpha, ctx->sms, ctx->dev_err, ctx->stream);
+    if (e != cudaErrorNotSupported) {
+      CK(e, "gemv launch");
+      return WAVO_OK;
+    }
   }
   CK(wv::launch_gemv(a, lda, wt, w, l->d8, l->bias, c, ldc, int(rows), int(l->cols), int(l->k),
                      epilogue, alpha, ctx->stream),
