@@ -296,7 +296,9 @@ def test_gemv(gpu, ty):
     (32, 1280, 1280),     # Whisper's d x d projections: k over a cluster of seven
     (5, 5120, 1280),      # the FFN's first projection: clusters of three
     (32, 1280, 5120),     # the FFN's second: clusters of eight
-    (17, 40000, 256),     # many tiles: persistent CTAs, two accumulators, the ring across tiles
+    (17, 40000, 256),     # many tiles: two or three a CTA, sharing the X chunks
+    (3, 80000, 64),       # five tiles a CTA (512 TMEM columns)
+    (2, 128, 8192),       # one tile, a long k over eight CTAs: the X slots reused many times
 ])
 @pytest.mark.parametrize("epi", ["bias", "gelu", "residual", "gelu_residual", "silu", "tanh"])
 def test_gemv_rows_tc(gpu, rows, n, k, epi):

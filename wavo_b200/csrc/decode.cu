@@ -510,39 +510,50 @@ __global__ void __launch_bounds__(256)
 // features of a tile are the UMMA's M = 128 rows (the A operand, straight from W's TMA tiles) and
 // X = [hi rows 0-31; lo rows 32-63] is the N = 64 operand, so that no UMMA row is wasted and TMEM
 // lane f holds feature f with hi·W in columns 0-31 and lo·W in columns 32-63: each epilogue thread
-// owns one feature of all 32 rows and adds its two halves in registers. W (exact in f16) streams
-// through a ring of 64-column chunks; X is built once per CTA from coalesced loads of a.
+// owns one feature of all 32 rows and adds its two halves in registers.
 //
-// Work split: with at least about one 128-feature tile per SM (the logits over a vocabulary) the
-// grid is persistent, one CTA per SM looping over tiles with the whole k, two TMEM accumulators so
-// that the epilogue of one tile overlaps the UMMAs of the next, and the ring running ahead across
-// tiles. With fewer tiles, k is split over a cluster of up to 8 CTAs (one tile each); the CTAs stage
-// their partial sums in shared memory and reduce them through distributed shared memory, each CTA
-// finishing a share of the rows in a fixed order, so that every epilogue (GELU, SiLU, the residual
-// add) sees the whole sum and the result does not depend on timing.
+// Both operands arrive by TMA through rings, k outermost: for each 64-column chunk of k the CTA
+// loads the rows of a as an f32 [32][64] box (zero fill past `rows` and k) into an X slot, where
+// one warp converts it in place to the hi/lo rows in the UMMA's 128-byte swizzle, and then streams
+// the W chunk of each of its tiles (up to 8, one 64-column TMEM accumulator each). X needs only a
+// few slots, and the rest of shared memory goes to the W ring, deep enough to keep HBM busy. (Plain
+// loads of a, replicated over every CTA, are limited by the small L1 that the large shared-memory
+// carve-out leaves: few lines in flight per SM. TMA is not.)
 //
-// Roles (256 threads): warp 4 lane 0 loads W, warp 5 lane 0 issues the UMMAs, warps 0-3 (TMEM
-// subpartitions 0-3) run the epilogue; all eight warps build X. The W loads before the first tile
-// do not depend on the previous kernel of the stream and start before griddepcontrol.wait.
+// Work split: with at least about one 128-feature tile per SM (the logits over a vocabulary) each
+// CTA takes tiles blockIdx.x, + gridDim.x, ... with the whole k. With fewer tiles, k is split over
+// a cluster of up to 8 CTAs (one tile each): the CTAs stage their partial sums in shared memory and
+// CTA q finishes rows q, q + ks, ..., adding every CTA's partials (read through distributed shared
+// memory) in rank order, so that every epilogue (GELU, SiLU, the residual add) sees the whole sum
+// and the result does not depend on timing. The epilogue is a template parameter: one small body
+// per kernel, unrolled over the 32 rows.
+//
+// Roles (256 threads): warp 4 lane 0 loads W, warp 7 lane 0 loads the rows of a, warp 5 lane 0
+// issues the UMMAs, warps 0-3 (TMEM subpartitions 0-3) convert the X chunks (warp s those of slot s,
+// so that each waits on its slot's phases in order) and then run the epilogue. The W loads that fit
+// the ring do not depend on the previous kernel of the stream and start before griddepcontrol.wait.
 constexpr int GT_N = 128;           // features per tile (UMMA M)
-constexpr int GT_KMAX = 1280;       // k per CTA: X is kr / 64 chunks of [64 rows][128 B]
+constexpr int GT_TMAX = 8;          // tiles per CTA (8 x 64 TMEM columns)
 constexpr int GT_THREADS = 256;
 constexpr int GT_MAX_CLUSTER = 8;   // portable cluster size
-constexpr int GT_MAX_STAGES = 4;
+constexpr int GT_XS = 4;            // X slots
+constexpr int GT_MAX_STAGES = 12;   // W ring slots
 constexpr int GT_SMEM_MAX = 232448; // 227 KB per CTA
 constexpr uint32_t GT_X_CHUNK = 8192, GT_W_CHUNK = 16384;
 
 struct __align__(8) GtBarriers {
   uint64_t full[GT_MAX_STAGES];
   uint64_t empty[GT_MAX_STAGES];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
+  uint64_t x_loaded[GT_XS];  // the f32 box of the slot's X chunk landed
+  uint64_t x_ready[GT_XS];   // converted (hi/lo, swizzled)
+  uint64_t x_empty[GT_XS];   // the UMMAs of every tile are done with it
+  uint64_t acc_full;         // every UMMA of the CTA completed
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-__host__ __device__ constexpr size_t gt_smem_bytes(int nch, int stages) {
-  return 1024 + size_t(nch) * GT_X_CHUNK + size_t(stages) * GT_W_CHUNK + sizeof(GtBarriers);
+__host__ __device__ constexpr size_t gt_smem_bytes(int stages) {
+  return 1024 + size_t(GT_XS) * GT_X_CHUNK + size_t(stages) * GT_W_CHUNK + sizeof(GtBarriers);
 }
 
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
@@ -551,57 +562,88 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ float gemv_epilogue(int epi, float v, float old, float alpha) {
-  switch (epi) {
-    case kBias: return v;
-    case kSilu: return v / (1.0f + expf(-v));
-    case kRelu: return fmaxf(v, 0.0f);
-    case kResidual: return old + alpha * v;
-    case kGelu: return gelu_g(v);
-    case kGeluResidual: return old + gelu_g(v);
-    default: return tanhf(fminf(fmaxf(v, -10.0f), 10.0f));
+template <int EPI>
+__device__ __forceinline__ float gemv_epilogue(float v, float old, float alpha) {
+  if constexpr (EPI == kBias) return v;
+  else if constexpr (EPI == kSilu) return v / (1.0f + expf(-v));
+  else if constexpr (EPI == kRelu) return fmaxf(v, 0.0f);
+  else if constexpr (EPI == kResidual) return old + alpha * v;
+  else if constexpr (EPI == kGelu) return gelu_g(v);
+  else if constexpr (EPI == kGeluResidual) return old + gelu_g(v);
+  else return tanhf(fminf(fmaxf(v, -10.0f), 10.0f));
+}
+
+// X chunk in place: the f32 box [32 rows][64] (256-byte rows, as TMA wrote it) becomes hi rows 0-31
+// and lo rows 32-63 of 128 bytes in the 128-byte swizzle. Lane l takes the 16-byte units l % 8 of
+// rows l / 8, l / 8 + 4, ...: every value is read into registers before the warp writes any.
+__device__ __forceinline__ void gt_convert_chunk(uint8_t *slot, uint32_t lane) {
+  const int u = int(lane & 7);
+  float4 v[8][2];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + int(lane >> 3);
+    const float4 *src = reinterpret_cast<const float4 *>(slot + r * 256 + u * 32);
+    v[it][0] = src[0];
+    v[it][1] = src[1];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + int(lane >> 3);
+    const float x[8] = {v[it][0].x, v[it][0].y, v[it][0].z, v[it][0].w,
+                        v[it][1].x, v[it][1].y, v[it][1].z, v[it][1].w};
+    float lo[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) lo[e] = x[e] - __half2float(__float2half_rn(x[e]));
+    const int off = (u ^ (r & 7)) << 4;
+    *reinterpret_cast<uint4 *>(slot + r * 128 + off) =
+        make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]),
+                   pack_half2(x[6], x[7]));
+    *reinterpret_cast<uint4 *>(slot + (r + 32) * 128 + off) =
+        make_uint4(pack_half2(lo[0], lo[1]), pack_half2(lo[2], lo[3]), pack_half2(lo[4], lo[5]),
+                   pack_half2(lo[6], lo[7]));
   }
 }
 
-__device__ __forceinline__ bool gemv_reads_c(int epi) {
-  return epi == kResidual || epi == kGeluResidual;
-}
-
+template <int EPI>
 __global__ void __launch_bounds__(GT_THREADS, 1)
-    gemv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const float *__restrict__ a,
-                   long long lda, const float *__restrict__ bias, float *__restrict__ c,
-                   long long ldc, int rows, int n, int k, int kr, int stages, int tiles, int epi,
-                   float alpha, int *err) {
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap map_w,
+                   const __grid_constant__ CUtensorMap map_a, const float *__restrict__ bias,
+                   float *__restrict__ c, long long ldc, int rows, int n, int k, int kr,
+                   int stages, int tiles, float alpha, int *err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  const int ks = int(gridDim.y);  // CTAs of a cluster along k (1: persistent over the tiles)
+  constexpr bool kReadsC = EPI == kResidual || EPI == kGeluResidual;
+  const int ks = int(gridDim.y);  // CTAs of a cluster along k (1: the whole k)
   const int k0 = int(blockIdx.y) * kr;
   const int kn = min(kr, k - k0);
   const int nch = (kn + 63) / 64;
-  uint8_t *sx = smem;                            // X: [nch][64 rows][128 B], 128-byte swizzle
-  uint8_t *sw = smem + (kr / 64) * GT_X_CHUNK;   // W ring: [stages][128 features][128 B]
+  uint8_t *sx = smem;                             // X slots: [GT_XS][8 KB]
+  uint8_t *sw = smem + GT_XS * GT_X_CHUNK;        // W ring: [stages][128 features][128 B]
   GtBarriers *bar = reinterpret_cast<GtBarriers *>(sw + stages * GT_W_CHUNK);
   const uint32_t warp = warp_id(), lane = lane_id();
-  // This CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ... (exactly one when k is split).
-  const int my_tiles =
-      ks > 1 ? 1 : (tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
-  const int total = my_tiles * nch;  // W chunks through the ring
+  // This CTA's tiles: blockIdx.x + t·gridDim.x for t < T (one when k is split; at most GT_TMAX).
+  const int T = ks > 1 ? 1 : (tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+  const int total = nch * T;  // W chunks g = ch·T + t
+  const uint32_t tcols = T <= 2 ? 128u : T <= 4 ? 256u : 512u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&bar->full[s], 1);
       mbar_init(&bar->empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&bar->acc_full[b], 1);
-      mbar_init(&bar->acc_empty[b], 4);
+    for (int s = 0; s < GT_XS; ++s) {
+      mbar_init(&bar->x_loaded[s], 1);
+      mbar_init(&bar->x_ready[s], 1);
+      mbar_init(&bar->x_empty[s], 1);
     }
+    mbar_init(&bar->acc_full, 1);
     bar->abort = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(&bar->tmem_base, 128);  // two accumulators of 64 columns
+    tmem_alloc(&bar->tmem_base, tcols);  // one accumulator of 64 columns a tile
     tmem_relinquish();
   }
   tc_fence_before();
@@ -610,101 +652,59 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   griddep_launch_dependents();
   const uint32_t tmem = bar->tmem_base;
   const Abort ab{&bar->abort, err};
-  // W chunk g of this CTA: tile g / nch, k chunk g % nch, into ring slot g % stages.
-  const auto w_load = [&](int g) {
-    const int slot = g % stages;
-    const int tile = int(blockIdx.x) + (g / nch) * int(gridDim.x);
-    mbar_arrive_expect_tx(&bar->full[slot], GT_W_CHUNK);
-    tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], k0 + (g % nch) * 64,
-                tile * GT_N);
-  };
+  const int pre = total < stages ? total : stages;
   if (warp == 4 && lane == 0) {
     prefetch_tmap(&map_w);
-    for (int g = 0; g < stages && g < total; ++g) w_load(g);  // W does not wait for the stream
+    for (int g = 0; g < pre; ++g) {  // W does not wait for the previous kernel of the stream
+      const int slot = g % stages;
+      mbar_arrive_expect_tx(&bar->full[slot], GT_W_CHUNK);
+      tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], k0 + (g / T) * 64,
+                  (int(blockIdx.x) + (g % T) * int(gridDim.x)) * GT_N);
+    }
   }
   griddep_wait();  // the previous kernel of the stream has completed (a and c are ready)
 
-  // X: row r < 32 of the CTA's k-range as hi = f16(a) in X row r and lo = f16(a - hi) in X row
-  // r + 32; zeros past `rows` and past k. Warp w takes rows w, w + 8, w + 16, w + 24 (two at a
-  // time, every load of the pair in flight before the first conversion), lane l the float4s l,
-  // l + 32, ... of a row, so that each load instruction reads consecutive bytes.
-  {
-    const int q4 = nch * 16;  // float4 columns of the chunks (up to 320)
+  if (warp == 4) {
+    if (lane == 0) {  // W producer
 #pragma unroll 1
-    for (int i = 0; i < 4; i += 2) {
-      float4 v[2][10];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = int(warp) + 8 * (i + h);
-        const float *ar = a + (long long)row * lda + k0;
-#pragma unroll
-        for (int j = 0; j < 10; ++j) {
-          const int kk = 4 * (int(lane) + 32 * j);
-          v[h][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          if (row < rows && kk < kn) {
-            v[h][j] = *reinterpret_cast<const float4 *>(ar + kk);
-            if (kk + 4 > kn) {  // k not a multiple of 4: the tail of the last float4 is zero
-              if (kk + 1 >= kn) v[h][j].y = 0.0f;
-              if (kk + 2 >= kn) v[h][j].z = 0.0f;
-              v[h][j].w = 0.0f;
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = int(warp) + 8 * (i + h);
-#pragma unroll
-        for (int j = 0; j < 10; ++j) {
-          const int c4 = int(lane) + 32 * j;
-          if (c4 >= q4) continue;
-          const int kk = 4 * c4;
-          const float x[4] = {v[h][j].x, v[h][j].y, v[h][j].z, v[h][j].w};
-          float lo[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) lo[e] = x[e] - __half2float(__float2half_rn(x[e]));
-          // 16-byte unit (kk % 64) / 8 of the row in the 128-byte swizzle, this float4's half.
-          const int off = (kk >> 6) * int(GT_X_CHUNK) + ((((kk & 63) >> 3) ^ (row & 7)) * 16) +
-                          ((kk >> 2) & 1) * 8;
-          *reinterpret_cast<uint2 *>(sx + off + row * 128) =
-              make_uint2(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]));
-          *reinterpret_cast<uint2 *>(sx + off + (row + 32) * 128) =
-              make_uint2(pack_half2(lo[0], lo[1]), pack_half2(lo[2], lo[3]));
-        }
+      for (int g = pre; g < total; ++g) {
+        const int slot = g % stages;
+        if (!mbar_wait(&bar->empty[slot], ((g / stages) - 1) & 1, ab, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&bar->full[slot], GT_W_CHUNK);
+        tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], k0 + (g / T) * 64,
+                    (int(blockIdx.x) + (g % T) * int(gridDim.x)) * GT_N);
       }
     }
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
-  float *part = reinterpret_cast<float *>(sw);  // split k: this CTA's partial sums [32][128]
-  if (warp == 4) {
-    if (lane == 0) {
+  } else if (warp == 7) {
+    if (lane == 0) {  // X producer: the rows of a, chunk by chunk
+      prefetch_tmap(&map_a);
 #pragma unroll 1
-      for (int g = stages; g < total; ++g) {
-        if (!mbar_wait(&bar->empty[g % stages], ((g / stages) - 1) & 1, ab, kErrTimeoutProducer))
+      for (int ch = 0; ch < nch; ++ch) {
+        const int s = ch % GT_XS;
+        if (ch >= GT_XS &&
+            !mbar_wait(&bar->x_empty[s], ((ch / GT_XS) - 1) & 1, ab, kErrTimeoutProducer))
           break;
-        w_load(g);
+        mbar_arrive_expect_tx(&bar->x_loaded[s], GT_X_CHUNK);
+        tma_load_2d(sx + s * GT_X_CHUNK, &map_a, &bar->x_loaded[s], k0 + ch * 64, 0);
       }
     }
   } else if (warp == 5) {
-    if (lane == 0) {
+    if (lane == 0) {  // UMMA issuer
       const uint64_t dx0 = sdesc_sw128(smem_u32(sx), 16, 1024);
       const uint64_t dw0 = sdesc_sw128(smem_u32(sw), 16, 1024);
       constexpr uint32_t IDESC = idesc_f16(128, 64, 0);
-      int g = 0;
       bool ok = true;
 #pragma unroll 1
-      for (int i = 0; i < my_tiles && ok; ++i) {
-        const int buf = i & 1;
-        if (i >= 2 && !mbar_wait(&bar->acc_empty[buf], ((i >> 1) - 1) & 1, ab, kErrTimeoutMma))
+      for (int ch = 0; ch < nch && ok; ++ch) {
+        const int s = ch % GT_XS;
+        if (!mbar_wait(&bar->x_ready[s], (ch / GT_XS) & 1, ab, kErrTimeoutMma)) {
+          ok = false;
           break;
-        tc_fence_after();
-        const uint32_t d = tmem + uint32_t(buf * 64);
+        }
+        const uint64_t dx = dx0 + uint64_t((s * GT_X_CHUNK) >> 4);
 #pragma unroll 1
-        for (int ch = 0; ch < nch; ++ch, ++g) {
+        for (int t = 0; t < T; ++t) {
+          const int g = ch * T + t;
           const int slot = g % stages;
           if (!mbar_wait(&bar->full[slot], (g / stages) & 1, ab, kErrTimeoutMma)) {
             ok = false;
@@ -712,58 +712,66 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
           }
           tc_fence_after();
           const uint64_t dw = dw0 + uint64_t((slot * GT_W_CHUNK) >> 4);
-          const uint64_t dx = dx0 + uint64_t((ch * GT_X_CHUNK) >> 4);
+          const uint32_t d = tmem + uint32_t(t * 64);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // 16 columns of k = 32 bytes a step
             umma_f16(d, dw + 2 * kk, dx + 2 * kk, IDESC, (ch > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&bar->empty[slot]);
         }
-        if (ok) umma_commit(&bar->acc_full[buf]);
+        umma_commit(&bar->x_empty[s]);
       }
+      if (ok) umma_commit(&bar->acc_full);
     }
   } else if (warp < 4) {
-    // Epilogue: lane l of warp w is feature 32w + l of the tile; TMEM columns 0-31 hold its hi·W
-    // of rows 0-31, columns 32-63 its lo·W.
+    // Converters: warp s takes the chunks of X slot s.
 #pragma unroll 1
-    for (int i = 0; i < my_tiles; ++i) {
-      const int buf = i & 1;
-      const int tile = int(blockIdx.x) + i * int(gridDim.x);
-      if (!mbar_wait_warp(&bar->acc_full[buf], (i >> 1) & 1, ab, kErrTimeoutConsumer)) break;
-      tc_fence_after();
-      uint32_t hi[32], lo[32];
-      const uint32_t taddr = tmem + ((warp * 32u) << 16) + uint32_t(buf * 64);
-      tmem_ld32(taddr, hi);
-      tmem_ld32(taddr + 32, lo);
-      tmem_wait_ld();
-      tc_fence_before();
+    for (int ch = int(warp); ch < nch; ch += GT_XS) {
+      const int s = ch % GT_XS;
+      if (!mbar_wait_warp(&bar->x_loaded[s], (ch / GT_XS) & 1, ab, kErrTimeoutConsumer)) break;
+      gt_convert_chunk(sx + s * GT_X_CHUNK, lane);
+      fence_proxy_async_smem();  // the UMMAs read the chunk through the async proxy
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->acc_empty[buf]);
-      const int fl = int(warp) * 32 + int(lane);
-      if (ks == 1) {
-        const int f = tile * GT_N + fl;
-        if (f < n) {
-          const float b = bias[f];
-          const bool rd = gemv_reads_c(epi);
+      if (lane == 0) mbar_arrive(&bar->x_ready[s]);
+    }
+  }
+  float *part = reinterpret_cast<float *>(sx);  // split k: this CTA's partials [32][128] (X is free)
+  if (warp < 4) {
+    // Epilogue: lane l of warp w is feature 32w + l of each tile; TMEM columns 64t .. 64t + 31
+    // hold its hi·W of rows 0-31 for tile t, the next 32 its lo·W.
+    const int fl = int(warp) * 32 + int(lane);
+    if (mbar_wait_warp(&bar->acc_full, 0, ab, kErrTimeoutConsumer)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int t = 0; t < T; ++t) {
+        uint32_t hi[32], lo[32];
+        const uint32_t taddr = tmem + ((warp * 32u) << 16) + uint32_t(t * 64);
+        tmem_ld32(taddr, hi);
+        tmem_ld32(taddr + 32, lo);
+        tmem_wait_ld();
+        if (ks == 1) {
+          const int f = (int(blockIdx.x) + t * int(gridDim.x)) * GT_N + fl;
+          if (f < n) {
+            const float b = bias[f];
 #pragma unroll
-          for (int r = 0; r < 32; ++r) {
-            if (r < rows) {
-              float *cp = c + (long long)r * ldc + f;
-              const float v = (__uint_as_float(hi[r]) + __uint_as_float(lo[r])) + b;
-              *cp = gemv_epilogue(epi, v, rd ? *cp : 0.0f, alpha);
+            for (int r = 0; r < 32; ++r) {
+              if (r < rows) {
+                float *cp = c + (long long)r * ldc + f;
+                const float v = (__uint_as_float(hi[r]) + __uint_as_float(lo[r])) + b;
+                *cp = gemv_epilogue<EPI>(v, kReadsC ? *cp : 0.0f, alpha);
+              }
             }
           }
-        }
-      } else {
+        } else {
 #pragma unroll
-        for (int r = 0; r < 32; ++r)
-          part[r * GT_N + fl] = __uint_as_float(hi[r]) + __uint_as_float(lo[r]);
+          for (int r = 0; r < 32; ++r)
+            part[r * GT_N + fl] = __uint_as_float(hi[r]) + __uint_as_float(lo[r]);
+        }
       }
     }
   }
   if (ks > 1) {
-    // Every CTA of the cluster has its partial sums in shared memory; CTA q finishes rows q,
-    // q + ks, ... (threads 0-127 and 128-255 take alternate rows of that set), adding the CTAs'
-    // sums in rank order.
+    // Every CTA of the cluster has its partials in shared memory; CTA q finishes rows q, q + ks, ...
+    // (threads 0-127 and 128-255 take alternate ones), adding the CTAs' partials in rank order.
     __syncwarp();
     cluster_sync();
     const uint32_t rank = cluster_ctarank();
@@ -771,20 +779,18 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
     const int f = int(blockIdx.x) * GT_N + fl;
     if (f < n) {
       const float b = bias[f];
-      const bool rd = gemv_reads_c(epi);
-      uint32_t peer[GT_MAX_CLUSTER];
-#pragma unroll
-      for (int p = 0; p < GT_MAX_CLUSTER; ++p)
-        peer[p] = p < ks ? mapa_shared(part + fl, uint32_t(p)) : 0u;
 #pragma unroll 1
       for (int r = int(rank) + ks * int(threadIdx.x >> 7); r < rows; r += 2 * ks) {
-        float v = 0.0f;
+        float p8[GT_MAX_CLUSTER];
 #pragma unroll
         for (int p = 0; p < GT_MAX_CLUSTER; ++p)
-          if (p < ks) v += ld_cluster_f32(peer[p] + uint32_t(r * GT_N * 4));
+          p8[p] = p < ks ? ld_cluster_f32(mapa_shared(part + r * GT_N + fl, uint32_t(p))) : 0.0f;
+        float v = 0.0f;
+#pragma unroll
+        for (int p = 0; p < GT_MAX_CLUSTER; ++p) v += p8[p];
         v += b;
         float *cp = c + (long long)r * ldc + f;
-        *cp = gemv_epilogue(epi, v, rd ? *cp : 0.0f, alpha);
+        *cp = gemv_epilogue<EPI>(v, kReadsC ? *cp : 0.0f, alpha);
       }
     }
     __syncwarp();
@@ -793,7 +799,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 128);
+  if (warp == 0) tmem_dealloc(tmem, tcols);
 }
 
 }  // namespace
@@ -906,38 +912,22 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map_w128,
-                           const float *bias, float *c, long long ldc, int rows, int n, int k,
-                           int epilogue, float alpha, int sms, int *err, cudaStream_t s) {
-  if (rows <= 0 || n <= 0) return cudaSuccess;
-  if (rows > 32 || k <= 0 || sms <= 0) return cudaErrorInvalidValue;
-  // About one CTA per SM: tiles x k-splits, the splits of a tile one cluster (at most 8 CTAs); with
-  // a tile per SM or more, one persistent CTA per SM over the tiles with the whole k.
-  const int tiles = (n + GT_N - 1) / GT_N;
-  int ks = tiles < sms ? sms / tiles : 1;
-  if (ks > GT_MAX_CLUSTER) ks = GT_MAX_CLUSTER;
-  if (ks < 1) ks = 1;
-  int kr = ((k + ks - 1) / ks + 63) / 64 * 64;
-  if (kr > GT_KMAX) kr = GT_KMAX;
-  ks = (k + kr - 1) / kr;
-  if (ks > GT_MAX_CLUSTER) return cudaErrorNotSupported;  // k above 8 x 1280
-  kr = ((k + ks - 1) / ks + 63) / 64 * 64;                // the same splits, evenly
-  const int nch = kr / 64;
-  int stages = int((GT_SMEM_MAX - gt_smem_bytes(nch, 0)) / GT_W_CHUNK);
-  if (stages > GT_MAX_STAGES) stages = GT_MAX_STAGES;
-  if (stages < 2) return cudaErrorNotSupported;
-  const size_t smem = gt_smem_bytes(nch, stages);
+template <int EPI>
+cudaError_t launch_gemv_tc_epi(dim3 grid, int ks, size_t smem, cudaStream_t s,
+                               const CUtensorMap &map_w, const CUtensorMap &map_a,
+                               const float *bias, float *c, long long ldc, int rows, int n, int k,
+                               int kr, int stages, int tiles, float alpha, int *err) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GT_SMEM_MAX);
+    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM_MAX);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = ks > 1 ? dim3(tiles, ks) : dim3(tiles < sms ? tiles : sms, 1);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(GT_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -950,8 +940,46 @@ cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = ks > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel, map_w128, a, lda, bias, c, ldc, rows, n, k, kr,
-                            stages, tiles, epilogue, alpha, err);
+  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<EPI>, map_w, map_a, bias, c, ldc, rows, n, k, kr,
+                            stages, tiles, alpha, err);
+}
+
+cudaError_t launch_gemv_tc(const CUtensorMap &map_a, const CUtensorMap &map_w128,
+                           const float *bias, float *c, long long ldc, int rows, int n, int k,
+                           int epilogue, float alpha, int sms, int *err, cudaStream_t s) {
+  if (rows <= 0 || n <= 0) return cudaSuccess;
+  if (rows > 32 || k <= 0 || sms <= 0) return cudaErrorInvalidValue;
+  // About one CTA per SM. With fewer tiles than SMs, k splits over a cluster of up to 8 CTAs a tile;
+  // otherwise each CTA takes every gridDim.x-th tile (at most GT_TMAX) with the whole k.
+  const int tiles = (n + GT_N - 1) / GT_N;
+  int ks = tiles < sms ? sms / tiles : 1;
+  if (ks > GT_MAX_CLUSTER) ks = GT_MAX_CLUSTER;
+  if (ks > (k + 63) / 64) ks = (k + 63) / 64;
+  if (ks < 1) ks = 1;
+  int kr = ((k + ks - 1) / ks + 63) / 64 * 64;
+  ks = (k + kr - 1) / kr;
+  int grid = ks > 1 ? tiles : (tiles < sms ? tiles : sms);
+  if (ks == 1 && grid < (tiles + GT_TMAX - 1) / GT_TMAX) grid = (tiles + GT_TMAX - 1) / GT_TMAX;
+  int stages = int((GT_SMEM_MAX - gt_smem_bytes(0)) / GT_W_CHUNK);
+  if (stages > GT_MAX_STAGES) stages = GT_MAX_STAGES;
+  const size_t smem = gt_smem_bytes(stages);
+  const dim3 g(grid, ks);
+  switch (epilogue) {
+#define WV_GEMV_TC(E) \
+  case E:             \
+    return launch_gemv_tc_epi<E>(g, ks, smem, s, map_w128, map_a, bias, c, ldc, rows, n, k, kr, \
+                                 stages, tiles, alpha, err);
+    WV_GEMV_TC(kBias)
+    WV_GEMV_TC(kSilu)
+    WV_GEMV_TC(kRelu)
+    WV_GEMV_TC(kResidual)
+    WV_GEMV_TC(kGelu)
+    WV_GEMV_TC(kGeluResidual)
+    WV_GEMV_TC(kTanh)
+#undef WV_GEMV_TC
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace wv

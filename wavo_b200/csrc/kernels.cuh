@@ -174,10 +174,9 @@ cudaError_t launch_rope(const float *table, void *qkv, int x_f16, long long stri
                         int sections, cudaStream_t s);
 // Rows (<= 32) of f32 a through W of type wtype (0 f32 [n][k], 1 f16 [n][k], 8 int8 [n][k] with
 // f32 scales [n][k/32]) in f32: the reference's gemv (W not rounded to f16).
-// F16 weights, any epilogue, rows <= 32, lda % 4 == 0 and a 16-byte aligned: the tensor-core
-// gemv (split f16 rows of a, f32 accuracy) over W's 128-row 2D tensor map. Returns
-// cudaErrorNotSupported, launching nothing, for k above 8 x 1280.
-cudaError_t launch_gemv_tc(const float *a, long long lda, const CUtensorMap &map_w128,
+// F16 weights, any epilogue, rows <= 32: the tensor-core gemv (split f16 rows of a, f32 accuracy)
+// over W's 128-row 2D tensor map and a's map of f32 {64, 32} boxes (make_map_rows32).
+cudaError_t launch_gemv_tc(const CUtensorMap &map_a, const CUtensorMap &map_w128,
                            const float *bias, float *c, long long ldc, int rows, int n, int k,
                            int epilogue, float alpha, int sms, int *err, cudaStream_t s);
 cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,

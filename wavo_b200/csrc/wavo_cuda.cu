@@ -116,6 +116,22 @@ EncodeTiled encoder() {
 
 // A 3D f16 view {64, rows, cols / 64} of rows x cols (row stride ld elements; cols a multiple of
 // 64; chunk c = columns 64c..): boxes {64, box_rows, 2}, two 64-column chunks per TMA load.
+// f32 rows x cols (row stride ld elements) in boxes of 64 columns x 32 rows, no swizzle, zero fill
+// outside: the gemv's rows of a, one box per 64-column chunk.
+bool make_map_rows32(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld) {
+  EncodeTiled enc = encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 4) & 15u) || cols == 0 ||
+      rows == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {64, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map3(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
                uint32_t box_rows);
 
@@ -653,15 +669,13 @@ wavo_status wavo_gemv_rows(wavo_ctx *ctx, const float *a, uint32_t lda, const wa
                                             : static_cast<const void *>(l->w16);
   const int wt = f32w ? 0 : l->ty == WAVO_GGML_Q8_0 ? 8 : 1;
   // Pass::gemv writes l.cols outputs (src/gpu/mod.rs:1461-1467).
-  if (wt == 1) {
+  CUtensorMap map_a;
+  if (wt == 1 && make_map_rows32(&map_a, a, l->k, rows, lda)) {
     // F16 weights are exact in f16: the tensor-core form (split f16 rows, f32 accuracy).
-    const cudaError_t e =
-        wv::launch_gemv_tc(a, lda, l->map_w128, l->bias, c, ldc, int(rows), int(l->cols),
-                           int(l->k), epilogue, alpha, ctx->sms, ctx->dev_err, ctx->stream);
-    if (e != cudaErrorNotSupported) {
-      CK(e, "gemv launch");
-      return WAVO_OK;
-    }
+    CK(wv::launch_gemv_tc(map_a, l->map_w128, l->bias, c, ldc, int(rows), int(l->cols),
+                          int(l->k), epilogue, alpha, ctx->sms, ctx->dev_err, ctx->stream),
+       "gemv launch");
+    return WAVO_OK;
   }
   CK(wv::launch_gemv(a, lda, wt, w, l->d8, l->bias, c, ldc, int(rows), int(l->cols), int(l->k),
                      epilogue, alpha, ctx->stream),
