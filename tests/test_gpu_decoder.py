@@ -81,16 +81,19 @@ def test_pick_scripted_decode(gpu):
     assert -1.0 < np.mean(lps[:4]) < 0.0
 
 
-def test_pick_matches_oracle(gpu):
+@pytest.mark.parametrize("vocab,eot,no_ts,begin,rows,hmax", [
+    (3000, 2500, 2503, 2504, 24, 7),         # one CTA a row
+    (51866, 50257, 50364, 50365, 32, 200),   # Whisper large-v3's ids: seven CTAs a row
+])
+def test_pick_matches_oracle(gpu, vocab, eot, no_ts, begin, rows, hmax):
     # Random logits at a Whisper-like split (text, EOT, <|notimestamps|>, timestamps) and random
     # histories: the same token, log-probability and edited logits as the oracle's pick.
     rng = np.random.default_rng(3)
-    vocab, eot, no_ts, begin = 3000, 2500, 2503, 2504
-    rows = 24
     hists = []
     for r in range(rows):
-        n = int(rng.integers(0, 7))
-        h = [int(rng.integers(begin, vocab)) if rng.random() < 0.5 else int(rng.integers(0, eot))
+        n = int(rng.integers(0, hmax))
+        p_ts = 0.0 if r % 4 == 1 else 0.5  # some histories without a timestamp
+        h = [int(rng.integers(begin, vocab)) if rng.random() < p_ts else int(rng.integers(0, eot))
              for _ in range(n)]
         hists.append(h)
     logits = (rng.standard_normal((rows, vocab)) * 3).astype(np.float32)
