@@ -19,6 +19,8 @@ namespace {
 __global__ void pack_cache_kernel(const float *__restrict__ x, long long src, long long stride,
                                   uint32_t *__restrict__ cache, int rows, int d, int cols, int col,
                                   long long x_batch, long long cache_batch) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   const long long total = (long long)rows * d;  // d pairs per row (K: d/2, V: d/2)
   const int half = d / 2;
   const float *xb = x + blockIdx.y * x_batch;
@@ -66,6 +68,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 5)
     attend_kernel(const float *__restrict__ q, long long q_stride, const uint32_t *__restrict__ kv,
                   long long kv_stride, float *__restrict__ part, float *__restrict__ o,
                   long long o_stride, int n, int cols, int hd, float scale) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   __shared__ float qs[128];
   __shared__ float ps[ATT_KEYS];
   __shared__ float red[ATT_THREADS / 32];
@@ -240,6 +244,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 5)
 // (decode.wgsl:124-147).
 __global__ void combine_kernel(const float *__restrict__ part, float *__restrict__ o,
                                long long o_stride, int splits, int hd) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   const int h = blockIdx.x, b = blockIdx.y, heads = gridDim.x;
   const float *base = part + ((long long)b * heads + h) * splits * (hd + 2);
   float m = -INFINITY;
@@ -811,9 +817,8 @@ cudaError_t launch_pack_cache(const float *x, long long src, long long stride, u
   if (total <= 0 || batch <= 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 4096) blocks = 4096;
-  pack_cache_kernel<<<dim3(int(blocks), batch), 256, 0, s>>>(x, src, stride, cache, rows, d, cols,
-                                                             col, x_batch, cache_batch);
-  return cudaGetLastError();
+  return launch_pdl(pack_cache_kernel, dim3(int(blocks), batch), dim3(256), 0, s, x, src, stride,
+                    cache, rows, d, cols, col, x_batch, cache_batch);
 }
 
 size_t attend_part_floats(int n, int heads, int hd, int batch) {
@@ -828,6 +833,9 @@ cudaError_t launch_attend(const float *q, long long q_stride, const uint32_t *kv
   const int splits = (n + ATT_KEYS - 1) / ATT_KEYS;
   dim3 grid(splits, heads, batch);
   const float scale = 1.0f / sqrtf(float(hd));
+  // Plain launches: started early beside the projection before it (a programmatic launch), the
+  // many waves of this HBM-bound kernel ran measurably slower (the decoder's cross attention 61 ->
+  // 77 us). Both still let the next kernel of the stream launch early.
   attend_kernel<<<grid, ATT_THREADS, 0, s>>>(q, q_stride, kv, kv_stride, part, o, o_stride, n, cols,
                                              hd, scale);
   cudaError_t e = cudaGetLastError();

@@ -24,6 +24,8 @@ __global__ void embed_kernel(const void *__restrict__ w, int wtype, const float 
                              const float *__restrict__ bias, const float *__restrict__ positions,
                              const int *__restrict__ tokens, int k, int pos, float *__restrict__ x,
                              long long ldx) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   const int b = int(blockIdx.y);
   const long long t = tokens[b];
   for (int c = int(blockIdx.x * blockDim.x + threadIdx.x); c < k; c += int(gridDim.x * blockDim.x)) {
@@ -256,6 +258,8 @@ __global__ void __launch_bounds__(PK_THREADS)
                         const int *__restrict__ begin_suppress, int n_begin, int eot, int no_ts,
                         int begin, int max_initial, int *__restrict__ tokens,
                         float *__restrict__ logprobs, int slice) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   __shared__ uint32_t bits[PK_SLICE / 32];  // the suppression lists' ids in this slice
   __shared__ PickPart part;
   __shared__ float wf[PK_THREADS / 32][6];
@@ -475,8 +479,8 @@ cudaError_t launch_embed(const void *w, int wtype, const float *d8, const float 
                          float *x, long long ldx, cudaStream_t s) {
   if (rows <= 0 || k <= 0) return cudaSuccess;
   const dim3 grid((k + 255) / 256, rows);
-  embed_kernel<<<grid, 256, 0, s>>>(w, wtype, d8, bias, positions, tokens, k, pos, x, ldx);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, grid, dim3(256), 0, s, w, wtype, d8, bias, positions, tokens, k,
+                    pos, x, ldx);
 }
 
 cudaError_t launch_pick(float *logits, long long ld, int rows, int vocab, int *history,
@@ -491,13 +495,15 @@ cudaError_t launch_pick(float *logits, long long ld, int rows, int vocab, int *h
     cfg.gridDim = dim3(nct, rows);
     cfg.blockDim = dim3(PK_THREADS);
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = unsigned(nct);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, pick_cluster_kernel, logits, ld, vocab, history, hist_len,
                               max_hist, suppress, n_suppress, begin_suppress, n_begin, eot, no_ts,
                               begin, max_initial, tokens, logprobs, slice);

@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(32 * LN_WARPS)
                       const float *__restrict__ b, OutT *__restrict__ y, int rows, int cols,
                       int mode, const float *__restrict__ table, const int *__restrict__ positions,
                       OutT *__restrict__ yr, int hd) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   extern __shared__ float ln_rows[];  // rotary: one normalised row per warp
   const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31u);
   const int r = int(blockIdx.x) * LN_WARPS + warp;
@@ -159,6 +161,8 @@ __global__ void __launch_bounds__(DW_CH)
                   const float *__restrict__ bias, void *__restrict__ zout, int ch, int kernel,
                   const int *__restrict__ seg_start, const int *__restrict__ seg_len, int single_t,
                   const float *__restrict__ n_w, const float *__restrict__ n_b, int y_f16) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   extern __shared__ float dw_win[];  // [DW_FRAMES + kernel - 1][DW_CH]
   const int seg = int(blockIdx.z);
   const int T = seg_len ? seg_len[seg] : single_t;
@@ -240,17 +244,16 @@ cudaError_t launch_layer_norm(const float *x, const float *w, const float *b, vo
                        reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(y) |
                        reinterpret_cast<uintptr_t>(yr);
   const bool vec = cols % 128 == 0 && (al & 15u) == 0;
-#define LN_LAUNCH(T, V)                                                                       \
-  layer_norm_kernel<T, V><<<grid, 32 * LN_WARPS, smem, s>>>(x, w, b, static_cast<T *>(y), rows, \
-                                                            cols, mode, table, positions,     \
-                                                            static_cast<T *>(yr), hd)
-  if (y_f16) {
-    if (vec) LN_LAUNCH(__half, true); else LN_LAUNCH(__half, false);
-  } else {
-    if (vec) LN_LAUNCH(float, true); else LN_LAUNCH(float, false);
-  }
+#define LN_LAUNCH(T, V)                                                                        \
+  launch_pdl(layer_norm_kernel<T, V>, grid, dim3(32 * LN_WARPS), smem, s, x, w, b,               \
+             static_cast<T *>(y), rows, cols, mode, table, positions, static_cast<T *>(yr), hd)
+  cudaError_t e;
+  if (y_f16)
+    e = vec ? LN_LAUNCH(__half, true) : LN_LAUNCH(__half, false);
+  else
+    e = vec ? LN_LAUNCH(float, true) : LN_LAUNCH(float, false);
 #undef LN_LAUNCH
-  return cudaGetLastError();
+  return e;
 }
 
 int layer_norm_max_cols() { return 32 * LN_MAXV; }
@@ -277,9 +280,8 @@ cudaError_t launch_dwconv(const float *h, const float *taps, const float *bias, 
   const dim3 grid((max_len + DW_FRAMES - 1) / DW_FRAMES, (ch + DW_CH - 1) / DW_CH, nseg);
   auto f = kernel == 5 ? dwconv_kernel<5> : kernel == 9 ? dwconv_kernel<9>
          : kernel == 15 ? dwconv_kernel<15> : kernel == 31 ? dwconv_kernel<31> : dwconv_kernel<0>;
-  f<<<grid, DW_CH, smem, s>>>(h, taps, bias, z, ch, kernel, seg_start, seg_len,
-                              seg_len ? 0 : max_len, n_w, n_b, y_f16);
-  return cudaGetLastError();
+  return launch_pdl(f, grid, dim3(DW_CH), smem, s, h, taps, bias, z, ch, kernel, seg_start,
+                    seg_len, seg_len ? 0 : max_len, n_w, n_b, y_f16);
 }
 
 }  // namespace wv

@@ -931,6 +931,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 // f32 rows to f16 rows, zero padded to ld_out columns.
 __global__ void cast_rows_kernel(const float *__restrict__ in, long long ld_in,
                                  __half *__restrict__ out, long long ld_out, int rows, int cols) {
+  griddep_launch_dependents();
+  griddep_wait();  // the previous kernel of the stream has completed (programmatic launch)
   for (long long row = blockIdx.y; row < rows; row += gridDim.y) {
     const float *src = in + row * ld_in;
     __half *dst = out + row * ld_out;
@@ -1134,8 +1136,8 @@ cudaError_t launch_cast_rows(const float *in, long long ld_in, __half *out, long
   int bx = int((pairs + threads - 1) / threads);
   if (bx > 64) bx = 64;
   dim3 grid(bx, rows < 65535 ? rows : 65535);
-  cast_rows_kernel<<<grid, threads, 0, s>>>(in, ld_in, out, ld_out, rows, cols);
-  return cudaGetLastError();
+  return launch_pdl(cast_rows_kernel, grid, dim3(threads), 0, s, in, ld_in, out, ld_out, rows,
+                    cols);
 }
 
 }  // namespace wv
