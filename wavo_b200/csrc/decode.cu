@@ -633,6 +633,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   const int T = ks > 1 ? 1 : (tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
   const int total = nch * T;  // W chunks g = ch·T + t
   const uint32_t tcols = T <= 2 ? 128u : T <= 4 ? 256u : 512u;
+  // The CTA's chunks in a rotated order (chunk ch is k column k0 + 64·((ch + rot) mod nch)), so that
+  // the CTAs do not all ask L2 for the same rows of a at once.
+  const int rot = int(blockIdx.x) % nch;
+  const auto kchunk = [&](int ch) { return k0 + ((ch + rot) % nch) * 64; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -664,7 +668,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
     for (int g = 0; g < pre; ++g) {  // W does not wait for the previous kernel of the stream
       const int slot = g % stages;
       mbar_arrive_expect_tx(&bar->full[slot], GT_W_CHUNK);
-      tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], k0 + (g / T) * 64,
+      tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], kchunk(g / T),
                   (int(blockIdx.x) + (g % T) * int(gridDim.x)) * GT_N);
     }
   }
@@ -677,7 +681,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
         const int slot = g % stages;
         if (!mbar_wait(&bar->empty[slot], ((g / stages) - 1) & 1, ab, kErrTimeoutProducer)) break;
         mbar_arrive_expect_tx(&bar->full[slot], GT_W_CHUNK);
-        tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], k0 + (g / T) * 64,
+        tma_load_2d(sw + slot * GT_W_CHUNK, &map_w, &bar->full[slot], kchunk(g / T),
                     (int(blockIdx.x) + (g % T) * int(gridDim.x)) * GT_N);
       }
     }
@@ -691,7 +695,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
             !mbar_wait(&bar->x_empty[s], ((ch / GT_XS) - 1) & 1, ab, kErrTimeoutProducer))
           break;
         mbar_arrive_expect_tx(&bar->x_loaded[s], GT_X_CHUNK);
-        tma_load_2d(sx + s * GT_X_CHUNK, &map_a, &bar->x_loaded[s], k0 + ch * 64, 0);
+        tma_load_2d(sx + s * GT_X_CHUNK, &map_a, &bar->x_loaded[s], kchunk(ch), 0);
       }
     }
   } else if (warp == 5) {
@@ -745,6 +749,14 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
     // Epilogue: lane l of warp w is feature 32w + l of each tile; TMEM columns 64t .. 64t + 31
     // hold its hi·W of rows 0-31 for tile t, the next 32 its lo·W.
     const int fl = int(warp) * 32 + int(lane);
+    // The bias of every tile, loaded while the UMMAs run (a load per tile after them would expose
+    // its latency each time).
+    float bt[GT_TMAX];
+#pragma unroll
+    for (int t = 0; t < GT_TMAX; ++t) {
+      const int f = (int(blockIdx.x) + t * int(gridDim.x)) * GT_N + fl;
+      bt[t] = ks == 1 && t < T && f < n ? bias[f] : 0.0f;
+    }
     if (mbar_wait_warp(&bar->acc_full, 0, ab, kErrTimeoutConsumer)) {
       tc_fence_after();
 #pragma unroll 1
@@ -757,7 +769,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
         if (ks == 1) {
           const int f = (int(blockIdx.x) + t * int(gridDim.x)) * GT_N + fl;
           if (f < n) {
-            const float b = bias[f];
+            float b = bt[0];
+#pragma unroll
+            for (int q = 1; q < GT_TMAX; ++q)
+              if (q == t) b = bt[q];
 #pragma unroll
             for (int r = 0; r < 32; ++r) {
               if (r < rows) {
