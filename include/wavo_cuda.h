@@ -64,6 +64,7 @@ typedef enum wavo_epilogue {
 
 typedef struct wavo_ctx wavo_ctx;
 typedef struct wavo_linear wavo_linear;
+typedef struct wavo_gguf wavo_gguf;
 typedef struct wavo_graph wavo_graph;
 
 /* ---- device and context: replaces Gpu::new (src/gpu/mod.rs:461-578) -------------------- */
@@ -119,6 +120,52 @@ void wavo_linear_destroy(wavo_linear *l);
 /* Linear::width (src/gpu/mod.rs:408-413): output columns including the dual ones. */
 uint32_t wavo_linear_width(const wavo_linear *l);
 uint32_t wavo_linear_k(const wavo_linear *l);
+
+/* ---- GGUF files: replaces gguf::Gguf / gguf::Tensor (src/gguf.rs) ----------------------------
+ * Host calls without a context: errors read from wavo_last_error(NULL). A wavo_gguf may be read
+ * from many threads at once. */
+
+/* Gguf::open (src/gguf.rs:122-128): reads and checks the header (GGUF v3; tensors F32, F16 or Q8_0,
+ * inside the file); tensor data is read when used. */
+wavo_status wavo_gguf_open(const char *path, wavo_gguf **out);
+void wavo_gguf_close(wavo_gguf *g);
+/* The tensors in file order. */
+uint32_t wavo_gguf_tensor_count(const wavo_gguf *g);
+const char *wavo_gguf_tensor_name(const wavo_gguf *g, uint32_t i);
+/* Gguf::tensor (src/gguf.rs:241-249): the tensor `name`, which must have exactly the ggml-order
+ * dims (dims[0] contiguous; NULL skips the check); its GGUF type and data bytes. */
+wavo_status wavo_gguf_tensor(const wavo_gguf *g, const char *name, const uint64_t *dims,
+                             uint32_t n_dims, int *ggml_type, uint64_t *bytes);
+/* The tensor's dims (up to cap of them written); returns how many it has, 0 if there is none. */
+uint32_t wavo_gguf_tensor_dims(const wavo_gguf *g, const char *name, uint64_t *dims, uint32_t cap);
+/* Tensor::read (src/gguf.rs:258-272): `bytes` of the tensor's data from byte `offset` (host). */
+wavo_status wavo_gguf_read(const wavo_gguf *g, const char *name, uint64_t offset, void *dst,
+                           uint64_t bytes);
+/* Metadata (src/gguf.rs:190-240 `get` / `optional` / `array`): has (1/0); an integer of any GGUF
+ * integer type; an f32/f64; a bool; a UTF-8 string (a pointer into the header, not
+ * NUL-terminated, valid until close); an array's item type and length; and all items of an array
+ * as integers, floats or strings (a NULL output for a kind the array does not hold). */
+int wavo_gguf_has(const wavo_gguf *g, const char *key);
+wavo_status wavo_gguf_get_int(const wavo_gguf *g, const char *key, int64_t *v);
+wavo_status wavo_gguf_get_float(const wavo_gguf *g, const char *key, double *v);
+wavo_status wavo_gguf_get_bool(const wavo_gguf *g, const char *key, int *v);
+wavo_status wavo_gguf_get_str(const wavo_gguf *g, const char *key, const char **s, uint64_t *len);
+wavo_status wavo_gguf_array(const wavo_gguf *g, const char *key, uint32_t *item_type,
+                            uint64_t *len);
+wavo_status wavo_gguf_array_items(const wavo_gguf *g, const char *key, int64_t *ints,
+                                  double *floats, const char **strs, uint64_t *lens,
+                                  uint64_t cap);
+
+/* Gpu::linear over GGUF tensors (src/gpu/mod.rs:758-827 `upload_linear`): the tensors `names`
+ * (same type and k = elements / last dim, k % 32 == 0) stacked by rows, with a bias as in
+ * wavo_linear_create. The tensors' bytes are streamed from the file to the device in pinned
+ * pieces and turned into the device forms there (Q8_0 blocks into the int8 values, scales and f16
+ * copy that the GEMM, its Q8_0 prologue and the gemv read through TMA): the same layer as
+ * wavo_linear_create on the same bytes. Waits for the upload; serialised with the context's
+ * other calls. */
+wavo_status wavo_linear_from_gguf(wavo_ctx *ctx, const wavo_gguf *g, const char *const *names,
+                                  uint32_t count, const float *bias, size_t bias_len,
+                                  wavo_linear **out);
 
 /* ---- projections: replaces Pass::gemm (src/gpu/mod.rs:1394-1425) and Pass::gemv (1461-1467) */
 

@@ -44,6 +44,22 @@ SIGNATURES = {
     "wavo_sync": ([_vp, _u32], _st),
     "wavo_linear_create": ([_vp, _i32, _u32, _u32, _vp, _vp, _sz, ctypes.POINTER(_vp)], _st),
     "wavo_linear_destroy": ([_vp], None),
+    "wavo_linear_from_gguf": ([_vp, _vp, _vp, _u32, _vp, _sz, ctypes.POINTER(_vp)], _st),
+    "wavo_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], _st),
+    "wavo_gguf_close": ([_vp], None),
+    "wavo_gguf_tensor_count": ([_vp], _u32),
+    "wavo_gguf_tensor_name": ([_vp, _u32], ctypes.c_char_p),
+    "wavo_gguf_tensor": ([_vp, ctypes.c_char_p, _vp, _u32, ctypes.POINTER(_i32),
+                          ctypes.POINTER(_u64)], _st),
+    "wavo_gguf_tensor_dims": ([_vp, ctypes.c_char_p, _vp, _u32], _u32),
+    "wavo_gguf_read": ([_vp, ctypes.c_char_p, _u64, _vp, _u64], _st),
+    "wavo_gguf_has": ([_vp, ctypes.c_char_p], _i32),
+    "wavo_gguf_get_int": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)], _st),
+    "wavo_gguf_get_float": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)], _st),
+    "wavo_gguf_get_bool": ([_vp, ctypes.c_char_p, ctypes.POINTER(_i32)], _st),
+    "wavo_gguf_get_str": ([_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_u64)], _st),
+    "wavo_gguf_array": ([_vp, ctypes.c_char_p, ctypes.POINTER(_u32), ctypes.POINTER(_u64)], _st),
+    "wavo_gguf_array_items": ([_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp, _u64], _st),
     "wavo_linear_width": ([_vp], _u32),
     "wavo_linear_k": ([_vp], _u32),
     "wavo_gemm": ([_vp, _vp, _i32, _u32, _vp, _vp, _i32, _u32, _u32, _i32, _f32], _st),

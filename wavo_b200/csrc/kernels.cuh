@@ -183,6 +183,15 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
                         const float *scales, const float *bias, float *c, long long ldc, int rows,
                         int n, int k, int epilogue, float alpha, cudaStream_t s);
 
+// ---- GGUF loads (gguf.cu) ----------------------------------------------------------------------
+
+// Raw Q8_0 blocks of rows x k weights into q8 [n][k] int8, d8 [n][k/32] f32, s16t [k/32][n] f16 and
+// w16 [n][k] f16 (q·d rounded); rows past `rows` are left as they are (the caller zeroes them).
+cudaError_t launch_build_q8(const uint8_t *raw, int rows, int k, int n, int8_t *q8, float *d8,
+                            __half *s16t, __half *w16, cudaStream_t s);
+// w16[i] = f16(w32[i]) for i < count (count a multiple of 4).
+cudaError_t launch_build_f16(const float *w32, long long count, __half *w16, cudaStream_t s);
+
 // ---- self-checks (selftest.cu) -------------------------------------------------------------
 
 // One warp waits on an mbarrier nothing arms, giving up after `limit` cycles (raises *err).

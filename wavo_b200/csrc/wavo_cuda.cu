@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "../../include/wavo_cuda.h"
+#include "gguf.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
 
@@ -31,6 +32,9 @@ struct wavo_ctx {
   size_t ws_bytes = 0;
   bool capturing = false;
   int q8_mode = WAVO_Q8_AUTO;  // wavo_set_q8_gemm
+  // wavo_linear_from_gguf: two pinned pieces of the file in flight to the device.
+  void *stage[2] = {nullptr, nullptr};
+  cudaEvent_t stage_ev[2] = {nullptr, nullptr};
   std::mutex mu;
   std::string err;
 };
@@ -82,6 +86,22 @@ wavo_status fail(wavo_ctx *c, wavo_status s, const char *fmt, ...) {
     t_last_err = buf;
   return s;
 }
+
+}  // namespace
+
+namespace wv {
+int fail_free(int status, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_err = buf;
+  return status;
+}
+}  // namespace wv
+
+namespace {
 
 wavo_status cuda_fail(wavo_ctx *c, cudaError_t e, const char *what) {
   return fail(c, e == cudaErrorMemoryAllocation ? WAVO_ENOMEM : WAVO_ECUDA, "%s: %s", what,
@@ -327,6 +347,10 @@ void wavo_destroy(wavo_ctx *ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
+  for (int i = 0; i < 2; ++i) {
+    if (ctx->stage[i]) cudaFreeHost(ctx->stage[i]);
+    if (ctx->stage_ev[i]) cudaEventDestroy(ctx->stage_ev[i]);
+  }
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
@@ -424,6 +448,29 @@ wavo_status wavo_sync(wavo_ctx *ctx, uint32_t timeout_ms) {
 
 // ---- linear layers ---------------------------------------------------------------------
 
+namespace {
+
+// The tensor maps of a linear layer whose device forms are in place (w16; q8 and s16t for Q8_0).
+bool linear_maps(wavo_linear *l) {
+  const uint32_t n = l->n, k = l->k;
+  if (!make_map(&l->map_w128, l->w16, k, n, k, 128) || !make_map(&l->map_w160, l->w16, k, n, k, 160) ||
+      !make_map(&l->map_w256, l->w16, k, n, k, 256) || !make_map(&l->map_h64, l->w16, k, n, k, 64) ||
+      !make_map(&l->map_h80, l->w16, k, n, k, 80) || !make_map(&l->map_h96, l->w16, k, n, k, 96))
+    return false;
+  l->has_q8map = l->q8 && make_map_i8(&l->map_q128, l->q8, k, n, k, 128) &&
+                 make_map_i8(&l->map_q160, l->q8, k, n, k, 160) &&
+                 make_map_i8(&l->map_q256, l->q8, k, n, k, 256) &&
+                 make_map_s16(&l->map_s128, l->s16t, n, k / 32, 128) &&
+                 make_map_s16(&l->map_s160, l->s16t, n, k / 32, 160) &&
+                 make_map_s16(&l->map_s256, l->s16t, n, k / 32, 256);
+  l->has3 = k % 64 == 0 && make_map3(&l->map3_h64, l->w16, k, n, k, 64) &&
+            make_map3(&l->map3_h80, l->w16, k, n, k, 80) &&
+            make_map3(&l->map3_h96, l->w16, k, n, k, 96);
+  return true;
+}
+
+}  // namespace
+
 wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k, const void *data,
                                const float *bias, size_t bias_len, wavo_linear **out) {
   if (!ctx || !out || !data) return WAVO_EINVAL;
@@ -513,21 +560,147 @@ wavo_status wavo_linear_create(wavo_ctx *ctx, int ty, uint32_t rows, uint32_t k,
     std::lock_guard<std::mutex> g(ctx->mu);
     return cuda_fail(ctx, e, "linear upload");
   }
-  if (!make_map(&l->map_w128, l->w16, k, n, k, 128) || !make_map(&l->map_w160, l->w16, k, n, k, 160) ||
-      !make_map(&l->map_w256, l->w16, k, n, k, 256) || !make_map(&l->map_h64, l->w16, k, n, k, 64) ||
-      !make_map(&l->map_h80, l->w16, k, n, k, 80) || !make_map(&l->map_h96, l->w16, k, n, k, 96)) {
+  if (!linear_maps(l)) {
     wavo_linear_destroy(l);
     return fail(ctx, WAVO_ECUDA, "linear: tensor map");
   }
-  l->has_q8map = l->q8 && make_map_i8(&l->map_q128, l->q8, k, n, k, 128) &&
-                 make_map_i8(&l->map_q160, l->q8, k, n, k, 160) &&
-                 make_map_i8(&l->map_q256, l->q8, k, n, k, 256) &&
-                 make_map_s16(&l->map_s128, l->s16t, n, k / 32, 128) &&
-                 make_map_s16(&l->map_s160, l->s16t, n, k / 32, 160) &&
-                 make_map_s16(&l->map_s256, l->s16t, n, k / 32, 256);
-  l->has3 = k % 64 == 0 && make_map3(&l->map3_h64, l->w16, k, n, k, 64) &&
-            make_map3(&l->map3_h80, l->w16, k, n, k, 80) &&
-            make_map3(&l->map3_h96, l->w16, k, n, k, 96);
+  *out = l;
+  return WAVO_OK;
+}
+
+// Gpu::linear over GGUF tensors (src/gpu/mod.rs:758-827 `upload_linear`): the named tensors,
+// stacked by rows, streamed from the file in pieces through two pinned buffers (the read of one
+// piece overlaps the copy of the other), raw as the file holds them; then one kernel turns them
+// into every device form the kernels read (w16; w32 for F32; q8, d8 and the transposed f16 scales
+// for Q8_0), and the tensor maps are made. F16 bytes land in w16 as they are, F32 in w32. The
+// weights never pass through host code element by element.
+wavo_status wavo_linear_from_gguf(wavo_ctx *ctx, const wavo_gguf *g, const char *const *names,
+                                  uint32_t count, const float *bias, size_t bias_len,
+                                  wavo_linear **out) {
+  if (!ctx || !out) return WAVO_EINVAL;
+  *out = nullptr;
+  if (!g || !names || count == 0) return fail(ctx, WAVO_EINVAL, "linear from GGUF: no tensors");
+  std::vector<const wavo_gguf::Info *> ts;
+  uint64_t rows64 = 0, k = 0;
+  int ty = -1;
+  for (uint32_t i = 0; i < count; ++i) {
+    auto it = names[i] ? g->tensors.find(names[i]) : g->tensors.end();
+    if (it == g->tensors.end())
+      return fail(ctx, WAVO_EINVAL, "missing tensor %s", names[i] ? names[i] : "(null)");
+    const wavo_gguf::Info &t = it->second;
+    uint64_t len = 1;
+    for (uint64_t d : t.dims) len *= d;
+    const uint64_t r = t.dims.empty() ? 1 : t.dims.back();
+    if (r == 0) return fail(ctx, WAVO_EINVAL, "tensor %s is empty", names[i]);
+    if (i == 0) {
+      ty = t.ty;
+      k = len / r;
+    } else if (t.ty != ty || len / r != k) {
+      return fail(ctx, WAVO_EINVAL, "stacked weights differ in type or shape");
+    }
+    rows64 += r;
+    ts.push_back(&t);
+  }
+  if (k == 0 || k % 32 != 0 || rows64 > 0x7fffffffu || k > 0x7fffffffu)
+    return fail(ctx, WAVO_EINVAL, "linear layer %llu->%llu: needs k %% 32 == 0",
+                (unsigned long long)k, (unsigned long long)rows64);
+  const uint32_t rows = uint32_t(rows64);
+  const uint32_t dual = bias_len > rows ? uint32_t(bias_len - rows) : 0;
+  if ((bias_len != 0 && bias_len < rows) || dual > rows)
+    return fail(ctx, WAVO_EINVAL, "linear layer %llu->%u: bias has %zu values",
+                (unsigned long long)k, rows, bias_len);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  cudaSetDevice(ctx->device);
+  const uint32_t n = (rows + 63) / 64 * 64;
+  const uint32_t cols = rows % 32 == 0 ? rows : n;
+  wavo_linear *l = new (std::nothrow) wavo_linear();
+  if (!l) return fail(ctx, WAVO_ENOMEM, "linear");
+  l->device = ctx->device;
+  l->ty = ty;
+  l->rows = rows;
+  l->n = n;
+  l->cols = cols;
+  l->k = uint32_t(k);
+  l->dual = dual;
+  const size_t nk = size_t(n) * k;
+  uint8_t *raw = nullptr;  // where the file's bytes land
+  cudaError_t e = cudaSuccess;
+  auto dev = [&](void **p, size_t bytes) {
+    if (e == cudaSuccess && (e = cudaMalloc(p, bytes)) == cudaSuccess)
+      e = cudaMemsetAsync(*p, 0, bytes, ctx->stream);  // rows past `rows` stay zero
+  };
+  dev(reinterpret_cast<void **>(&l->w16), nk * 2);
+  if (ty == WAVO_GGML_F16) {
+    raw = reinterpret_cast<uint8_t *>(l->w16);
+  } else if (ty == WAVO_GGML_F32) {
+    dev(reinterpret_cast<void **>(&l->w32), nk * 4);
+    raw = reinterpret_cast<uint8_t *>(l->w32);
+  } else {
+    dev(reinterpret_cast<void **>(&l->q8), nk);
+    dev(reinterpret_cast<void **>(&l->d8), nk / 32 * 4);
+    dev(reinterpret_cast<void **>(&l->s16t), nk / 32 * 2);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&raw), size_t(rows) * k / 32 * 34);
+  }
+  // Pinned pieces (allocated once per context); a piece is refilled once its copy has run.
+  const size_t piece = size_t(34) << 17;  // 4.25 MB: whole Q8_0 blocks
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+    if (!ctx->stage[i]) e = cudaHostAlloc(&ctx->stage[i], piece, cudaHostAllocDefault);
+    if (e == cudaSuccess && !ctx->stage_ev[i])
+      e = cudaEventCreateWithFlags(&ctx->stage_ev[i], cudaEventDisableTiming);
+  }
+  bool io_ok = true;
+  uint64_t at = 0;
+  int which = 0;
+  bool used[2] = {false, false};
+  for (size_t t = 0; t < ts.size() && e == cudaSuccess && io_ok; ++t) {
+    const uint64_t base = g->data + ts[t]->offset, size = ts[t]->bytes;
+    for (uint64_t off = 0; off < size && e == cudaSuccess; off += piece) {
+      const uint64_t len = std::min<uint64_t>(piece, size - off);
+      if (used[which] && (e = cudaEventSynchronize(ctx->stage_ev[which])) != cudaSuccess) break;
+      if (base + off + len <= g->head.size()) {
+        std::memcpy(ctx->stage[which], g->head.data() + base + off, size_t(len));
+      } else if (!wv::gguf_pread(g, ctx->stage[which], len, base + off)) {
+        io_ok = false;
+        break;
+      }
+      if ((e = cudaMemcpyAsync(raw + at + off, ctx->stage[which], size_t(len),
+                               cudaMemcpyHostToDevice, ctx->stream)) != cudaSuccess ||
+          (e = cudaEventRecord(ctx->stage_ev[which], ctx->stream)) != cudaSuccess)
+        break;
+      used[which] = true;
+      which ^= 1;
+    }
+    at += size;
+  }
+  if (e == cudaSuccess && io_ok) {
+    if (ty == WAVO_GGML_Q8_0)
+      e = wv::launch_build_q8(raw, int(rows), int(k), int(n), l->q8, l->d8, l->s16t, l->w16,
+                              ctx->stream);
+    else if (ty == WAVO_GGML_F32)
+      e = wv::launch_build_f16(l->w32, (long long)rows * (long long)k, l->w16, ctx->stream);
+  }
+  std::vector<float> bpad(std::max<size_t>(n, size_t(cols) + dual), 0.0f);
+  if (bias && bias_len) {
+    std::memcpy(bpad.data(), bias, size_t(rows) * 4);
+    if (dual) std::memcpy(bpad.data() + cols, bias + rows, size_t(dual) * 4);
+  }
+  if (e == cudaSuccess && (e = cudaMalloc(reinterpret_cast<void **>(&l->bias), bpad.size() * 4)) == cudaSuccess)
+    e = cudaMemcpyAsync(l->bias, bpad.data(), bpad.size() * 4, cudaMemcpyHostToDevice, ctx->stream);
+  const cudaError_t es = cudaStreamSynchronize(ctx->stream);  // bpad and the pieces are host memory
+  if (e == cudaSuccess) e = es;
+  if (ty == WAVO_GGML_Q8_0 && raw) cudaFree(raw);
+  if (!io_ok) {
+    wavo_linear_destroy(l);
+    return fail(ctx, WAVO_EINVAL, "linear from GGUF: reading %s failed", g->path.c_str());
+  }
+  if (e != cudaSuccess) {
+    wavo_linear_destroy(l);
+    return cuda_fail(ctx, e, "linear from GGUF");
+  }
+  if (!linear_maps(l)) {
+    wavo_linear_destroy(l);
+    return fail(ctx, WAVO_ECUDA, "linear: tensor map");
+  }
   *out = l;
   return WAVO_OK;
 }

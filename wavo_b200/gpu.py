@@ -72,6 +72,31 @@ class Linear:
         self.dual = int(L.lib().wavo_linear_width(h)) - self.cols
         del self._buf
 
+    @classmethod
+    def from_gguf(cls, gpu: "Gpu", gguf, names: list[str], bias=None) -> "Linear":
+        """`Gpu::linear(&[Tensor], bias)` with the tensors streamed from a GGUF file
+        (`wavo_linear_from_gguf`)."""
+        self = cls.__new__(cls)
+        b = None
+        if bias is not None and len(bias):
+            b = np.ascontiguousarray(bias, np.float32)
+        self._bias = b
+        arr = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        h = ctypes.c_void_p()
+        check(L.lib().wavo_linear_from_gguf(gpu.ctx, gguf.h, arr, len(names),
+                                            None if b is None else b.ctypes.data,
+                                            0 if b is None else b.size, ctypes.byref(h)), gpu.ctx)
+        self.h = h
+        ty, _ = gguf.tensor(names[0])
+        dims = gguf.dims(names[0])
+        self.k = int(np.prod(dims)) // dims[-1]
+        self.rows = sum(gguf.dims(n)[-1] for n in names)
+        self.ty = ty
+        self.n = (self.rows + 63) // 64 * 64
+        self.cols = self.rows if self.rows % 32 == 0 else self.n
+        self.dual = int(L.lib().wavo_linear_width(h)) - self.cols
+        return self
+
     def width(self) -> int:
         """`Linear::width`: output columns including the dual ones."""
         return self.cols + self.dual
@@ -112,6 +137,10 @@ class Gpu:
 
     def linear(self, ggml_type: int, rows: int, k: int, data, bias=None) -> Linear:
         return Linear(self, ggml_type, rows, k, data, bias)
+
+    def linear_from_gguf(self, gguf, names: list[str], bias=None) -> Linear:
+        """`Gpu::linear` over GGUF tensors, streamed from the file to the device."""
+        return Linear.from_gguf(self, gguf, names, bias)
 
     def buffer(self, n: int, dtype=torch.float32) -> torch.Tensor:
         """`Gpu::buffer`: zeroed device memory."""
