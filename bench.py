@@ -937,8 +937,176 @@ class C4Full(Workload):
         return dt, audio, f"1 window through {steps} of 224 steps"
 
 
+class C5Load:
+    """§8 f3: C5's projection weights (24 layers of Q8_0 q, k, v, out and linear_pos, d = 1024,
+    the C5 distributions: int8 ~U[-127, 127], f16 scales |N(0, 0.02)| / 127) loaded from a GGUF
+    file into device-ready layers, as a model load does (src/gpu/mod.rs:758-827): per layer the
+    stacked [q; k; v] projection, the output and the position projection through
+    wavo_linear_from_gguf, which streams the file's bytes to the device in pinned pieces and builds
+    the kernels' forms there. A step loads all 72 layers (133.7 MB of tensor data) from the page
+    cache and frees them again."""
+    LAYERS, D = 24, 1024
+    METRIC = "GGUF weight load GB/s"
+    UNIT = "GB/s"
+    scaling = "weak"
+    _path = None
+
+    @classmethod
+    def path(cls) -> str:
+        if cls._path is None or not os.path.exists(cls._path):
+            import tempfile
+            from wavo_b200 import gguf as G
+            rng = np.random.default_rng(5000)
+            d = cls.D
+            tensors = []
+            for layer in range(cls.LAYERS):
+                for name in ("attn_q", "attn_k", "attn_v", "attn_out", "linear_pos"):
+                    nb = d * d // 32
+                    blk = np.empty((nb, 34), np.uint8)
+                    sc = (np.abs(rng.standard_normal(nb)) * 0.02 / 127).astype(np.float16)
+                    blk[:, :2] = sc.view(np.uint8).reshape(nb, 2)
+                    blk[:, 2:] = rng.integers(-127, 128, (nb, 32), dtype=np.int8).view(np.uint8)
+                    tensors.append((f"blk.{layer}.{name}.weight", [d, d], G.TY_Q8_0, blk.tobytes()))
+            fd, p = tempfile.mkstemp(suffix=".gguf")
+            os.close(fd)
+            G.write_gguf(p, [("general.architecture", G.STR, "parakeet")], tensors)
+            import atexit
+            atexit.register(lambda: os.path.exists(p) and os.remove(p))
+            cls._path = p
+        return cls._path
+
+    @classmethod
+    def layers(cls):
+        for layer in range(cls.LAYERS):
+            b = f"blk.{layer}."
+            yield [b + "attn_q.weight", b + "attn_k.weight", b + "attn_v.weight"]
+            yield [b + "attn_out.weight"]
+            yield [b + "linear_pos.weight"]
+
+    @classmethod
+    def total_bytes(cls) -> int:
+        return cls.LAYERS * 5 * cls.D * cls.D // 32 * 34
+
+    @classmethod
+    def config(cls):
+        return {"workload": WORKLOAD_NAMES["c5load"], "layers": cls.LAYERS, "d_model": cls.D,
+                "weights": "Q8_0, C5's distributions", "tensor_bytes": cls.total_bytes(),
+                "source": "a GGUF v3 file in the page cache",
+                "parallelism": "each GPU loads its own copy, no collective"}
+
+    @classmethod
+    def cpu_sample(cls):
+        # The reference loader's host work (src/gpu/mod.rs:793-827 with src/gguf.rs:258-272): the
+        # file read in pieces of 8192 Q8_0 blocks (the native reader's pread), each block's scale
+        # and 32 values split into the two mapped buffers; here into host arrays (numpy).
+        from wavo_b200 import gguf as G
+        g = G.Gguf(cls.path())
+        piece = 34 << 13
+        t0 = time.perf_counter()
+        for names in cls.layers():
+            total = sum(g.tensor(n)[1] for n in names)
+            data = np.empty(total // 34 * 32, np.uint8)
+            scales = np.empty(total // 34 * 2, np.uint8)
+            blk = 0
+            for n in names:
+                size = g.tensor(n)[1]
+                for off in range(0, size, piece):
+                    b = np.frombuffer(g.read(n, off, min(piece, size - off)), np.uint8).reshape(-1, 34)
+                    data[blk * 32:(blk + len(b)) * 32] = b[:, 2:].ravel()
+                    scales[blk * 2:(blk + len(b)) * 2] = b[:, :2].ravel()
+                    blk += len(b)
+        dt = time.perf_counter() - t0
+        g.close()
+        return dt, cls.total_bytes() / 1e9, "all 72 layers' bytes read in pieces and split (numpy)"
+
+
+def run_load(args):
+    """§8 f3 measurement: GGUF -> device-ready layers, GB/s of tensor data (`--config c5load`)."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from wavo_b200 import gguf as G
+    from wavo_b200.gpu import Gpu
+    W = C5Load
+    gpu = Gpu(local)
+    path = W.path()
+    g = G.Gguf(path)
+    stream = torch.cuda.current_stream(local)
+
+    def step():
+        # The layers' loads are timed; freeing them afterwards (a device-wide cudaFree each) is not
+        # part of loading a model.
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        t0 = time.perf_counter()
+        lins = [gpu.linear_from_gguf(g, names) for names in W.layers()]
+        gpu.sync()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = max(e0.elapsed_time(e1), (time.perf_counter() - t0) * 1e3)
+        del lins
+        return t
+
+    for _ in range(args.warmup):
+        step()
+    gpu.sync()
+    if world > 1:
+        dist.barrier()
+    with Clocks(local) as clocks:
+        ms = sum(step() for _ in range(args.steps)) / args.steps
+    # The bound: a pinned host -> device copy of the same size on this host.
+    src = torch.empty(W.total_bytes(), dtype=torch.uint8).pin_memory()
+    dst = torch.empty(W.total_bytes(), dtype=torch.uint8, device="cuda")
+    best = None
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dst.copy_(src, non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = a.elapsed_time(b)
+        best = t if best is None else min(best, t)
+    pcie = W.total_bytes() / (best * 1e-3) / 1e9
+    from wavo_b200.runner import max_over_ranks
+    (ms,) = max_over_ranks([ms], device="cuda")
+    if rank == 0:
+        gbs = world * W.total_bytes() / (ms * 1e-3) / 1e9
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            W.cpu_sample()
+            dt, gb, sample = W.cpu_sample()
+            cpu = {"value": gb / dt, "unit": W.UNIT, "cores": 1, "kind": "port", "sample": sample}
+        line = {"metric": W.METRIC, "value": gbs, "unit": W.UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
+                "dtype": "q8_0", "data": "synthetic (seeded, C5's weight distributions)",
+                "config": W.config(),
+                "e2e": {"value": gbs, "unit": W.UNIT, "h2d_bytes_per_step": W.total_bytes(),
+                        "d2h_bytes_per_step": 0,
+                        "copies": "the load is the host -> device path itself"},
+                "gpu_launches": 72 * args.steps,
+                "roofline": {"bound": "pcie", "kernel": "wavo_linear_from_gguf",
+                             "achieved": gbs / world, "peak": pcie, "unit": "GB/s",
+                             "frac": gbs / world / pcie,
+                             "peak_source": "measured pinned host->device copy of the same bytes",
+                             "traffic": None},
+                "clocks": clocks.summary(), "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    g.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c4full": C4Full, "c5": C5,
-             "c5block": C5Block}
+             "c5block": C5Block, "c5load": C5Load}
 WORKLOAD_NAMES = {
     "c1": "C1: Parakeet rel-pos MHSA layer, f32 weights, batch 1, T=138",
     "c2": "C2: Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500",
@@ -952,6 +1120,8 @@ WORKLOAD_NAMES = {
               "device (LayerNorms, attention, FFN, logits, pick)",
     "c5block": "C5 blocks: Parakeet-0.6B FastConformer blocks (FFN, rel-pos MHSA, conv module, "
                "norms), 24 blocks, 400 segments of U[120,300] frames, Q8_0 weights",
+    "c5load": "C5 weights from GGUF: 24 layers of Q8_0 q/k/v/out/linear_pos (d 1024) loaded from a "
+              "GGUF file into device-ready layers",
 }
 
 
@@ -973,7 +1143,8 @@ def run_reference(args):
         times.append(dt)
     t = float(np.mean(times))
     value = audio / t
-    line = {"metric": getattr(W, "METRIC", METRIC), "value": value, "unit": UNIT, "n_gpus": args.gpus,
+    unit = getattr(W, "UNIT", UNIT)
+    line = {"metric": getattr(W, "METRIC", METRIC), "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
             "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
@@ -981,10 +1152,10 @@ def run_reference(args):
                        "sample": sample + " per step; value = the sample's audio seconds over "
                                  "its CPU time (the layers and segments are alike, so the rate "
                                  "carries over to the whole workload)"},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": unit, "cores": O.threads(), "kind": "port",
                              "sample": sample + " per step (CPU oracle restating the "
                              "reference's src/cpu attention path)"},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -1000,11 +1171,13 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = {"c1": 2000, "c2": 200, "c3": 100, "c4": 10, "c5": 30}[args.config]
+        args.steps = {"c1": 2000, "c2": 200, "c3": 100, "c4": 10, "c5": 30}.get(args.config, 5)
     if args.impl == "reference":
         if args.steps > 20:
             args.steps = 5
         return run_reference(args)
+    if args.config == "c5load":
+        return run_load(args)
 
     import torch
     import torch.distributed as dist

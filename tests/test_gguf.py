@@ -121,3 +121,25 @@ def test_written_files_round_trip(tmp_path):
         assert g.tensor("t.q8") == (G.TY_Q8_0, 40 * 128 // 32 * 34)
         assert np.abs(g.to_f32("t.q8") - wq).max() <= np.abs(wq).max() / 127
         g.close()
+
+
+def test_large_reads_in_parallel_parts_and_clean_exit(tmp_path):
+    # A tensor over 1 MiB is read as several ranges by the library's reader threads; the bytes must
+    # be the file's, and a process that used them must still exit on its own.
+    import subprocess
+    import sys
+    rng = np.random.default_rng(3)
+    w = rng.standard_normal(3 * 2**20 // 4 + 17 * 32).astype(np.float32)
+    p = str(tmp_path / "big.gguf")
+    G.write_gguf(p, [], [("big", [32, w.size // 32], G.TY_F32, w.tobytes())])
+    g = G.Gguf(p)
+    assert g.read("big") == w.tobytes()
+    assert g.read("big", 1000, 2_500_000) == w.tobytes()[1000:2_501_000]
+    g.close()
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from wavo_b200 import gguf as G\n"
+            "g = G.Gguf(%r)\n"
+            "assert len(g.read('big')) == %d\n") % (os.path.dirname(os.path.dirname(__file__)), p,
+                                                    w.size * 4)
+    r = subprocess.run([sys.executable, "-c", code], timeout=120)
+    assert r.returncode == 0

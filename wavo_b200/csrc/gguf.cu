@@ -9,8 +9,14 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
+#include <condition_variable>
 #include <cstring>
+#include <deque>
+#include <functional>
+#include <mutex>
 #include <new>
+#include <thread>
 
 #include "../../include/wavo_cuda.h"
 #include "gguf.cuh"
@@ -233,16 +239,87 @@ bool lookup(const wavo_gguf *g, const char *key, Value &v, Reader *rest = nullpt
 
 namespace wv {
 
-bool gguf_pread(const wavo_gguf *g, void *dst, uint64_t bytes, uint64_t off) {
-  uint8_t *p = static_cast<uint8_t *>(dst);
+namespace {
+
+bool pread_all(int fd, uint8_t *p, uint64_t bytes, uint64_t off) {
   while (bytes) {
-    const ssize_t got = pread(g->fd, p, bytes > (1u << 30) ? (1u << 30) : size_t(bytes), off_t(off));
+    const ssize_t got = pread(fd, p, bytes > (1u << 30) ? (1u << 30) : size_t(bytes), off_t(off));
     if (got <= 0) return false;
     p += got;
     off += uint64_t(got);
     bytes -= uint64_t(got);
   }
   return true;
+}
+
+// A few reader threads shared by every load of the process: a large piece of a file is read as
+// several ranges at once (one thread copies from the page cache at a fraction of what the host's
+// memory and the PCIe link take).
+class ReadPool {
+ public:
+  static constexpr int kHelpers = 3;
+  // Never destroyed: its detached threads wait on its members until the process ends.
+  static ReadPool &get() {
+    static ReadPool *pool = new ReadPool();
+    return *pool;
+  }
+  // Runs fn(0..parts-1), part 0 on the calling thread; true if every part returned true.
+  bool run(int parts, const std::function<bool(int)> &fn) {
+    std::unique_lock<std::mutex> lk(run_mu_);  // one multi-part read at a time
+    int left = parts - 1;
+    bool ok = true;
+    std::mutex m;
+    std::condition_variable cv;
+    {
+      std::lock_guard<std::mutex> q(mu_);
+      for (int i = 1; i < parts; ++i)
+        tasks_.push_back([&, i] {
+          const bool r = fn(i);
+          std::lock_guard<std::mutex> g(m);
+          ok = ok && r;
+          if (--left == 0) cv.notify_one();
+        });
+    }
+    cv_.notify_all();
+    const bool r0 = fn(0);
+    std::unique_lock<std::mutex> g(m);
+    cv.wait(g, [&] { return left == 0; });
+    return ok && r0;
+  }
+
+ private:
+  ReadPool() {
+    for (int i = 0; i < kHelpers; ++i) std::thread([this] { loop(); }).detach();
+  }
+  void loop() {
+    while (true) {
+      std::function<void()> t;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [this] { return !tasks_.empty(); });
+        t = std::move(tasks_.front());
+        tasks_.pop_front();
+      }
+      t();
+    }
+  }
+  std::mutex mu_, run_mu_;
+  std::condition_variable cv_;
+  std::deque<std::function<void()>> tasks_;
+};
+
+}  // namespace
+
+bool gguf_pread(const wavo_gguf *g, void *dst, uint64_t bytes, uint64_t off) {
+  uint8_t *p = static_cast<uint8_t *>(dst);
+  const uint64_t min_part = 1u << 20;
+  const int parts = int(std::min<uint64_t>(ReadPool::kHelpers + 1, (bytes + min_part - 1) / min_part));
+  if (parts <= 1) return pread_all(g->fd, p, bytes, off);
+  const uint64_t per = (bytes + parts - 1) / parts;
+  return ReadPool::get().run(parts, [&](int i) {
+    const uint64_t a = uint64_t(i) * per, n = std::min(per, bytes - std::min(bytes, a));
+    return n == 0 || pread_all(g->fd, p + a, n, off + a);
+  });
 }
 
 }  // namespace wv

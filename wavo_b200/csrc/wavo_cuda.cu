@@ -60,6 +60,7 @@ struct wavo_linear {
   CUtensorMap map_q128, map_q160, map_q256;
   CUtensorMap map_s128, map_s160, map_s256;
   bool has_q8map = false;
+  void *block = nullptr;     // wavo_linear_from_gguf: every buffer above in one allocation
 };
 
 struct wavo_graph {
@@ -623,23 +624,42 @@ wavo_status wavo_linear_from_gguf(wavo_ctx *ctx, const wavo_gguf *g, const char 
   l->k = uint32_t(k);
   l->dual = dual;
   const size_t nk = size_t(n) * k;
+  const size_t nbias = std::max<size_t>(n, size_t(cols) + dual);
+  // Every device form in one allocation (one cudaMalloc and one cudaFree a layer), zeroed so that
+  // the rows past `rows` are zero; Q8_0's raw blocks land in the context's scratch.
+  size_t sz[6] = {nk * 2, ty == WAVO_GGML_F32 ? nk * 4 : 0, ty == WAVO_GGML_Q8_0 ? nk : 0,
+                  ty == WAVO_GGML_Q8_0 ? nk / 32 * 4 : 0, ty == WAVO_GGML_Q8_0 ? nk / 32 * 2 : 0,
+                  nbias * 4};
+  size_t offs[6], total = 0;
+  for (int i = 0; i < 6; ++i) {
+    offs[i] = total;
+    total += align_up(sz[i], 256);
+  }
   uint8_t *raw = nullptr;  // where the file's bytes land
-  cudaError_t e = cudaSuccess;
-  auto dev = [&](void **p, size_t bytes) {
-    if (e == cudaSuccess && (e = cudaMalloc(p, bytes)) == cudaSuccess)
-      e = cudaMemsetAsync(*p, 0, bytes, ctx->stream);  // rows past `rows` stay zero
-  };
-  dev(reinterpret_cast<void **>(&l->w16), nk * 2);
+  cudaError_t e = cudaMalloc(&l->block, total);
+  if (e == cudaSuccess) e = cudaMemsetAsync(l->block, 0, total, ctx->stream);
+  if (e == cudaSuccess) {
+    uint8_t *b = static_cast<uint8_t *>(l->block);
+    l->w16 = reinterpret_cast<__half *>(b + offs[0]);
+    if (sz[1]) l->w32 = reinterpret_cast<float *>(b + offs[1]);
+    if (sz[2]) {
+      l->q8 = reinterpret_cast<int8_t *>(b + offs[2]);
+      l->d8 = reinterpret_cast<float *>(b + offs[3]);
+      l->s16t = reinterpret_cast<__half *>(b + offs[4]);
+    }
+    l->bias = reinterpret_cast<float *>(b + offs[5]);
+  }
   if (ty == WAVO_GGML_F16) {
     raw = reinterpret_cast<uint8_t *>(l->w16);
   } else if (ty == WAVO_GGML_F32) {
-    dev(reinterpret_cast<void **>(&l->w32), nk * 4);
     raw = reinterpret_cast<uint8_t *>(l->w32);
-  } else {
-    dev(reinterpret_cast<void **>(&l->q8), nk);
-    dev(reinterpret_cast<void **>(&l->d8), nk / 32 * 4);
-    dev(reinterpret_cast<void **>(&l->s16t), nk / 32 * 2);
-    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&raw), size_t(rows) * k / 32 * 34);
+  } else if (e == cudaSuccess) {
+    void *ws = nullptr;
+    if (workspace(ctx, size_t(rows) * k / 32 * 34, &ws) != WAVO_OK) {
+      wavo_linear_destroy(l);
+      return WAVO_ENOMEM;
+    }
+    raw = static_cast<uint8_t *>(ws);
   }
   // Pinned pieces (allocated once per context); a piece is refilled once its copy has run.
   const size_t piece = size_t(34) << 17;  // 4.25 MB: whole Q8_0 blocks
@@ -679,16 +699,16 @@ wavo_status wavo_linear_from_gguf(wavo_ctx *ctx, const wavo_gguf *g, const char 
     else if (ty == WAVO_GGML_F32)
       e = wv::launch_build_f16(l->w32, (long long)rows * (long long)k, l->w16, ctx->stream);
   }
-  std::vector<float> bpad(std::max<size_t>(n, size_t(cols) + dual), 0.0f);
+  std::vector<float> bpad(nbias, 0.0f);
   if (bias && bias_len) {
     std::memcpy(bpad.data(), bias, size_t(rows) * 4);
     if (dual) std::memcpy(bpad.data() + cols, bias + rows, size_t(dual) * 4);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(l->bias, bpad.data(), bpad.size() * 4, cudaMemcpyHostToDevice,
+                          ctx->stream);
   }
-  if (e == cudaSuccess && (e = cudaMalloc(reinterpret_cast<void **>(&l->bias), bpad.size() * 4)) == cudaSuccess)
-    e = cudaMemcpyAsync(l->bias, bpad.data(), bpad.size() * 4, cudaMemcpyHostToDevice, ctx->stream);
   const cudaError_t es = cudaStreamSynchronize(ctx->stream);  // bpad and the pieces are host memory
   if (e == cudaSuccess) e = es;
-  if (ty == WAVO_GGML_Q8_0 && raw) cudaFree(raw);
   if (!io_ok) {
     wavo_linear_destroy(l);
     return fail(ctx, WAVO_EINVAL, "linear from GGUF: reading %s failed", g->path.c_str());
@@ -708,12 +728,16 @@ wavo_status wavo_linear_from_gguf(wavo_ctx *ctx, const wavo_gguf *g, const char 
 void wavo_linear_destroy(wavo_linear *l) {
   if (!l) return;
   cudaSetDevice(l->device);
-  cudaFree(l->w16);
-  cudaFree(l->w32);
-  cudaFree(l->q8);
-  cudaFree(l->d8);
-  cudaFree(l->s16t);
-  cudaFree(l->bias);
+  if (l->block) {
+    cudaFree(l->block);
+  } else {
+    cudaFree(l->w16);
+    cudaFree(l->w32);
+    cudaFree(l->q8);
+    cudaFree(l->d8);
+    cudaFree(l->s16t);
+    cudaFree(l->bias);
+  }
   delete l;
 }
 

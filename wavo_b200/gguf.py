@@ -38,6 +38,8 @@ class Gguf:
         self.path = str(path)
 
     def close(self) -> None:
+        if L is None or L.lib is None:  # interpreter shutdown: the process releases the file
+            return
         if getattr(self, "h", None) is not None and self.h.value:
             L.lib().wavo_gguf_close(self.h)
             self.h = None

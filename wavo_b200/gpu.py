@@ -103,7 +103,7 @@ class Linear:
 
     def __del__(self):
         h = getattr(self, "h", None)
-        if h is not None and h.value:
+        if h is not None and h.value and L is not None and L.lib is not None:
             L.lib().wavo_linear_destroy(h)
             self.h = None
 
@@ -124,6 +124,8 @@ class Gpu:
         check(L.lib().wavo_set_stream(self.ctx, stream.cuda_stream), self.ctx)
 
     def close(self) -> None:
+        if L is None or L.lib is None:  # interpreter shutdown: the process releases the device
+            return
         if getattr(self, "ctx", None) is not None and self.ctx.value:
             L.lib().wavo_destroy(self.ctx)
             self.ctx = None
