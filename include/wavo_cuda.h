@@ -121,6 +121,23 @@ void wavo_linear_destroy(wavo_linear *l);
 uint32_t wavo_linear_width(const wavo_linear *l);
 uint32_t wavo_linear_k(const wavo_linear *l);
 
+/* ---- the log-mel frontend: replaces parakeet::frontend::Frontend (src/parakeet/frontend.rs) ---
+ * 16 kHz pcm (device f32) to 128 log-mel bins a 10 ms frame, time-major: pre-emphasis, Hann(400)
+ * in an FFT of 512 (f64, the reference's operations in its order), power to f32, the Slaney
+ * filterbank, ln(mel + 2^-24). The first frontend call on a context makes its tables (a device
+ * allocation): make it before any stream capture. */
+
+/* Frontend::log_mel (src/parakeet/frontend.rs:74-108): frames f0 .. f1 of the whole pcm
+ * (f1 <= samples / 160 + 1), each computed from only the samples it covers, into mel
+ * [f1 - f0][128]. */
+wavo_status wavo_log_mel(wavo_ctx *ctx, const float *pcm, uint64_t samples, uint64_t f0,
+                         uint64_t f1, float *mel);
+/* Frontend::compute (src/parakeet/frontend.rs:50-70): all samples / 160 + 1 frames, each mel bin
+ * normalised over all frames but the last (unbiased, + 1e-5), the last frame zero; *frames gets
+ * the count, 0 (and nothing written) below 3 frames. mel holds samples / 160 + 1 rows of 128. */
+wavo_status wavo_mel_features(wavo_ctx *ctx, const float *pcm, uint64_t samples, float *mel,
+                              uint64_t *frames);
+
 /* ---- GGUF files: replaces gguf::Gguf / gguf::Tensor (src/gguf.rs) ----------------------------
  * Host calls without a context: errors read from wavo_last_error(NULL). A wavo_gguf may be read
  * from many threads at once. */

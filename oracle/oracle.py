@@ -70,6 +70,12 @@ def lib():
         L.wo_linear_free.argtypes = [ctypes.c_void_p]
         L.wo_gemm.argtypes = [_f, ctypes.c_void_p, _f, _sz, ctypes.c_int, ctypes.c_float]
         L.wo_gemv.argtypes = [_f, ctypes.c_void_p, _f, ctypes.c_int, ctypes.c_float]
+        _d = ctypes.POINTER(ctypes.c_double)
+        L.wo_fft.argtypes = [_d, _sz, _d, _d]
+        L.wo_log_mel.argtypes = [_f, _sz, _sz, _sz, _f]
+        L.wo_mel_features.argtypes = [_f, _sz, _f]
+        L.wo_mel_features.restype = _sz
+        L.wo_frontend_tables.argtypes = [_d, _f]
         L.wo_set_threads.argtypes = [ctypes.c_int]
         L.wo_threads.restype = ctypes.c_int
         L.wo_set_vnni.argtypes = [ctypes.c_int]
@@ -259,3 +265,46 @@ def q8_0_bytes(values: np.ndarray, scale_mode: str = "absmax") -> bytes:
             q = np.zeros(32, np.int8)
         out += np.float16(d).tobytes() + q.tobytes()
     return bytes(out)
+
+
+# ---- the log-mel frontend (src/parakeet/frontend.rs, src/fft.rs) ----------------------------------
+
+MELS, HOP = 128, 160
+
+
+def _pd(a: np.ndarray):
+    assert a.dtype == np.float64 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+
+
+def fft(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """src/fft.rs `Fft::<f64>::new(n).forward(x)`: the DFT of n real values (re, im)."""
+    x = np.ascontiguousarray(x, np.float64)
+    re, im = np.empty(x.size), np.empty(x.size)
+    lib().wo_fft(_pd(x), x.size, _pd(re), _pd(im))
+    return re, im
+
+
+def log_mel(pcm: np.ndarray, f0: int, f1: int) -> np.ndarray:
+    """src/parakeet/frontend.rs:74-108 `Frontend::log_mel`: frames [f0, f1) of 16 kHz pcm."""
+    pcm = np.ascontiguousarray(pcm, np.float32)
+    out = np.empty((f1 - f0, MELS), np.float32)
+    lib().wo_log_mel(_p(pcm), pcm.size, f0, f1, _p(out))
+    return out
+
+
+def mel_features(pcm: np.ndarray) -> np.ndarray:
+    """src/parakeet/frontend.rs:50-70 `Frontend::compute`: normalised log-mel [frames][128], empty
+    below 3 frames."""
+    pcm = np.ascontiguousarray(pcm, np.float32)
+    frames = pcm.size // HOP + 1
+    out = np.empty((max(frames, 1), MELS), np.float32)
+    n = lib().wo_mel_features(_p(pcm), pcm.size, _p(out))
+    return out[:n] if n else np.empty((0, MELS), np.float32)
+
+
+def frontend_tables() -> tuple[np.ndarray, np.ndarray]:
+    """The Hann window [512] (f64) and the Slaney filterbank [128][257] (f32)."""
+    w, f = np.empty(512), np.empty((MELS, 257), np.float32)
+    lib().wo_frontend_tables(_pd(w), _p(f))
+    return w, f

@@ -677,7 +677,221 @@ void quantize(const float *x, int16_t *q, float *d, size_t blocks) {
 
 }  // namespace
 
+// ---- the log-mel frontend (src/parakeet/frontend.rs, src/fft.rs) -----------------------------
+
+namespace {
+
+constexpr double kTau = 6.283185307179586;
+
+// src/fft.rs:40-143 `Fft<f64>`: radix-2 decimation in time down to naive DFTs of the odd factor,
+// the data in Stockham order; every multiply-add fused as the reference's `mul_add`.
+struct RealFft {
+  size_t n = 0, leaf = 0, blocks = 0;
+  std::vector<size_t> perm;
+  std::vector<double> lcos, lsin;  // [j][k]
+  std::vector<double> tcos, tsin;  // [stage][n / 2]
+  explicit RealFft(size_t n_) : n(n_) {
+    size_t tz = 0;
+    while (((n >> tz) & 1) == 0) ++tz;
+    leaf = n >> tz;
+    blocks = n / leaf;
+    std::vector<size_t> starts{0};
+    while (starts.size() < blocks) {
+      std::vector<size_t> next;
+      for (size_t v : starts) next.push_back(2 * v);
+      for (size_t v : starts) next.push_back(2 * v + 1);
+      starts = next;
+    }
+    for (size_t i = 0; i < n; ++i) perm.push_back(starts[i % blocks] + i / blocks * blocks);
+    auto trig = [&](size_t i, std::vector<double> &c, std::vector<double> &s) {
+      const double phase = kTau * double(i) / double(n);
+      c.push_back(std::cos(phase));
+      s.push_back(std::sin(phase));
+    };
+    for (size_t i = 0; i < leaf * leaf; ++i) trig(i / leaf * (i % leaf) * blocks % n, lcos, lsin);
+    for (size_t size = 2 * leaf; size <= n; size *= 2)
+      for (size_t i = 0; i < n / 2; ++i) trig(i / (n / size) * (n / size), tcos, tsin);
+  }
+  // re and im of the n real values x (src/fft.rs:86-143 `run`, `leaves`, `stage`).
+  void forward(const double *x, double *re, double *im) const {
+    const size_t stages = tcos.size() / (n / 2);
+    std::vector<double> buf(4 * n, 0.0);
+    double *front = buf.data(), *back = buf.data() + 2 * n;
+    double *src = stages % 2 == 0 ? back : front, *dst = stages % 2 == 0 ? front : back;
+    for (size_t v = 0; v < n; ++v) src[v] = x[perm[v]];
+    for (size_t k = 0; k < leaf; ++k) {
+      double *r = dst + k * blocks, *m = dst + n + k * blocks;
+      for (size_t g = 0; g < blocks; ++g) {
+        r[g] = src[g];
+        m[g] = 0.0;
+      }
+      for (size_t j = 1; j < leaf; ++j) {
+        const double c = lcos[j * leaf + k], s = lsin[j * leaf + k];
+        const double *xs = src + j * blocks;
+        for (size_t g = 0; g < blocks; ++g) {
+          r[g] = std::fma(xs[g], c, r[g]);
+          m[g] = std::fma(-xs[g], s, m[g]);
+        }
+      }
+    }
+    const size_t half = n / 2;
+    for (size_t st = 0; st < stages; ++st) {
+      std::swap(src, dst);
+      const double *sr = src, *si = src + n, *cs = tcos.data() + st * half, *sn = tsin.data() + st * half;
+      double *dr = dst, *di = dst + n;
+      for (size_t i = 0; i < half; ++i) {
+        const double c = cs[i], s = sn[i], a = sr[2 * i], xv = sr[2 * i + 1], b = si[2 * i],
+                     y = si[2 * i + 1];
+        dr[i] = std::fma(s, y, std::fma(c, xv, a));
+        di[i] = std::fma(-s, xv, std::fma(c, y, b));
+        dr[i + half] = std::fma(-s, y, std::fma(-c, xv, a));
+        di[i + half] = std::fma(s, xv, std::fma(-c, y, b));
+      }
+    }
+    std::memcpy(re, dst, n * sizeof(double));
+    std::memcpy(im, dst + n, n * sizeof(double));
+  }
+};
+
+constexpr size_t kMels = 128, kNfft = 512, kWindow = 400, kHop = 160, kBins = kNfft / 2 + 1;
+constexpr float kPreEmphasis = 0.97f, kFMax = 8000.0f;
+const float kLogEps = 1.0f / float(1 << 24);
+
+// src/parakeet/frontend.rs:110-140 `slaney_filterbank`: librosa's mel(16000, 512, 128, 0, 8000,
+// norm='slaney') computed in f64, stored as f32.
+std::vector<float> slaney_filterbank() {
+  const double fsp = 200.0 / 3.0, min_log_hz = 1000.0;
+  const double min_log_mel = min_log_hz / fsp, log_step = std::log(6.4) / 27.0;
+  auto hz_to_mel = [&](double hz) {
+    return hz < min_log_hz ? hz / fsp : min_log_mel + std::log(hz / min_log_hz) / log_step;
+  };
+  auto mel_to_hz = [&](double mel) {
+    return mel < min_log_mel ? mel * fsp : min_log_hz * std::exp(log_step * (mel - min_log_mel));
+  };
+  const double mel_max = hz_to_mel(double(kFMax));
+  std::vector<double> hz(kMels + 2);
+  for (size_t m = 0; m < kMels + 2; ++m) hz[m] = mel_to_hz(mel_max * double(m) / double(kMels + 1));
+  std::vector<float> out(kMels * kBins, 0.0f);
+  for (size_t m = 0; m < kMels; ++m) {
+    const double enorm = 2.0 / (hz[m + 2] - hz[m]);
+    for (size_t k = 0; k < kBins; ++k) {
+      const double f = 16000.0 * double(k) / double(kNfft);
+      const double lower = (f - hz[m]) / (hz[m + 1] - hz[m]);
+      const double upper = (hz[m + 2] - f) / (hz[m + 2] - hz[m + 1]);
+      out[m * kBins + k] = float(std::max(std::min(lower, upper), 0.0) * enorm);
+    }
+  }
+  return out;
+}
+
+struct Frontend {
+  std::vector<double> window;
+  std::vector<float> filters;
+  std::vector<std::pair<size_t, size_t>> spans;
+  RealFft fft{kNfft};
+  Frontend() {
+    const size_t pad = (kNfft - kWindow) / 2;
+    for (size_t i = 0; i < kNfft; ++i) {
+      const size_t k = i - pad;  // wraps below pad, as the reference's wrapping_sub
+      window.push_back(k < kWindow ? 0.5 - 0.5 * std::cos(2.0 * M_PI * double(k) / double(kWindow - 1))
+                                   : 0.0);
+    }
+    filters = slaney_filterbank();
+    for (size_t m = 0; m < kMels; ++m) {
+      const float *f = filters.data() + m * kBins;
+      size_t lo = 0;
+      while (lo < kBins && f[lo] == 0.0f) ++lo;
+      if (lo == kBins) {
+        spans.push_back({0, 0});
+        continue;
+      }
+      size_t hi = kBins;
+      while (hi > lo && f[hi - 1] == 0.0f) --hi;
+      spans.push_back({lo, hi});
+    }
+  }
+  // src/parakeet/frontend.rs:74-108 `log_mel`: frames [f0, f1) of the whole pcm, time-major.
+  void log_mel(const float *pcm, size_t n_pcm, size_t f0, size_t f1, float *out) const {
+    const size_t frames = f1 - f0;
+    const size_t pad = f0 * kHop;
+    const size_t len = (frames ? frames - 1 : 0) * kHop + kNfft;
+    std::vector<double> padded(len);
+    for (size_t q = 0; q < len; ++q) {
+      const size_t j = pad + q;
+      double v = 0.0;
+      if (j >= kNfft / 2) {
+        const size_t i = j - kNfft / 2;
+        if (i == 0)
+          v = double(pcm[0]);
+        else if (i < n_pcm)
+          v = double(pcm[i]) - double(kPreEmphasis) * double(pcm[i - 1]);
+      }
+      padded[q] = v;
+    }
+    std::vector<double> frame(kNfft), re(kNfft), im(kNfft);
+    std::vector<float> power(kBins);
+    for (size_t t = 0; t < frames; ++t) {
+      for (size_t i = 0; i < kNfft; ++i) frame[i] = padded[t * kHop + i] * window[i];
+      fft.forward(frame.data(), re.data(), im.data());
+      for (size_t k = 0; k < kBins; ++k) power[k] = float(re[k] * re[k] + im[k] * im[k]);
+      for (size_t m = 0; m < kMels; ++m) {
+        float e = 0.0f;
+        for (size_t k = spans[m].first; k < spans[m].second; ++k)
+          e = std::fma(filters[m * kBins + k], power[k], e);
+        out[t * kMels + m] = std::log(e + kLogEps);
+      }
+    }
+  }
+};
+
+const Frontend &frontend() {
+  static const Frontend f;
+  return f;
+}
+
+}  // namespace
+
 extern "C" {
+
+// src/fft.rs `Fft::<f64>::new(n).forward(x)`: re and im of n real values.
+void wo_fft(const double *x, size_t n, double *re, double *im) { RealFft(n).forward(x, re, im); }
+
+// src/parakeet/frontend.rs:74-108 `Frontend::log_mel(pcm, f0..f1)`: [f1 - f0][128] f32.
+void wo_log_mel(const float *pcm, size_t n_pcm, size_t f0, size_t f1, float *out) {
+  frontend().log_mel(pcm, n_pcm, f0, f1, out);
+}
+
+// src/parakeet/frontend.rs:50-70 `Frontend::compute`: the log-mel of every frame, each mel bin
+// normalised over all frames but the last (f64 sums in frame order), the last zero. Returns the
+// frames (pcm / 160 + 1), 0 below 3 (nothing written).
+size_t wo_mel_features(const float *pcm, size_t n_pcm, float *out) {
+  const size_t frames = n_pcm / kHop + 1;
+  if (frames < 3) return 0;
+  frontend().log_mel(pcm, n_pcm, 0, frames, out);
+  const size_t n = frames - 1;
+  for (size_t m = 0; m < kMels; ++m) {
+    double sum = 0.0;
+    for (size_t t = 0; t < n; ++t) sum += double(out[t * kMels + m]);
+    const double mean = sum / double(n);
+    double var = 0.0;
+    for (size_t t = 0; t < n; ++t) {
+      const double d = double(out[t * kMels + m]) - mean;
+      var += d * d;
+    }
+    var /= double(n - 1);
+    const double inv = 1.0 / (std::sqrt(var) + double(1e-5f));
+    for (size_t t = 0; t < n; ++t) out[t * kMels + m] = float((double(out[t * kMels + m]) - mean) * inv);
+    out[n * kMels + m] = 0.0f;
+  }
+  return frames;
+}
+
+// The frontend's tables: the Hann window [512] (f64) and the Slaney filterbank [128][257] (f32).
+void wo_frontend_tables(double *window, float *filters) {
+  const Frontend &f = frontend();
+  std::memcpy(window, f.window.data(), kNfft * sizeof(double));
+  std::memcpy(filters, f.filters.data(), kMels * kBins * sizeof(float));
+}
 
 void wo_set_vnni(int mode) { g_vnni = mode; }
 int wo_vnni(void) {

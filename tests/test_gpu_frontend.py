@@ -1,0 +1,97 @@
+"""The Parakeet log-mel frontend on the device (src/parakeet/frontend.rs) through the C ABI, against
+the oracle's restatement of the reference (CPU): the log-mel of every frame, frame ranges, the
+normalised features, short and silent inputs; the reference's tolerance (max-abs 2e-3, rel-L2
+1e-3), and the measured error is far below it (the spectrum is the reference's bit for bit)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    from wavo_b200.gpu import Gpu
+    g = Gpu(0)
+    yield g
+    g.sync()
+    g.close()
+
+
+def speech_like(seconds: float, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    n = int(seconds * 16000)
+    t = np.arange(n) / 16000.0
+    x = 0.05 * rng.standard_normal(n)
+    for f in (180.0, 440.0, 1250.0, 3300.0):
+        x += 0.2 * np.sin(2 * np.pi * f * t + rng.uniform(0, 6)) * (0.5 + 0.5 * np.sin(2 * np.pi * 1.3 * t))
+    return x.astype(np.float32)
+
+
+def close(got, want):
+    err = np.abs(got.astype(np.float64) - want)
+    rel = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+    assert err.max() <= 2e-3 and rel <= 1e-3, (err.max(), rel)
+    return err.max()
+
+
+def gpu_log_mel(gpu, pcm, f0, f1):
+    p = torch.from_numpy(pcm).cuda()
+    mel = torch.zeros(f1 - f0, 128, device="cuda")
+    gpu.log_mel(p, f0, f1, mel)
+    gpu.sync()
+    return mel.cpu().numpy()
+
+
+@pytest.mark.parametrize("seconds", [1.0, 7.3])
+def test_log_mel_matches_oracle(gpu, seconds):
+    pcm = speech_like(seconds, 1)
+    frames = pcm.size // 160 + 1
+    got = gpu_log_mel(gpu, pcm, 0, frames)
+    want = O.log_mel(pcm, 0, frames)
+    assert close(got, want) < 1e-4
+    # The spectrum is the reference's: the log-mel agrees but for the last bit of ln.
+    assert (got == want).mean() > 0.5
+
+
+def test_log_mel_frame_ranges(gpu):
+    # src/parakeet/frontend.rs:152-161 `frame_ranges` on the device.
+    pcm = (np.sin(np.arange(16000, dtype=np.float32) * np.float32(0.01)) * np.float32(0.5)).astype(np.float32)
+    whole = gpu_log_mel(gpu, pcm, 0, 101)
+    close(whole, O.log_mel(pcm, 0, 101))
+    for a, b in ((0, 1), (0, 7), (3, 40), (95, 101), (100, 101)):
+        np.testing.assert_array_equal(gpu_log_mel(gpu, pcm, a, b), whole[a:b])
+
+
+@pytest.mark.parametrize("seconds,seed", [(0.02, 2), (3.0, 3), (75.0, 4)])
+def test_mel_features_match_oracle(gpu, seconds, seed):
+    pcm = speech_like(seconds, seed)
+    want = O.mel_features(pcm)
+    mel = torch.zeros(pcm.size // 160 + 1, 128, device="cuda")
+    n = gpu.mel_features(torch.from_numpy(pcm).cuda(), mel)
+    gpu.sync()
+    assert n == want.shape[0]
+    got = mel.cpu().numpy()[:n]
+    close(got, want)
+    assert (got[-1] == 0).all()
+
+
+def test_mel_features_short_and_silent(gpu):
+    # src/parakeet/frontend.rs:143-150 `short_input`, and silence (zero variance).
+    mel = torch.full((8, 128), 7.0, device="cuda")
+    assert gpu.mel_features(torch.full((319,), 0.1, device="cuda"), mel) == 0
+    gpu.sync()
+    assert (mel.cpu().numpy() == 7.0).all()  # nothing written
+    assert gpu.mel_features(torch.full((320,), 0.1, device="cuda"), mel) == 3
+    gpu.sync()
+    got = mel.cpu().numpy()[:3]
+    assert np.isfinite(got).all()
+    close(got, O.mel_features(np.full(320, 0.1, np.float32)))
+    silent = np.zeros(16000, np.float32)
+    mel = torch.zeros(101, 128, device="cuda")
+    assert gpu.mel_features(torch.from_numpy(silent).cuda(), mel) == 101
+    gpu.sync()
+    np.testing.assert_array_equal(mel.cpu().numpy(), O.mel_features(silent))

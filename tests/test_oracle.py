@@ -386,3 +386,44 @@ def test_pick_restates_reference_rules():
         gen.append(tok)
     assert gen == [T, 3, T + 4]
     assert -1.0 < float(np.mean(lps)) < 0.0
+
+
+# ---- the log-mel frontend ----------------------------------------------------------------------
+
+def test_fft_matches_a_dft():
+    # src/fft.rs:150-175 `matches_a_dft` (f64, tolerance 1e-10), and numpy's FFT besides.
+    for n in (320, 360, 400, 512, 15):
+        x = np.array([((i * 7919 % 1000) / 500.0 - 1.0) * 0.3 for i in range(n)])
+        re, im = O.fft(x)
+        k = np.arange(n)
+        phase = 2 * np.pi * ((k[:, None] * k[None, :]) % n) / n
+        assert np.abs(re - (x[None, :] * np.cos(phase)).sum(1)).max() < 1e-10
+        assert np.abs(im + (x[None, :] * np.sin(phase)).sum(1)).max() < 1e-10
+        ref = np.fft.fft(x)
+        assert np.abs(re - ref.real).max() < 1e-10 and np.abs(im - ref.imag).max() < 1e-10
+
+
+def test_frontend_short_input():
+    # src/parakeet/frontend.rs:143-150 `short_input`.
+    assert O.mel_features(np.full(319, 0.1, np.float32)).size == 0
+    mel = O.mel_features(np.full(320, 0.1, np.float32))
+    assert mel.shape == (3, O.MELS) and np.isfinite(mel).all()
+
+
+def test_frontend_frame_ranges():
+    # src/parakeet/frontend.rs:152-161 `frame_ranges`: a range of frames equals those frames of the
+    # whole audio, at the edges too.
+    pcm = (np.sin(np.arange(16000, dtype=np.float32) * np.float32(0.01)) * np.float32(0.5)).astype(np.float32)
+    whole = O.log_mel(pcm, 0, 101)
+    for a, b in ((0, 1), (0, 7), (3, 40), (95, 101), (100, 101)):
+        np.testing.assert_array_equal(O.log_mel(pcm, a, b), whole[a:b])
+
+
+def test_frontend_filterbank_and_window():
+    # librosa's Slaney mel filters peak at 2 / (f[m+2] - f[m]) and partition the band: each bin of
+    # 0-8 kHz lies under at most two filters; the window is a symmetric Hann of 400 centred in 512.
+    w, f = O.frontend_tables()
+    assert (w[:56] == 0).all() and (w[456:] == 0).all() and w[56] == 0.0
+    np.testing.assert_allclose(w[56:456], w[56:456][::-1], atol=1e-15)
+    assert ((f > 0).sum(axis=0) <= 2).all() and (f >= 0).all()
+    assert f.shape == (128, 257) and (f.sum(axis=1) > 0).all()

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 SOURCES = ["wavo_cuda.cu", "gemm.cu", "attention.cu", "attention_fa.cu", "decode.cu", "selftest.cu",
-           "encoder.cu", "decoder.cu", "gguf.cu"]
+           "encoder.cu", "decoder.cu", "gguf.cu", "frontend.cu"]
 HEADERS = ["ptx.cuh", "kernels.cuh", "softmax.cuh", "gguf.cuh"]
 SO = os.path.join(HERE, "libwavo_cuda.so")
 STATIC = os.path.join(HERE, "libwavo_cuda.a")

@@ -1,0 +1,270 @@
+// The Parakeet log-mel frontend on the device (src/parakeet/frontend.rs, src/fft.rs): pre-emphasis
+// in f64, a symmetric Hann(400) centred in an f64 FFT of 512, power cast to f32, the Slaney
+// filterbank as f32 fused multiply-adds in bin order, ln(mel + 2^-24), then each mel bin normalised
+// over all frames but the last, which is zero. The FFT performs the reference's operations in its
+// order (radix-2 decimation in time, Stockham order, every multiply-add fused, the same cos/sin
+// table), so the spectrum is the reference's bit for bit; the reductions of the normalisation are
+// f64 sums in a fixed order (chunks of frames, then the chunks in order).
+//
+//   log_mel_kernel   one warp a frame (four frames a CTA): the windowed frame in the first stage's
+//                    order, nine butterfly stages between two shared-memory buffers (16-byte
+//                    loads of each butterfly's input pair), the power spectrum, then four mel bins
+//                    a lane over their filter spans.
+//   mel_sum_kernel   per chunk of 1024 frames, a thread a mel bin: the f64 sum of the values (or of
+//                    the squared deviations from the mean) in frame order (coalesced rows).
+//   mel_stats_kernel the chunk sums in order: the mean, then 1 / (unbiased std + 1e-5).
+//   mel_norm_kernel  (x - mean)·inv to f32; the last frame zero.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <vector>
+
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace wv {
+namespace {
+
+constexpr int FE_MELS = 128, FE_NFFT = 512, FE_WINDOW = 400, FE_HOP = 160, FE_BINS = 257;
+constexpr int FE_STAGES = 9, FE_HALF = FE_NFFT / 2;
+constexpr int FE_WARPS = 4;
+constexpr int FE_CHUNK = 1024;
+
+__global__ void __launch_bounds__(32 * FE_WARPS)
+    log_mel_kernel(const float *__restrict__ pcm, long long n_pcm, long long f0, int frames,
+                   const FrontendTables tab, float *__restrict__ mel) {
+  griddep_launch_dependents();
+  griddep_wait();
+  extern __shared__ double fe_smem[];
+  const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+  const int t = int(blockIdx.x) * FE_WARPS + warp;
+  if (t >= frames) return;  // whole warps leave; no block-wide barrier follows
+  double *ar = fe_smem + warp * 4 * FE_NFFT, *ai = ar + FE_NFFT;
+  double *br = ai + FE_NFFT, *bi = br + FE_NFFT;
+  // The windowed frame in the first stage's order: v = perm(i) reads sample i (src/fft.rs:89-92).
+  const long long j0 = (f0 + t) * FE_HOP;  // the frame's first index in the padded signal
+  for (int v = lane; v < FE_NFFT; v += 32) {
+    const int i = tab.perm[v];
+    const long long j = j0 + i - FE_NFFT / 2;  // the pcm index of padded sample j0 + i
+    double s = 0.0;
+    if (j == 0)
+      s = double(pcm[0]);
+    else if (j > 0 && j < n_pcm)
+      s = __dsub_rn(double(pcm[j]), __dmul_rn(double(0.97f), double(pcm[j - 1])));
+    ar[v] = __dmul_rn(s, tab.window[i]);
+    ai[v] = 0.0;
+  }
+  __syncwarp();
+  // Nine radix-2 stages (src/fft.rs:131-143): output i reads inputs 2i and 2i + 1.
+  double *sr = ar, *si = ai, *dr = br, *di = bi;
+#pragma unroll 1
+  for (int st = 0; st < FE_STAGES; ++st) {
+    const double *cs = tab.tcos + st * FE_HALF, *sn = tab.tsin + st * FE_HALF;
+#pragma unroll 4
+    for (int q = 0; q < FE_HALF / 32; ++q) {
+      const int i = lane + 32 * q;
+      const double c = cs[i], s = sn[i];
+      const double2 xr = reinterpret_cast<const double2 *>(sr)[i];
+      const double2 xi = reinterpret_cast<const double2 *>(si)[i];
+      const double a = xr.x, x = xr.y, b = xi.x, y = xi.y;
+      dr[i] = fma(s, y, fma(c, x, a));
+      di[i] = fma(-s, x, fma(c, y, b));
+      dr[i + FE_HALF] = fma(-s, y, fma(-c, x, a));
+      di[i + FE_HALF] = fma(s, x, fma(-c, y, b));
+    }
+    __syncwarp();
+    double *tr = sr, *ti = si;
+    sr = dr;
+    si = di;
+    dr = tr;
+    di = ti;
+  }
+  // The power spectrum (f64 products and sum, cast to f32) over the freed buffer.
+  float *power = reinterpret_cast<float *>(dr);
+  for (int k = lane; k < FE_BINS; k += 32)
+    power[k] = float(__dadd_rn(__dmul_rn(sr[k], sr[k]), __dmul_rn(si[k], si[k])));
+  __syncwarp();
+  float *out = mel + (long long)t * FE_MELS;
+#pragma unroll
+  for (int q = 0; q < FE_MELS / 32; ++q) {
+    const int m = lane + 32 * q;
+    const float *f = tab.filters + m * FE_BINS;
+    float e = 0.0f;
+    for (int k = tab.span_lo[m]; k < tab.span_hi[m]; ++k) e = fmaf(f[k], power[k], e);
+    out[m] = logf(__fadd_rn(e, 1.0f / float(1 << 24)));
+  }
+}
+
+// Per chunk of FE_CHUNK frames of the first n, thread m: the f64 sum in frame order of mel values
+// (mean == nullptr) or of their squared deviations from mean[m].
+__global__ void mel_sum_kernel(const float *__restrict__ mel, long long n,
+                               const double *__restrict__ mean, double *__restrict__ part) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int m = int(threadIdx.x);
+  const long long t0 = (long long)blockIdx.x * FE_CHUNK;
+  const long long t1 = t0 + FE_CHUNK < n ? t0 + FE_CHUNK : n;
+  double s = 0.0;
+  const double mu = mean ? mean[m] : 0.0;
+  for (long long t = t0; t < t1; ++t) {
+    const double x = double(mel[t * FE_MELS + m]);
+    if (mean) {
+      const double d = __dsub_rn(x, mu);
+      s = __dadd_rn(s, __dmul_rn(d, d));
+    } else {
+      s = __dadd_rn(s, x);
+    }
+  }
+  part[(long long)blockIdx.x * FE_MELS + m] = s;
+}
+
+// The chunk sums in order: mean = Σ / n (var == nullptr), or inv = 1 / (sqrt(Σ / (n - 1)) + 1e-5).
+__global__ void mel_stats_kernel(const double *__restrict__ part, int chunks, long long n,
+                                 double *__restrict__ out, int is_var) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int m = int(threadIdx.x);
+  double s = 0.0;
+  for (int c = 0; c < chunks; ++c) s = __dadd_rn(s, part[(long long)c * FE_MELS + m]);
+  out[m] = is_var ? 1.0 / __dadd_rn(sqrt(s / double(n - 1)), double(1e-5f)) : s / double(n);
+}
+
+__global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
+                                const double *__restrict__ mean, const double *__restrict__ inv) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= frames * FE_MELS) return;
+  const int m = int(i % FE_MELS);
+  const long long t = i / FE_MELS;
+  mel[i] = t == frames - 1 ? 0.0f : float(__dmul_rn(__dsub_rn(double(mel[i]), mean[m]), inv[m]));
+}
+
+}  // namespace
+
+// ---- tables (host), as src/fft.rs:46-66 and src/parakeet/frontend.rs:30-47, 110-140 build them --
+
+size_t frontend_table_bytes() {
+  return FE_NFFT * 2 + 2 * FE_STAGES * FE_HALF * 8 + FE_NFFT * 8 + FE_MELS * FE_BINS * 4 +
+         2 * FE_MELS * 4 + 256;
+}
+
+cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *out) {
+  const int n = FE_NFFT;
+  std::vector<int> starts{0};
+  while (int(starts.size()) < n) {  // leaf 1: all 512 points are radix-2 blocks
+    std::vector<int> next;
+    for (int v : starts) next.push_back(2 * v);
+    for (int v : starts) next.push_back(2 * v + 1);
+    starts = next;
+  }
+  std::vector<uint16_t> perm(n);
+  for (int i = 0; i < n; ++i) perm[i] = uint16_t(starts[i]);
+  std::vector<double> tcos, tsin;
+  const double tau = 6.283185307179586;
+  for (int size = 2; size <= n; size *= 2)
+    for (int i = 0; i < n / 2; ++i) {
+      const int idx = i / (n / size) * (n / size);
+      const double phase = tau * double(idx) / double(n);
+      tcos.push_back(std::cos(phase));
+      tsin.push_back(std::sin(phase));
+    }
+  std::vector<double> window(n);
+  for (int i = 0; i < n; ++i) {
+    const int k = i - (FE_NFFT - FE_WINDOW) / 2;
+    window[i] = k >= 0 && k < FE_WINDOW
+                    ? 0.5 - 0.5 * std::cos(2.0 * M_PI * double(k) / double(FE_WINDOW - 1))
+                    : 0.0;
+  }
+  // Slaney filterbank (librosa mel(16000, 512, 128, 0, 8000, norm='slaney')) in f64, stored f32.
+  const double fsp = 200.0 / 3.0, min_log_hz = 1000.0, min_log_mel = min_log_hz / fsp;
+  const double log_step = std::log(6.4) / 27.0;
+  auto hz_to_mel = [&](double hz) {
+    return hz < min_log_hz ? hz / fsp : min_log_mel + std::log(hz / min_log_hz) / log_step;
+  };
+  auto mel_to_hz = [&](double mel) {
+    return mel < min_log_mel ? mel * fsp : min_log_hz * std::exp(log_step * (mel - min_log_mel));
+  };
+  const double mel_max = hz_to_mel(8000.0);
+  std::vector<double> hz(FE_MELS + 2);
+  for (int m = 0; m < FE_MELS + 2; ++m) hz[m] = mel_to_hz(mel_max * double(m) / double(FE_MELS + 1));
+  std::vector<float> filters(FE_MELS * FE_BINS);
+  std::vector<int> lo(FE_MELS), hi(FE_MELS);
+  for (int m = 0; m < FE_MELS; ++m) {
+    const double enorm = 2.0 / (hz[m + 2] - hz[m]);
+    for (int k = 0; k < FE_BINS; ++k) {
+      const double f = 16000.0 * double(k) / double(FE_NFFT);
+      const double lower = (f - hz[m]) / (hz[m + 1] - hz[m]);
+      const double upper = (hz[m + 2] - f) / (hz[m + 2] - hz[m + 1]);
+      filters[m * FE_BINS + k] = float(std::fmax(std::fmin(lower, upper), 0.0) * enorm);
+    }
+    int a = 0;
+    while (a < FE_BINS && filters[m * FE_BINS + a] == 0.0f) ++a;
+    int b = FE_BINS;
+    while (b > a && filters[m * FE_BINS + b - 1] == 0.0f) --b;
+    lo[m] = a == FE_BINS ? 0 : a;
+    hi[m] = a == FE_BINS ? 0 : b;
+  }
+  uint8_t *p = static_cast<uint8_t *>(dev);
+  size_t at = 0;
+  auto put = [&](const void *src, size_t bytes) -> void * {
+    at = (at + 15) / 16 * 16;
+    void *d = p + at;
+    at += bytes;
+    cudaMemcpyAsync(d, src, bytes, cudaMemcpyHostToDevice, s);
+    return d;
+  };
+  out->perm = static_cast<const uint16_t *>(put(perm.data(), perm.size() * 2));
+  out->tcos = static_cast<const double *>(put(tcos.data(), tcos.size() * 8));
+  out->tsin = static_cast<const double *>(put(tsin.data(), tsin.size() * 8));
+  out->window = static_cast<const double *>(put(window.data(), window.size() * 8));
+  out->filters = static_cast<const float *>(put(filters.data(), filters.size() * 4));
+  out->span_lo = static_cast<const int *>(put(lo.data(), lo.size() * 4));
+  out->span_hi = static_cast<const int *>(put(hi.data(), hi.size() * 4));
+  return cudaStreamSynchronize(s);  // the host vectors go out of scope
+}
+
+cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int frames,
+                           const FrontendTables &tab, float *mel, cudaStream_t s) {
+  if (frames <= 0) return cudaSuccess;
+  const size_t smem = size_t(FE_WARPS) * 4 * FE_NFFT * 8;  // 64 KB
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(log_mel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  return launch_pdl(log_mel_kernel, dim3((frames + FE_WARPS - 1) / FE_WARPS), dim3(32 * FE_WARPS),
+                    smem, s, pcm, n_pcm, f0, frames, tab, mel);
+}
+
+size_t mel_norm_scratch_bytes(long long frames) {
+  const long long chunks = (frames + FE_CHUNK - 1) / FE_CHUNK;
+  return size_t(chunks) * FE_MELS * 8 + 2 * FE_MELS * 8;
+}
+
+cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStream_t s) {
+  const long long n = frames - 1;  // statistics over all frames but the last
+  if (n < 2) return cudaErrorInvalidValue;
+  const int chunks = int((n + FE_CHUNK - 1) / FE_CHUNK);
+  double *part = static_cast<double *>(scratch);
+  double *mean = part + (long long)chunks * FE_MELS, *inv = mean + FE_MELS;
+  cudaError_t e;
+  if ((e = launch_pdl(mel_sum_kernel, dim3(chunks), dim3(FE_MELS), 0, s, (const float *)mel, n,
+                      (const double *)nullptr, part)) != cudaSuccess ||
+      (e = launch_pdl(mel_stats_kernel, dim3(1), dim3(FE_MELS), 0, s, (const double *)part,
+                      chunks, n, mean, 0)) != cudaSuccess ||
+      (e = launch_pdl(mel_sum_kernel, dim3(chunks), dim3(FE_MELS), 0, s, (const float *)mel, n,
+                      (const double *)mean, part)) != cudaSuccess ||
+      (e = launch_pdl(mel_stats_kernel, dim3(1), dim3(FE_MELS), 0, s, (const double *)part,
+                      chunks, n, inv, 1)) != cudaSuccess)
+    return e;
+  const long long total = frames * FE_MELS;
+  return launch_pdl(mel_norm_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, mel,
+                    frames, (const double *)mean, (const double *)inv);
+}
+
+}  // namespace wv

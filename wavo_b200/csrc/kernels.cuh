@@ -183,6 +183,26 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
                         const float *scales, const float *bias, float *c, long long ldc, int rows,
                         int n, int k, int epilogue, float alpha, cudaStream_t s);
 
+// ---- the log-mel frontend (frontend.cu) ----------------------------------------------------------
+
+// Device tables of the frontend: the FFT's first-stage order, its nine stages' cos and sin, the
+// Hann window, the Slaney filterbank [128][257] and each filter's nonzero bins [lo, hi).
+struct FrontendTables {
+  const uint16_t *perm;
+  const double *tcos, *tsin, *window;
+  const float *filters;
+  const int *span_lo, *span_hi;
+};
+size_t frontend_table_bytes();
+// Fills `dev` (frontend_table_bytes()) with the tables and points `out` at them (waits for `s`).
+cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *out);
+// mel [frames][128] = the log-mel of frames f0 .. f0 + frames of the 16 kHz pcm (n_pcm samples).
+cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int frames,
+                           const FrontendTables &tab, float *mel, cudaStream_t s);
+// Each mel bin normalised over frames 0 .. frames - 2, the last frame zeroed (frames >= 3).
+size_t mel_norm_scratch_bytes(long long frames);
+cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStream_t s);
+
 // ---- GGUF loads (gguf.cu) ----------------------------------------------------------------------
 
 // Raw Q8_0 blocks of rows x k weights into q8 [n][k] int8, d8 [n][k/32] f32, s16t [k/32][n] f16 and

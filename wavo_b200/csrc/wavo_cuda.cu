@@ -35,6 +35,9 @@ struct wavo_ctx {
   // wavo_linear_from_gguf: two pinned pieces of the file in flight to the device.
   void *stage[2] = {nullptr, nullptr};
   cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+  // The log-mel frontend's tables (made by the first frontend call).
+  void *fe_dev = nullptr;
+  wv::FrontendTables fe_tab{};
   std::mutex mu;
   std::string err;
 };
@@ -353,6 +356,7 @@ void wavo_destroy(wavo_ctx *ctx) {
     if (ctx->stage_ev[i]) cudaEventDestroy(ctx->stage_ev[i]);
   }
   if (ctx->dev_err) cudaFree(ctx->dev_err);
+  if (ctx->fe_dev) cudaFree(ctx->fe_dev);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
 }
@@ -1215,6 +1219,62 @@ wavo_status wavo_pick(wavo_ctx *ctx, float *logits, uint32_t ld, uint32_t rows, 
                      int(n_suppress), begin_suppress, int(n_begin), int(eot), int(no_timestamps),
                      int(begin), int(max_initial), tokens, logprobs, ctx->stream),
      "pick launch");
+  return WAVO_OK;
+}
+
+// ---- the log-mel frontend ----------------------------------------------------------------
+
+namespace {
+
+wavo_status frontend_tables(wavo_ctx *ctx) {
+  if (ctx->fe_dev) return WAVO_OK;
+  if (ctx->capturing)
+    return fail(ctx, WAVO_EINVAL, "log-mel: make the first frontend call before a capture");
+  CK(cudaMalloc(&ctx->fe_dev, wv::frontend_table_bytes()), "log-mel tables");
+  const cudaError_t e = wv::frontend_tables_upload(ctx->fe_dev, ctx->stream, &ctx->fe_tab);
+  if (e != cudaSuccess) {
+    cudaFree(ctx->fe_dev);
+    ctx->fe_dev = nullptr;
+    return cuda_fail(ctx, e, "log-mel tables");
+  }
+  return WAVO_OK;
+}
+
+}  // namespace
+
+wavo_status wavo_log_mel(wavo_ctx *ctx, const float *pcm, uint64_t samples, uint64_t f0,
+                         uint64_t f1, float *mel) {
+  if (!ctx) return WAVO_EINVAL;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  const uint64_t frames = samples / 160 + 1;
+  if (!pcm || !mel || samples == 0) return fail(ctx, WAVO_EINVAL, "log-mel: NULL buffer or no samples");
+  if (f0 >= f1 || f1 > frames || f1 - f0 > 0x7fffffffu)
+    return fail(ctx, WAVO_EINVAL, "log-mel: frames %llu..%llu of %llu", (unsigned long long)f0,
+                (unsigned long long)f1, (unsigned long long)frames);
+  cudaSetDevice(ctx->device);
+  wavo_status st = frontend_tables(ctx);
+  if (st != WAVO_OK) return st;
+  CK(wv::launch_log_mel(pcm, (long long)samples, (long long)f0, int(f1 - f0), ctx->fe_tab, mel,
+                        ctx->stream),
+     "log-mel launch");
+  return WAVO_OK;
+}
+
+wavo_status wavo_mel_features(wavo_ctx *ctx, const float *pcm, uint64_t samples, float *mel,
+                              uint64_t *frames) {
+  if (!ctx || !frames) return WAVO_EINVAL;
+  *frames = 0;
+  const uint64_t n = samples / 160 + 1;
+  if (n < 3) return WAVO_OK;  // too few frames for the normalisation: no features
+  if (n > 0x7fffffffu) return fail(ctx, WAVO_EINVAL, "mel features: %llu frames", (unsigned long long)n);
+  wavo_status st = wavo_log_mel(ctx, pcm, samples, 0, n, mel);
+  if (st != WAVO_OK) return st;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  void *ws = nullptr;
+  st = workspace(ctx, wv::mel_norm_scratch_bytes((long long)n), &ws);
+  if (st != WAVO_OK) return st;
+  CK(wv::launch_mel_norm(mel, (long long)n, ws, ctx->stream), "mel normalisation launch");
+  *frames = n;
   return WAVO_OK;
 }
 

@@ -140,6 +140,17 @@ class Gpu:
     def linear(self, ggml_type: int, rows: int, k: int, data, bias=None) -> Linear:
         return Linear(self, ggml_type, rows, k, data, bias)
 
+    def log_mel(self, pcm: torch.Tensor, f0: int, f1: int, mel: torch.Tensor) -> None:
+        """`Frontend::log_mel`: frames f0..f1 of the 16 kHz pcm into mel [f1 - f0][128]."""
+        check(L.lib().wavo_log_mel(self.ctx, _ptr(pcm), pcm.numel(), f0, f1, _ptr(mel)), self.ctx)
+
+    def mel_features(self, pcm: torch.Tensor, mel: torch.Tensor) -> int:
+        """`Frontend::compute`: the normalised features into mel; returns the frames (0 below 3)."""
+        n = ctypes.c_uint64()
+        check(L.lib().wavo_mel_features(self.ctx, _ptr(pcm), pcm.numel(), _ptr(mel),
+                                        ctypes.byref(n)), self.ctx)
+        return n.value
+
     def linear_from_gguf(self, gguf, names: list[str], bias=None) -> Linear:
         """`Gpu::linear` over GGUF tensors, streamed from the file to the device."""
         return Linear.from_gguf(self, gguf, names, bias)
