@@ -937,6 +937,94 @@ class C4Full(Workload):
         return dt, audio, f"1 window through {steps} of 224 steps"
 
 
+class C5Mel(Workload):
+    """§8 f4: the log-mel features of C5's audio on the device (src/parakeet/frontend.rs): 400
+    segments of U[120, 300] encoder frames (8 mel frames each, 1280 samples of 16 kHz pcm a frame),
+    each segment's features computed and normalised on their own as the reference computes a piece
+    (wavo_mel_features: pre-emphasis, Hann(400), f64 FFT of 512, power, 128 Slaney mel bins, ln,
+    per-bin normalisation). Input: the segments' pcm; output: their [frames][128] features."""
+    METRIC = "log-mel audio-sec/sec"
+    FRAME_S = 0.08
+    bound = "hbm"
+    dtype = "f64 FFT, f32 mel"
+
+    def __init__(self, gpu, rank, world, seed=5000):
+        import torch
+        self.gpu, self.world = gpu, world
+        lengths = segment_lengths(seed, 400, 120, 300)
+        self.all_lengths = lengths
+        self.plan, mine = shard(lengths, rank, world, lambda t: t)
+        self.order = mine
+        self.lengths = [lengths[i] for i in mine]
+        self.samples = [t * 8 * 160 for t in self.lengths]
+        self.frames = [n // 160 + 1 for n in self.samples]
+        self.seg_rows, self.out_width = [t * 8 * 160 // 160 + 1 for t in lengths], 128
+        rng = np.random.default_rng(seed + 1 + rank)
+        total = sum(self.samples)
+        t = np.arange(total) / 16000.0
+        pcm = (0.05 * rng.standard_normal(total) + 0.2 * np.sin(2 * np.pi * 440.0 * t)).astype(np.float32)
+        dev = gpu.torch_device
+        self.pcm_host = torch.from_numpy(pcm).pin_memory()
+        self.pcm = self.pcm_host.to(dev)
+        rows = sum(self.frames)
+        self.mel = torch.zeros(rows, 128, device=dev)
+        self.mel_host = torch.empty(rows, 128).pin_memory()
+        self.s0 = np.concatenate([[0], np.cumsum(self.samples)[:-1]]).astype(int)
+        self.r0 = np.concatenate([[0], np.cumsum(self.frames)[:-1]]).astype(int)
+
+    def record(self, p, timer=None):
+        tick = timer or (lambda name, fn: fn())
+        for i in range(len(self.samples)):
+            a, n, r, f = int(self.s0[i]), self.samples[i], int(self.r0[i]), self.frames[i]
+            tick("mel_features", lambda a=a, n=n, r=r, f=f: self.gpu.mel_features(
+                self.pcm[a:a + n], self.mel[r:r + f]))
+
+    def inputs(self):
+        return [(self.pcm, self.pcm_host)]
+
+    def outputs(self):
+        return [(self.mel_host, self.mel)]
+
+    def launches(self):
+        return 6 * len(self.samples)
+
+    def work(self):
+        # HBM bytes: the pcm read (a frame's 512-sample window overlaps the next three: each
+        # sample once) and the features written, read and written again by the normalisation.
+        # Per call (a segment), averaged over the segments.
+        per = 4.0 * sum(self.samples) + 3 * 2 * 4.0 * 128 * sum(self.frames)
+        return {"mel_features": per / len(self.samples)}
+
+    def audio_s(self):
+        return sum(self.lengths) * self.FRAME_S
+
+    def total_audio_s(self, world):
+        return sum(self.all_lengths) * self.FRAME_S
+
+    def config(self):
+        return {"workload": WORKLOAD_NAMES["c5mel"], "segments": len(self.all_lengths),
+                "total_mel_frames": int(sum(t * 8 + 1 for t in self.all_lengths)),
+                "audio_s": sum(self.all_lengths) * self.FRAME_S, "n_fft": 512, "mels": 128,
+                "l2": "inputs larger than L2 (430 MB of pcm)",
+                "parallelism": f"segments sharded LPT over {self.world} GPU(s), no collective"}
+
+    @staticmethod
+    def cpu_sample(seed=5000):
+        # 16 of the 400 segments (every 25th) through the oracle's frontend (the reference's
+        # Frontend::compute restated), scaled by audio seconds.
+        from oracle import oracle as O
+        lens = segment_lengths(seed, 400, 120, 300)[::25]
+        rng = np.random.default_rng(seed)
+        pcms = [(0.05 * rng.standard_normal(t * 1280) + 0.2 * np.sin(
+            2 * np.pi * 440.0 * np.arange(t * 1280) / 16000.0)).astype(np.float32) for t in lens]
+        from concurrent.futures import ThreadPoolExecutor
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(os.cpu_count() or 1) as ex:  # ctypes calls release the GIL
+            list(ex.map(O.mel_features, pcms))
+        dt = time.perf_counter() - t0
+        return dt, sum(lens) * 0.08, "16 of the 400 segments (every 25th), a thread a segment"
+
+
 class C5Load:
     """§8 f3: C5's projection weights (24 layers of Q8_0 q, k, v, out and linear_pos, d = 1024,
     the C5 distributions: int8 ~U[-127, 127], f16 scales |N(0, 0.02)| / 127) loaded from a GGUF
@@ -1106,7 +1194,7 @@ def run_load(args):
 
 
 WORKLOADS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c4full": C4Full, "c5": C5,
-             "c5block": C5Block, "c5load": C5Load}
+             "c5block": C5Block, "c5load": C5Load, "c5mel": C5Mel}
 WORKLOAD_NAMES = {
     "c1": "C1: Parakeet rel-pos MHSA layer, f32 weights, batch 1, T=138",
     "c2": "C2: Whisper large-v3-turbo encoder self-attention, 32 layers, T=1500",
@@ -1120,6 +1208,8 @@ WORKLOAD_NAMES = {
               "device (LayerNorms, attention, FFN, logits, pick)",
     "c5block": "C5 blocks: Parakeet-0.6B FastConformer blocks (FFN, rel-pos MHSA, conv module, "
                "norms), 24 blocks, 400 segments of U[120,300] frames, Q8_0 weights",
+    "c5mel": "C5 log-mel: Parakeet's frontend (f64 FFT of 512, 128 Slaney mel bins, per-segment "
+             "normalisation) over C5's 400 segments of U[120,300] encoder frames of 16 kHz audio",
     "c5load": "C5 weights from GGUF: 24 layers of Q8_0 q/k/v/out/linear_pos (d 1024) loaded from a "
               "GGUF file into device-ready layers",
 }

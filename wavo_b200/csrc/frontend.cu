@@ -10,8 +10,9 @@
 //                    order, nine butterfly stages between two shared-memory buffers (16-byte
 //                    loads of each butterfly's input pair), the power spectrum, then four mel bins
 //                    a lane over their filter spans.
-//   mel_sum_kernel   per chunk of 1024 frames, a thread a mel bin: the f64 sum of the values (or of
-//                    the squared deviations from the mean) in frame order (coalesced rows).
+//   mel_sum_kernel   per chunk of 64 frames, a thread a mel bin: the f64 sum of the values (or of
+//                    the squared deviations from the mean) in frame order (coalesced rows, eight
+//                    loads in flight).
 //   mel_stats_kernel the chunk sums in order: the mean, then 1 / (unbiased std + 1e-5).
 //   mel_norm_kernel  (x - mean)·inv to f32; the last frame zero.
 #include <cuda_runtime.h>
@@ -28,7 +29,7 @@ namespace {
 constexpr int FE_MELS = 128, FE_NFFT = 512, FE_WINDOW = 400, FE_HOP = 160, FE_BINS = 257;
 constexpr int FE_STAGES = 9, FE_HALF = FE_NFFT / 2;
 constexpr int FE_WARPS = 4;
-constexpr int FE_CHUNK = 1024;
+constexpr int FE_CHUNK = 64;
 
 __global__ void __launch_bounds__(32 * FE_WARPS)
     log_mel_kernel(const float *__restrict__ pcm, long long n_pcm, long long f0, int frames,
@@ -106,6 +107,7 @@ __global__ void mel_sum_kernel(const float *__restrict__ mel, long long n,
   const long long t1 = t0 + FE_CHUNK < n ? t0 + FE_CHUNK : n;
   double s = 0.0;
   const double mu = mean ? mean[m] : 0.0;
+#pragma unroll 8
   for (long long t = t0; t < t1; ++t) {
     const double x = double(mel[t * FE_MELS + m]);
     if (mean) {
