@@ -138,6 +138,21 @@ wavo_status wavo_log_mel(wavo_ctx *ctx, const float *pcm, uint64_t samples, uint
 wavo_status wavo_mel_features(wavo_ctx *ctx, const float *pcm, uint64_t samples, float *mel,
                               uint64_t *frames);
 
+/* Parakeet's 8x conv subsampling (src/parakeet/cpu.rs:60-174, GPU src/parakeet/encoder.rs:103-121):
+ * from mel [frames][128] (of which `valid` are audio, the rest padding), conv0 (3x3, stride 2, 1 ->
+ * ch) + ReLU, conv2 (depthwise 3x3, stride 2) with its rows from half(half(valid)) on zero, conv3
+ * (pointwise, the linear layer ch -> ch) + ReLU, conv5 (depthwise), conv6 (pointwise) + ReLU,
+ * [t][16][ch] to [t][ch·16], and the output projection `out` (16·ch -> d) + bias into x [t][d],
+ * t = half(half(half(frames - 1))) with half(n) = (n - 1) / 2 + 1 (*t_out gets it). Taps are
+ * device f32 [9][ch] (time tap, then frequency tap), biases [ch]; ch % 32 == 0. The intermediate
+ * images go to `scratch` (device, 256-byte aligned, wavo_subsample_scratch_bytes of them). */
+uint64_t wavo_subsample_scratch_bytes(uint32_t frames, uint32_t ch);
+wavo_status wavo_subsample(wavo_ctx *ctx, const float *mel, uint32_t frames, uint32_t valid,
+                           uint32_t ch, const float *w0, const float *b0, const float *w2,
+                           const float *b2, const wavo_linear *conv3, const float *w5,
+                           const float *b5, const wavo_linear *conv6, const wavo_linear *out,
+                           float *x, void *scratch, uint32_t *t_out);
+
 /* ---- GGUF files: replaces gguf::Gguf / gguf::Tensor (src/gguf.rs) ----------------------------
  * Host calls without a context: errors read from wavo_last_error(NULL). A wavo_gguf may be read
  * from many threads at once. */

@@ -76,6 +76,9 @@ def lib():
         L.wo_mel_features.argtypes = [_f, _sz, _f]
         L.wo_mel_features.restype = _sz
         L.wo_frontend_tables.argtypes = [_d, _f]
+        L.wo_subsample.argtypes = [_f, _sz, _sz, _sz, _f, _f, _f, _f, ctypes.c_void_p, _f, _f,
+                                   ctypes.c_void_p, ctypes.c_void_p, _f]
+        L.wo_subsample.restype = _sz
         L.wo_set_threads.argtypes = [ctypes.c_int]
         L.wo_threads.restype = ctypes.c_int
         L.wo_set_vnni.argtypes = [ctypes.c_int]
@@ -308,3 +311,19 @@ def frontend_tables() -> tuple[np.ndarray, np.ndarray]:
     w, f = np.empty(512), np.empty((MELS, 257), np.float32)
     lib().wo_frontend_tables(_pd(w), _p(f))
     return w, f
+
+
+def subsample(mel: np.ndarray, valid: int, taps: dict, conv3: "Linear", conv6: "Linear",
+              out: "Linear") -> np.ndarray:
+    """src/parakeet/cpu.rs:60-98: Parakeet's 8x conv subsampling of mel [frames][128] (valid frames
+    of them) into x [t][d]; taps: w0, b0, w2, b2, w5, b5 (3x3 taps [9][ch], biases [ch])."""
+    mel = np.ascontiguousarray(mel, np.float32)
+    frames = mel.shape[0]
+    h = lambda n: (n - 1) // 2 + 1  # noqa: E731
+    t = h(h(h(frames - 1)))
+    ch = taps["b0"].size
+    x = np.zeros((t, out.n), np.float32)
+    c = {k: np.ascontiguousarray(v, np.float32) for k, v in taps.items()}
+    lib().wo_subsample(_p(mel), frames, valid, ch, _p(c["w0"]), _p(c["b0"]), _p(c["w2"]),
+                       _p(c["b2"]), conv3._h, _p(c["w5"]), _p(c["b5"]), conv6._h, out._h, _p(x))
+    return x

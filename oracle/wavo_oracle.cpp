@@ -1024,3 +1024,85 @@ void wo_gemv(const float *x, const void *lp, float *c, int epi, float alpha) {
 }
 
 }  // extern "C"
+
+// ---- Parakeet's 8x conv subsampling (src/parakeet/cpu.rs:60-174) --------------------------------
+
+namespace {
+
+inline size_t half_up(size_t n) { return (n - 1) / 2 + 1; }  // src/gpu/mod.rs:1068-1070 `half`
+
+// src/parakeet/cpu.rs:151-174 `depthwise`: 3x3, stride 2, padding 1, + bias, over the image
+// [t][f][ch] into [half(t)][half(f)][ch]; taps [9][ch] (time tap, then frequency tap). The whole
+// image at once (the reference's chunks of rows give the same rows).
+void depthwise(const float *x, const float *w, const float *b, size_t t, size_t f, size_t ch,
+               float *y, size_t rows) {
+  const size_t fo_n = half_up(f);
+  for (size_t k = 0; k < rows; ++k)
+    for (size_t fo = 0; fo < fo_n; ++fo) {
+      float *yy = y + (k * fo_n + fo) * ch;
+      for (size_t c = 0; c < ch; ++c) yy[c] = b[c];
+      for (size_t tap = 0; tap < 9; ++tap) {
+        const size_t ti = 2 * k + tap / 3, fi = 2 * fo + tap % 3;
+        if (ti < 1 || ti > t || fi < 1 || fi > f) continue;
+        const float *xx = x + ((ti - 1) * f + fi - 1) * ch;
+        for (size_t c = 0; c < ch; ++c) yy[c] += w[tap * ch + c] * xx[c];
+      }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+// src/parakeet/cpu.rs:60-98 `Encoder::run` up to the conformer: conv0 (3x3 stride 2, 1 -> ch) +
+// ReLU over the valid mel frames, conv2 (depthwise) with its rows from half(half(valid)) on zero,
+// conv3 (pointwise) + ReLU, conv5 (depthwise), conv6 (pointwise) + ReLU, [t][f][ch] to
+// [t][ch * f], and the output projection: x [t][d], t = half(half(half(frames - 1))).
+size_t wo_subsample(const float *mel, size_t frames, size_t valid, size_t ch, const float *w0,
+                    const float *b0, const float *w2, const float *b2, const void *conv3,
+                    const float *w5, const float *b5, const void *conv6, const void *out,
+                    float *x) {
+  const size_t mels = 128;
+  const size_t t1 = half_up(valid), f1 = half_up(mels), f2 = half_up(f1), t2 = half_up(half_up(frames));
+  const size_t t = half_up(half_up(half_up(frames - 1))), f = half_up(f2);
+  // conv0 + ReLU for rows below t1 (the reference computes them per conv2 row, the same values).
+  std::vector<float> c0(t1 * f1 * ch);
+  for (size_t r = 0; r < t1; ++r)
+    for (size_t c = 0; c < f1; ++c) {
+      float *px = c0.data() + (r * f1 + c) * ch;
+      for (size_t q = 0; q < ch; ++q) px[q] = b0[q];
+      for (size_t tap = 0; tap < 9; ++tap) {
+        const size_t tm = 2 * r + tap / 3 - 1, fm = 2 * c + tap % 3 - 1;  // wraps below 0
+        const float v = tm < valid && fm < mels ? mel[tm * mels + fm] : 0.0f;
+        for (size_t q = 0; q < ch; ++q) px[q] += w0[tap * ch + q] * v;
+      }
+      for (size_t q = 0; q < ch; ++q) px[q] = std::max(px[q], 0.0f);
+    }
+  // conv2 over conv0 (rows past t1 zero), its rows from half(t1) on zero.
+  std::vector<float> a(t2 * f2 * ch, 0.0f);
+  const size_t live = half_up(t1);
+  for (size_t k = 0; k < t2 && k < live; ++k)
+    for (size_t fo = 0; fo < f2; ++fo) {
+      float *yy = a.data() + (k * f2 + fo) * ch;
+      for (size_t q = 0; q < ch; ++q) yy[q] = b2[q];
+      for (size_t tap = 0; tap < 9; ++tap) {
+        const size_t r = 2 * k + tap / 3 - 1;  // conv0 row, wraps below 0
+        const size_t c = 2 * fo + tap % 3 - 1;
+        if (c >= f1) continue;
+        const float *xx = r < t1 ? c0.data() + (r * f1 + c) * ch : nullptr;
+        for (size_t q = 0; q < ch; ++q) yy[q] += w2[tap * ch + q] * (xx ? xx[q] : 0.0f);
+      }
+    }
+  std::vector<float> b(a.size());
+  wo_gemm(a.data(), conv3, b.data(), t2 * f2, 2 /* relu */, 1.0f);
+  std::vector<float> h(t * f * ch);
+  depthwise(b.data(), w5, b5, t2, f2, ch, h.data(), t);
+  std::vector<float> y(h.size());
+  wo_gemm(h.data(), conv6, y.data(), t * f, 2, 1.0f);
+  for (size_t r = 0; r < t; ++r)
+    for (size_t e = 0; e < f * ch; ++e) h[r * f * ch + e] = y[r * f * ch + (e % f) * ch + e / f];
+  wo_gemm(h.data(), out, x, t, 0 /* bias */, 1.0f);
+  return t;
+}
+
+}  // extern "C"

@@ -95,3 +95,39 @@ def test_mel_features_short_and_silent(gpu):
     assert gpu.mel_features(torch.from_numpy(silent).cuda(), mel) == 101
     gpu.sync()
     np.testing.assert_array_equal(mel.cpu().numpy(), O.mel_features(silent))
+
+
+@pytest.mark.parametrize("frames,valid,seed", [(801, 801, 1), (801, 520, 2), (97, 97, 3)])
+def test_subsample_matches_oracle(gpu, frames, valid, seed):
+    # Parakeet's 8x conv subsampling (src/parakeet/cpu.rs:60-174) at its width (256 channels),
+    # F16 pointwise and output weights, against the oracle's CPU restatement (its f16 GEMM path).
+    ch, d = 256, 512
+    rng = np.random.default_rng(seed)
+    mel = rng.standard_normal((frames, 128)).astype(np.float32)
+    taps = {k: (rng.standard_normal((9, ch)) * 0.3).astype(np.float32) for k in ("w0", "w2", "w5")}
+    taps.update({k: (rng.standard_normal(ch) * 0.1).astype(np.float32) for k in ("b0", "b2", "b5")})
+    w3 = (rng.standard_normal((ch, ch)) * 0.06).astype(np.float16)
+    w6 = (rng.standard_normal((ch, ch)) * 0.06).astype(np.float16)
+    wo = (rng.standard_normal((d, 16 * ch)) * 0.02).astype(np.float16)
+    b3, b6 = (rng.standard_normal((2, ch)) * 0.1).astype(np.float32)
+    bo = (rng.standard_normal(d) * 0.1).astype(np.float32)
+    O.set_vnni(0)
+    try:
+        want = O.subsample(mel, valid, taps,
+                           O.Linear(O.TY_F16, ch, ch, w3.tobytes(), b3),
+                           O.Linear(O.TY_F16, ch, ch, w6.tobytes(), b6),
+                           O.Linear(O.TY_F16, d, 16 * ch, wo.tobytes(), bo))
+    finally:
+        O.set_vnni(-1)
+    l3 = gpu.linear(O.TY_F16, ch, ch, w3.tobytes(), b3)
+    l6 = gpu.linear(O.TY_F16, ch, ch, w6.tobytes(), b6)
+    lo = gpu.linear(O.TY_F16, d, 16 * ch, wo.tobytes(), bo)
+    dt = {k: torch.from_numpy(v).cuda() for k, v in taps.items()}
+    x = torch.zeros(want.shape[0], d, device="cuda")
+    t = gpu.subsample(torch.from_numpy(mel).cuda(), valid, dt, l3, l6, lo, x)
+    gpu.sync()
+    assert t == want.shape[0]
+    got = x.cpu().numpy()
+    err = np.abs(got - want).max() / max(1.0, np.abs(want).max())
+    rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 2e-3 and rel <= 1e-3, (err, rel)

@@ -427,3 +427,77 @@ def test_frontend_filterbank_and_window():
     np.testing.assert_allclose(w[56:456], w[56:456][::-1], atol=1e-15)
     assert ((f > 0).sum(axis=0) <= 2).all() and (f >= 0).all()
     assert f.shape == (128, 257) and (f.sum(axis=1) > 0).all()
+
+
+def _subsample_numpy(mel, valid, tp, w3, b3, w6, b6, wo, bo):
+    """Parakeet's subsampling written again with numpy (the same convolutions, a different code)
+    to check the oracle's restatement; the GEMMs here are f64 on the f16-rounded operands."""
+    h = lambda n: (n - 1) // 2 + 1  # noqa: E731
+    frames, ch = mel.shape[0], tp["b0"].size
+    t1, f1 = h(valid), 64
+    f2, t2, t, f = 32, h(h(frames)), h(h(h(frames - 1))), 16
+    m = np.zeros((valid + 2, 130), np.float64)
+    m[1:valid + 1, 1:129] = mel[:valid]
+    c0 = np.zeros((t1 + 2, f1 + 2, ch))
+    for r in range(t1):
+        for c in range(f1):
+            acc = tp["b0"].astype(np.float64).copy()
+            for tap in range(9):
+                tm, fm = 2 * r + tap // 3, 2 * c + tap % 3
+                v = m[tm, fm] if tm < valid + 2 else 0.0
+                acc += tp["w0"][tap] * v
+            c0[r + 1, c + 1] = np.maximum(acc, 0)
+    a = np.zeros((t2, f2, ch))
+    for k in range(min(t2, h(t1))):
+        for fo in range(f2):
+            acc = tp["b2"].astype(np.float64).copy()
+            for tap in range(9):
+                acc += tp["w2"][tap] * c0[2 * k + tap // 3, 2 * fo + tap % 3]
+            a[k, fo] = acc
+    half_ = lambda x: x.astype(np.float16).astype(np.float64)  # noqa: E731
+    b = np.maximum(half_(a.reshape(-1, ch)) @ half_(w3).T + b3, 0).reshape(t2, f2, ch)
+    bp = np.zeros((t2 + 2, f2 + 2, ch))
+    bp[1:t2 + 1, 1:f2 + 1] = b
+    y = np.zeros((t, f, ch))
+    for k in range(t):
+        for fo in range(f):
+            acc = tp["b5"].astype(np.float64).copy()
+            for tap in range(9):
+                acc += tp["w5"][tap] * bp[2 * k + tap // 3, 2 * fo + tap % 3]
+            y[k, fo] = acc
+    y = np.maximum(half_(y.reshape(-1, ch)) @ half_(w6).T + b6, 0).reshape(t, f, ch)
+    flat = y.transpose(0, 2, 1).reshape(t, ch * f)
+    return half_(flat) @ half_(wo).T + bo
+
+
+def subsample_case(frames, valid, ch, d, seed):
+    rng = np.random.default_rng(seed)
+    mel = rng.standard_normal((frames, 128)).astype(np.float32)
+    tp = {k: (rng.standard_normal((9, ch)) * 0.3).astype(np.float32) for k in ("w0", "w2", "w5")}
+    tp.update({k: (rng.standard_normal(ch) * 0.1).astype(np.float32) for k in ("b0", "b2", "b5")})
+    w3, w6 = (rng.standard_normal((2, ch, ch)) * 0.1).astype(np.float32)
+    wo = (rng.standard_normal((d, 16 * ch)) * 0.05).astype(np.float32)
+    b3, b6, bo = (rng.standard_normal((3, max(ch, d))) * 0.1).astype(np.float32)
+    b3, b6, bo = b3[:ch].copy(), b6[:ch].copy(), bo[:d].copy()
+    return mel, tp, w3, b3, w6, b6, wo, bo
+
+
+@pytest.mark.parametrize("frames,valid", [(97, 97), (97, 60), (33, 33)])
+def test_subsample_restatement(frames, valid):
+    ch, d = 32, 64
+    mel, tp, w3, b3, w6, b6, wo, bo = subsample_case(frames, valid, ch, d, frames + valid)
+    O.set_vnni(0)
+    try:
+        l3 = O.Linear(O.TY_F16, ch, ch, w3.astype(np.float16).tobytes(), b3)
+        l6 = O.Linear(O.TY_F16, ch, ch, w6.astype(np.float16).tobytes(), b6)
+        lo = O.Linear(O.TY_F16, d, 16 * ch, wo.astype(np.float16).tobytes(), bo)
+        got = O.subsample(mel, valid, tp, l3, l6, lo)
+    finally:
+        O.set_vnni(-1)
+    want = _subsample_numpy(mel, valid, tp, w3.astype(np.float16).astype(np.float32), b3,
+                            w6.astype(np.float16).astype(np.float32), b6,
+                            wo.astype(np.float16).astype(np.float32), bo)
+    h = lambda n: (n - 1) // 2 + 1  # noqa: E731
+    assert got.shape == (h(h(h(frames - 1))), d)
+    err = np.abs(got - want).max() / max(1.0, np.abs(want).max())
+    assert err < 2e-3, err

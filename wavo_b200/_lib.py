@@ -47,6 +47,9 @@ SIGNATURES = {
     "wavo_linear_from_gguf": ([_vp, _vp, _vp, _u32, _vp, _sz, ctypes.POINTER(_vp)], _st),
     "wavo_log_mel": ([_vp, _vp, _u64, _u64, _u64, _vp], _st),
     "wavo_mel_features": ([_vp, _vp, _u64, _vp, ctypes.POINTER(_u64)], _st),
+    "wavo_subsample_scratch_bytes": ([_u32, _u32], _u64),
+    "wavo_subsample": ([_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                        _vp, _vp, ctypes.POINTER(_u32)], _st),
     "wavo_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], _st),
     "wavo_gguf_close": ([_vp], None),
     "wavo_gguf_tensor_count": ([_vp], _u32),

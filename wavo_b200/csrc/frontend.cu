@@ -15,6 +15,9 @@
 //                    loads in flight).
 //   mel_stats_kernel the chunk sums in order: the mean, then 1 / (unbiased std + 1e-5).
 //   mel_norm_kernel  (x - mean)·inv to f32; the last frame zero.
+//   conv02_kernel / dw3s2_kernel / flatten_kernel
+//                    Parakeet's 8x conv subsampling around the pointwise GEMMs
+//                    (src/parakeet/cpu.rs:60-174).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -142,6 +145,91 @@ __global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
   mel[i] = t == frames - 1 ? 0.0f : float(__dmul_rn(__dsub_rn(double(mel[i]), mean[m]), inv[m]));
 }
 
+// ---- Parakeet's 8x conv subsampling (src/parakeet/cpu.rs:100-174) -------------------------------
+//
+// Each output element by one thread (channels fastest: coalesced rows), in the reference's
+// operation order: a bias, then each tap's product added (separate roundings, no fused
+// multiply-add), taps in order.
+
+// conv0 (3x3, stride 2, one input channel) + ReLU at conv0 row r, column c, channel q: zero outside
+// rows 0 .. t1 - 1 (the reference zero-fills those rows).
+__device__ __forceinline__ float conv0_at(const float *__restrict__ mel, int valid, int t1, int r,
+                                          int c, int q, int ch, const float *__restrict__ w0,
+                                          const float *__restrict__ b0) {
+  if (r < 0 || r >= t1) return 0.0f;
+  float p = b0[q];
+#pragma unroll
+  for (int tap = 0; tap < 9; ++tap) {
+    const int tm = 2 * r + tap / 3 - 1, fm = 2 * c + tap % 3 - 1;
+    const float v = tm >= 0 && tm < valid && fm >= 0 && fm < 128 ? mel[(long long)tm * 128 + fm] : 0.0f;
+    p = __fadd_rn(p, __fmul_rn(w0[tap * ch + q], v));
+  }
+  return fmaxf(p, 0.0f);
+}
+
+// conv2 (depthwise 3x3, stride 2) over conv0 + ReLU into a [t2][32][ch]; rows from live on zero.
+__global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, int t2, int live,
+                              int ch, const float *__restrict__ w0, const float *__restrict__ b0,
+                              const float *__restrict__ w2, const float *__restrict__ b2,
+                              float *__restrict__ a) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)t2 * 32 * ch;
+  if (i >= total) return;
+  const int q = int(i % ch);
+  const int fo = int((i / ch) % 32);
+  const int k = int(i / ((long long)32 * ch));
+  if (k >= live) {
+    a[i] = 0.0f;
+    return;
+  }
+  float y = b2[q];
+#pragma unroll 1
+  for (int tap = 0; tap < 9; ++tap) {
+    const int c = 2 * fo + tap % 3 - 1;
+    if (c < 0 || c >= 64) continue;
+    const float v = conv0_at(mel, valid, t1, 2 * k + tap / 3 - 1, c, q, ch, w0, b0);
+    y = __fadd_rn(y, __fmul_rn(w2[tap * ch + q], v));
+  }
+  a[i] = y;
+}
+
+// Depthwise 3x3, stride 2, padding 1, + bias over x [t][f][ch] into y [rows][half(f)][ch].
+__global__ void dw3s2_kernel(const float *__restrict__ x, int t, int f, int ch, int rows,
+                             const float *__restrict__ w, const float *__restrict__ b,
+                             float *__restrict__ y) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int fo_n = (f - 1) / 2 + 1;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * fo_n * ch) return;
+  const int q = int(i % ch);
+  const int fo = int((i / ch) % fo_n);
+  const int k = int(i / ((long long)fo_n * ch));
+  float v = b[q];
+#pragma unroll
+  for (int tap = 0; tap < 9; ++tap) {
+    const int ti = 2 * k + tap / 3, fi = 2 * fo + tap % 3;
+    if (ti < 1 || ti > t || fi < 1 || fi > f) continue;
+    v = __fadd_rn(v, __fmul_rn(w[tap * ch + q], x[((long long)(ti - 1) * f + fi - 1) * ch + q]));
+  }
+  y[i] = v;
+}
+
+// [t][f][ch] to [t][ch·f] (src/parakeet/cpu.rs:85-90).
+__global__ void flatten_kernel(const float *__restrict__ y, int t, int f, int ch,
+                               float *__restrict__ h) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long row = (long long)f * ch;
+  if (i >= (long long)t * row) return;
+  const long long r = i / row;
+  const int e = int(i - r * row);
+  h[i] = y[r * row + (e % f) * ch + e / f];
+}
+
 }  // namespace
 
 // ---- tables (host), as src/fft.rs:46-66 and src/parakeet/frontend.rs:30-47, 110-140 build them --
@@ -267,6 +355,32 @@ cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStr
   const long long total = frames * FE_MELS;
   return launch_pdl(mel_norm_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, mel,
                     frames, (const double *)mean, (const double *)inv);
+}
+
+}  // namespace wv
+
+namespace wv {
+
+cudaError_t launch_conv02(const float *mel, int valid, int t2, int ch, const float *w0,
+                          const float *b0, const float *w2, const float *b2, float *a,
+                          cudaStream_t s) {
+  const int t1 = (valid - 1) / 2 + 1, live = (t1 - 1) / 2 + 1;
+  const long long total = (long long)t2 * 32 * ch;
+  return launch_pdl(conv02_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, mel, valid,
+                    t1, t2, live, ch, w0, b0, w2, b2, a);
+}
+
+cudaError_t launch_dw3s2(const float *x, int t, int f, int ch, int rows, const float *w,
+                         const float *b, float *y, cudaStream_t s) {
+  const long long total = (long long)rows * ((f - 1) / 2 + 1) * ch;
+  return launch_pdl(dw3s2_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, x, t, f, ch,
+                    rows, w, b, y);
+}
+
+cudaError_t launch_flatten(const float *y, int t, int f, int ch, float *h, cudaStream_t s) {
+  const long long total = (long long)t * f * ch;
+  return launch_pdl(flatten_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, y, t, f,
+                    ch, h);
 }
 
 }  // namespace wv

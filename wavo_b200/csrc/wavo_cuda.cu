@@ -1278,6 +1278,76 @@ wavo_status wavo_mel_features(wavo_ctx *ctx, const float *pcm, uint64_t samples,
   return WAVO_OK;
 }
 
+// ---- Parakeet's conv subsampling ------------------------------------------------------------
+
+namespace {
+inline uint64_t half_up(uint64_t n) { return (n - 1) / 2 + 1; }
+struct SubsampleLayout {
+  uint64_t t2, t, a_bytes, h_bytes, total;
+};
+SubsampleLayout subsample_layout(uint64_t frames, uint64_t ch) {
+  SubsampleLayout L{};
+  L.t2 = half_up(half_up(frames));
+  L.t = half_up(half_up(half_up(frames - 1)));
+  L.a_bytes = align_up(L.t2 * 32 * ch * 4, 256);
+  L.h_bytes = align_up(L.t * 16 * ch * 4, 256);
+  L.total = 2 * L.a_bytes + 3 * L.h_bytes;
+  return L;
+}
+}  // namespace
+
+uint64_t wavo_subsample_scratch_bytes(uint32_t frames, uint32_t ch) {
+  return frames >= 2 && ch ? subsample_layout(frames, ch).total : 0;
+}
+
+wavo_status wavo_subsample(wavo_ctx *ctx, const float *mel, uint32_t frames, uint32_t valid,
+                           uint32_t ch, const float *w0, const float *b0, const float *w2,
+                           const float *b2, const wavo_linear *conv3, const float *w5,
+                           const float *b5, const wavo_linear *conv6, const wavo_linear *out,
+                           float *x, void *scratch, uint32_t *t_out) {
+  if (!ctx) return WAVO_EINVAL;
+  if (!mel || !w0 || !b0 || !w2 || !b2 || !w5 || !b5 || !conv3 || !conv6 || !out || !x || !scratch)
+    return fail(ctx, WAVO_EINVAL, "subsample: NULL argument");
+  if (frames < 2 || valid == 0 || valid > frames || ch == 0 || ch % 32 != 0 || ch > 4096)
+    return fail(ctx, WAVO_EINVAL, "subsample: %u frames (%u valid), %u channels", frames, valid, ch);
+  if (conv3->k != ch || conv3->cols != ch || conv3->dual || conv6->k != ch || conv6->cols != ch ||
+      conv6->dual || out->k != 16 * ch || out->dual)
+    return fail(ctx, WAVO_EINVAL, "subsample: the pointwise layers must be %u -> %u and the output "
+                "projection %u -> d", ch, ch, 16 * ch);
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u)
+    return fail(ctx, WAVO_EINVAL, "subsample: scratch must be 256-byte aligned");
+  const SubsampleLayout L = subsample_layout(frames, ch);
+  uint8_t *sp = static_cast<uint8_t *>(scratch);
+  float *a = reinterpret_cast<float *>(sp), *b = reinterpret_cast<float *>(sp + L.a_bytes);
+  float *h = reinterpret_cast<float *>(sp + 2 * L.a_bytes);
+  float *y = reinterpret_cast<float *>(sp + 2 * L.a_bytes + L.h_bytes);
+  float *flat = reinterpret_cast<float *>(sp + 2 * L.a_bytes + 2 * L.h_bytes);
+  const int t2 = int(L.t2), t = int(L.t);
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    cudaSetDevice(ctx->device);
+    CK(wv::launch_conv02(mel, int(valid), t2, int(ch), w0, b0, w2, b2, a, ctx->stream),
+       "subsample conv0/conv2 launch");
+  }
+  wavo_status st = wavo_gemm(ctx, a, WAVO_F32, ch, conv3, b, WAVO_F32, ch, uint32_t(t2) * 32,
+                             WAVO_EPI_RELU, 1.0f);
+  if (st != WAVO_OK) return st;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    CK(wv::launch_dw3s2(b, t2, 32, int(ch), t, w5, b5, h, ctx->stream), "subsample conv5 launch");
+  }
+  st = wavo_gemm(ctx, h, WAVO_F32, ch, conv6, y, WAVO_F32, ch, uint32_t(t) * 16, WAVO_EPI_RELU, 1.0f);
+  if (st != WAVO_OK) return st;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    CK(wv::launch_flatten(y, t, 16, int(ch), flat, ctx->stream), "subsample flatten launch");
+  }
+  st = wavo_gemm(ctx, flat, WAVO_F32, 16 * ch, out, x, WAVO_F32, 0, uint32_t(t), WAVO_EPI_BIAS, 1.0f);
+  if (st != WAVO_OK) return st;
+  if (t_out) *t_out = uint32_t(t);
+  return WAVO_OK;
+}
+
 // ---- rope --------------------------------------------------------------------------------
 
 wavo_status wavo_rope_rows(wavo_ctx *ctx, const float *table, void *qkv, int dtype,

@@ -151,6 +151,23 @@ class Gpu:
                                         ctypes.byref(n)), self.ctx)
         return n.value
 
+    def subsample(self, mel: torch.Tensor, valid: int, taps: dict, conv3: Linear, conv6: Linear,
+                  out: Linear, x: torch.Tensor, scratch: torch.Tensor | None = None) -> int:
+        """Parakeet's 8x conv subsampling of mel [frames][128] into x [t][d]; taps: device f32
+        w0, b0, w2, b2, w5, b5 ([9][ch] taps, [ch] biases). Returns t."""
+        frames, ch = mel.shape[0], taps["b0"].numel()
+        if scratch is None:
+            nbytes = int(L.lib().wavo_subsample_scratch_bytes(frames, ch))
+            scratch = torch.empty(nbytes + 256, dtype=torch.uint8, device=self.torch_device)
+        base = (scratch.data_ptr() + 255) // 256 * 256
+        t = ctypes.c_uint32()
+        check(L.lib().wavo_subsample(self.ctx, _ptr(mel), frames, valid, ch, _ptr(taps["w0"]),
+                                     _ptr(taps["b0"]), _ptr(taps["w2"]), _ptr(taps["b2"]), conv3.h,
+                                     _ptr(taps["w5"]), _ptr(taps["b5"]), conv6.h, out.h, _ptr(x),
+                                     base, ctypes.byref(t)), self.ctx)
+        self._keep = scratch  # the launches read it until the stream passes them
+        return t.value
+
     def linear_from_gguf(self, gguf, names: list[str], bias=None) -> Linear:
         """`Gpu::linear` over GGUF tensors, streamed from the file to the device."""
         return Linear.from_gguf(self, gguf, names, bias)
