@@ -938,12 +938,17 @@ class C4Full(Workload):
 
 
 class C5Mel(Workload):
-    """§8 f4: the log-mel features of C5's audio on the device (src/parakeet/frontend.rs): 400
-    segments of U[120, 300] encoder frames (8 mel frames each, 1280 samples of 16 kHz pcm a frame),
-    each segment's features computed and normalised on their own as the reference computes a piece
-    (wavo_mel_features: pre-emphasis, Hann(400), f64 FFT of 512, power, 128 Slaney mel bins, ln,
-    per-bin normalisation). Input: the segments' pcm; output: their [frames][128] features."""
-    METRIC = "log-mel audio-sec/sec"
+    """§8 f4: the step before the encoder on the device for C5's audio: 400 segments of U[120, 300]
+    encoder frames (1280 samples of 16 kHz pcm an encoder frame), each as the reference runs a
+    piece: the log-mel features computed and normalised on their own (wavo_mel_features:
+    pre-emphasis, Hann(400), f64 FFT of 512, power, 128 Slaney mel bins, ln, per-bin
+    normalisation; src/parakeet/frontend.rs), then Parakeet-0.6B's 8x conv subsampling
+    (wavo_subsample: 256 channels, F16 pointwise and output weights ~N(0, 0.02), d 1024;
+    src/parakeet/encoder.rs:103-121). Input: the segments' pcm; output: the encoder's input rows
+    [Σ frames][1024]."""
+    METRIC = "frontend audio-sec/sec"
+    CH, D = 256, 1024
+    BOUNDS = {"mel_features": "hbm", "subsample": "tensor"}
     FRAME_S = 0.08
     bound = "hbm"
     dtype = "f64 FFT, f32 mel"
@@ -968,32 +973,64 @@ class C5Mel(Workload):
         self.pcm = self.pcm_host.to(dev)
         rows = sum(self.frames)
         self.mel = torch.zeros(rows, 128, device=dev)
-        self.mel_host = torch.empty(rows, 128).pin_memory()
         self.s0 = np.concatenate([[0], np.cumsum(self.samples)[:-1]]).astype(int)
         self.r0 = np.concatenate([[0], np.cumsum(self.frames)[:-1]]).astype(int)
+        self.x0 = np.concatenate([[0], np.cumsum(self.lengths)[:-1]]).astype(int)
+        wrng = np.random.default_rng(seed)
+        ch, d = self.CH, self.D
+        self.taps = {k: gpu.upload((wrng.standard_normal((9, ch)) * 0.3).astype(np.float32))
+                     for k in ("w0", "w2", "w5")}
+        self.taps.update({k: gpu.upload((wrng.standard_normal(ch) * 0.1).astype(np.float32))
+                          for k in ("b0", "b2", "b5")})
+        from wavo_b200 import GGML_F16
+        self.conv3 = gpu.linear(GGML_F16, ch, ch, normal_f16(wrng, (ch, ch), 0.02).tobytes(),
+                                wrng.standard_normal(ch).astype(np.float32) * 0.02)
+        self.conv6 = gpu.linear(GGML_F16, ch, ch, normal_f16(wrng, (ch, ch), 0.02).tobytes(),
+                                wrng.standard_normal(ch).astype(np.float32) * 0.02)
+        self.out = gpu.linear(GGML_F16, d, 16 * ch, normal_f16(wrng, (d, 16 * ch), 0.02).tobytes(),
+                              wrng.standard_normal(d).astype(np.float32) * 0.02)
+        from wavo_b200 import _lib as L
+        nbytes = int(L.lib().wavo_subsample_scratch_bytes(max(self.frames), ch))
+        self.scratch = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+        self.x = torch.zeros(sum(self.lengths), d, device=dev)
+        self.x_host = torch.empty(sum(self.lengths), d).pin_memory()
+        self.seg_rows, self.out_width = list(lengths), d
 
     def record(self, p, timer=None):
         tick = timer or (lambda name, fn: fn())
         for i in range(len(self.samples)):
             a, n, r, f = int(self.s0[i]), self.samples[i], int(self.r0[i]), self.frames[i]
+            x0, t = int(self.x0[i]), self.lengths[i]
             tick("mel_features", lambda a=a, n=n, r=r, f=f: self.gpu.mel_features(
                 self.pcm[a:a + n], self.mel[r:r + f]))
+            tick("subsample", lambda r=r, f=f, x0=x0, t=t: self.gpu.subsample(
+                self.mel[r:r + f], f, self.taps, self.conv3, self.conv6, self.out,
+                self.x[x0:x0 + t], self.scratch))
 
     def inputs(self):
         return [(self.pcm, self.pcm_host)]
 
     def outputs(self):
-        return [(self.mel_host, self.mel)]
+        return [(self.x_host, self.x)]
 
     def launches(self):
-        return 6 * len(self.samples)
+        # mel_features: the log-mel and five normalisation kernels; subsample: conv0/conv2, conv5,
+        # the flatten, and three GEMMs (each a cast of its rows to f16 and the GEMM itself).
+        return (6 + 3 + 6) * len(self.samples)
 
     def work(self):
-        # HBM bytes: the pcm read (a frame's 512-sample window overlaps the next three: each
-        # sample once) and the features written, read and written again by the normalisation.
-        # Per call (a segment), averaged over the segments.
-        per = 4.0 * sum(self.samples) + 3 * 2 * 4.0 * 128 * sum(self.frames)
-        return {"mel_features": per / len(self.samples)}
+        # Per call (a segment), averaged over the segments. mel_features: HBM bytes (the pcm read
+        # once, the features written, read and written again by the normalisation); subsample:
+        # flop (the convs' and GEMMs' multiply-adds).
+        n = len(self.samples)
+        mel = 4.0 * sum(self.samples) + 3 * 2 * 4.0 * 128 * sum(self.frames)
+        ch, d = self.CH, self.D
+        flop = 0.0
+        for f, t in zip(self.frames, self.lengths):
+            t1, t2 = (f - 1) // 2 + 1, ((f - 1) // 2) // 2 + 1
+            flop += 2 * 9 * 9 * t2 * 32 * ch + 2 * t2 * 32 * ch * ch + 2 * 9 * t * 16 * ch
+            flop += 2 * t * 16 * ch * ch + 2 * t * 16 * ch * d
+        return {"mel_features": mel / n, "subsample": flop / n}
 
     def audio_s(self):
         return sum(self.lengths) * self.FRAME_S
@@ -1005,24 +1042,36 @@ class C5Mel(Workload):
         return {"workload": WORKLOAD_NAMES["c5mel"], "segments": len(self.all_lengths),
                 "total_mel_frames": int(sum(t * 8 + 1 for t in self.all_lengths)),
                 "audio_s": sum(self.all_lengths) * self.FRAME_S, "n_fft": 512, "mels": 128,
+                "subsampling": f"8x, {self.CH} channels, d {self.D}, F16 pointwise weights",
                 "l2": "inputs larger than L2 (430 MB of pcm)",
                 "parallelism": f"segments sharded LPT over {self.world} GPU(s), no collective"}
 
     @staticmethod
     def cpu_sample(seed=5000):
-        # 16 of the 400 segments (every 25th) through the oracle's frontend (the reference's
-        # Frontend::compute restated), scaled by audio seconds.
+        # 16 of the 400 segments (every 25th) through the oracle's frontend and subsampling (the
+        # reference's Frontend::compute and the CPU encoder's subsampling restated; its GEMMs on the
+        # host's threads), scaled by audio seconds.
         from oracle import oracle as O
         lens = segment_lengths(seed, 400, 120, 300)[::25]
         rng = np.random.default_rng(seed)
         pcms = [(0.05 * rng.standard_normal(t * 1280) + 0.2 * np.sin(
             2 * np.pi * 440.0 * np.arange(t * 1280) / 16000.0)).astype(np.float32) for t in lens]
+        ch, d = C5Mel.CH, C5Mel.D
+        taps = {k: (rng.standard_normal((9, ch)) * 0.3).astype(np.float32) for k in ("w0", "w2", "w5")}
+        taps.update({k: (rng.standard_normal(ch) * 0.1).astype(np.float32) for k in ("b0", "b2", "b5")})
+        l3 = O.Linear(O.TY_F16, ch, ch, normal_f16(rng, (ch, ch), 0.02).tobytes(), np.zeros(ch, np.float32))
+        l6 = O.Linear(O.TY_F16, ch, ch, normal_f16(rng, (ch, ch), 0.02).tobytes(), np.zeros(ch, np.float32))
+        lo = O.Linear(O.TY_F16, d, 16 * ch, normal_f16(rng, (d, 16 * ch), 0.02).tobytes(),
+                      np.zeros(d, np.float32))
         from concurrent.futures import ThreadPoolExecutor
         t0 = time.perf_counter()
         with ThreadPoolExecutor(os.cpu_count() or 1) as ex:  # ctypes calls release the GIL
-            list(ex.map(O.mel_features, pcms))
+            mels = list(ex.map(O.mel_features, pcms))
+        for m in mels:
+            O.subsample(m, m.shape[0], taps, l3, l6, lo)
         dt = time.perf_counter() - t0
-        return dt, sum(lens) * 0.08, "16 of the 400 segments (every 25th), a thread a segment"
+        return dt, sum(lens) * 0.08, ("16 of the 400 segments (every 25th): log-mel a thread a "
+                                      "segment, subsampling with multithreaded GEMMs")
 
 
 class C5Load:
@@ -1208,8 +1257,9 @@ WORKLOAD_NAMES = {
               "device (LayerNorms, attention, FFN, logits, pick)",
     "c5block": "C5 blocks: Parakeet-0.6B FastConformer blocks (FFN, rel-pos MHSA, conv module, "
                "norms), 24 blocks, 400 segments of U[120,300] frames, Q8_0 weights",
-    "c5mel": "C5 log-mel: Parakeet's frontend (f64 FFT of 512, 128 Slaney mel bins, per-segment "
-             "normalisation) over C5's 400 segments of U[120,300] encoder frames of 16 kHz audio",
+    "c5mel": "C5 frontend: Parakeet's log-mel (f64 FFT of 512, 128 Slaney mel bins, per-segment "
+             "normalisation) and 8x conv subsampling (256 channels, d 1024) over C5's 400 "
+             "segments of U[120,300] encoder frames of 16 kHz audio",
     "c5load": "C5 weights from GGUF: 24 layers of Q8_0 q/k/v/out/linear_pos (d 1024) loaded from a "
               "GGUF file into device-ready layers",
 }
@@ -1472,7 +1522,8 @@ def main():
         clk = clocks.summary()
         tclk = top_clocks.summary()
         clock_frac = None
-        if wl.bound == "hbm":
+        bound = getattr(wl, "BOUNDS", {}).get(top, wl.bound)
+        if bound == "hbm":
             achieved = work[top] / (per_top * 1e-3) / 1e9
             peak, unit, src = peaks["hbm"], "GB/s", "HBM copy"
         else:
@@ -1511,7 +1562,7 @@ def main():
                     "pipelined": "step k+1's H2D and step k's D2H on two copy streams overlap "
                                  "step k (pinned staging, device copies in and out)"},
             "gpu_launches": wl.launches() * args.steps,
-            "roofline": {"bound": wl.bound, "kernel": top, "achieved": achieved, "peak": peak,
+            "roofline": {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak,
                          "unit": unit, "frac": achieved / peak,
                          "frac_of_sustained": clock_frac, "ms_per_launch": per_top,
                          "clocks_while_timed": tclk,

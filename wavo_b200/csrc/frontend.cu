@@ -151,48 +151,59 @@ __global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
 // operation order: a bias, then each tap's product added (separate roundings, no fused
 // multiply-add), taps in order.
 
-// conv0 (3x3, stride 2, one input channel) + ReLU at conv0 row r, column c, channel q: zero outside
-// rows 0 .. t1 - 1 (the reference zero-fills those rows).
-__device__ __forceinline__ float conv0_at(const float *__restrict__ mel, int valid, int t1, int r,
-                                          int c, int q, int ch, const float *__restrict__ w0,
-                                          const float *__restrict__ b0) {
-  if (r < 0 || r >= t1) return 0.0f;
-  float p = b0[q];
-#pragma unroll
-  for (int tap = 0; tap < 9; ++tap) {
-    const int tm = 2 * r + tap / 3 - 1, fm = 2 * c + tap % 3 - 1;
-    const float v = tm >= 0 && tm < valid && fm >= 0 && fm < 128 ? mel[(long long)tm * 128 + fm] : 0.0f;
-    p = __fadd_rn(p, __fmul_rn(w0[tap * ch + q], v));
-  }
-  return fmaxf(p, 0.0f);
-}
-
-// conv2 (depthwise 3x3, stride 2) over conv0 + ReLU into a [t2][32][ch]; rows from live on zero.
+// conv2 (depthwise 3x3, stride 2) over conv0 (3x3, stride 2, one input channel) + ReLU into
+// a [t2][32][ch], rows from live on zero. A CTA takes conv2 row k, a thread a channel (its taps and
+// biases in registers) over the row's 32 columns; the seven mel rows 4k - 3 .. 4k + 3 the row
+// reads are staged in shared memory with zeros past the valid frames and the band's edges. conv0
+// is evaluated where conv2 reads it (zero outside rows 0 .. t1 - 1, as the reference zero-fills).
 __global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, int t2, int live,
                               int ch, const float *__restrict__ w0, const float *__restrict__ b0,
                               const float *__restrict__ w2, const float *__restrict__ b2,
                               float *__restrict__ a) {
   griddep_launch_dependents();
   griddep_wait();
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long total = (long long)t2 * 32 * ch;
-  if (i >= total) return;
-  const int q = int(i % ch);
-  const int fo = int((i / ch) % 32);
-  const int k = int(i / ((long long)32 * ch));
-  if (k >= live) {
-    a[i] = 0.0f;
-    return;
+  __shared__ float ms[7][130];  // mel rows 4k - 3 + i, columns -1 .. 128
+  const int k = int(blockIdx.x);
+  for (int e = threadIdx.x; e < 7 * 130; e += blockDim.x) {
+    const int i = e / 130, c = e % 130 - 1;
+    const int tm = 4 * k - 3 + i;
+    ms[i][c + 1] = tm >= 0 && tm < valid && c >= 0 && c < 128 ? mel[(long long)tm * 128 + c] : 0.0f;
   }
-  float y = b2[q];
+  __syncthreads();
+  for (int q = threadIdx.x; q < ch; q += blockDim.x) {
+    float* out = a + (long long)k * 32 * ch + q;
+    if (k >= live) {
+      for (int fo = 0; fo < 32; ++fo) out[fo * ch] = 0.0f;
+      continue;
+    }
+    float c0w[9], c2w[9];
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+      c0w[tap] = w0[tap * ch + q];
+      c2w[tap] = w2[tap * ch + q];
+    }
+    const float bias0 = b0[q], bias2 = b2[q];
 #pragma unroll 1
-  for (int tap = 0; tap < 9; ++tap) {
-    const int c = 2 * fo + tap % 3 - 1;
-    if (c < 0 || c >= 64) continue;
-    const float v = conv0_at(mel, valid, t1, 2 * k + tap / 3 - 1, c, q, ch, w0, b0);
-    y = __fadd_rn(y, __fmul_rn(w2[tap * ch + q], v));
+    for (int fo = 0; fo < 32; ++fo) {
+      float y = bias2;
+#pragma unroll
+      for (int tap = 0; tap < 9; ++tap) {
+        const int c = 2 * fo + tap % 3 - 1;  // conv0 column
+        if (c < 0 || c >= 64) continue;
+        const int r = 2 * k + tap / 3 - 1;   // conv0 row
+        float v = 0.0f;
+        if (r >= 0 && r < t1) {
+          float p = bias0;
+#pragma unroll
+          for (int t0 = 0; t0 < 9; ++t0)  // mel row 2r + t0 / 3 - 1 = 4k - 3 + (2 (tap / 3) + t0 / 3)
+            p = __fadd_rn(p, __fmul_rn(c0w[t0], ms[2 * (tap / 3) + t0 / 3][2 * c + t0 % 3]));
+          v = fmaxf(p, 0.0f);
+        }
+        y = __fadd_rn(y, __fmul_rn(c2w[tap], v));
+      }
+      out[fo * ch] = y;
+    }
   }
-  a[i] = y;
 }
 
 // Depthwise 3x3, stride 2, padding 1, + bias over x [t][f][ch] into y [rows][half(f)][ch].
@@ -365,8 +376,7 @@ cudaError_t launch_conv02(const float *mel, int valid, int t2, int ch, const flo
                           const float *b0, const float *w2, const float *b2, float *a,
                           cudaStream_t s) {
   const int t1 = (valid - 1) / 2 + 1, live = (t1 - 1) / 2 + 1;
-  const long long total = (long long)t2 * 32 * ch;
-  return launch_pdl(conv02_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, mel, valid,
+  return launch_pdl(conv02_kernel, dim3(unsigned(t2)), dim3(ch < 256 ? ch : 256), 0, s, mel, valid,
                     t1, t2, live, ch, w0, b0, w2, b2, a);
 }
 
