@@ -152,14 +152,26 @@ __global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
 // multiply-add), taps in order.
 
 // conv2 (depthwise 3x3, stride 2) over conv0 (3x3, stride 2, one input channel) + ReLU into
-// a [t2][32][ch], rows from live on zero. A CTA takes conv2 row k, a thread a channel (its taps and
-// biases in registers) over the row's 32 columns; the seven mel rows 4k - 3 .. 4k + 3 the row
-// reads are staged in shared memory with zeros past the valid frames and the band's edges. conv0
-// is evaluated where conv2 reads it (zero outside rows 0 .. t1 - 1, as the reference zero-fills).
+// a [t2][32][ch] as f16 (the pointwise GEMM's operand, which rounds its rows to f16 as the
+// reference's GEMM does), rows from live on zero. A CTA takes conv2 row k, a thread a channel (its
+// taps and biases in registers) over the row's 32 columns; the seven mel rows 4k - 3 .. 4k + 3
+// the row reads are staged in shared memory with zeros past the valid frames and the band's
+// edges. conv0 is evaluated where conv2 reads it (zero outside rows 0 .. t1 - 1, as the reference
+// zero-fills), each value once along the row: a 3x3 window of it slides two columns a step.
+__device__ __forceinline__ float conv0_px(const float (&ms)[7][130], int i0, int c, int r, int t1,
+                                          const float (&w)[9], float bias) {
+  if (c < 0 || c >= 64 || r < 0 || r >= t1) return 0.0f;
+  float p = bias;
+#pragma unroll
+  for (int t0 = 0; t0 < 9; ++t0)
+    p = __fadd_rn(p, __fmul_rn(w[t0], ms[i0 + t0 / 3][2 * c + t0 % 3]));
+  return fmaxf(p, 0.0f);
+}
+
 __global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, int t2, int live,
                               int ch, const float *__restrict__ w0, const float *__restrict__ b0,
                               const float *__restrict__ w2, const float *__restrict__ b2,
-                              float *__restrict__ a) {
+                              __half *__restrict__ a) {
   griddep_launch_dependents();
   griddep_wait();
   __shared__ float ms[7][130];  // mel rows 4k - 3 + i, columns -1 .. 128
@@ -171,9 +183,9 @@ __global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, 
   }
   __syncthreads();
   for (int q = threadIdx.x; q < ch; q += blockDim.x) {
-    float* out = a + (long long)k * 32 * ch + q;
+    __half *out = a + (long long)k * 32 * ch + q;
     if (k >= live) {
-      for (int fo = 0; fo < 32; ++fo) out[fo * ch] = 0.0f;
+      for (int fo = 0; fo < 32; ++fo) out[fo * ch] = __float2half_rn(0.0f);
       continue;
     }
     float c0w[9], c2w[9];
@@ -183,25 +195,25 @@ __global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, 
       c2w[tap] = w2[tap * ch + q];
     }
     const float bias0 = b0[q], bias2 = b2[q];
+    // win[rr][cc]: conv0 at row 2k - 1 + rr (staged mel rows from 2rr on), column 2fo - 1 + cc.
+    float win[3][3];
+#pragma unroll
+    for (int rr = 0; rr < 3; ++rr) win[rr][2] = 0.0f;  // column -1 (becomes cc = 0 below)
 #pragma unroll 1
     for (int fo = 0; fo < 32; ++fo) {
+#pragma unroll
+      for (int rr = 0; rr < 3; ++rr) {
+        win[rr][0] = win[rr][2];
+        win[rr][1] = conv0_px(ms, 2 * rr, 2 * fo, 2 * k - 1 + rr, t1, c0w, bias0);
+        win[rr][2] = conv0_px(ms, 2 * rr, 2 * fo + 1, 2 * k - 1 + rr, t1, c0w, bias0);
+      }
       float y = bias2;
 #pragma unroll
       for (int tap = 0; tap < 9; ++tap) {
-        const int c = 2 * fo + tap % 3 - 1;  // conv0 column
-        if (c < 0 || c >= 64) continue;
-        const int r = 2 * k + tap / 3 - 1;   // conv0 row
-        float v = 0.0f;
-        if (r >= 0 && r < t1) {
-          float p = bias0;
-#pragma unroll
-          for (int t0 = 0; t0 < 9; ++t0)  // mel row 2r + t0 / 3 - 1 = 4k - 3 + (2 (tap / 3) + t0 / 3)
-            p = __fadd_rn(p, __fmul_rn(c0w[t0], ms[2 * (tap / 3) + t0 / 3][2 * c + t0 % 3]));
-          v = fmaxf(p, 0.0f);
-        }
-        y = __fadd_rn(y, __fmul_rn(c2w[tap], v));
+        if (fo == 0 && tap % 3 == 0) continue;  // column -1: outside conv0, no term
+        y = __fadd_rn(y, __fmul_rn(c2w[tap], win[tap / 3][tap % 3]));
       }
-      out[fo * ch] = y;
+      out[fo * ch] = __float2half_rn(y);
     }
   }
 }
@@ -209,7 +221,7 @@ __global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, 
 // Depthwise 3x3, stride 2, padding 1, + bias over x [t][f][ch] into y [rows][half(f)][ch].
 __global__ void dw3s2_kernel(const float *__restrict__ x, int t, int f, int ch, int rows,
                              const float *__restrict__ w, const float *__restrict__ b,
-                             float *__restrict__ y) {
+                             __half *__restrict__ y) {
   griddep_launch_dependents();
   griddep_wait();
   const int fo_n = (f - 1) / 2 + 1;
@@ -225,12 +237,12 @@ __global__ void dw3s2_kernel(const float *__restrict__ x, int t, int f, int ch, 
     if (ti < 1 || ti > t || fi < 1 || fi > f) continue;
     v = __fadd_rn(v, __fmul_rn(w[tap * ch + q], x[((long long)(ti - 1) * f + fi - 1) * ch + q]));
   }
-  y[i] = v;
+  y[i] = __float2half_rn(v);  // the pointwise GEMM's operand (rounded to f16 there as well)
 }
 
 // [t][f][ch] to [t][ch·f] (src/parakeet/cpu.rs:85-90).
 __global__ void flatten_kernel(const float *__restrict__ y, int t, int f, int ch,
-                               float *__restrict__ h) {
+                               __half *__restrict__ h) {
   griddep_launch_dependents();
   griddep_wait();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -238,7 +250,7 @@ __global__ void flatten_kernel(const float *__restrict__ y, int t, int f, int ch
   if (i >= (long long)t * row) return;
   const long long r = i / row;
   const int e = int(i - r * row);
-  h[i] = y[r * row + (e % f) * ch + e / f];
+  h[i] = __float2half_rn(y[r * row + (e % f) * ch + e / f]);  // the output GEMM's f16 operand
 }
 
 }  // namespace
@@ -373,7 +385,7 @@ cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStr
 namespace wv {
 
 cudaError_t launch_conv02(const float *mel, int valid, int t2, int ch, const float *w0,
-                          const float *b0, const float *w2, const float *b2, float *a,
+                          const float *b0, const float *w2, const float *b2, __half *a,
                           cudaStream_t s) {
   const int t1 = (valid - 1) / 2 + 1, live = (t1 - 1) / 2 + 1;
   return launch_pdl(conv02_kernel, dim3(unsigned(t2)), dim3(ch < 256 ? ch : 256), 0, s, mel, valid,
@@ -381,13 +393,13 @@ cudaError_t launch_conv02(const float *mel, int valid, int t2, int ch, const flo
 }
 
 cudaError_t launch_dw3s2(const float *x, int t, int f, int ch, int rows, const float *w,
-                         const float *b, float *y, cudaStream_t s) {
+                         const float *b, __half *y, cudaStream_t s) {
   const long long total = (long long)rows * ((f - 1) / 2 + 1) * ch;
   return launch_pdl(dw3s2_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, x, t, f, ch,
                     rows, w, b, y);
 }
 
-cudaError_t launch_flatten(const float *y, int t, int f, int ch, float *h, cudaStream_t s) {
+cudaError_t launch_flatten(const float *y, int t, int f, int ch, __half *h, cudaStream_t s) {
   const long long total = (long long)t * f * ch;
   return launch_pdl(flatten_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, y, t, f,
                     ch, h);

@@ -203,15 +203,15 @@ cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int 
 size_t mel_norm_scratch_bytes(long long frames);
 cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStream_t s);
 
-// Parakeet's subsampling around its GEMMs: conv0 + ReLU + conv2 from the mel image into a
-// [t2][32][ch] (rows from half(half(valid)) on zero); a depthwise 3x3 stride-2 conv of x [t][f][ch]
-// into y [rows][half(f)][ch]; [t][f][ch] to [t][ch·f].
+// Parakeet's subsampling around its GEMMs, each output the next GEMM's f16 operand: conv0 + ReLU
+// + conv2 from the mel image into a [t2][32][ch] (rows from half(half(valid)) on zero); a depthwise
+// 3x3 stride-2 conv of x [t][f][ch] into y [rows][half(f)][ch]; [t][f][ch] to [t][ch·f].
 cudaError_t launch_conv02(const float *mel, int valid, int t2, int ch, const float *w0,
-                          const float *b0, const float *w2, const float *b2, float *a,
+                          const float *b0, const float *w2, const float *b2, __half *a,
                           cudaStream_t s);
 cudaError_t launch_dw3s2(const float *x, int t, int f, int ch, int rows, const float *w,
-                         const float *b, float *y, cudaStream_t s);
-cudaError_t launch_flatten(const float *y, int t, int f, int ch, float *h, cudaStream_t s);
+                         const float *b, __half *y, cudaStream_t s);
+cudaError_t launch_flatten(const float *y, int t, int f, int ch, __half *h, cudaStream_t s);
 
 // ---- GGUF loads (gguf.cu) ----------------------------------------------------------------------
 

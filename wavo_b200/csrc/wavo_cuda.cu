@@ -1318,10 +1318,12 @@ wavo_status wavo_subsample(wavo_ctx *ctx, const float *mel, uint32_t frames, uin
     return fail(ctx, WAVO_EINVAL, "subsample: scratch must be 256-byte aligned");
   const SubsampleLayout L = subsample_layout(frames, ch);
   uint8_t *sp = static_cast<uint8_t *>(scratch);
-  float *a = reinterpret_cast<float *>(sp), *b = reinterpret_cast<float *>(sp + L.a_bytes);
-  float *h = reinterpret_cast<float *>(sp + 2 * L.a_bytes);
+  // The GEMMs' operands (a, h, flat) are f16, their outputs (b, y) f32.
+  __half *a = reinterpret_cast<__half *>(sp);
+  float *b = reinterpret_cast<float *>(sp + L.a_bytes);
+  __half *h = reinterpret_cast<__half *>(sp + 2 * L.a_bytes);
   float *y = reinterpret_cast<float *>(sp + 2 * L.a_bytes + L.h_bytes);
-  float *flat = reinterpret_cast<float *>(sp + 2 * L.a_bytes + 2 * L.h_bytes);
+  __half *flat = reinterpret_cast<__half *>(sp + 2 * L.a_bytes + 2 * L.h_bytes);
   const int t2 = int(L.t2), t = int(L.t);
   {
     std::lock_guard<std::mutex> g(ctx->mu);
@@ -1329,20 +1331,20 @@ wavo_status wavo_subsample(wavo_ctx *ctx, const float *mel, uint32_t frames, uin
     CK(wv::launch_conv02(mel, int(valid), t2, int(ch), w0, b0, w2, b2, a, ctx->stream),
        "subsample conv0/conv2 launch");
   }
-  wavo_status st = wavo_gemm(ctx, a, WAVO_F32, ch, conv3, b, WAVO_F32, ch, uint32_t(t2) * 32,
+  wavo_status st = wavo_gemm(ctx, a, WAVO_F16, ch, conv3, b, WAVO_F32, ch, uint32_t(t2) * 32,
                              WAVO_EPI_RELU, 1.0f);
   if (st != WAVO_OK) return st;
   {
     std::lock_guard<std::mutex> g(ctx->mu);
     CK(wv::launch_dw3s2(b, t2, 32, int(ch), t, w5, b5, h, ctx->stream), "subsample conv5 launch");
   }
-  st = wavo_gemm(ctx, h, WAVO_F32, ch, conv6, y, WAVO_F32, ch, uint32_t(t) * 16, WAVO_EPI_RELU, 1.0f);
+  st = wavo_gemm(ctx, h, WAVO_F16, ch, conv6, y, WAVO_F32, ch, uint32_t(t) * 16, WAVO_EPI_RELU, 1.0f);
   if (st != WAVO_OK) return st;
   {
     std::lock_guard<std::mutex> g(ctx->mu);
     CK(wv::launch_flatten(y, t, 16, int(ch), flat, ctx->stream), "subsample flatten launch");
   }
-  st = wavo_gemm(ctx, flat, WAVO_F32, 16 * ch, out, x, WAVO_F32, 0, uint32_t(t), WAVO_EPI_BIAS, 1.0f);
+  st = wavo_gemm(ctx, flat, WAVO_F16, 16 * ch, out, x, WAVO_F32, 0, uint32_t(t), WAVO_EPI_BIAS, 1.0f);
   if (st != WAVO_OK) return st;
   if (t_out) *t_out = uint32_t(t);
   return WAVO_OK;
