@@ -856,6 +856,16 @@ class C4Full(Workload):
         for pos in range(self.STEPS):
             self.dec.record_step(p, pos, tick)
 
+    def profile_unit(self, p):
+        """One greedy step (at position 13, after the steps before it, which are not profiled)."""
+        self.dec.hist_len.zero_()
+        for pos in range(13):
+            self.dec.record_step(p, pos)
+        self.gpu.sync()
+        import torch
+        torch.cuda.profiler.start()
+        self.dec.record_step(p, 13)
+
     def host_gather(self, rank):
         return None  # each rank reads back its own windows' tokens
 
@@ -1006,6 +1016,15 @@ class C5Mel(Workload):
             tick("subsample", lambda r=r, f=f, x0=x0, t=t: self.gpu.subsample(
                 self.mel[r:r + f], f, self.taps, self.conv3, self.conv6, self.out,
                 self.x[x0:x0 + t], self.scratch))
+
+    def profile_unit(self, p):
+        """The first two segments' log-mel and subsampling, for a launch list."""
+        calls = []
+        self.record(p, lambda name, fn: calls.append(fn))
+        import torch
+        torch.cuda.profiler.start()
+        for fn in calls[:4]:
+            fn()
 
     def inputs(self):
         return [(self.pcm, self.pcm_host)]
@@ -1308,6 +1327,10 @@ def main():
     ap.add_argument("--config", default="c5", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="wavo", choices=["wavo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="for an ncu capture (--profile-from-start off): warm the workload up, then "
+                         "run one unit of it (one decoder step, two segments, or one whole step) "
+                         "between cudaProfilerStart and cudaProfilerStop, and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
@@ -1348,6 +1371,19 @@ def main():
     gpu.reserve(256 << 20)
     wl = WORKLOADS[args.config](gpu, rank, world)
     stream = torch.cuda.current_stream(local)
+    if args.profile:
+        for _ in range(2):
+            wl.record(gpu.pass_())
+        gpu.sync()
+        unit = getattr(wl, "profile_unit", None)
+        if unit is None:
+            torch.cuda.profiler.start()
+            wl.record(gpu.pass_())
+        else:
+            unit(gpu.pass_())  # starts the profiler after its own lead-in
+        gpu.sync()
+        torch.cuda.profiler.stop()
+        return
 
     for _ in range(2):  # eager warm-up (also configures the kernels before the capture)
         wl.record(gpu.pass_())

@@ -6,10 +6,12 @@
 // table), so the spectrum is the reference's bit for bit; the reductions of the normalisation are
 // f64 sums in a fixed order (chunks of frames, then the chunks in order).
 //
-//   log_mel_kernel   one warp a frame (four frames a CTA): the windowed frame in the first stage's
-//                    order, nine butterfly stages between two shared-memory buffers (16-byte
-//                    loads of each butterfly's input pair), the power spectrum, then four mel bins
-//                    a lane over their filter spans.
+//   log_mel_kernel   a warp a frame at a time (13 warps, one CTA an SM, looping over frames): the
+//                    tables copied once into shared memory, the frame's pcm staged from
+//                    registers (the next frame's fetched during this one's FFT), the windowed
+//                    frame in the first stage's order, nine butterfly stages between two
+//                    shared-memory buffers (16-byte loads of each butterfly's input pair), the
+//                    power spectrum, four mel bins a lane.
 //   mel_sum_kernel   per chunk of 64 frames, a thread a mel bin: the f64 sum of the values (or of
 //                    the squared deviations from the mean) in frame order (coalesced rows, eight
 //                    loads in flight).
@@ -21,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <memory>
 #include <vector>
 
 #include "kernels.cuh"
@@ -31,71 +34,148 @@ namespace {
 
 constexpr int FE_MELS = 128, FE_NFFT = 512, FE_WINDOW = 400, FE_HOP = 160, FE_BINS = 257;
 constexpr int FE_STAGES = 9, FE_HALF = FE_NFFT / 2;
-constexpr int FE_WARPS = 4;
+constexpr int FE_WARPS = 13;  // one CTA an SM: 13 frames in flight (16 KB of buffers each)
 constexpr int FE_CHUNK = 64;
 
-__global__ void __launch_bounds__(32 * FE_WARPS)
+constexpr int FE_SPAN_MAX = 16;  // FFT bins in a mel bin's nonzero span (12 for the Slaney bank)
+constexpr int FE_STAGE_P = FE_NFFT + 1;               // pcm samples a frame reads
+constexpr int FE_PF = (FE_STAGE_P + 31) / 32;         // of them a lane's (17)
+
+// Shared tables of a CTA, built once on the host as one image in this layout: the 256 twiddles
+// (every stage's twiddle is one of them: output i of the stage to blocks of `size` takes index
+// i / (512 / size) · (512 / size)), the window in the first stage's order, that order, and the
+// filterbank as each mel bin's nonzero span, weight k of bin m at fw[k][m] (a warp's lanes read
+// consecutive words).
+struct FeShared {
+  double twc[256], tws[256], win[FE_NFFT];
+  float fw[FE_SPAN_MAX][FE_MELS];
+  int lo[FE_MELS], len[FE_MELS];
+  uint16_t perm[FE_NFFT];
+};
+static_assert(sizeof(FeShared) % 16 == 0, "the image is copied in 16-byte words");
+constexpr size_t FE_SMEM = sizeof(FeShared) + size_t(FE_WARPS) * 4 * FE_NFFT * 8;
+
+// The frame's pcm is staged with a word of padding every 16: the first stage's order reads it at a
+// stride of 16 words, which the padding spreads over all 32 banks.
+__device__ __forceinline__ int fe_pad(int p) { return p + (p >> 4); }
+
+// A lane's share of frame t's pcm (samples (f0 + t)·160 − 257 + p, p = lane + 32·q; 0 outside).
+__device__ __forceinline__ void fe_fetch(const float *__restrict__ pcm, long long n_pcm,
+                                         long long j0, int lane, float (&pf)[FE_PF]) {
+#pragma unroll
+  for (int q = 0; q < FE_PF; ++q) {
+    const int p = lane + 32 * q;
+    const long long idx = j0 - FE_NFFT / 2 - 1 + p;
+    pf[q] = p < FE_STAGE_P && idx >= 0 && idx < n_pcm ? __ldg(pcm + idx) : 0.0f;
+  }
+}
+
+__global__ void __launch_bounds__(32 * FE_WARPS, 1)
     log_mel_kernel(const float *__restrict__ pcm, long long n_pcm, long long f0, int frames,
                    const FrontendTables tab, float *__restrict__ mel) {
+  extern __shared__ double fe_smem[];
+  FeShared &sh = *reinterpret_cast<FeShared *>(fe_smem);
+  {  // the constant tables, every load in flight at once, before the wait
+    constexpr int WORDS = int(sizeof(FeShared) / 16);
+    constexpr int PER = (WORDS + 32 * FE_WARPS - 1) / (32 * FE_WARPS);
+    const uint4 *src = static_cast<const uint4 *>(tab.image);
+    uint4 *dst = reinterpret_cast<uint4 *>(fe_smem);
+    uint4 w[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int e = int(threadIdx.x) + 32 * FE_WARPS * q;
+      if (e < WORDS) w[q] = __ldg(src + e);
+    }
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int e = int(threadIdx.x) + 32 * FE_WARPS * q;
+      if (e < WORDS) dst[e] = w[q];
+    }
+  }
   griddep_launch_dependents();
   griddep_wait();
-  extern __shared__ double fe_smem[];
+  __syncthreads();
   const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
-  const int t = int(blockIdx.x) * FE_WARPS + warp;
-  if (t >= frames) return;  // whole warps leave; no block-wide barrier follows
-  double *ar = fe_smem + warp * 4 * FE_NFFT, *ai = ar + FE_NFFT;
+  double *ar = fe_smem + sizeof(FeShared) / 8 + warp * 4 * FE_NFFT, *ai = ar + FE_NFFT;
   double *br = ai + FE_NFFT, *bi = br + FE_NFFT;
-  // The windowed frame in the first stage's order: v = perm(i) reads sample i (src/fft.rs:89-92).
-  const long long j0 = (f0 + t) * FE_HOP;  // the frame's first index in the padded signal
-  for (int v = lane; v < FE_NFFT; v += 32) {
-    const int i = tab.perm[v];
-    const long long j = j0 + i - FE_NFFT / 2;  // the pcm index of padded sample j0 + i
-    double s = 0.0;
-    if (j == 0)
-      s = double(pcm[0]);
-    else if (j > 0 && j < n_pcm)
-      s = __dsub_rn(double(pcm[j]), __dmul_rn(double(0.97f), double(pcm[j - 1])));
-    ar[v] = __dmul_rn(s, tab.window[i]);
-    ai[v] = 0.0;
-  }
-  __syncwarp();
-  // Nine radix-2 stages (src/fft.rs:131-143): output i reads inputs 2i and 2i + 1.
-  double *sr = ar, *si = ai, *dr = br, *di = bi;
+  float *stage = reinterpret_cast<float *>(br);  // the frame's pcm, before the first stage
+  const int step = int(gridDim.x) * FE_WARPS;
+  int t = int(blockIdx.x) * FE_WARPS + warp;
+  float pf[FE_PF];
+  if (t < frames) fe_fetch(pcm, n_pcm, (f0 + t) * FE_HOP, lane, pf);
 #pragma unroll 1
-  for (int st = 0; st < FE_STAGES; ++st) {
-    const double *cs = tab.tcos + st * FE_HALF, *sn = tab.tsin + st * FE_HALF;
-#pragma unroll 4
-    for (int q = 0; q < FE_HALF / 32; ++q) {
-      const int i = lane + 32 * q;
-      const double c = cs[i], s = sn[i];
-      const double2 xr = reinterpret_cast<const double2 *>(sr)[i];
-      const double2 xi = reinterpret_cast<const double2 *>(si)[i];
-      const double a = xr.x, x = xr.y, b = xi.x, y = xi.y;
-      dr[i] = fma(s, y, fma(c, x, a));
-      di[i] = fma(-s, x, fma(c, y, b));
-      dr[i + FE_HALF] = fma(-s, y, fma(-c, x, a));
-      di[i + FE_HALF] = fma(s, x, fma(-c, y, b));
+  for (; t < frames; t += step) {
+    const long long j0 = (f0 + t) * FE_HOP;  // the frame's first padded index + 256
+    // Stage the frame's pcm (545 words with the padding, inside the second buffer), then fetch
+    // the next frame's while this one is transformed.
+#pragma unroll
+    for (int q = 0; q < FE_PF; ++q) {
+      const int p = lane + 32 * q;
+      if (p < FE_STAGE_P) stage[fe_pad(p)] = pf[q];
+    }
+    if (t + step < frames) fe_fetch(pcm, n_pcm, (f0 + t + step) * FE_HOP, lane, pf);
+    __syncwarp();
+    // The windowed, pre-emphasised frame in the first stage's order (src/fft.rs:89-92).
+    double xs[FE_NFFT / 32];
+#pragma unroll
+    for (int q = 0; q < FE_NFFT / 32; ++q) {
+      const int v = lane + 32 * q;
+      const int i = sh.perm[v];
+      const long long j = j0 + i - FE_NFFT / 2;  // the pcm index of padded sample j0 + i
+      double s = 0.0;
+      if (j == 0)
+        s = double(stage[fe_pad(i + 1)]);
+      else if (j > 0 && j < n_pcm)
+        s = __dsub_rn(double(stage[fe_pad(i + 1)]), __dmul_rn(double(0.97f), double(stage[fe_pad(i)])));
+      xs[q] = __dmul_rn(s, sh.win[v]);
+    }
+    __syncwarp();  // the staged pcm is read before the buffer is reused
+#pragma unroll
+    for (int q = 0; q < FE_NFFT / 32; ++q) {
+      ar[lane + 32 * q] = xs[q];
+      ai[lane + 32 * q] = 0.0;
     }
     __syncwarp();
-    double *tr = sr, *ti = si;
-    sr = dr;
-    si = di;
-    dr = tr;
-    di = ti;
-  }
-  // The power spectrum (f64 products and sum, cast to f32) over the freed buffer.
-  float *power = reinterpret_cast<float *>(dr);
-  for (int k = lane; k < FE_BINS; k += 32)
-    power[k] = float(__dadd_rn(__dmul_rn(sr[k], sr[k]), __dmul_rn(si[k], si[k])));
-  __syncwarp();
-  float *out = mel + (long long)t * FE_MELS;
+    // Nine radix-2 stages (src/fft.rs:131-143): output i reads inputs 2i and 2i + 1.
+    double *sr = ar, *si = ai, *dr = br, *di = bi;
+#pragma unroll 1
+    for (int st = 0; st < FE_STAGES; ++st) {
+      const int sh_bits = 8 - st;
 #pragma unroll
-  for (int q = 0; q < FE_MELS / 32; ++q) {
-    const int m = lane + 32 * q;
-    const float *f = tab.filters + m * FE_BINS;
-    float e = 0.0f;
-    for (int k = tab.span_lo[m]; k < tab.span_hi[m]; ++k) e = fmaf(f[k], power[k], e);
-    out[m] = logf(__fadd_rn(e, 1.0f / float(1 << 24)));
+      for (int q = 0; q < FE_HALF / 32; ++q) {
+        const int i = lane + 32 * q;
+        const int idx = (i >> sh_bits) << sh_bits;
+        const double c = sh.twc[idx], s = sh.tws[idx];
+        const double2 xr = reinterpret_cast<const double2 *>(sr)[i];
+        const double2 xi = reinterpret_cast<const double2 *>(si)[i];
+        const double a = xr.x, x = xr.y, b = xi.x, y = xi.y;
+        dr[i] = fma(s, y, fma(c, x, a));
+        di[i] = fma(-s, x, fma(c, y, b));
+        dr[i + FE_HALF] = fma(-s, y, fma(-c, x, a));
+        di[i + FE_HALF] = fma(s, x, fma(-c, y, b));
+      }
+      __syncwarp();
+      double *tr = sr, *ti = si;
+      sr = dr;
+      si = di;
+      dr = tr;
+      di = ti;
+    }
+    // The power spectrum (f64 products and sum, cast to f32) over the freed buffer.
+    float *power = reinterpret_cast<float *>(dr);
+    for (int k = lane; k < FE_BINS; k += 32)
+      power[k] = float(__dadd_rn(__dmul_rn(sr[k], sr[k]), __dmul_rn(si[k], si[k])));
+    __syncwarp();
+    float *out = mel + (long long)t * FE_MELS;
+#pragma unroll
+    for (int q = 0; q < FE_MELS / 32; ++q) {
+      const int m = lane + 32 * q;
+      const float *pw = power + sh.lo[m];
+      float e = 0.0f;
+      for (int k = 0; k < sh.len[m]; ++k) e = fmaf(sh.fw[k][m], pw[k], e);
+      out[m] = logf(__fadd_rn(e, 1.0f / float(1 << 24)));
+    }
+    __syncwarp();  // power (in dr) is read before the next frame stages its pcm into br
   }
 }
 
@@ -157,27 +237,32 @@ __global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
 // taps and biases in registers) over the row's 32 columns; the seven mel rows 4k - 3 .. 4k + 3
 // the row reads are staged in shared memory with zeros past the valid frames and the band's
 // edges. conv0 is evaluated where conv2 reads it (zero outside rows 0 .. t1 - 1, as the reference
-// zero-fills), each value once along the row: a 3x3 window of it slides two columns a step.
-__device__ __forceinline__ float conv0_px(const float (&ms)[7][130], int i0, int c, int r, int t1,
+// zero-fills), each value once along the row: a 3x3 window of it slides two columns a step, and
+// the step's two conv0 columns read mel columns 4fo - 1 .. 4fo + 3 of each staged row (one 16-byte
+// and one 4-byte load a row: the loads are the same for every thread of the CTA).
+constexpr int C02_W = 132;  // a staged row: mel columns -1 .. 130 (16-byte aligned rows)
+
+// conv0 at one pixel from its 3x3 mel patch p[dr][dc], in the reference's order.
+__device__ __forceinline__ float conv0_px(float p00, float p01, float p02, float p10, float p11,
+                                          float p12, float p20, float p21, float p22,
                                           const float (&w)[9], float bias) {
-  if (c < 0 || c >= 64 || r < 0 || r >= t1) return 0.0f;
+  const float v[9] = {p00, p01, p02, p10, p11, p12, p20, p21, p22};
   float p = bias;
 #pragma unroll
-  for (int t0 = 0; t0 < 9; ++t0)
-    p = __fadd_rn(p, __fmul_rn(w[t0], ms[i0 + t0 / 3][2 * c + t0 % 3]));
+  for (int t0 = 0; t0 < 9; ++t0) p = __fadd_rn(p, __fmul_rn(w[t0], v[t0]));
   return fmaxf(p, 0.0f);
 }
 
-__global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, int t2, int live,
+__global__ void __launch_bounds__(256, 3) conv02_kernel(const float *__restrict__ mel, int valid, int t1, int t2, int live,
                               int ch, const float *__restrict__ w0, const float *__restrict__ b0,
                               const float *__restrict__ w2, const float *__restrict__ b2,
                               __half *__restrict__ a) {
   griddep_launch_dependents();
   griddep_wait();
-  __shared__ float ms[7][130];  // mel rows 4k - 3 + i, columns -1 .. 128
+  __shared__ __align__(16) float ms[7][C02_W];  // mel rows 4k - 3 + i, columns -1 .. 130
   const int k = int(blockIdx.x);
-  for (int e = threadIdx.x; e < 7 * 130; e += blockDim.x) {
-    const int i = e / 130, c = e % 130 - 1;
+  for (int e = threadIdx.x; e < 7 * C02_W; e += blockDim.x) {
+    const int i = e / C02_W, c = e % C02_W - 1;
     const int tm = 4 * k - 3 + i;
     ms[i][c + 1] = tm >= 0 && tm < valid && c >= 0 && c < 128 ? mel[(long long)tm * 128 + c] : 0.0f;
   }
@@ -195,17 +280,37 @@ __global__ void conv02_kernel(const float *__restrict__ mel, int valid, int t1, 
       c2w[tap] = w2[tap * ch + q];
     }
     const float bias0 = b0[q], bias2 = b2[q];
+    bool row_in[3];  // conv0 row 2k - 1 + rr exists (the reference zero-fills outside)
+#pragma unroll
+    for (int rr = 0; rr < 3; ++rr) row_in[rr] = 2 * k - 1 + rr >= 0 && 2 * k - 1 + rr < t1;
     // win[rr][cc]: conv0 at row 2k - 1 + rr (staged mel rows from 2rr on), column 2fo - 1 + cc.
     float win[3][3];
 #pragma unroll
     for (int rr = 0; rr < 3; ++rr) win[rr][2] = 0.0f;  // column -1 (becomes cc = 0 below)
 #pragma unroll 1
     for (int fo = 0; fo < 32; ++fo) {
+      float m[7][5];  // mel columns 4fo - 1 .. 4fo + 3 of the seven staged rows
+#pragma unroll
+      for (int i = 0; i < 7; ++i) {
+        const float4 v = *reinterpret_cast<const float4 *>(&ms[i][4 * fo]);
+        m[i][0] = v.x;
+        m[i][1] = v.y;
+        m[i][2] = v.z;
+        m[i][3] = v.w;
+        m[i][4] = ms[i][4 * fo + 4];
+      }
 #pragma unroll
       for (int rr = 0; rr < 3; ++rr) {
+        const int r = 2 * rr;
         win[rr][0] = win[rr][2];
-        win[rr][1] = conv0_px(ms, 2 * rr, 2 * fo, 2 * k - 1 + rr, t1, c0w, bias0);
-        win[rr][2] = conv0_px(ms, 2 * rr, 2 * fo + 1, 2 * k - 1 + rr, t1, c0w, bias0);
+        win[rr][1] = row_in[rr] ? conv0_px(m[r][0], m[r][1], m[r][2], m[r + 1][0], m[r + 1][1],
+                                           m[r + 1][2], m[r + 2][0], m[r + 2][1], m[r + 2][2],
+                                           c0w, bias0)
+                                : 0.0f;
+        win[rr][2] = row_in[rr] ? conv0_px(m[r][2], m[r][3], m[r][4], m[r + 1][2], m[r + 1][3],
+                                           m[r + 1][4], m[r + 2][2], m[r + 2][3], m[r + 2][4],
+                                           c0w, bias0)
+                                : 0.0f;
       }
       float y = bias2;
 #pragma unroll
@@ -257,10 +362,7 @@ __global__ void flatten_kernel(const float *__restrict__ y, int t, int f, int ch
 
 // ---- tables (host), as src/fft.rs:46-66 and src/parakeet/frontend.rs:30-47, 110-140 build them --
 
-size_t frontend_table_bytes() {
-  return FE_NFFT * 2 + 2 * FE_STAGES * FE_HALF * 8 + FE_NFFT * 8 + FE_MELS * FE_BINS * 4 +
-         2 * FE_MELS * 4 + 256;
-}
+size_t frontend_table_bytes() { return sizeof(FeShared); }
 
 cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *out) {
   const int n = FE_NFFT;
@@ -271,23 +373,22 @@ cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *ou
     for (int v : starts) next.push_back(2 * v + 1);
     starts = next;
   }
-  std::vector<uint16_t> perm(n);
-  for (int i = 0; i < n; ++i) perm[i] = uint16_t(starts[i]);
-  std::vector<double> tcos, tsin;
+  std::unique_ptr<FeShared> owner(new FeShared());  // the image (18 KB), zero-filled
+  FeShared &img = *owner;
+  for (int i = 0; i < n; ++i) img.perm[i] = uint16_t(starts[i]);
+  // The stages' twiddles: stage `size` takes cos/sin(tau·idx/512) at idx = i / (512 / size) ·
+  // (512 / size), one of these 256.
   const double tau = 6.283185307179586;
-  for (int size = 2; size <= n; size *= 2)
-    for (int i = 0; i < n / 2; ++i) {
-      const int idx = i / (n / size) * (n / size);
-      const double phase = tau * double(idx) / double(n);
-      tcos.push_back(std::cos(phase));
-      tsin.push_back(std::sin(phase));
-    }
-  std::vector<double> window(n);
-  for (int i = 0; i < n; ++i) {
-    const int k = i - (FE_NFFT - FE_WINDOW) / 2;
-    window[i] = k >= 0 && k < FE_WINDOW
-                    ? 0.5 - 0.5 * std::cos(2.0 * M_PI * double(k) / double(FE_WINDOW - 1))
-                    : 0.0;
+  for (int idx = 0; idx < n / 2; ++idx) {
+    const double phase = tau * double(idx) / double(n);
+    img.twc[idx] = std::cos(phase);
+    img.tws[idx] = std::sin(phase);
+  }
+  for (int v = 0; v < n; ++v) {  // the window, read in the first stage's order
+    const int k = int(starts[v]) - (FE_NFFT - FE_WINDOW) / 2;
+    img.win[v] = k >= 0 && k < FE_WINDOW
+                     ? 0.5 - 0.5 * std::cos(2.0 * M_PI * double(k) / double(FE_WINDOW - 1))
+                     : 0.0;
   }
   // Slaney filterbank (librosa mel(16000, 512, 128, 0, 8000, norm='slaney')) in f64, stored f32.
   const double fsp = 200.0 / 3.0, min_log_hz = 1000.0, min_log_mel = min_log_hz / fsp;
@@ -318,40 +419,40 @@ cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *ou
     lo[m] = a == FE_BINS ? 0 : a;
     hi[m] = a == FE_BINS ? 0 : b;
   }
-  uint8_t *p = static_cast<uint8_t *>(dev);
-  size_t at = 0;
-  auto put = [&](const void *src, size_t bytes) -> void * {
-    at = (at + 15) / 16 * 16;
-    void *d = p + at;
-    at += bytes;
-    cudaMemcpyAsync(d, src, bytes, cudaMemcpyHostToDevice, s);
-    return d;
-  };
-  out->perm = static_cast<const uint16_t *>(put(perm.data(), perm.size() * 2));
-  out->tcos = static_cast<const double *>(put(tcos.data(), tcos.size() * 8));
-  out->tsin = static_cast<const double *>(put(tsin.data(), tsin.size() * 8));
-  out->window = static_cast<const double *>(put(window.data(), window.size() * 8));
-  out->filters = static_cast<const float *>(put(filters.data(), filters.size() * 4));
-  out->span_lo = static_cast<const int *>(put(lo.data(), lo.size() * 4));
-  out->span_hi = static_cast<const int *>(put(hi.data(), hi.size() * 4));
-  return cudaStreamSynchronize(s);  // the host vectors go out of scope
+  for (int m = 0; m < FE_MELS; ++m) {
+    if (hi[m] - lo[m] > FE_SPAN_MAX) return cudaErrorInvalidValue;
+    img.lo[m] = lo[m];
+    img.len[m] = hi[m] - lo[m];
+    for (int k = lo[m]; k < hi[m]; ++k) img.fw[k - lo[m]][m] = filters[m * FE_BINS + k];
+  }
+  cudaError_t e = cudaMemcpyAsync(dev, &img, sizeof(FeShared), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // before the host image is freed
+  out->image = dev;
+  return e;
 }
 
 cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int frames,
                            const FrontendTables &tab, float *mel, cudaStream_t s) {
   if (frames <= 0) return cudaSuccess;
-  const size_t smem = size_t(FE_WARPS) * 4 * FE_NFFT * 8;  // 64 KB
+  // The shared tables, then four 512-point complex f64 buffers a warp (16 KB).
+  const size_t smem = FE_SMEM;
   static bool configured[64] = {};
+  static int sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(log_mel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(smem));
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  return launch_pdl(log_mel_kernel, dim3((frames + FE_WARPS - 1) / FE_WARPS), dim3(32 * FE_WARPS),
-                    smem, s, pcm, n_pcm, f0, frames, tab, mel);
+  // One CTA an SM at most, each warp looping over frames (the tables load once a CTA).
+  int ctas = (frames + FE_WARPS - 1) / FE_WARPS;
+  if (ctas > sms[dev]) ctas = sms[dev];
+  return launch_pdl(log_mel_kernel, dim3(ctas), dim3(32 * FE_WARPS), smem, s, pcm, n_pcm, f0,
+                    frames, tab, mel);
 }
 
 size_t mel_norm_scratch_bytes(long long frames) {

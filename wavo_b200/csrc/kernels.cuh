@@ -185,13 +185,11 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
 
 // ---- the log-mel frontend (frontend.cu) ----------------------------------------------------------
 
-// Device tables of the frontend: the FFT's first-stage order, its nine stages' cos and sin, the
-// Hann window, the Slaney filterbank [128][257] and each filter's nonzero bins [lo, hi).
+// Device tables of the frontend, one image that the log-mel kernel copies into shared memory: the
+// FFT's twiddles and first-stage order, the Hann window in that order, and the Slaney filterbank
+// as each mel bin's nonzero span of FFT bins.
 struct FrontendTables {
-  const uint16_t *perm;
-  const double *tcos, *tsin, *window;
-  const float *filters;
-  const int *span_lo, *span_hi;
+  const void *image;
 };
 size_t frontend_table_bytes();
 // Fills `dev` (frontend_table_bytes()) with the tables and points `out` at them (waits for `s`).
