@@ -153,6 +153,20 @@ wavo_status wavo_subsample(wavo_ctx *ctx, const float *mel, uint32_t frames, uin
                            const float *b5, const wavo_linear *conv6, const wavo_linear *out,
                            float *x, void *scratch, uint32_t *t_out);
 
+/* wavo_subsample over n segments in one call (the reference subsamples each piece on its own,
+ * src/parakeet/cpu.rs:60-174 per piece; each segment's rows here equal that call's): segment s's
+ * frames[s] mel rows (valid[s] of them audio) follow segment s - 1's in `mel`, and its t_s output
+ * rows follow segment s - 1's in x (t_out[s] gets t_s when t_out is not NULL). conv0/conv2, conv3
+ * and conv5 run segment by segment; conv6, the flatten and the output projection once over every
+ * segment's rows. scratch: wavo_subsample_batch_scratch_bytes of device memory, 256-byte aligned. */
+uint64_t wavo_subsample_batch_scratch_bytes(const uint32_t *frames, uint32_t n, uint32_t ch);
+wavo_status wavo_subsample_batch(wavo_ctx *ctx, const float *mel, const uint32_t *frames,
+                                 const uint32_t *valid, uint32_t n, uint32_t ch, const float *w0,
+                                 const float *b0, const float *w2, const float *b2,
+                                 const wavo_linear *conv3, const float *w5, const float *b5,
+                                 const wavo_linear *conv6, const wavo_linear *out, float *x,
+                                 void *scratch, uint32_t *t_out);
+
 /* ---- GGUF files: replaces gguf::Gguf / gguf::Tensor (src/gguf.rs) ----------------------------
  * Host calls without a context: errors read from wavo_last_error(NULL). A wavo_gguf may be read
  * from many threads at once. */

@@ -131,3 +131,71 @@ def test_subsample_matches_oracle(gpu, frames, valid, seed):
     err = np.abs(got - want).max() / max(1.0, np.abs(want).max())
     rel = np.linalg.norm(got - want) / np.linalg.norm(want)
     assert err <= 2e-3 and rel <= 1e-3, (err, rel)
+
+
+def test_subsample_batch_matches_each_segment(gpu):
+    # wavo_subsample_batch over ragged segments (padding rows in some, a 2-frame one, one longer
+    # than the rest) against the oracle segment by segment, and against wavo_subsample per segment
+    # (conv6 and the output projection run over every segment's rows at once there).
+    ch, d = 256, 384
+    rng = np.random.default_rng(11)
+    frames = [801, 97, 2, 333, 1201, 64]
+    valid = [801, 60, 2, 333, 1000, 64]
+    mels = [rng.standard_normal((f, 128)).astype(np.float32) for f in frames]
+    taps = {k: (rng.standard_normal((9, ch)) * 0.3).astype(np.float32) for k in ("w0", "w2", "w5")}
+    taps.update({k: (rng.standard_normal(ch) * 0.1).astype(np.float32) for k in ("b0", "b2", "b5")})
+    w3 = (rng.standard_normal((ch, ch)) * 0.06).astype(np.float16)
+    w6 = (rng.standard_normal((ch, ch)) * 0.06).astype(np.float16)
+    wo = (rng.standard_normal((d, 16 * ch)) * 0.02).astype(np.float16)
+    b3, b6 = (rng.standard_normal((2, ch)) * 0.1).astype(np.float32)
+    bo = (rng.standard_normal(d) * 0.1).astype(np.float32)
+    O.set_vnni(0)
+    try:
+        wants = [O.subsample(m, v, taps, O.Linear(O.TY_F16, ch, ch, w3.tobytes(), b3),
+                             O.Linear(O.TY_F16, ch, ch, w6.tobytes(), b6),
+                             O.Linear(O.TY_F16, d, 16 * ch, wo.tobytes(), bo))
+                 for m, v in zip(mels, valid)]
+    finally:
+        O.set_vnni(-1)
+    l3 = gpu.linear(O.TY_F16, ch, ch, w3.tobytes(), b3)
+    l6 = gpu.linear(O.TY_F16, ch, ch, w6.tobytes(), b6)
+    lo = gpu.linear(O.TY_F16, d, 16 * ch, wo.tobytes(), bo)
+    dt = {k: torch.from_numpy(v).cuda() for k, v in taps.items()}
+    rows = sum(w.shape[0] for w in wants)
+    x = torch.full((rows, d), float("nan"), device="cuda")
+    ts = gpu.subsample_batch(torch.from_numpy(np.concatenate(mels)).cuda(), frames, valid, dt,
+                             l3, l6, lo, x)
+    gpu.sync()
+    assert ts == [w.shape[0] for w in wants]
+    got = x.cpu().numpy()
+    r = 0
+    for m, v, want in zip(mels, valid, wants):
+        part = got[r:r + want.shape[0]]
+        err = np.abs(part - want).max() / max(1.0, np.abs(want).max())
+        rel = np.linalg.norm(part - want) / np.linalg.norm(want)
+        assert err <= 2e-3 and rel <= 1e-3, (err, rel)
+        one = torch.zeros(want.shape[0], d, device="cuda")
+        gpu.subsample(torch.from_numpy(m).cuda(), v, dt, l3, l6, lo, one)
+        gpu.sync()
+        np.testing.assert_allclose(part, one.cpu().numpy(), rtol=0, atol=1e-5 * max(1.0, np.abs(want).max()))
+        r += want.shape[0]
+
+
+def test_subsample_batch_rejects_bad_segments(gpu):
+    from wavo_b200 import _lib as L
+    ch = 256
+    rng = np.random.default_rng(12)
+    taps = {k: torch.from_numpy((rng.standard_normal((9, ch)) * 0.3).astype(np.float32)).cuda()
+            for k in ("w0", "w2", "w5")}
+    taps.update({k: torch.zeros(ch, device="cuda") for k in ("b0", "b2", "b5")})
+    w = np.zeros((ch, ch), np.float16)
+    l3 = gpu.linear(O.TY_F16, ch, ch, w.tobytes(), np.zeros(ch, np.float32))
+    lo = gpu.linear(O.TY_F16, 64, 16 * ch, np.zeros((64, 16 * ch), np.float16).tobytes(),
+                    np.zeros(64, np.float32))
+    mel = torch.zeros(200, 128, device="cuda")
+    x = torch.zeros(64, 64, device="cuda")
+    scratch = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    for frames, valid in (([100, 1], [100, 1]), ([100, 100], [100, 0]), ([100, 50], [100, 51])):
+        with pytest.raises(L.WavoError):
+            gpu.subsample_batch(mel, frames, valid, taps, l3, l3, lo, x, scratch)
+    assert gpu.subsample_batch(mel, [], [], taps, l3, l3, lo, x, scratch) == []

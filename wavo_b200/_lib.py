@@ -50,6 +50,9 @@ SIGNATURES = {
     "wavo_subsample_scratch_bytes": ([_u32, _u32], _u64),
     "wavo_subsample": ([_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                         _vp, _vp, ctypes.POINTER(_u32)], _st),
+    "wavo_subsample_batch_scratch_bytes": ([_vp, _u32, _u32], _u64),
+    "wavo_subsample_batch": ([_vp, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                              _vp, _vp, _vp, _vp, _vp], _st),
     "wavo_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], _st),
     "wavo_gguf_close": ([_vp], None),
     "wavo_gguf_tensor_count": ([_vp], _u32),

@@ -1350,6 +1350,104 @@ wavo_status wavo_subsample(wavo_ctx *ctx, const float *mel, uint32_t frames, uin
   return WAVO_OK;
 }
 
+namespace {
+// The batch's scratch: conv0/conv2's image and conv3's output for the largest segment (reused
+// segment after segment), then conv5's, conv6's and the flatten's images of every segment.
+struct SubsampleBatchLayout {
+  uint64_t a_bytes, h_bytes, total, rows;  // rows: the segments' output rows
+};
+bool subsample_batch_layout(const uint32_t *frames, uint32_t n, uint64_t ch,
+                            SubsampleBatchLayout *L) {
+  uint64_t t2_max = 0, rows = 0;
+  for (uint32_t s = 0; s < n; ++s) {
+    if (frames[s] < 2) return false;
+    const SubsampleLayout one = subsample_layout(frames[s], ch);
+    t2_max = one.t2 > t2_max ? one.t2 : t2_max;
+    rows += one.t;
+  }
+  L->rows = rows;
+  L->a_bytes = align_up(t2_max * 32 * ch * 4, 256);
+  L->h_bytes = align_up(rows * 16 * ch * 4, 256);
+  L->total = 2 * L->a_bytes + 3 * L->h_bytes;
+  return true;
+}
+}  // namespace
+
+uint64_t wavo_subsample_batch_scratch_bytes(const uint32_t *frames, uint32_t n, uint32_t ch) {
+  SubsampleBatchLayout L{};
+  return frames && n && ch && subsample_batch_layout(frames, n, ch, &L) ? L.total : 0;
+}
+
+wavo_status wavo_subsample_batch(wavo_ctx *ctx, const float *mel, const uint32_t *frames,
+                                 const uint32_t *valid, uint32_t n, uint32_t ch, const float *w0,
+                                 const float *b0, const float *w2, const float *b2,
+                                 const wavo_linear *conv3, const float *w5, const float *b5,
+                                 const wavo_linear *conv6, const wavo_linear *out, float *x,
+                                 void *scratch, uint32_t *t_out) {
+  if (!ctx) return WAVO_EINVAL;
+  if (n == 0) return WAVO_OK;
+  if (!mel || !frames || !valid || !w0 || !b0 || !w2 || !b2 || !w5 || !b5 || !conv3 || !conv6 ||
+      !out || !x || !scratch)
+    return fail(ctx, WAVO_EINVAL, "subsample batch: NULL argument");
+  for (uint32_t s = 0; s < n; ++s)
+    if (frames[s] < 2 || valid[s] == 0 || valid[s] > frames[s])
+      return fail(ctx, WAVO_EINVAL, "subsample batch: segment %u has %u frames (%u valid)", s,
+                  frames[s], valid[s]);
+  if (ch == 0 || ch % 32 != 0 || ch > 4096)
+    return fail(ctx, WAVO_EINVAL, "subsample batch: %u channels", ch);
+  if (conv3->k != ch || conv3->cols != ch || conv3->dual || conv6->k != ch || conv6->cols != ch ||
+      conv6->dual || out->k != 16 * ch || out->dual)
+    return fail(ctx, WAVO_EINVAL, "subsample batch: the pointwise layers must be %u -> %u and the "
+                "output projection %u -> d", ch, ch, 16 * ch);
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u)
+    return fail(ctx, WAVO_EINVAL, "subsample batch: scratch must be 256-byte aligned");
+  SubsampleBatchLayout L{};
+  subsample_batch_layout(frames, n, ch, &L);
+  if (L.rows * 16 > UINT32_MAX)
+    return fail(ctx, WAVO_EINVAL, "subsample batch: %llu output rows", (unsigned long long)L.rows);
+  uint8_t *sp = static_cast<uint8_t *>(scratch);
+  __half *a = reinterpret_cast<__half *>(sp);
+  float *b = reinterpret_cast<float *>(sp + L.a_bytes);
+  __half *h = reinterpret_cast<__half *>(sp + 2 * L.a_bytes);
+  float *y = reinterpret_cast<float *>(sp + 2 * L.a_bytes + L.h_bytes);
+  __half *flat = reinterpret_cast<__half *>(sp + 2 * L.a_bytes + 2 * L.h_bytes);
+  // Per segment (its conv3 output, 32 KB a conv2 row, stays in L2 for conv5): conv0/conv2, conv3,
+  // conv5 into the segment's rows of h.
+  uint64_t mel_row = 0, row = 0;
+  for (uint32_t s = 0; s < n; ++s) {
+    const SubsampleLayout one = subsample_layout(frames[s], ch);
+    const int t2 = int(one.t2), t = int(one.t);
+    {
+      std::lock_guard<std::mutex> g(ctx->mu);
+      cudaSetDevice(ctx->device);
+      CK(wv::launch_conv02(mel + mel_row * 128, int(valid[s]), t2, int(ch), w0, b0, w2, b2, a,
+                           ctx->stream),
+         "subsample conv0/conv2 launch");
+    }
+    wavo_status st = wavo_gemm(ctx, a, WAVO_F16, ch, conv3, b, WAVO_F32, ch, uint32_t(t2) * 32,
+                               WAVO_EPI_RELU, 1.0f);
+    if (st != WAVO_OK) return st;
+    {
+      std::lock_guard<std::mutex> g(ctx->mu);
+      CK(wv::launch_dw3s2(b, t2, 32, int(ch), t, w5, b5, h + row * 16 * ch, ctx->stream),
+         "subsample conv5 launch");
+    }
+    if (t_out) t_out[s] = uint32_t(t);
+    mel_row += frames[s];
+    row += uint64_t(t);
+  }
+  // Every segment's rows at once: conv6, the flatten (row by row), the output projection.
+  const uint32_t rows = uint32_t(L.rows);
+  wavo_status st = wavo_gemm(ctx, h, WAVO_F16, ch, conv6, y, WAVO_F32, ch, rows * 16,
+                             WAVO_EPI_RELU, 1.0f);
+  if (st != WAVO_OK) return st;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    CK(wv::launch_flatten(y, int(rows), 16, int(ch), flat, ctx->stream), "subsample flatten launch");
+  }
+  return wavo_gemm(ctx, flat, WAVO_F16, 16 * ch, out, x, WAVO_F32, 0, rows, WAVO_EPI_BIAS, 1.0f);
+}
+
 // ---- rope --------------------------------------------------------------------------------
 
 wavo_status wavo_rope_rows(wavo_ctx *ctx, const float *table, void *qkv, int dtype,

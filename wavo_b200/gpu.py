@@ -168,6 +168,26 @@ class Gpu:
         self._keep = scratch  # the launches read it until the stream passes them
         return t.value
 
+    def subsample_batch(self, mel: torch.Tensor, frames, valid, taps: dict, conv3: Linear,
+                        conv6: Linear, out: Linear, x: torch.Tensor,
+                        scratch: torch.Tensor | None = None) -> list[int]:
+        """subsample over segments whose mel rows (frames[s] each, valid[s] of them audio) follow
+        one another in mel; their output rows follow one another in x. Returns each t_s."""
+        n, ch = len(frames), taps["b0"].numel()
+        fr = (ctypes.c_uint32 * max(n, 1))(*[int(f) for f in frames])
+        va = (ctypes.c_uint32 * max(n, 1))(*[int(v) for v in valid])
+        ts = (ctypes.c_uint32 * max(n, 1))()
+        if scratch is None:
+            nbytes = int(L.lib().wavo_subsample_batch_scratch_bytes(fr, n, ch))
+            scratch = torch.empty(nbytes + 256, dtype=torch.uint8, device=self.torch_device)
+        base = (scratch.data_ptr() + 255) // 256 * 256
+        check(L.lib().wavo_subsample_batch(self.ctx, _ptr(mel), fr, va, n, ch, _ptr(taps["w0"]),
+                                           _ptr(taps["b0"]), _ptr(taps["w2"]), _ptr(taps["b2"]),
+                                           conv3.h, _ptr(taps["w5"]), _ptr(taps["b5"]), conv6.h,
+                                           out.h, _ptr(x), base, ts), self.ctx)
+        self._keep = scratch  # the launches read it until the stream passes them
+        return list(ts)[:n]
+
     def linear_from_gguf(self, gguf, names: list[str], bias=None) -> Linear:
         """`Gpu::linear` over GGUF tensors, streamed from the file to the device."""
         return Linear.from_gguf(self, gguf, names, bias)
