@@ -3,19 +3,20 @@
 // filterbank as f32 fused multiply-adds in bin order, ln(mel + 2^-24), then each mel bin normalised
 // over all frames but the last, which is zero. The FFT performs the reference's operations in its
 // order (radix-2 decimation in time, Stockham order, every multiply-add fused, the same cos/sin
-// table), so the spectrum is the reference's bit for bit; the reductions of the normalisation are
-// f64 sums in a fixed order (chunks of frames, then the chunks in order).
+// table), so the spectrum is the reference's bit for bit; the normalisation's statistics are f64
+// sums of each bin's values and squares in a fixed order (a warp's frames in turn, a CTA's warps,
+// the CTAs), its squared deviations Σx² − mean·Σx.
 //
-//   log_mel_kernel   a warp a frame at a time (13 warps, one CTA an SM, looping over frames): the
+//   log_mel_kernel   a warp a frame at a time (16 warps, one CTA an SM, looping over frames): the
 //                    tables copied once into shared memory, the frame's pcm staged from
 //                    registers (the next frame's fetched during this one's FFT), the windowed
-//                    frame in the first stage's order, nine butterfly stages between two
-//                    shared-memory buffers (16-byte loads of each butterfly's input pair), the
-//                    power spectrum, four mel bins a lane.
-//   mel_sum_kernel   per chunk of 64 frames, a thread a mel bin: the f64 sum of the values (or of
-//                    the squared deviations from the mean) in frame order (coalesced rows, eight
-//                    loads in flight).
-//   mel_stats_kernel the chunk sums in order: the mean, then 1 / (unbiased std + 1e-5).
+//                    frame in registers, 16 complex values a lane, the nine butterfly stages in
+//                    three register phases with two exchanges through the warp's shared buffer,
+//                    the power spectrum, four mel bins a lane.
+//                    For the normalised features it also sums each bin's values and squares
+//                    over the frames it takes (f64, in a fixed order: a warp's frames in turn,
+//                    the CTA's warps in order).
+//   mel_stats_kernel the CTAs' sums in order: the mean, then 1 / (unbiased std + 1e-5).
 //   mel_norm_kernel  (x - mean)·inv to f32; the last frame zero.
 //   conv02_kernel / dw3s2_kernel / flatten_kernel
 //                    Parakeet's 8x conv subsampling around the pointwise GEMMs
@@ -33,31 +34,59 @@ namespace wv {
 namespace {
 
 constexpr int FE_MELS = 128, FE_NFFT = 512, FE_WINDOW = 400, FE_HOP = 160, FE_BINS = 257;
-constexpr int FE_STAGES = 9, FE_HALF = FE_NFFT / 2;
-constexpr int FE_WARPS = 13;  // one CTA an SM: 13 frames in flight (16 KB of buffers each)
-constexpr int FE_CHUNK = 64;
+
+constexpr int FE_WARPS = 12;  // one CTA an SM: 12 frames in flight (8 KB of buffer, 164 registers)
 
 constexpr int FE_SPAN_MAX = 16;  // FFT bins in a mel bin's nonzero span (12 for the Slaney bank)
 constexpr int FE_STAGE_P = FE_NFFT + 1;               // pcm samples a frame reads
 constexpr int FE_PF = (FE_STAGE_P + 31) / 32;         // of them a lane's (17)
+constexpr int FE_TWL = 23;                            // a lane's twiddles of stages 4..8
 
+// The FFT in registers. Stage t of the reference's radix-2 Stockham FFT (output i from inputs 2i
+// and 2i + 1, to positions i and i + 256) moves the element of label L from position rotr^t(L) to
+// rotr^(t+1)(L) (9-bit rotations), pairing the labels that differ in bit t; label L starts at
+// position L (the sample perm(L) = bitrev9(L)) and ends at frequency bin L. A lane holds 16 labels:
+// stages 0-3 with label bits 0-3 in its registers (lane = bits 4-8), stages 4-7 with bits 4-7
+// (lane = bits 0-3, 8), stage 8 with bits 0-2, 8 (lane = bits 3-7); the labels move between these
+// layouts through the warp's shared buffer twice. Every butterfly has the reference's inputs,
+// twiddle (idx = the label's low t bits · 2^(8-t)) and fused multiply-adds, so the spectrum is
+// the same bit for bit.
+//
 // Shared tables of a CTA, built once on the host as one image in this layout: the 256 twiddles
-// (every stage's twiddle is one of them: output i of the stage to blocks of `size` takes index
-// i / (512 / size) · (512 / size)), the window in the first stage's order, that order, and the
-// filterbank as each mel bin's nonzero span, weight k of bin m at fw[k][m] (a warp's lanes read
-// consecutive words).
+// (cos, sin)(tau·idx/512); each lane's twiddles of stages 4-8 ([k][lane]: stage 4 one, 5 two, 6
+// four, 7 eight, 8 eight); the window by sample index; the filterbank as each mel bin's nonzero
+// span, weight k of bin m at fw[k][m] (a warp's lanes read consecutive words).
 struct FeShared {
-  double twc[256], tws[256], win[FE_NFFT];
+  double2 tw[256];
+  double2 twl[FE_TWL][32];
+  double win[FE_NFFT];
   float fw[FE_SPAN_MAX][FE_MELS];
   int lo[FE_MELS], len[FE_MELS];
-  uint16_t perm[FE_NFFT];
 };
 static_assert(sizeof(FeShared) % 16 == 0, "the image is copied in 16-byte words");
-constexpr size_t FE_SMEM = sizeof(FeShared) + size_t(FE_WARPS) * 4 * FE_NFFT * 8;
+constexpr size_t FE_BUF = FE_NFFT * sizeof(double2);  // a warp's buffer: the labels' exchange
+// Then the warps' per-bin sums of the features and of their squares for the normalisation
+// ([warp][2][128] f64).
+constexpr size_t FE_ACC = size_t(FE_WARPS) * 2 * FE_MELS * 8;
+constexpr size_t FE_SMEM = sizeof(FeShared) + size_t(FE_WARPS) * FE_BUF + FE_ACC;
 
-// The frame's pcm is staged with a word of padding every 16: the first stage's order reads it at a
-// stride of 16 words, which the padding spreads over all 32 banks.
-__device__ __forceinline__ int fe_pad(int p) { return p + (p >> 4); }
+// Where label L sits in the exchange buffer: its low three bits XOR a function of bits 3-7, so
+// that every quarter-warp's eight 16-byte accesses of each layout fall in distinct bank groups.
+__device__ __forceinline__ int fe_phys(int L) { return L ^ (((L >> 4) ^ (L >> 3)) & 7); }
+
+// The butterfly of src/fft.rs:131-143: (a, b) at position 2i, (x, y) at 2i + 1, twiddle w; the
+// results go to i (a, b) and i + 256 (x, y).
+__device__ __forceinline__ void fe_bfly(double &a, double &b, double &x, double &y, double2 w) {
+  const double c = w.x, s = w.y;
+  const double r0 = fma(s, y, fma(c, x, a));
+  const double i0 = fma(-s, x, fma(c, y, b));
+  const double r1 = fma(-s, y, fma(-c, x, a));
+  const double i1 = fma(s, x, fma(-c, y, b));
+  a = r0;
+  b = i0;
+  x = r1;
+  y = i1;
+}
 
 // A lane's share of frame t's pcm (samples (f0 + t)·160 − 257 + p, p = lane + 32·q; 0 outside).
 __device__ __forceinline__ void fe_fetch(const float *__restrict__ pcm, long long n_pcm,
@@ -72,7 +101,10 @@ __device__ __forceinline__ void fe_fetch(const float *__restrict__ pcm, long lon
 
 __global__ void __launch_bounds__(32 * FE_WARPS, 1)
     log_mel_kernel(const float *__restrict__ pcm, long long n_pcm, long long f0, int frames,
-                   const FrontendTables tab, float *__restrict__ mel) {
+                   const FrontendTables tab, float *__restrict__ mel, int stat_frames,
+                   double *__restrict__ part) {
+  // part != nullptr: also this CTA's per-bin f64 sums of the features of frames < stat_frames and
+  // of their squares (part[blockIdx][0][m], part[blockIdx][1][m]), its warps added in order.
   extern __shared__ double fe_smem[];
   FeShared &sh = *reinterpret_cast<FeShared *>(fe_smem);
   {  // the constant tables, every load in flight at once, before the wait
@@ -96,9 +128,15 @@ __global__ void __launch_bounds__(32 * FE_WARPS, 1)
   griddep_wait();
   __syncthreads();
   const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
-  double *ar = fe_smem + sizeof(FeShared) / 8 + warp * 4 * FE_NFFT, *ai = ar + FE_NFFT;
-  double *br = ai + FE_NFFT, *bi = br + FE_NFFT;
-  float *stage = reinterpret_cast<float *>(br);  // the frame's pcm, before the first stage
+  double2 *xb = reinterpret_cast<double2 *>(reinterpret_cast<char *>(fe_smem) + sizeof(FeShared) +
+                                            size_t(warp) * FE_BUF);
+  float *stage = reinterpret_cast<float *>(xb);  // the frame's pcm, before the first exchange
+  double *acc = reinterpret_cast<double *>(reinterpret_cast<char *>(fe_smem) + sizeof(FeShared) +
+                                           size_t(FE_WARPS) * FE_BUF) +
+                warp * 2 * FE_MELS;
+#pragma unroll
+  for (int q = 0; q < FE_MELS / 32; ++q) acc[lane + 32 * q] = acc[FE_MELS + lane + 32 * q] = 0.0;
+  const int lrev = int(__brev(unsigned(lane)) >> 27);  // bitrev5(lane)
   const int step = int(gridDim.x) * FE_WARPS;
   int t = int(blockIdx.x) * FE_WARPS + warp;
   float pf[FE_PF];
@@ -106,65 +144,81 @@ __global__ void __launch_bounds__(32 * FE_WARPS, 1)
 #pragma unroll 1
   for (; t < frames; t += step) {
     const long long j0 = (f0 + t) * FE_HOP;  // the frame's first padded index + 256
-    // Stage the frame's pcm (545 words with the padding, inside the second buffer), then fetch
-    // the next frame's while this one is transformed.
+    // Stage the frame's pcm, then fetch the next frame's while this one is transformed.
 #pragma unroll
     for (int q = 0; q < FE_PF; ++q) {
       const int p = lane + 32 * q;
-      if (p < FE_STAGE_P) stage[fe_pad(p)] = pf[q];
+      if (p < FE_STAGE_P) stage[p] = pf[q];
     }
     if (t + step < frames) fe_fetch(pcm, n_pcm, (f0 + t + step) * FE_HOP, lane, pf);
     __syncwarp();
-    // The windowed, pre-emphasised frame in the first stage's order (src/fft.rs:89-92).
-    double xs[FE_NFFT / 32];
+    // Label lane·16 + r: position lane·16 + r holds sample bitrev4(r)·32 + bitrev5(lane),
+    // pre-emphasised and windowed (src/fft.rs:89-92).
+    double re[16], im[16];
 #pragma unroll
-    for (int q = 0; q < FE_NFFT / 32; ++q) {
-      const int v = lane + 32 * q;
-      const int i = sh.perm[v];
+    for (int r = 0; r < 16; ++r) {
+      const int rrev = ((r & 1) << 3) | ((r & 2) << 1) | ((r & 4) >> 1) | ((r & 8) >> 3);
+      const int i = (rrev << 5) | lrev;
       const long long j = j0 + i - FE_NFFT / 2;  // the pcm index of padded sample j0 + i
       double s = 0.0;
       if (j == 0)
-        s = double(stage[fe_pad(i + 1)]);
+        s = double(stage[i + 1]);
       else if (j > 0 && j < n_pcm)
-        s = __dsub_rn(double(stage[fe_pad(i + 1)]), __dmul_rn(double(0.97f), double(stage[fe_pad(i)])));
-      xs[q] = __dmul_rn(s, sh.win[v]);
+        s = __dsub_rn(double(stage[i + 1]), __dmul_rn(double(0.97f), double(stage[i])));
+      re[r] = __dmul_rn(s, sh.win[i]);
+      im[r] = 0.0;
     }
-    __syncwarp();  // the staged pcm is read before the buffer is reused
+    // Stages 0-3: label bit t is register bit t; the twiddle is the same for every lane.
 #pragma unroll
-    for (int q = 0; q < FE_NFFT / 32; ++q) {
-      ar[lane + 32 * q] = xs[q];
-      ai[lane + 32 * q] = 0.0;
-    }
-    __syncwarp();
-    // Nine radix-2 stages (src/fft.rs:131-143): output i reads inputs 2i and 2i + 1.
-    double *sr = ar, *si = ai, *dr = br, *di = bi;
-#pragma unroll 1
-    for (int st = 0; st < FE_STAGES; ++st) {
-      const int sh_bits = 8 - st;
+    for (int st = 0; st < 4; ++st)
 #pragma unroll
-      for (int q = 0; q < FE_HALF / 32; ++q) {
-        const int i = lane + 32 * q;
-        const int idx = (i >> sh_bits) << sh_bits;
-        const double c = sh.twc[idx], s = sh.tws[idx];
-        const double2 xr = reinterpret_cast<const double2 *>(sr)[i];
-        const double2 xi = reinterpret_cast<const double2 *>(si)[i];
-        const double a = xr.x, x = xr.y, b = xi.x, y = xi.y;
-        dr[i] = fma(s, y, fma(c, x, a));
-        di[i] = fma(-s, x, fma(c, y, b));
-        dr[i + FE_HALF] = fma(-s, y, fma(-c, x, a));
-        di[i + FE_HALF] = fma(s, x, fma(-c, y, b));
+      for (int r0 = 0; r0 < 16; ++r0) {
+        if ((r0 >> st) & 1) continue;
+        const int r1 = r0 | (1 << st);
+        fe_bfly(re[r0], im[r0], re[r1], im[r1], sh.tw[(r0 & ((1 << st) - 1)) << (8 - st)]);
       }
-      __syncwarp();
-      double *tr = sr, *ti = si;
-      sr = dr;
-      si = di;
-      dr = tr;
-      di = ti;
+    __syncwarp();  // the staged pcm is read before the buffer takes the labels
+#pragma unroll
+    for (int r = 0; r < 16; ++r) xb[fe_phys((lane << 4) | r)] = make_double2(re[r], im[r]);
+    __syncwarp();
+    // Stages 4-7: label bits 4-7 in the registers (each lane reads back the slots it writes).
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const double2 v = xb[fe_phys((lane & 15) | (r << 4) | ((lane >> 4) << 8))];
+      re[r] = v.x;
+      im[r] = v.y;
     }
-    // The power spectrum (f64 products and sum, cast to f32) over the freed buffer.
-    float *power = reinterpret_cast<float *>(dr);
-    for (int k = lane; k < FE_BINS; k += 32)
-      power[k] = float(__dadd_rn(__dmul_rn(sr[k], sr[k]), __dmul_rn(si[k], si[k])));
+#pragma unroll
+    for (int st = 4; st < 8; ++st) {
+      const int bit = st - 4, base = (1 << bit) - 1;  // stage st's first twl row
+#pragma unroll
+      for (int r0 = 0; r0 < 16; ++r0) {
+        if ((r0 >> bit) & 1) continue;
+        const int r1 = r0 | (1 << bit);
+        fe_bfly(re[r0], im[r0], re[r1], im[r1], sh.twl[base + (r0 & ((1 << bit) - 1))][lane]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      xb[fe_phys((lane & 15) | (r << 4) | ((lane >> 4) << 8))] = make_double2(re[r], im[r]);
+    __syncwarp();
+    // Stage 8: label bits 0-2 and 8 in the registers.
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const double2 v = xb[fe_phys((r & 7) | (lane << 3) | ((r >> 3) << 8))];
+      re[r] = v.x;
+      im[r] = v.y;
+    }
+    __syncwarp();  // every label read before the power spectrum takes the buffer
+#pragma unroll
+    for (int r0 = 0; r0 < 8; ++r0) fe_bfly(re[r0], im[r0], re[r0 + 8], im[r0 + 8], sh.twl[15 + r0][lane]);
+    // The power spectrum (f64 products and sum, cast to f32): bins lane·8 + r, and bin 256.
+    float *power = reinterpret_cast<float *>(xb);
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      power[(lane << 3) | r] =
+          float(__dadd_rn(__dmul_rn(re[r], re[r]), __dmul_rn(im[r], im[r])));
+    if (lane == 0) power[256] = float(__dadd_rn(__dmul_rn(re[8], re[8]), __dmul_rn(im[8], im[8])));
     __syncwarp();
     float *out = mel + (long long)t * FE_MELS;
 #pragma unroll
@@ -173,45 +227,42 @@ __global__ void __launch_bounds__(32 * FE_WARPS, 1)
       const float *pw = power + sh.lo[m];
       float e = 0.0f;
       for (int k = 0; k < sh.len[m]; ++k) e = fmaf(sh.fw[k][m], pw[k], e);
-      out[m] = logf(__fadd_rn(e, 1.0f / float(1 << 24)));
+      const float v = logf(__fadd_rn(e, 1.0f / float(1 << 24)));
+      out[m] = v;
+      if (t < stat_frames) {  // a lane's own bins: no other lane touches these words
+        const double x = double(v);
+        acc[m] = __dadd_rn(acc[m], x);
+        acc[FE_MELS + m] = __dadd_rn(acc[FE_MELS + m], __dmul_rn(x, x));
+      }
     }
-    __syncwarp();  // power (in dr) is read before the next frame stages its pcm into br
+    __syncwarp();  // power is read before the next frame stages its pcm
+  }
+  if (part == nullptr) return;  // uniform over the CTA
+  __syncthreads();
+  const double *all = acc - warp * 2 * FE_MELS;
+  for (int e = int(threadIdx.x); e < 2 * FE_MELS; e += blockDim.x) {
+    double v = 0.0;
+    for (int w = 0; w < FE_WARPS; ++w) v = __dadd_rn(v, all[w * 2 * FE_MELS + e]);
+    part[(long long)blockIdx.x * 2 * FE_MELS + e] = v;
   }
 }
 
-// Per chunk of FE_CHUNK frames of the first n, thread m: the f64 sum in frame order of mel values
-// (mean == nullptr) or of their squared deviations from mean[m].
-__global__ void mel_sum_kernel(const float *__restrict__ mel, long long n,
-                               const double *__restrict__ mean, double *__restrict__ part) {
+// The CTAs' sums in order (thread m a bin): mean = Σx / n and, from Σx² − mean·Σx (the squared
+// deviations' sum), inv = 1 / (sqrt(Σ(x − mean)² / (n − 1)) + 1e-5).
+__global__ void mel_stats_kernel(const double *__restrict__ part, int ctas, long long n,
+                                 double *__restrict__ mean, double *__restrict__ inv) {
   griddep_launch_dependents();
   griddep_wait();
   const int m = int(threadIdx.x);
-  const long long t0 = (long long)blockIdx.x * FE_CHUNK;
-  const long long t1 = t0 + FE_CHUNK < n ? t0 + FE_CHUNK : n;
-  double s = 0.0;
-  const double mu = mean ? mean[m] : 0.0;
-#pragma unroll 8
-  for (long long t = t0; t < t1; ++t) {
-    const double x = double(mel[t * FE_MELS + m]);
-    if (mean) {
-      const double d = __dsub_rn(x, mu);
-      s = __dadd_rn(s, __dmul_rn(d, d));
-    } else {
-      s = __dadd_rn(s, x);
-    }
+  double sx = 0.0, sq = 0.0;
+  for (int c = 0; c < ctas; ++c) {
+    sx = __dadd_rn(sx, part[(long long)c * 2 * FE_MELS + m]);
+    sq = __dadd_rn(sq, part[(long long)c * 2 * FE_MELS + FE_MELS + m]);
   }
-  part[(long long)blockIdx.x * FE_MELS + m] = s;
-}
-
-// The chunk sums in order: mean = Σ / n (var == nullptr), or inv = 1 / (sqrt(Σ / (n - 1)) + 1e-5).
-__global__ void mel_stats_kernel(const double *__restrict__ part, int chunks, long long n,
-                                 double *__restrict__ out, int is_var) {
-  griddep_launch_dependents();
-  griddep_wait();
-  const int m = int(threadIdx.x);
-  double s = 0.0;
-  for (int c = 0; c < chunks; ++c) s = __dadd_rn(s, part[(long long)c * FE_MELS + m]);
-  out[m] = is_var ? 1.0 / __dadd_rn(sqrt(s / double(n - 1)), double(1e-5f)) : s / double(n);
+  const double mu = sx / double(n);
+  const double ss = fmax(__dsub_rn(sq, __dmul_rn(mu, sx)), 0.0);
+  mean[m] = mu;
+  inv[m] = 1.0 / __dadd_rn(sqrt(ss / double(n - 1)), double(1e-5f));
 }
 
 __global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
@@ -365,28 +416,29 @@ __global__ void flatten_kernel(const float *__restrict__ y, int t, int f, int ch
 size_t frontend_table_bytes() { return sizeof(FeShared); }
 
 cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *out) {
+  // The first stage's order (src/fft.rs: all 512 points radix-2 blocks, the even samples before
+  // the odd ones at every level) is the 9-bit reversal, which the kernel computes.
   const int n = FE_NFFT;
-  std::vector<int> starts{0};
-  while (int(starts.size()) < n) {  // leaf 1: all 512 points are radix-2 blocks
-    std::vector<int> next;
-    for (int v : starts) next.push_back(2 * v);
-    for (int v : starts) next.push_back(2 * v + 1);
-    starts = next;
-  }
-  std::unique_ptr<FeShared> owner(new FeShared());  // the image (18 KB), zero-filled
+  std::unique_ptr<FeShared> owner(new FeShared());  // the image (29 KB), zero-filled
   FeShared &img = *owner;
-  for (int i = 0; i < n; ++i) img.perm[i] = uint16_t(starts[i]);
-  // The stages' twiddles: stage `size` takes cos/sin(tau·idx/512) at idx = i / (512 / size) ·
-  // (512 / size), one of these 256.
+  // The twiddles: stage t's butterfly on label L0 (bit t clear) takes cos/sin(tau·idx/512) at
+  // idx = (L0 mod 2^t)·2^(8-t), the reference's i / (512 / size) · (512 / size).
   const double tau = 6.283185307179586;
   for (int idx = 0; idx < n / 2; ++idx) {
     const double phase = tau * double(idx) / double(n);
-    img.twc[idx] = std::cos(phase);
-    img.tws[idx] = std::sin(phase);
+    img.tw[idx] = make_double2(std::cos(phase), std::sin(phase));
   }
-  for (int v = 0; v < n; ++v) {  // the window, read in the first stage's order
-    const int k = int(starts[v]) - (FE_NFFT - FE_WINDOW) / 2;
-    img.win[v] = k >= 0 && k < FE_WINDOW
+  auto tw_of = [&](int t, int L0) { return img.tw[(L0 & ((1 << t) - 1)) << (8 - t)]; };
+  for (int l = 0; l < 32; ++l) {
+    for (int t = 4; t < 8; ++t)  // labels (l mod 16) | r·16 | (l / 16)·256: r's low t-4 bits
+      for (int rl = 0; rl < (1 << (t - 4)); ++rl)
+        img.twl[(1 << (t - 4)) - 1 + rl][l] = tw_of(t, (l & 15) | (rl << 4));
+    for (int r0 = 0; r0 < 8; ++r0)  // labels r0 | l·8 (| 256)
+      img.twl[15 + r0][l] = tw_of(8, r0 | (l << 3));
+  }
+  for (int i = 0; i < n; ++i) {  // the window by sample index
+    const int k = i - (FE_NFFT - FE_WINDOW) / 2;
+    img.win[i] = k >= 0 && k < FE_WINDOW
                      ? 0.5 - 0.5 * std::cos(2.0 * M_PI * double(k) / double(FE_WINDOW - 1))
                      : 0.0;
   }
@@ -431,54 +483,64 @@ cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *ou
   return e;
 }
 
-cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int frames,
-                           const FrontendTables &tab, float *mel, cudaStream_t s) {
-  if (frames <= 0) return cudaSuccess;
-  // The shared tables, then four 512-point complex f64 buffers a warp (16 KB).
-  const size_t smem = FE_SMEM;
+namespace {
+int log_mel_ctas(int frames, cudaError_t *err) {
+  // One CTA an SM at most, each warp looping over frames (the tables load once a CTA).
   static bool configured[64] = {};
   static int sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64) return cudaErrorInvalidDevice;
+  *err = cudaSuccess;
+  if (dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return 0;
+  }
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(log_mel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(smem));
+                                         int(FE_SMEM));
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      *err = e;
+      return 0;
+    }
     configured[dev] = true;
   }
-  // One CTA an SM at most, each warp looping over frames (the tables load once a CTA).
-  int ctas = (frames + FE_WARPS - 1) / FE_WARPS;
-  if (ctas > sms[dev]) ctas = sms[dev];
-  return launch_pdl(log_mel_kernel, dim3(ctas), dim3(32 * FE_WARPS), smem, s, pcm, n_pcm, f0,
-                    frames, tab, mel);
+  const int ctas = (frames + FE_WARPS - 1) / FE_WARPS;
+  return ctas < sms[dev] ? ctas : sms[dev];
+}
+}  // namespace
+
+cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int frames,
+                           const FrontendTables &tab, float *mel, cudaStream_t s) {
+  if (frames <= 0) return cudaSuccess;
+  cudaError_t e;
+  const int ctas = log_mel_ctas(frames, &e);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(log_mel_kernel, dim3(ctas), dim3(32 * FE_WARPS), FE_SMEM, s, pcm, n_pcm, f0,
+                    frames, tab, mel, 0, (double *)nullptr);
 }
 
-size_t mel_norm_scratch_bytes(long long frames) {
-  const long long chunks = (frames + FE_CHUNK - 1) / FE_CHUNK;
-  return size_t(chunks) * FE_MELS * 8 + 2 * FE_MELS * 8;
-}
+size_t mel_features_scratch_bytes(int sms) { return (size_t(sms) * 2 + 2) * FE_MELS * 8; }
 
-cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStream_t s) {
+cudaError_t launch_mel_features(const float *pcm, long long n_pcm, int frames,
+                                const FrontendTables &tab, float *mel, void *scratch, int sms,
+                                cudaStream_t s) {
   const long long n = frames - 1;  // statistics over all frames but the last
   if (n < 2) return cudaErrorInvalidValue;
-  const int chunks = int((n + FE_CHUNK - 1) / FE_CHUNK);
-  double *part = static_cast<double *>(scratch);
-  double *mean = part + (long long)chunks * FE_MELS, *inv = mean + FE_MELS;
   cudaError_t e;
-  if ((e = launch_pdl(mel_sum_kernel, dim3(chunks), dim3(FE_MELS), 0, s, (const float *)mel, n,
-                      (const double *)nullptr, part)) != cudaSuccess ||
-      (e = launch_pdl(mel_stats_kernel, dim3(1), dim3(FE_MELS), 0, s, (const double *)part,
-                      chunks, n, mean, 0)) != cudaSuccess ||
-      (e = launch_pdl(mel_sum_kernel, dim3(chunks), dim3(FE_MELS), 0, s, (const float *)mel, n,
-                      (const double *)mean, part)) != cudaSuccess ||
-      (e = launch_pdl(mel_stats_kernel, dim3(1), dim3(FE_MELS), 0, s, (const double *)part,
-                      chunks, n, inv, 1)) != cudaSuccess)
+  const int ctas = log_mel_ctas(frames, &e);
+  if (e != cudaSuccess) return e;
+  if (ctas > sms) return cudaErrorInvalidValue;  // the scratch holds sms CTAs' sums
+  double *part = static_cast<double *>(scratch);
+  double *mean = part + (long long)sms * 2 * FE_MELS, *inv = mean + FE_MELS;
+  if ((e = launch_pdl(log_mel_kernel, dim3(ctas), dim3(32 * FE_WARPS), FE_SMEM, s, pcm, n_pcm,
+                      0LL, frames, tab, mel, int(n), part)) != cudaSuccess ||
+      (e = launch_pdl(mel_stats_kernel, dim3(1), dim3(FE_MELS), 0, s, (const double *)part, ctas,
+                      n, mean, inv)) != cudaSuccess)
     return e;
-  const long long total = frames * FE_MELS;
+  const long long total = (long long)frames * FE_MELS;
   return launch_pdl(mel_norm_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, mel,
-                    frames, (const double *)mean, (const double *)inv);
+                    (long long)frames, (const double *)mean, (const double *)inv);
 }
 
 }  // namespace wv

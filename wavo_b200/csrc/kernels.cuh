@@ -198,8 +198,14 @@ cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *ou
 cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int frames,
                            const FrontendTables &tab, float *mel, cudaStream_t s);
 // Each mel bin normalised over frames 0 .. frames - 2, the last frame zeroed (frames >= 3).
-size_t mel_norm_scratch_bytes(long long frames);
-cudaError_t launch_mel_norm(float *mel, long long frames, void *scratch, cudaStream_t s);
+// mel [frames][128] = the normalised log-mel features of all frames of the pcm (frames =
+// n_pcm / 160 + 1 ≥ 3): each bin less its mean over all frames but the last, times 1 / (the
+// unbiased std + 1e-5); the last frame zero. scratch: mel_features_scratch_bytes(sms) bytes, sms =
+// the device's SM count.
+size_t mel_features_scratch_bytes(int sms);
+cudaError_t launch_mel_features(const float *pcm, long long n_pcm, int frames,
+                                const FrontendTables &tab, float *mel, void *scratch, int sms,
+                                cudaStream_t s);
 
 // Parakeet's subsampling around its GEMMs, each output the next GEMM's f16 operand: conv0 + ReLU
 // + conv2 from the mel image into a [t2][32][ch] (rows from half(half(valid)) on zero); a depthwise

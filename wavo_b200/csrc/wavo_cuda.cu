@@ -1267,13 +1267,17 @@ wavo_status wavo_mel_features(wavo_ctx *ctx, const float *pcm, uint64_t samples,
   const uint64_t n = samples / 160 + 1;
   if (n < 3) return WAVO_OK;  // too few frames for the normalisation: no features
   if (n > 0x7fffffffu) return fail(ctx, WAVO_EINVAL, "mel features: %llu frames", (unsigned long long)n);
-  wavo_status st = wavo_log_mel(ctx, pcm, samples, 0, n, mel);
-  if (st != WAVO_OK) return st;
+  if (!pcm || !mel) return fail(ctx, WAVO_EINVAL, "mel features: NULL buffer");
   std::lock_guard<std::mutex> g(ctx->mu);
-  void *ws = nullptr;
-  st = workspace(ctx, wv::mel_norm_scratch_bytes((long long)n), &ws);
+  cudaSetDevice(ctx->device);
+  wavo_status st = frontend_tables(ctx);
   if (st != WAVO_OK) return st;
-  CK(wv::launch_mel_norm(mel, (long long)n, ws, ctx->stream), "mel normalisation launch");
+  void *ws = nullptr;
+  st = workspace(ctx, wv::mel_features_scratch_bytes(ctx->sms), &ws);
+  if (st != WAVO_OK) return st;
+  CK(wv::launch_mel_features(pcm, (long long)samples, int(n), ctx->fe_tab, mel, ws, ctx->sms,
+                             ctx->stream),
+     "mel features launch");
   *frames = n;
   return WAVO_OK;
 }
