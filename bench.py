@@ -1042,10 +1042,10 @@ class C5Mel(Workload):
         return [(self.x_host, self.x)]
 
     def launches(self):
-        # mel_features: the log-mel and five normalisation kernels a segment; subsample:
-        # conv0/conv2, the conv3 GEMM and conv5 a segment, then the conv6 GEMM, the flatten and
-        # the output GEMM once.
-        return (6 + 3) * len(self.samples) + 3
+        # mel_features: the log-mel (with the normalisation's sums) and the normalisation a
+        # segment; subsample: conv0/conv2, the conv3 GEMM and conv5 a segment, then the conv6
+        # GEMM, the flatten and the output GEMM once.
+        return (2 + 3) * len(self.samples) + 3
 
     def work(self):
         # Per call. mel_features (a segment, averaged over the segments): HBM bytes (the pcm read

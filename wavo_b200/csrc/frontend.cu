@@ -16,7 +16,8 @@
 //                    For the normalised features it also sums each bin's values and squares
 //                    over the frames it takes (f64, in a fixed order: a warp's frames in turn,
 //                    the CTA's warps in order).
-//   mel_stats_kernel the CTAs' sums in order: the mean, then 1 / (unbiased std + 1e-5).
+//                    The last CTA to finish adds the CTAs' sums in order: the mean, then
+//                    1 / (unbiased std + 1e-5).
 //   mel_norm_kernel  (x - mean)·inv to f32; the last frame zero.
 //   conv02_kernel / dw3s2_kernel / flatten_kernel
 //                    Parakeet's 8x conv subsampling around the pointwise GEMMs
@@ -102,10 +103,12 @@ __device__ __forceinline__ void fe_fetch(const float *__restrict__ pcm, long lon
 __global__ void __launch_bounds__(32 * FE_WARPS, 1)
     log_mel_kernel(const float *__restrict__ pcm, long long n_pcm, long long f0, int frames,
                    const FrontendTables tab, float *__restrict__ mel, int stat_frames,
-                   double *__restrict__ part) {
+                   double *__restrict__ part, double *__restrict__ stats) {
   // part != nullptr: also this CTA's per-bin f64 sums of the features of frames < stat_frames and
-  // of their squares (part[blockIdx][0][m], part[blockIdx][1][m]), its warps added in order.
-  extern __shared__ double fe_smem[];
+  // of their squares (part[blockIdx][0][m], part[blockIdx][1][m]), its warps added in order; the
+  // last CTA to finish adds the CTAs' sums in order and writes each bin's mean (stats[m]) and
+  // 1 / (sqrt(Σ(x − mean)² / (n − 1)) + 1e-5) (stats[128 + m]), Σ(x − mean)² = Σx² − mean·Σx.
+  extern __shared__ __align__(16) double fe_smem[];
   FeShared &sh = *reinterpret_cast<FeShared *>(fe_smem);
   {  // the constant tables, every load in flight at once, before the wait
     constexpr int WORDS = int(sizeof(FeShared) / 16);
@@ -239,30 +242,57 @@ __global__ void __launch_bounds__(32 * FE_WARPS, 1)
   }
   if (part == nullptr) return;  // uniform over the CTA
   __syncthreads();
-  const double *all = acc - warp * 2 * FE_MELS;
+  double *all = acc - warp * 2 * FE_MELS;
   for (int e = int(threadIdx.x); e < 2 * FE_MELS; e += blockDim.x) {
     double v = 0.0;
     for (int w = 0; w < FE_WARPS; ++w) v = __dadd_rn(v, all[w * 2 * FE_MELS + e]);
     part[(long long)blockIdx.x * 2 * FE_MELS + e] = v;
   }
-}
-
-// The CTAs' sums in order (thread m a bin): mean = Σx / n and, from Σx² − mean·Σx (the squared
-// deviations' sum), inv = 1 / (sqrt(Σ(x − mean)² / (n − 1)) + 1e-5).
-__global__ void mel_stats_kernel(const double *__restrict__ part, int ctas, long long n,
-                                 double *__restrict__ mean, double *__restrict__ inv) {
-  griddep_launch_dependents();
-  griddep_wait();
-  const int m = int(threadIdx.x);
-  double sx = 0.0, sq = 0.0;
-  for (int c = 0; c < ctas; ++c) {
-    sx = __dadd_rn(sx, part[(long long)c * 2 * FE_MELS + m]);
-    sq = __dadd_rn(sq, part[(long long)c * 2 * FE_MELS + FE_MELS + m]);
+  // The last CTA (no waiting: the others have published their sums before counting themselves).
+  __threadfence();
+  __syncthreads();
+  __shared__ int is_last;
+  if (threadIdx.x == 0) is_last = atomicAdd(tab.count, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // Thread (g, cp): columns 2cp, 2cp + 1 of the 256 (Σx of the bins, then Σx²) over CTAs
+  // g·per .. (g + 1)·per − 1 in order, 16-byte loads sixteen CTAs at a time; then the G groups in
+  // order.
+  constexpr int G = 32 * FE_WARPS / FE_MELS;
+  const int cp = int(threadIdx.x) % FE_MELS, g = int(threadIdx.x) / FE_MELS;
+  const int ctas = int(gridDim.x), per = (ctas + G - 1) / G;
+  const int c0 = g * per, c1 = min(c0 + per, ctas);
+  double2 sum = make_double2(0.0, 0.0);
+  constexpr int B = 16;
+  for (int c = c0; c < c1; c += B) {
+    double2 v[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j)
+      v[j] = __ldcg(reinterpret_cast<const double2 *>(part + (long long)min(c + j, c1 - 1) * 2 *
+                                                                 FE_MELS) + cp);
+#pragma unroll
+    for (int j = 0; j < B; ++j)
+      if (c + j < c1) sum = make_double2(__dadd_rn(sum.x, v[j].x), __dadd_rn(sum.y, v[j].y));
   }
-  const double mu = sx / double(n);
-  const double ss = fmax(__dsub_rn(sq, __dmul_rn(mu, sx)), 0.0);
-  mean[m] = mu;
-  inv[m] = 1.0 / __dadd_rn(sqrt(ss / double(n - 1)), double(1e-5f));
+  double2 *red = reinterpret_cast<double2 *>(all);  // [G][128] (the warps' sums are spent)
+  red[g * FE_MELS + cp] = sum;
+  __syncthreads();
+  if (threadIdx.x < FE_MELS) {
+    const int m = int(threadIdx.x);
+    const double *r = reinterpret_cast<const double *>(red);  // [G][256]
+    double sx = 0.0, sq = 0.0;
+    for (int k = 0; k < G; ++k) {
+      sx = __dadd_rn(sx, r[k * 2 * FE_MELS + m]);
+      sq = __dadd_rn(sq, r[k * 2 * FE_MELS + FE_MELS + m]);
+    }
+    const long long n = stat_frames;
+    const double mu = sx / double(n);
+    const double ss = fmax(__dsub_rn(sq, __dmul_rn(mu, sx)), 0.0);
+    stats[m] = mu;
+    stats[FE_MELS + m] = 1.0 / __dadd_rn(sqrt(ss / double(n - 1)), double(1e-5f));
+  }
+  if (threadIdx.x == 0) atomicExch(tab.count, 0u);  // for the next launch
 }
 
 __global__ void mel_norm_kernel(float *__restrict__ mel, long long frames,
@@ -374,46 +404,59 @@ __global__ void __launch_bounds__(256, 3) conv02_kernel(const float *__restrict_
   }
 }
 
-// Depthwise 3x3, stride 2, padding 1, + bias over x [t][f][ch] into y [rows][half(f)][ch].
-__global__ void dw3s2_kernel(const float *__restrict__ x, int t, int f, int ch, int rows,
+// Depthwise 3x3, stride 2, padding 1, + bias over x [t][f][ch] into y [rows][half(f)][ch]: a CTA
+// an output row (blockIdx.x) and column (blockIdx.y), a thread a channel.
+__global__ void dw3s2_kernel(const float *__restrict__ x, int t, int f, int ch,
                              const float *__restrict__ w, const float *__restrict__ b,
                              __half *__restrict__ y) {
   griddep_launch_dependents();
   griddep_wait();
-  const int fo_n = (f - 1) / 2 + 1;
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)rows * fo_n * ch) return;
-  const int q = int(i % ch);
-  const int fo = int((i / ch) % fo_n);
-  const int k = int(i / ((long long)fo_n * ch));
-  float v = b[q];
+  const int k = int(blockIdx.x), fo = int(blockIdx.y);
+  __half *out = y + ((long long)k * gridDim.y + fo) * ch;
+  for (int q = int(threadIdx.x); q < ch; q += blockDim.x) {
+    // Every tap's operands loaded at once (a tap outside the image reads a clamped in-range
+    // element and adds nothing), then the products added in tap order.
+    float xv[9], wv[9];
 #pragma unroll
-  for (int tap = 0; tap < 9; ++tap) {
-    const int ti = 2 * k + tap / 3, fi = 2 * fo + tap % 3;
-    if (ti < 1 || ti > t || fi < 1 || fi > f) continue;
-    v = __fadd_rn(v, __fmul_rn(w[tap * ch + q], x[((long long)(ti - 1) * f + fi - 1) * ch + q]));
+    for (int tap = 0; tap < 9; ++tap) {
+      const int ti = min(max(2 * k + tap / 3, 1), t), fi = min(max(2 * fo + tap % 3, 1), f);
+      xv[tap] = x[((long long)(ti - 1) * f + fi - 1) * ch + q];
+      wv[tap] = w[tap * ch + q];
+    }
+    float v = b[q];
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+      const int ti = 2 * k + tap / 3, fi = 2 * fo + tap % 3;  // uniform over the CTA
+      if (ti >= 1 && ti <= t && fi >= 1 && fi <= f) v = __fadd_rn(v, __fmul_rn(wv[tap], xv[tap]));
+    }
+    out[q] = __float2half_rn(v);  // the pointwise GEMM's operand (rounded to f16 there as well)
   }
-  y[i] = __float2half_rn(v);  // the pointwise GEMM's operand (rounded to f16 there as well)
 }
 
-// [t][f][ch] to [t][ch·f] (src/parakeet/cpu.rs:85-90).
-__global__ void flatten_kernel(const float *__restrict__ y, int t, int f, int ch,
-                               __half *__restrict__ h) {
+// [t][16][ch] to [t][ch·16] (src/parakeet/cpu.rs:85-90): a CTA a row (blockIdx.x) and 256
+// channels (blockIdx.y); thread c reads its 16 values (a warp's loads coalesced) and writes them as
+// 32 contiguous bytes of the output GEMM's f16 operand.
+constexpr int FL_F = 16;
+__global__ void __launch_bounds__(256) flatten_kernel(const float *__restrict__ y, int ch,
+                                                      __half *__restrict__ h) {
   griddep_launch_dependents();
   griddep_wait();
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long row = (long long)f * ch;
-  if (i >= (long long)t * row) return;
-  const long long r = i / row;
-  const int e = int(i - r * row);
-  h[i] = __float2half_rn(y[r * row + (e % f) * ch + e / f]);  // the output GEMM's f16 operand
+  const int c = int(blockIdx.y) * 256 + int(threadIdx.x);
+  if (c >= ch) return;
+  const long long row = (long long)blockIdx.x * FL_F * ch;
+  __align__(16) __half o[FL_F];
+#pragma unroll
+  for (int j = 0; j < FL_F; ++j) o[j] = __float2half_rn(y[row + (long long)j * ch + c]);
+  uint4 *d = reinterpret_cast<uint4 *>(h + row + (long long)c * FL_F);
+  d[0] = reinterpret_cast<const uint4 *>(o)[0];
+  d[1] = reinterpret_cast<const uint4 *>(o)[1];
 }
 
 }  // namespace
 
 // ---- tables (host), as src/fft.rs:46-66 and src/parakeet/frontend.rs:30-47, 110-140 build them --
 
-size_t frontend_table_bytes() { return sizeof(FeShared); }
+size_t frontend_table_bytes() { return sizeof(FeShared) + 256; }  // the image, then a counter
 
 cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *out) {
   // The first stage's order (src/fft.rs: all 512 points radix-2 blocks, the even samples before
@@ -478,8 +521,11 @@ cudaError_t frontend_tables_upload(void *dev, cudaStream_t s, FrontendTables *ou
     for (int k = lo[m]; k < hi[m]; ++k) img.fw[k - lo[m]][m] = filters[m * FE_BINS + k];
   }
   cudaError_t e = cudaMemcpyAsync(dev, &img, sizeof(FeShared), cudaMemcpyHostToDevice, s);
+  unsigned *count = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(dev) + sizeof(FeShared));
+  if (e == cudaSuccess) e = cudaMemsetAsync(count, 0, sizeof(unsigned), s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // before the host image is freed
   out->image = dev;
+  out->count = count;
   return e;
 }
 
@@ -517,7 +563,7 @@ cudaError_t launch_log_mel(const float *pcm, long long n_pcm, long long f0, int 
   const int ctas = log_mel_ctas(frames, &e);
   if (e != cudaSuccess) return e;
   return launch_pdl(log_mel_kernel, dim3(ctas), dim3(32 * FE_WARPS), FE_SMEM, s, pcm, n_pcm, f0,
-                    frames, tab, mel, 0, (double *)nullptr);
+                    frames, tab, mel, 0, (double *)nullptr, (double *)nullptr);
 }
 
 size_t mel_features_scratch_bytes(int sms) { return (size_t(sms) * 2 + 2) * FE_MELS * 8; }
@@ -534,9 +580,7 @@ cudaError_t launch_mel_features(const float *pcm, long long n_pcm, int frames,
   double *part = static_cast<double *>(scratch);
   double *mean = part + (long long)sms * 2 * FE_MELS, *inv = mean + FE_MELS;
   if ((e = launch_pdl(log_mel_kernel, dim3(ctas), dim3(32 * FE_WARPS), FE_SMEM, s, pcm, n_pcm,
-                      0LL, frames, tab, mel, int(n), part)) != cudaSuccess ||
-      (e = launch_pdl(mel_stats_kernel, dim3(1), dim3(FE_MELS), 0, s, (const double *)part, ctas,
-                      n, mean, inv)) != cudaSuccess)
+                      0LL, frames, tab, mel, int(n), part, mean)) != cudaSuccess)
     return e;
   const long long total = (long long)frames * FE_MELS;
   return launch_pdl(mel_norm_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, mel,
@@ -557,15 +601,18 @@ cudaError_t launch_conv02(const float *mel, int valid, int t2, int ch, const flo
 
 cudaError_t launch_dw3s2(const float *x, int t, int f, int ch, int rows, const float *w,
                          const float *b, __half *y, cudaStream_t s) {
-  const long long total = (long long)rows * ((f - 1) / 2 + 1) * ch;
-  return launch_pdl(dw3s2_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, x, t, f, ch,
-                    rows, w, b, y);
+  const int fo_n = (f - 1) / 2 + 1;
+  if (rows <= 0) return cudaSuccess;
+  if (fo_n > 65535) return cudaErrorInvalidValue;
+  return launch_pdl(dw3s2_kernel, dim3(unsigned(rows), unsigned(fo_n)), dim3(ch < 256 ? ch : 256),
+                    0, s, x, t, f, ch, w, b, y);
 }
 
 cudaError_t launch_flatten(const float *y, int t, int f, int ch, __half *h, cudaStream_t s) {
-  const long long total = (long long)t * f * ch;
-  return launch_pdl(flatten_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, y, t, f,
-                    ch, h);
+  if (t <= 0) return cudaSuccess;
+  if (f != FL_F || ch % 32 != 0) return cudaErrorInvalidValue;
+  return launch_pdl(flatten_kernel, dim3(unsigned(t), unsigned((ch + 255) / 256)), dim3(256), 0, s,
+                    y, ch, h);
 }
 
 }  // namespace wv

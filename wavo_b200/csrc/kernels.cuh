@@ -190,6 +190,7 @@ cudaError_t launch_gemv(const float *a, long long lda, int wtype, const void *w,
 // as each mel bin's nonzero span of FFT bins.
 struct FrontendTables {
   const void *image;
+  unsigned *count;  // the log-mel CTAs that have published their sums (0 between launches)
 };
 size_t frontend_table_bytes();
 // Fills `dev` (frontend_table_bytes()) with the tables and points `out` at them (waits for `s`).
